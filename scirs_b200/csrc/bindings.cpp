@@ -1,0 +1,49 @@
+// Python bindings of the sm_100a kernels (module scirs_b200._C).
+#include "host_common.h"
+
+namespace scirs {
+void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
+             c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
+             bool accumulate, int64_t splits, int64_t bn_force);
+void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Tensor y, torch::Tensor mean,
+                   torch::Tensor rstd, double eps);
+void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
+                   c10::optional<torch::Tensor> dresid, torch::Tensor dx, torch::Tensor dw, torch::Tensor db,
+                   torch::Tensor part);
+void xent_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss, int64_t V, double grad_scale,
+                  int64_t ignore_index);
+void xent_fwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss, int64_t V, int64_t ignore_index);
+void embedding_fwd(torch::Tensor tok, torch::Tensor wte, c10::optional<torch::Tensor> wpe, torch::Tensor out,
+                   int64_t S);
+void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor dwte, c10::optional<torch::Tensor> dwpe,
+                   int64_t S);
+void bias_grad(torch::Tensor dy, torch::Tensor out);
+void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch::Tensor state2, torch::Tensor grads,
+                c10::optional<torch::Tensor> params16, int64_t n_decay, c10::optional<torch::Tensor> decay_mask,
+                torch::Tensor hp, c10::optional<torch::Tensor> part, c10::optional<torch::Tensor> norm_out);
+void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                    bool causal, double scale);
+void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
+                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
+                    torch::Tensor delta, bool causal, double scale);
+}  // namespace scirs
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "scirs_b200 sm_100a kernels";
+  m.def("gemm", &scirs::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("a"), py::arg("b"), py::arg("out"),
+        py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("bias") = py::none(), py::arg("aux") = py::none(),
+        py::arg("out2") = py::none(), py::arg("accumulate") = false, py::arg("splits") = 0,
+        py::arg("bn_force") = 0);
+  m.def("layernorm_fwd", &scirs::layernorm_fwd);
+  m.def("layernorm_bwd", &scirs::layernorm_bwd);
+  m.def("xent_fwd_bwd", &scirs::xent_fwd_bwd);
+  m.def("xent_fwd", &scirs::xent_fwd);
+  m.def("embedding_fwd", &scirs::embedding_fwd);
+  m.def("embedding_bwd", &scirs::embedding_bwd);
+  m.def("bias_grad", &scirs::bias_grad);
+  m.def("optim_step", &scirs::optim_step);
+  m.def("flash_attn_fwd", &scirs::flash_attn_fwd);
+  m.def("flash_attn_bwd", &scirs::flash_attn_bwd);
+  m.def("status_read_and_clear", &scirs::status_read_and_clear);
+  m.def("num_sms", &scirs::num_sms);
+}

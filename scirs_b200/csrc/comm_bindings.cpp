@@ -1,0 +1,26 @@
+// Python bindings of the NVLink collective kernels (module scirs_b200._comm).
+#include "host_common.h"
+
+namespace scirs {
+std::tuple<int64_t, py::bytes> comm_create(int64_t device, int64_t rank, int64_t world, int64_t area_bytes);
+void comm_open_peers(int64_t id, std::vector<py::bytes> handles);
+void comm_destroy(int64_t id);
+void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double scale, int64_t blocks,
+                    double timeout_s);
+void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, double scale, int64_t blocks,
+                         double timeout_s);
+void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t blocks, double timeout_s);
+std::vector<int64_t> comm_timeout_probe(int64_t device, double timeout_s);
+}  // namespace scirs
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "scirs_b200 in-kernel NVLink collectives";
+  m.def("create", &scirs::comm_create);
+  m.def("open_peers", &scirs::comm_open_peers);
+  m.def("destroy", &scirs::comm_destroy);
+  m.def("allreduce", &scirs::comm_allreduce);
+  m.def("reduce_scatter", &scirs::comm_reduce_scatter);
+  m.def("allgather", &scirs::comm_allgather);
+  m.def("timeout_probe", &scirs::comm_timeout_probe);
+  m.def("status_read_and_clear", &scirs::status_read_and_clear);
+}

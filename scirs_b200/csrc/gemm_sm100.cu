@@ -1,0 +1,515 @@
+// Persistent bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   C[M,N] = op(A) * op(B)  with fp32 accumulation in TMEM and a fused epilogue.
+//
+// Operand forms (row-major storage, "major" = which dimension is contiguous):
+//   A K-major : a is [M, K]           A MN-major : a is [K, M]
+//   B K-major : b is [N, K] (C=A b^T) B MN-major : b is [K, N] (C=A b)
+// so one kernel family serves a Linear layer's forward (x W^T), data
+// gradient (dY W) and weight gradient (dY^T X) without transposes.
+//
+// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      : TMA producer (one thread), fills a STAGES-deep smem ring
+//   warp 1      : owns TMEM; one elected thread issues tcgen05.mma
+//   warps 2..5  : epilogue; tcgen05.ld from TMEM -> fused math -> global
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Reference parity: replaces the SIMT / WMMA GEMMs of the reference
+// (scirs2-core/src/gpu/kernels/gemm_f32.cu:4, scirs2-core/src/gpu/tensor_cores.rs:636,
+// scirs2-linalg/kernels/matmul_f32.cu:159) and the Dense layer's forward and
+// backward products (scirs2-neural/src/layers/dense.rs:174-212, :302-400).
+#include "host_common.h"
+
+namespace scirs {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+enum Epi : int {
+  EPI_BF16 = 0,       // C = acc (+ bias)
+  EPI_BIAS_GELU = 1,  // C2 = acc + bias (pre-activation), C = gelu(C2)
+  EPI_RESID = 2,      // C = acc (+ bias) + aux
+  EPI_DGELU = 3,      // C = acc * gelu'(aux)
+  EPI_F32 = 4,        // C(fp32) = acc, or += acc (atomic) when accumulating / split-K
+};
+
+struct Args {
+  int M, N, K;
+  int num_kb;
+  int splits;
+  int kb_per_split;
+  int m_blocks, n_blocks;
+  int num_units;
+  int group_m;
+  void* C;
+  long ldc;
+  void* C2;
+  long ldc2;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* aux;
+  long ldaux;
+  int atomic_out;
+  DevStatus* st;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void decode_unit(const Args& a, int u, int& m_blk, int& n_blk, int& split) {
+  split = u % a.splits;
+  int t = u / a.splits;
+  // grouped rasterisation: G m-blocks x all n-blocks per group, m fastest
+  int per_group = a.group_m * a.n_blocks;
+  int g = t / per_group;
+  int first_m = g * a.group_m;
+  int gsize = min(a.group_m, a.m_blocks - first_m);
+  int r = t % per_group;
+  m_blk = first_m + r % gsize;
+  n_blk = r / gsize;
+}
+
+template <int BN, int A_MN, int B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args args) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
+        int m_blk, n_blk, split;
+        decode_unit(args, u, m_blk, n_blk, split);
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(args.num_kb, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, args.st, 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + s * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          if (A_MN) {
+            tma_load_2d(sA, &tmA, &full[s], m_blk * BM, kb * BK);
+            tma_load_2d(sA + 8192, &tmA, &full[s], m_blk * BM + 64, kb * BK);
+          } else {
+            tma_load_2d(sA, &tmA, &full[s], kb * BK, m_blk * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h) tma_load_2d(sB + h * 8192, &tmB, &full[s], n_blk * BN + h * 64, kb * BK);
+          } else {
+            tma_load_2d(sB, &tmB, &full[s], kb * BK, n_blk * BN);
+          }
+        }
+      }
+      if (!ok) {
+        // Let copies already in flight land before the CTA exits.
+        for (int j = 1; j <= STAGES && it - j >= 0; ++j) {
+          const int i2 = it - j;
+          mbar_wait(&full[i2 % STAGES], (i2 / STAGES) & 1, nullptr, 0, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x, ++local) {
+        int m_blk, n_blk, split;
+        decode_unit(args, u, m_blk, n_blk, split);
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(args.num_kb, kb0 + args.kb_per_split);
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aph ^ 1, args.st, 2, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, args.st, 3, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t b_base = a_base + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                        : umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                        : umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            tc_mma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+      }
+      // Drain: make sure every MMA this thread issued has completed before
+      // TMEM is released at the end of the kernel.
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int u = blockIdx.x; u < args.num_units; u += gridDim.x, ++local) {
+      int m_blk, n_blk, split;
+      decode_unit(args, u, m_blk, n_blk, split);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], aph, args.st, 4, abort_flag)) break;
+      tc_fence_after();
+      const int row = m_blk * BM + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const int col0 = n_blk * BN + c;
+        if (col0 >= args.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(trow + c, r);
+        tc_wait_ld();
+        if (!row_ok) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (EPI == EPI_F32) {
+          float* out = reinterpret_cast<float*>(args.C) + (long)row * args.ldc + col0;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            if (col0 + g * 4 >= args.N) break;
+            float4 f = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+            if (args.atomic_out)
+              atomicAdd(reinterpret_cast<float4*>(out + 4 * g), f);
+            else
+              *reinterpret_cast<float4*>(out + 4 * g) = f;
+          }
+          continue;
+        }
+        if (EPI != EPI_DGELU && args.bias != nullptr) {
+          const uint4* bp = reinterpret_cast<const uint4*>(args.bias + col0);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (col0 + g * 8 >= args.N) break;
+            uint4 b4 = __ldg(bp + g);
+            uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              v[g * 8 + 2 * e] += bf16_lo(bw[e]);
+              v[g * 8 + 2 * e + 1] += bf16_hi(bw[e]);
+            }
+          }
+        }
+        if (EPI == EPI_RESID || EPI == EPI_DGELU) {
+          const uint4* ap = reinterpret_cast<const uint4*>(args.aux + (long)row * args.ldaux + col0);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (col0 + g * 8 >= args.N) break;
+            uint4 x4 = ap[g];
+            uint32_t xw[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float x0 = bf16_lo(xw[e]), x1 = bf16_hi(xw[e]);
+              if (EPI == EPI_RESID) {
+                v[g * 8 + 2 * e] += x0;
+                v[g * 8 + 2 * e + 1] += x1;
+              } else {
+                v[g * 8 + 2 * e] *= gelu_tanh_grad(x0);
+                v[g * 8 + 2 * e + 1] *= gelu_tanh_grad(x1);
+              }
+            }
+          }
+        }
+        if (EPI == EPI_BIAS_GELU) {
+          uint4* hp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C2) + (long)row * args.ldc2 + col0);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (col0 + g * 8 >= args.N) break;
+            uint4 o;
+            o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+            o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+            o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+            o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+            hp[g] = o;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+        }
+        uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C) + (long)row * args.ldc + col0);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (col0 + g * 8 >= args.N) break;
+          uint4 o;
+          o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+          o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+          o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+          o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+          op[g] = o;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct TmapKey {
+  const void* p;
+  uint64_t inner, outer, stride;
+  uint32_t bi, bo;
+  bool operator==(const TmapKey& o) const {
+    return p == o.p && inner == o.inner && outer == o.outer && stride == o.stride && bi == o.bi && bo == o.bo;
+  }
+};
+struct TmapHash {
+  size_t operator()(const TmapKey& k) const {
+    size_t h = std::hash<const void*>()(k.p);
+    h ^= std::hash<uint64_t>()(k.inner * 1315423911ull + k.outer * 2654435761ull + k.stride * 97 + k.bi * 31 + k.bo);
+    return h;
+  }
+};
+
+static std::mutex g_tm_mu;
+static std::unordered_map<TmapKey, CUtensorMap, TmapHash> g_tmaps;
+
+static CUtensorMap get_tmap(const void* p, uint64_t inner, uint64_t outer, uint64_t stride_bytes, uint32_t bi,
+                            uint32_t bo) {
+  TmapKey k{p, inner, outer, stride_bytes, bi, bo};
+  std::lock_guard<std::mutex> lk(g_tm_mu);
+  auto it = g_tmaps.find(k);
+  if (it != g_tmaps.end()) return it->second;
+  if (g_tmaps.size() > 4096) g_tmaps.clear();
+  CUtensorMap m = make_tmap_2d(p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, inner, outer, stride_bytes, bi, bo,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  g_tmaps.emplace(k, m);
+  return m;
+}
+
+template <int BN, int A_MN, int B_MN, int EPI>
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Args& args, int grid, cudaStream_t stream) {
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM));
+    attr_set[dev] = true;
+  }
+  kern<<<grid, kThreads, Cfg<BN>::SMEM, stream>>>(ta, tb, args);
+  SCIRS_CHECK_LAUNCH();
+}
+
+template <int BN, int A_MN, int B_MN>
+static void launch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Args& args, int grid,
+                       cudaStream_t s) {
+  switch (epi) {
+    case EPI_BF16: launch_t<BN, A_MN, B_MN, EPI_BF16>(ta, tb, args, grid, s); break;
+    case EPI_BIAS_GELU: launch_t<BN, A_MN, B_MN, EPI_BIAS_GELU>(ta, tb, args, grid, s); break;
+    case EPI_RESID: launch_t<BN, A_MN, B_MN, EPI_RESID>(ta, tb, args, grid, s); break;
+    case EPI_DGELU: launch_t<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, args, grid, s); break;
+    case EPI_F32: launch_t<BN, A_MN, B_MN, EPI_F32>(ta, tb, args, grid, s); break;
+    default: TORCH_CHECK(false, "bad epilogue ", epi);
+  }
+}
+
+template <int BN>
+static void launch_bn(int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Args& args,
+                      int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) launch_epi<BN, 0, 0>(epi, ta, tb, args, grid, s);
+  else if (!a_mn && b_mn) launch_epi<BN, 0, 1>(epi, ta, tb, args, grid, s);
+  else if (a_mn && !b_mn) launch_epi<BN, 1, 0>(epi, ta, tb, args, grid, s);
+  else launch_epi<BN, 1, 1>(epi, ta, tb, args, grid, s);
+}
+
+}  // namespace gemm
+
+// Python entry: see scirs_b200/ops/gemm.py for the calling convention.
+//   a        : bf16 2-D, [M,K] (a_mn=0) or [K,M] (a_mn=1)
+//   b        : bf16 2-D, [N,K] (b_mn=0) or [K,N] (b_mn=1)
+//   out      : bf16 [M,N] (epi 0-3) or fp32 [M,N] (epi 4)
+//   out2     : bf16 [M,N] pre-activation (epi 1)
+//   aux      : bf16 [M,N] residual (epi 2) / pre-activation (epi 3)
+//   accumulate (epi 4): add into out instead of overwriting
+//   splits   : split-K factor (0 = automatic; epi 4 only)
+void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
+             c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
+             bool accumulate, int64_t splits, int64_t bn_force) {
+  using namespace gemm;
+  CHECK_CUDA_TENSOR(a);
+  CHECK_CUDA_TENSOR(b);
+  CHECK_CUDA_TENSOR(out);
+  CHECK_DTYPE(a, at::kBFloat16);
+  CHECK_DTYPE(b, at::kBFloat16);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm operands must be 2-D");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm operands need unit inner stride");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm K mismatch: ", K, " vs ", Kb);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm out shape mismatch");
+  TORCH_CHECK(N % 8 == 0, "gemm N must be a multiple of 8");
+  TORCH_CHECK(K % 8 == 0 && M % 8 == 0, "gemm M and K must be multiples of 8");
+  if (epi == EPI_F32) {
+    CHECK_DTYPE(out, at::kFloat);
+  } else {
+    CHECK_DTYPE(out, at::kBFloat16);
+  }
+  TORCH_CHECK(out.stride(0) % 8 == 0, "out row stride must be a multiple of 8 elements");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0, "out must be 16-byte aligned");
+
+  const int dev = a.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  const int sms = num_sms(dev);
+
+  Args args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.num_kb = (int)((K + BK - 1) / BK);
+  args.m_blocks = (int)((M + BM - 1) / BM);
+  args.C = out.data_ptr();
+  args.ldc = out.stride(0);
+  args.st = status_ptr(dev);
+  args.group_m = 16;
+
+  if (bias.has_value() && bias->defined()) {
+    CHECK_DTYPE((*bias), at::kBFloat16);
+    TORCH_CHECK(bias->numel() >= N && bias->is_contiguous(), "bias must hold N contiguous values");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(bias->data_ptr()) & 15) == 0, "bias must be 16-byte aligned");
+    args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (epi == EPI_RESID || epi == EPI_DGELU) {
+    TORCH_CHECK(aux.has_value() && aux->defined(), "epilogue needs aux");
+    CHECK_DTYPE((*aux), at::kBFloat16);
+    TORCH_CHECK(aux->size(0) == M && aux->size(1) == N && aux->stride(1) == 1 && aux->stride(0) % 8 == 0,
+                "aux must be [M,N] with 16-byte aligned rows");
+    args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+    args.ldaux = aux->stride(0);
+  }
+  if (epi == EPI_BIAS_GELU) {
+    TORCH_CHECK(out2.has_value() && out2->defined(), "gelu epilogue needs out2");
+    CHECK_DTYPE((*out2), at::kBFloat16);
+    TORCH_CHECK(out2->size(0) == M && out2->size(1) == N && out2->stride(1) == 1 && out2->stride(0) % 8 == 0,
+                "out2 must be [M,N]");
+    args.C2 = out2->data_ptr();
+    args.ldc2 = out2->stride(0);
+  }
+
+  // Tile width: BN=256 unless BN=128 gives fewer waves for this shape.
+  int BN = 256;
+  {
+    auto cost = [&](int bn) {
+      long tiles = (long)args.m_blocks * ((N + bn - 1) / bn);
+      long waves = (tiles + sms - 1) / sms;
+      return waves * (bn + 48);
+    };
+    if (N <= 128 || cost(128) < cost(256)) BN = 128;
+  }
+  if (bn_force == 128 || bn_force == 256) BN = (int)bn_force;
+  args.n_blocks = (int)((N + BN - 1) / BN);
+  const long tiles = (long)args.m_blocks * args.n_blocks;
+
+  int sp = 1;
+  if (epi == EPI_F32) {
+    if (splits > 0) {
+      sp = (int)splits;
+    } else if (tiles < 2L * sms) {
+      sp = (int)std::min<long>((2L * sms + tiles - 1) / tiles, std::max(1, args.num_kb / 4));
+    }
+    sp = std::max(1, std::min(sp, args.num_kb));
+  }
+  args.kb_per_split = (args.num_kb + sp - 1) / sp;
+  sp = (args.num_kb + args.kb_per_split - 1) / args.kb_per_split;  // every split non-empty
+  args.splits = sp;
+  args.atomic_out = (epi == EPI_F32 && (accumulate || sp > 1)) ? 1 : 0;
+  if (epi == EPI_F32 && sp > 1 && !accumulate) out.zero_();
+  args.num_units = (int)(tiles * sp);
+  const int grid = (int)std::min<long>(args.num_units, sms);
+
+  // Tensor maps (SWIZZLE_128B, 64-element inner boxes).
+  const uint64_t lda_b = (uint64_t)a.stride(0) * 2, ldb_b = (uint64_t)b.stride(0) * 2;
+  CUtensorMap ta = a_mn ? get_tmap(a.data_ptr(), (uint64_t)M, (uint64_t)K, lda_b, 64, 64)
+                        : get_tmap(a.data_ptr(), (uint64_t)K, (uint64_t)M, lda_b, 64, BM);
+  CUtensorMap tb = b_mn ? get_tmap(b.data_ptr(), (uint64_t)N, (uint64_t)K, ldb_b, 64, 64)
+                        : get_tmap(b.data_ptr(), (uint64_t)K, (uint64_t)N, ldb_b, 64, (uint32_t)BN);
+
+  cudaStream_t s = cur_stream();
+  if (BN == 256) launch_bn<256>((int)a_mn, (int)b_mn, (int)epi, ta, tb, args, grid, s);
+  else launch_bn<128>((int)a_mn, (int)b_mn, (int)epi, ta, tb, args, grid, s);
+}
+
+}  // namespace scirs

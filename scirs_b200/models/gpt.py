@@ -1,0 +1,370 @@
+"""GPT-style decoder with a hand-scheduled forward/backward on sm_100a kernels.
+
+This is the framework's flagship training path. Instead of a tape, each
+block's forward and backward are written out as a fixed sequence of fused
+kernels over preallocated activation buffers:
+
+  forward (per block)                    backward (per block, reverse)
+  LN1            layernorm_fwd            fc2  dgrad*gelu' / wgrad / bias grad
+  QKV            gemm (+bias)             fc1  dgrad / wgrad / bias grad
+  attention      flash_attn_fwd           LN2  layernorm_bwd (+residual grad)
+  proj           gemm (+bias +residual)   proj dgrad / wgrad / bias grad
+  LN2            layernorm_fwd            attention flash_attn_bwd
+  fc1            gemm (+bias, GELU)       QKV  dgrad / wgrad / bias grad
+  fc2            gemm (+bias +residual)   LN1  layernorm_bwd (+residual grad)
+
+then the tied LM head (gemm), the fused softmax cross-entropy (forward and
+gradient in one pass, in place over the logits), its two backward GEMMs, the
+embedding backward and ONE fused AdamW launch over the flat parameter
+buffer. Weight gradients are accumulated in fp32 straight into the flat
+gradient buffer; as soon as a block's gradients are final its slice is
+handed to the gradient synchroniser (data parallel), which overlaps the
+NVLink all-reduce with the rest of the backward pass.
+
+Architecture and configuration names follow the reference GPT
+(scirs2-neural/src/models/architectures/gpt.rs:19-62 GPTConfig, :627
+gpt2_small; pre-LN block ln_1 -> attn -> +res -> ln_2 -> mlp(GELU) -> +res,
+final ln_f). Unlike the reference (whose attention is a placeholder
+`q + k + v`, gpt.rs:442-444, and whose backward is the identity, gpt.rs:456)
+this is the full causal-attention model with a tied LM head and exact
+gradients. Dropout is not applied (probabilities must be 0 in this engine).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from ..ops import kernels as K
+from ..utils.flat import FlatParams
+
+
+@dataclass
+class GPTConfig:
+    vocab_size: int = 50257
+    max_position_embeddings: int = 1024
+    hidden_size: int = 768
+    num_hidden_layers: int = 12
+    num_attention_heads: int = 12
+    intermediate_size: int = 3072
+    hidden_act: str = "gelu"
+    hidden_dropout_prob: float = 0.0
+    attention_probs_dropout_prob: float = 0.0
+    layer_norm_eps: float = 1e-5
+    initializer_range: float = 0.02
+    tie_word_embeddings: bool = True
+    pad_vocab_to: int = 128
+
+    @staticmethod
+    def gpt2_small() -> "GPTConfig":
+        return GPTConfig()
+
+    @staticmethod
+    def gpt2_medium() -> "GPTConfig":
+        return GPTConfig(hidden_size=1024, num_hidden_layers=24, num_attention_heads=16, intermediate_size=4096)
+
+    @staticmethod
+    def gpt2_large() -> "GPTConfig":
+        return GPTConfig(hidden_size=1280, num_hidden_layers=36, num_attention_heads=20, intermediate_size=5120)
+
+    @staticmethod
+    def tiny(vocab: int = 512, seq: int = 128) -> "GPTConfig":
+        return GPTConfig(
+            vocab_size=vocab,
+            max_position_embeddings=seq,
+            hidden_size=256,
+            num_hidden_layers=2,
+            num_attention_heads=4,
+            intermediate_size=1024,
+        )
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+    @property
+    def vocab_padded(self) -> int:
+        a = self.pad_vocab_to
+        return (self.vocab_size + a - 1) // a * a
+
+    def num_parameters(self, padded: bool = False) -> int:
+        d, f, L = self.hidden_size, self.intermediate_size, self.num_hidden_layers
+        v = self.vocab_padded if padded else self.vocab_size
+        per_layer = 4 * d * d + 4 * d + 2 * d * f + f + d + 4 * d
+        return v * d + self.max_position_embeddings * d + L * per_layer + 2 * d
+
+    def flops_per_token(self, seq: int) -> float:
+        """Training FLOPs per token (forward + backward), incl. causal attention."""
+        d, f, L = self.hidden_size, self.intermediate_size, self.num_hidden_layers
+        mm = L * (2 * d * 3 * d + 2 * d * d + 2 * 2 * d * f) + 2 * d * self.vocab_size
+        attn = L * 2 * 2 * seq * d * 0.5  # QK^T and PV, causal half
+        return 3.0 * (mm + attn)
+
+
+class _Acts:
+    """Preallocated activations for one micro-batch shape."""
+
+    def __init__(self, cfg: GPTConfig, B: int, S: int, device):
+        M, D, F, L = B * S, cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
+        H = cfg.num_attention_heads
+        bf, f32 = torch.bfloat16, torch.float32
+        e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=device)  # noqa: E731
+        self.B, self.S, self.M = B, S, M
+        self.x = [e(M, D) for _ in range(L + 1)]  # residual stream entering block l
+        self.ln1 = [e(M, D) for _ in range(L)]
+        self.mu1 = [e(M, dt=f32) for _ in range(L)]
+        self.rs1 = [e(M, dt=f32) for _ in range(L)]
+        self.qkv = [e(M, 3 * D) for _ in range(L)]
+        self.att = [e(M, D) for _ in range(L)]
+        self.lse = [e(B, H, S, dt=f32) for _ in range(L)]
+        self.xm = [e(M, D) for _ in range(L)]
+        self.ln2 = [e(M, D) for _ in range(L)]
+        self.mu2 = [e(M, dt=f32) for _ in range(L)]
+        self.rs2 = [e(M, dt=f32) for _ in range(L)]
+        self.h = [e(M, F) for _ in range(L)]
+        self.g = [e(M, F) for _ in range(L)]
+        self.lnf = e(M, D)
+        self.muf = e(M, dt=f32)
+        self.rsf = e(M, dt=f32)
+        self.logits = e(M, cfg.vocab_padded)
+        self.losses = e(M, dt=f32)
+        # backward scratch (shared by all blocks)
+        self.dres = e(M, D)
+        self.dres2 = e(M, D)
+        self.dln = e(M, D)
+        self.datt = e(M, D)
+        self.dqkv = e(M, 3 * D)
+        self.dh = e(M, F)
+        self.dq_acc = e(M * D, dt=f32)
+        self.delta = e(B * H * S, dt=f32)
+        self.ln_part = K.ln_partials(M, D, device)
+
+
+class GPTModel:
+    """GPT decoder trained with fused sm_100a kernels (see module docstring).
+
+    Usage::
+
+        model = GPTModel(GPTConfig.gpt2_small(), device="cuda")
+        opt = model.configure_adamw(lr=6e-4, weight_decay=0.1)
+        loss = model.train_step(tokens, targets)        # tokens/targets [B, S] int64
+    """
+
+    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0):
+        assert cfg.hidden_dropout_prob == 0 and cfg.attention_probs_dropout_prob == 0, "dropout must be 0"
+        assert cfg.head_dim in (64, 128), "head_dim must be 64 or 128"
+        self.cfg = cfg
+        self.device = torch.device(device)
+        D, F, Vp = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_padded
+        fp = FlatParams()
+        # Layout: [wte, wpe] [block 0] ... [block L-1, ln_f]; each block is a
+        # contiguous gradient bucket (ln_f rides with the last block).
+        fp.add("wte", (Vp, D), decay=True)
+        fp.add("wpe", (cfg.max_position_embeddings, D), decay=True)
+        self.bucket_bounds = [(0, fp.mark())]
+        for l in range(cfg.num_hidden_layers):
+            s = fp.mark()
+            p = f"h{l}."
+            fp.add(p + "attn.c_attn.weight", (3 * D, D), True)
+            fp.add(p + "attn.c_proj.weight", (D, D), True)
+            fp.add(p + "mlp.c_fc.weight", (F, D), True)
+            fp.add(p + "mlp.c_proj.weight", (D, F), True)
+            fp.add(p + "attn.c_attn.bias", (3 * D,), False)
+            fp.add(p + "attn.c_proj.bias", (D,), False)
+            fp.add(p + "mlp.c_fc.bias", (F,), False)
+            fp.add(p + "mlp.c_proj.bias", (D,), False)
+            fp.add(p + "ln_1.weight", (D,), False)
+            fp.add(p + "ln_1.bias", (D,), False)
+            fp.add(p + "ln_2.weight", (D,), False)
+            fp.add(p + "ln_2.bias", (D,), False)
+            if l == cfg.num_hidden_layers - 1:
+                fp.add("ln_f.weight", (D,), False)
+                fp.add("ln_f.bias", (D,), False)
+            self.bucket_bounds.append((s, fp.mark()))
+        fp.allocate(self.device)
+        self.fp = fp
+        self._init_weights(seed)
+        self._acts: _Acts | None = None
+        self.grad_sync = None  # set by parallel.DataParallel
+        self.optimizer = None
+        self.kernel_launches = 0
+
+    # ------------------------------------------------------------------ init
+    def _init_weights(self, seed: int):
+        cfg, fp = self.cfg, self.fp
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        std = cfg.initializer_range
+        for name in fp.order:
+            s = fp.slots[name]
+            if name.endswith("ln_1.weight") or name.endswith("ln_2.weight") or name == "ln_f.weight":
+                t = torch.ones(s.shape)
+            elif name.endswith("bias"):
+                t = torch.zeros(s.shape)
+            else:
+                sd = std
+                if name.endswith("c_proj.weight"):  # GPT-2 residual scaling
+                    sd = std / math.sqrt(2 * cfg.num_hidden_layers)
+                t = torch.randn(s.shape, generator=g) * sd
+                if name == "wte":
+                    t[cfg.vocab_size :] = 0.0  # padded rows never receive gradient
+            fp.m(name).copy_(t)
+        fp.sync_bf16()
+
+    def parameters_count(self) -> int:
+        return self.cfg.num_parameters()
+
+    def state_dict(self):
+        sd = self.fp.state_dict()
+        sd["wte"] = sd["wte"][: self.cfg.vocab_size].clone()
+        return sd
+
+    def load_state_dict(self, sd):
+        sd = dict(sd)
+        if "wte" in sd and sd["wte"].shape[0] == self.cfg.vocab_size:
+            w = torch.zeros(self.cfg.vocab_padded, self.cfg.hidden_size)
+            w[: self.cfg.vocab_size] = sd["wte"]
+            sd["wte"] = w
+        self.fp.load_state_dict(sd)
+
+    def acts(self, B: int, S: int) -> _Acts:
+        if self._acts is None or self._acts.B != B or self._acts.S != S:
+            self._acts = None
+            self._acts = _Acts(self.cfg, B, S, self.device)
+        return self._acts
+
+    # --------------------------------------------------------------- forward
+    def _forward(self, tokens: torch.Tensor, A: _Acts):
+        cfg, fp = self.cfg, self.fp
+        B, S, M = A.B, A.S, A.M
+        D, H, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.head_dim
+        eps = cfg.layer_norm_eps
+        n = 0
+        K.embedding_fwd(tokens, fp.w("wte"), fp.w("wpe")[:S], A.x[0], S)
+        n += 1
+        for l in range(cfg.num_hidden_layers):
+            p = f"h{l}."
+            K.layernorm_fwd(A.x[l], fp.w(p + "ln_1.weight"), fp.w(p + "ln_1.bias"), A.ln1[l], A.mu1[l], A.rs1[l], eps)
+            K.gemm(A.ln1[l], fp.w(p + "attn.c_attn.weight"), A.qkv[l], bias=fp.w(p + "attn.c_attn.bias"))
+            q, k, v = A.qkv[l].view(B, S, 3, H, hd).unbind(2)
+            K.flash_attn_fwd(q, k, v, A.att[l].view(B, S, H, hd), A.lse[l], causal=True)
+            K.gemm(A.att[l], fp.w(p + "attn.c_proj.weight"), A.xm[l], epi=K.EPI_RESID,
+                   bias=fp.w(p + "attn.c_proj.bias"), aux=A.x[l])
+            K.layernorm_fwd(A.xm[l], fp.w(p + "ln_2.weight"), fp.w(p + "ln_2.bias"), A.ln2[l], A.mu2[l], A.rs2[l], eps)
+            K.gemm(A.ln2[l], fp.w(p + "mlp.c_fc.weight"), A.g[l], epi=K.EPI_BIAS_GELU,
+                   bias=fp.w(p + "mlp.c_fc.bias"), out2=A.h[l])
+            K.gemm(A.g[l], fp.w(p + "mlp.c_proj.weight"), A.x[l + 1], epi=K.EPI_RESID,
+                   bias=fp.w(p + "mlp.c_proj.bias"), aux=A.xm[l])
+            n += 7
+        L = cfg.num_hidden_layers
+        K.layernorm_fwd(A.x[L], fp.w("ln_f.weight"), fp.w("ln_f.bias"), A.lnf, A.muf, A.rsf, eps)
+        K.gemm(A.lnf, fp.w("wte"), A.logits)
+        n += 2
+        return n
+
+    # -------------------------------------------------------------- backward
+    def _backward(self, tokens: torch.Tensor, A: _Acts):
+        cfg, fp = self.cfg, self.fp
+        B, S, M = A.B, A.S, A.M
+        D, H, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.head_dim
+        L = cfg.num_hidden_layers
+        n = 0
+        dlog = A.logits  # now holds dloss/dlogits
+        # LM head (tied to wte): dx_f = dlogits @ wte ; dwte += dlogits^T @ lnf
+        K.gemm(dlog, fp.w("wte"), A.dln, b_mn=True)
+        K.gemm(dlog, A.lnf, fp.g("wte"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
+        K.layernorm_bwd(A.dln, A.x[L], fp.w("ln_f.weight"), A.muf, A.rsf, A.dres, fp.g("ln_f.weight"),
+                        fp.g("ln_f.bias"), A.ln_part)
+        n += 4
+        for l in reversed(range(L)):
+            p = f"h{l}."
+            # fc2: x[l+1] = xm + g @ W2^T + b2
+            K.gemm(A.dres, fp.w(p + "mlp.c_proj.weight"), A.dh, b_mn=True, epi=K.EPI_DGELU, aux=A.h[l])
+            K.gemm(A.dres, A.g[l], fp.g(p + "mlp.c_proj.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
+            K.bias_grad(A.dres, fp.g(p + "mlp.c_proj.bias"))
+            # fc1: g = gelu(ln2 @ W1^T + b1)
+            K.gemm(A.dh, fp.w(p + "mlp.c_fc.weight"), A.dln, b_mn=True)
+            K.gemm(A.dh, A.ln2[l], fp.g(p + "mlp.c_fc.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
+            K.bias_grad(A.dh, fp.g(p + "mlp.c_fc.bias"))
+            # ln2 (+ residual gradient)
+            K.layernorm_bwd(A.dln, A.xm[l], fp.w(p + "ln_2.weight"), A.mu2[l], A.rs2[l], A.dres2,
+                            fp.g(p + "ln_2.weight"), fp.g(p + "ln_2.bias"), A.ln_part, dresid=A.dres)
+            # proj: xm = x + att @ Wp^T + bp
+            K.gemm(A.dres2, fp.w(p + "attn.c_proj.weight"), A.datt, b_mn=True)
+            K.gemm(A.dres2, A.att[l], fp.g(p + "attn.c_proj.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32,
+                   accumulate=True)
+            K.bias_grad(A.dres2, fp.g(p + "attn.c_proj.bias"))
+            # attention
+            q, k, v = A.qkv[l].view(B, S, 3, H, hd).unbind(2)
+            dq, dk, dv = A.dqkv.view(B, S, 3, H, hd).unbind(2)
+            K.flash_attn_bwd(A.datt.view(B, S, H, hd), q, k, v, A.att[l].view(B, S, H, hd), A.lse[l], dq, dk, dv,
+                             A.dq_acc, A.delta, causal=True)
+            # qkv
+            K.gemm(A.dqkv, fp.w(p + "attn.c_attn.weight"), A.dln, b_mn=True)
+            K.gemm(A.dqkv, A.ln1[l], fp.g(p + "attn.c_attn.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32,
+                   accumulate=True)
+            K.bias_grad(A.dqkv, fp.g(p + "attn.c_attn.bias"))
+            # ln1 (+ residual gradient) -> gradient of x[l]
+            K.layernorm_bwd(A.dln, A.x[l], fp.w(p + "ln_1.weight"), A.mu1[l], A.rs1[l], A.dres,
+                            fp.g(p + "ln_1.weight"), fp.g(p + "ln_1.bias"), A.ln_part, dresid=A.dres2)
+            n += 21
+            if self.grad_sync is not None:
+                self.grad_sync.bucket_ready(l + 1)
+        K.embedding_bwd(tokens, A.dres, fp.g("wte"), fp.g("wpe")[:S], S)
+        n += 1
+        if self.grad_sync is not None:
+            self.grad_sync.bucket_ready(0)
+        return n
+
+    # ----------------------------------------------------------------- API
+    def forward_backward(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One forward + backward; returns the mean loss (device scalar).
+        Gradients are accumulated into the flat gradient buffer."""
+        B, S = tokens.shape
+        A = self.acts(B, S)
+        tok = tokens.reshape(-1)
+        n = self._forward(tok, A)
+        K.xent_fwd_bwd(A.logits, targets.reshape(-1), A.losses, self.cfg.vocab_size, 1.0 / A.M)
+        n += 1
+        n += self._backward(tok, A)
+        self.kernel_launches += n
+        return A.losses.mean()
+
+    def zero_grad(self):
+        self.fp.grad.zero_()
+
+    def configure_adamw(self, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_grad_norm=1.0):
+        from ..optim.fused import FusedFlatOptimizer
+
+        self.optimizer = FusedFlatOptimizer(
+            self.fp, "adamw", lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, max_grad_norm=max_grad_norm
+        )
+        return self.optimizer
+
+    def train_step(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """zero_grad -> forward/backward -> gradient sync -> fused optimizer step."""
+        if self.optimizer is None:
+            self.configure_adamw()
+        self.zero_grad()
+        loss = self.forward_backward(tokens, targets)
+        if self.grad_sync is not None:
+            self.grad_sync.finish()
+        self.optimizer.step()
+        self.kernel_launches += self.optimizer.launches_per_step
+        return loss
+
+    @torch.no_grad()
+    def logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Forward only; returns logits [B, S, vocab_size] (a view)."""
+        B, S = tokens.shape
+        A = self.acts(B, S)
+        self._forward(tokens.reshape(-1), A)
+        return A.logits.view(B, S, -1)[..., : self.cfg.vocab_size]
+
+    @torch.no_grad()
+    def eval_loss(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        B, S = tokens.shape
+        A = self.acts(B, S)
+        self._forward(tokens.reshape(-1), A)
+        K.xent_fwd(A.logits, targets.reshape(-1), A.losses, self.cfg.vocab_size)
+        return A.losses.mean()

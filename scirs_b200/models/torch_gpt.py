@@ -1,0 +1,104 @@
+"""Plain-PyTorch GPT (nn.Module, cuBLAS GEMMs, SDPA attention, autograd).
+
+Two roles:
+  * numerical oracle for :class:`scirs_b200.models.gpt.GPTModel` (same
+    parameter names and layout, loadable from its state_dict);
+  * the PyTorch + cuBLAS + NCCL baseline arm of the benchmark (wrapped in
+    DistributedDataParallel with a bf16 gradient compression hook, autocast
+    bf16 compute over fp32 master weights, fused torch AdamW).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .gpt import GPTConfig
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: GPTConfig):
+        super().__init__()
+        D, Fd = cfg.hidden_size, cfg.intermediate_size
+        self.ln_1 = nn.LayerNorm(D, eps=cfg.layer_norm_eps)
+        self.attn = nn.Module()
+        self.attn.c_attn = nn.Linear(D, 3 * D)
+        self.attn.c_proj = nn.Linear(D, D)
+        self.ln_2 = nn.LayerNorm(D, eps=cfg.layer_norm_eps)
+        self.mlp = nn.Module()
+        self.mlp.c_fc = nn.Linear(D, Fd)
+        self.mlp.c_proj = nn.Linear(Fd, D)
+        self.H = cfg.num_attention_heads
+
+    def forward(self, x):
+        B, S, D = x.shape
+        h = self.ln_1(x)
+        qkv = self.attn.c_attn(h).view(B, S, 3, self.H, D // self.H)
+        q, k, v = qkv.unbind(2)
+        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
+        x = x + self.attn.c_proj(a.transpose(1, 2).reshape(B, S, D))
+        x = x + self.mlp.c_proj(F.gelu(self.mlp.c_fc(self.ln_2(x)), approximate="tanh"))
+        return x
+
+
+class TorchGPT(nn.Module):
+    def __init__(self, cfg: GPTConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.wte = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+        self.wpe = nn.Embedding(cfg.max_position_embeddings, cfg.hidden_size)
+        self.h = nn.ModuleList([Block(cfg) for _ in range(cfg.num_hidden_layers)])
+        self.ln_f = nn.LayerNorm(cfg.hidden_size, eps=cfg.layer_norm_eps)
+        self.apply(self._init)
+        for n, p in self.named_parameters():
+            if n.endswith("c_proj.weight"):
+                nn.init.normal_(p, 0.0, cfg.initializer_range / math.sqrt(2 * cfg.num_hidden_layers))
+
+    def _init(self, m):
+        if isinstance(m, nn.Linear):
+            nn.init.normal_(m.weight, 0.0, self.cfg.initializer_range)
+            nn.init.zeros_(m.bias)
+        elif isinstance(m, nn.Embedding):
+            nn.init.normal_(m.weight, 0.0, self.cfg.initializer_range)
+
+    def forward(self, tokens, targets=None):
+        B, S = tokens.shape
+        x = self.wte(tokens) + self.wpe(torch.arange(S, device=tokens.device))
+        for blk in self.h:
+            x = blk(x)
+        x = self.ln_f(x)
+        logits = x @ self.wte.weight.t()
+        if targets is None:
+            return logits
+        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
+
+    def load_flat_state(self, sd: dict):
+        """Load a GPTModel.state_dict() (names map 1:1; `wte`/`wpe` are the
+        embedding weights)."""
+        own = dict(self.named_parameters())
+        with torch.no_grad():
+            for k, v in sd.items():
+                name = _to_torch_name(k)
+                own[name].copy_(v[: own[name].shape[0]].reshape(own[name].shape))
+
+    def flat_grads(self) -> dict:
+        return {_from_torch_name(n): p.grad for n, p in self.named_parameters()}
+
+
+def _to_torch_name(k: str) -> str:
+    """Engine parameter name -> nn.Module parameter name."""
+    if k in ("wte", "wpe"):
+        return k + ".weight"
+    if k.startswith("h") and "." in k and k[1 : k.index(".")].isdigit():
+        return "h." + k[1:]
+    return k
+
+
+def _from_torch_name(n: str) -> str:
+    if n in ("wte.weight", "wpe.weight"):
+        return n[:-7]
+    if n.startswith("h."):
+        return "h" + n[2:]
+    return n

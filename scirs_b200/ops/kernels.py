@@ -1,0 +1,332 @@
+"""Thin, shape-checked wrappers around the sm_100a kernels.
+
+Every function takes preallocated outputs where the hot path wants them
+(no allocation inside a captured CUDA graph) and has a pure-PyTorch path for
+CPU tensors. The CPU path is the numerical oracle used by the tests.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _ext
+
+# GEMM epilogues (must match gemm_sm100.cu)
+EPI_BF16 = 0
+EPI_BIAS_GELU = 1
+EPI_RESID = 2
+EPI_DGELU = 3
+EPI_F32 = 4
+
+OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
+
+
+class _Stats:
+    """Counts native kernel launches issued through these wrappers."""
+
+    launches = 0
+
+
+STATS = _Stats()
+
+
+def _count(n: int = 1):
+    STATS.launches += n
+
+
+def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    """GELU, tanh approximation (the form the reference's CUDA kernel uses,
+    scirs2-core/src/gpu/kernels/ml/activation.rs:440-457)."""
+    return 0.5 * x * (1.0 + torch.tanh(math.sqrt(2.0 / math.pi) * (x + 0.044715 * x * x * x)))
+
+
+def gelu_tanh_grad(x: torch.Tensor) -> torch.Tensor:
+    k0 = math.sqrt(2.0 / math.pi)
+    u = k0 * (x + 0.044715 * x**3)
+    t = torch.tanh(u)
+    return 0.5 * (1 + t) + 0.5 * x * (1 - t * t) * k0 * (1 + 3 * 0.044715 * x * x)
+
+
+# ---------------------------------------------------------------------------
+# GEMM
+# ---------------------------------------------------------------------------
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    epi: int = EPI_BF16,
+    bias: torch.Tensor | None = None,
+    aux: torch.Tensor | None = None,
+    out2: torch.Tensor | None = None,
+    accumulate: bool = False,
+    splits: int = 0,
+    bn: int = 0,
+) -> torch.Tensor:
+    """out[M,N] = op(a) @ op(b) with a fused epilogue.
+
+    a: [M,K] (a_mn=False) or [K,M] (a_mn=True); b: [N,K] (b_mn=False, i.e.
+    out = a @ b.T) or [K,N] (b_mn=True, out = a @ b).
+
+    Epilogues: EPI_BF16 (+bias), EPI_BIAS_GELU (out2 = pre-activation,
+    out = gelu(out2)), EPI_RESID (+bias +aux), EPI_DGELU (out = acc *
+    gelu'(aux)), EPI_F32 (fp32 out, optionally accumulated).
+    """
+    if a.is_cuda:
+        _ext.kernels().gemm(a, b, out, int(a_mn), int(b_mn), int(epi), bias, aux, out2, accumulate, splits, bn)
+        _count(1)
+        return out
+    A = (a.t() if a_mn else a).float()
+    B = (b if b_mn else b.t()).float()
+    acc = A @ B
+    if epi == EPI_F32:
+        if accumulate:
+            out.add_(acc)
+        else:
+            out.copy_(acc)
+        return out
+    if bias is not None and epi != EPI_DGELU:
+        acc = acc + bias.float()
+    if epi == EPI_RESID:
+        acc = acc + aux.float()
+    elif epi == EPI_DGELU:
+        acc = acc * gelu_tanh_grad(aux.float())
+    elif epi == EPI_BIAS_GELU:
+        out2.copy_(acc)
+        acc = gelu_tanh(acc)
+    out.copy_(acc)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# LayerNorm
+# ---------------------------------------------------------------------------
+def layernorm_fwd(x, w, b, y, mean, rstd, eps=1e-5):
+    if x.is_cuda:
+        _ext.kernels().layernorm_fwd(x, w, b, y, mean, rstd, float(eps))
+        _count(1)
+        return y
+    xf = x.float()
+    mu = xf.mean(-1)
+    var = ((xf - mu[..., None]) ** 2).mean(-1)
+    rs = torch.rsqrt(var + eps)
+    y.copy_((xf - mu[..., None]) * rs[..., None] * w.float() + b.float())
+    mean.copy_(mu.reshape(mean.shape))
+    rstd.copy_(rs.reshape(rstd.shape))
+    return y
+
+
+def layernorm_bwd(dy, x, w, mean, rstd, dx, dw, db, part, dresid=None):
+    """dx = LN backward (+ dresid); dw/db (fp32) are accumulated into."""
+    if x.is_cuda:
+        _ext.kernels().layernorm_bwd(dy, x, w, mean, rstd, dresid, dx, dw, db, part)
+        _count(2)
+        return dx
+    D = x.shape[-1]
+    xf = x.float().reshape(-1, D)
+    g = dy.float().reshape(-1, D)
+    mu = mean.reshape(-1, 1)
+    rs = rstd.reshape(-1, 1)
+    xh = (xf - mu) * rs
+    dw.add_((g * xh).sum(0))
+    db.add_(g.sum(0))
+    gw = g * w.float()
+    o = rs * (gw - gw.mean(-1, keepdim=True) - xh * (gw * xh).mean(-1, keepdim=True))
+    if dresid is not None:
+        o = o + dresid.float().reshape(-1, D)
+    dx.copy_(o.reshape(dx.shape))
+    return dx
+
+
+def ln_partials(n_rows: int, D: int, device) -> torch.Tensor:
+    """Scratch for LayerNorm backward's per-block partial column sums."""
+    if device is not None and torch.device(device).type == "cuda":
+        sms = _ext.kernels().num_sms(torch.device(device).index or 0)
+        nb = max(1, min(2 * sms, (n_rows + 7) // 8))
+    else:
+        nb = 1
+    return torch.empty(nb * 2 * D, dtype=torch.float32, device=device)
+
+
+# ---------------------------------------------------------------------------
+# Cross entropy
+# ---------------------------------------------------------------------------
+def xent_fwd_bwd(logits, targets, loss, V, grad_scale, ignore_index=-100):
+    """In place: logits <- d(mean loss)/d logits * grad_scale; loss[row] = CE."""
+    if logits.is_cuda:
+        _ext.kernels().xent_fwd_bwd(logits, targets, loss, int(V), float(grad_scale), int(ignore_index))
+        _count(1)
+        return loss
+    lf = logits[:, :V].float()
+    lse = torch.logsumexp(lf, -1)
+    valid = (targets != ignore_index) & (targets >= 0) & (targets < V)
+    t = targets.clamp(0, V - 1)
+    l = lse - lf.gather(1, t[:, None])[:, 0]
+    loss.copy_(torch.where(valid, l, torch.zeros_like(l)))
+    p = torch.softmax(lf, -1)
+    p[torch.arange(p.shape[0]), t] -= 1.0
+    p = p * (grad_scale * valid.float())[:, None]
+    logits.zero_()
+    logits[:, :V].copy_(p)
+    return loss
+
+
+def xent_fwd(logits, targets, loss, V, ignore_index=-100):
+    if logits.is_cuda:
+        _ext.kernels().xent_fwd(logits, targets, loss, int(V), int(ignore_index))
+        _count(1)
+        return loss
+    lf = logits[:, :V].float()
+    lse = torch.logsumexp(lf, -1)
+    valid = (targets != ignore_index) & (targets >= 0) & (targets < V)
+    t = targets.clamp(0, V - 1)
+    l = lse - lf.gather(1, t[:, None])[:, 0]
+    loss.copy_(torch.where(valid, l, torch.zeros_like(l)))
+    return loss
+
+
+# ---------------------------------------------------------------------------
+# Embedding
+# ---------------------------------------------------------------------------
+def embedding_fwd(tok, wte, wpe, out, S):
+    if tok.is_cuda:
+        _ext.kernels().embedding_fwd(tok, wte, wpe, out, int(S))
+        _count(1)
+        return out
+    e = wte.float()[tok.reshape(-1)]
+    if wpe is not None:
+        pos = torch.arange(tok.numel(), device=tok.device) % S
+        e = e + wpe.float()[pos]
+    out.copy_(e.reshape(out.shape))
+    return out
+
+
+def embedding_bwd(tok, dout, dwte, dwpe, S):
+    if tok.is_cuda:
+        _ext.kernels().embedding_bwd(tok, dout, dwte, dwpe, int(S))
+        _count(1)
+        return
+    D = dwte.shape[1]
+    g = dout.float().reshape(-1, D)
+    dwte.index_add_(0, tok.reshape(-1), g)
+    if dwpe is not None:
+        pos = torch.arange(tok.numel(), device=tok.device) % S
+        dwpe.index_add_(0, pos, g)
+
+
+def bias_grad(dy, out):
+    """out (fp32, [N]) += column sums of dy [M, N]."""
+    if dy.is_cuda:
+        _ext.kernels().bias_grad(dy, out)
+        _count(1)
+        return out
+    out.add_(dy.float().sum(0))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+def attention_reference(q, k, v, causal, scale):
+    """fp32 reference: q/k/v [B, S, H, D] -> (o [B,S,H,D], lse [B,H,S])."""
+    qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    if causal:
+        S = s.shape[-1]
+        mask = torch.ones(S, S, dtype=torch.bool, device=s.device).triu(1)
+        s = s.masked_fill(mask, float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    p = torch.softmax(s, -1)
+    o = (p @ vf).transpose(1, 2)
+    return o, lse
+
+
+def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
+    """q/k/v/out: [B, S, H, D] token-major views (heads contiguous)."""
+    scale = scale if scale is not None else q.shape[-1] ** -0.5
+    if q.is_cuda:
+        _ext.kernels().flash_attn_fwd(q, k, v, out, lse, bool(causal), float(scale))
+        _count(1)
+        return out
+    o, l = attention_reference(q, k, v, causal, scale)
+    out.copy_(o)
+    lse.copy_(l.reshape(lse.shape))
+    return out
+
+
+def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=True, scale=None):
+    scale = scale if scale is not None else q.shape[-1] ** -0.5
+    if q.is_cuda:
+        _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, bool(causal), float(scale))
+        _count(3)
+        return
+    with torch.enable_grad():
+        qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+        o, _ = attention_reference(qf, kf, vf, causal, scale)
+        gq, gk, gv = torch.autograd.grad(o, (qf, kf, vf), dout.float())
+    dq.copy_(gq)
+    dk.copy_(gk)
+    dv.copy_(gv)
+
+
+# ---------------------------------------------------------------------------
+# Fused optimizer step over flat buffers
+# ---------------------------------------------------------------------------
+def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=None, norm_out=None, decay_mask=None):
+    """One fused step; hp (fp32 [9]) = lr, beta1|momentum|rho, beta2, eps, wd,
+    bias_corr1, bias_corr2, grad multiplier, max_norm."""
+    m = OPT_MODES[mode] if isinstance(mode, str) else int(mode)
+    if params.is_cuda:
+        _ext.kernels().optim_step(
+            m, params, state1, state2, grads, params16, int(n_decay), decay_mask, hp, part, norm_out
+        )
+        _count(2 if part is not None else 1)
+        return
+    h = hp.tolist()
+    lr, b1, b2, eps, wd, bc1, bc2, gmul, max_norm = h[:9]
+    g = grads.float() * gmul
+    if part is not None:
+        norm = float(grads.float().norm()) * abs(gmul)
+        if norm_out is not None:
+            norm_out.fill_(norm)
+        if not math.isfinite(norm):
+            return
+        if max_norm > 0 and norm > max_norm:
+            g = g * (max_norm / (norm + 1e-6))
+    n = params.numel()
+    wdv = torch.zeros(n, dtype=torch.float32, device=params.device)
+    if decay_mask is not None:
+        wdv = decay_mask.repeat_interleave(64)[:n].float() * wd
+    else:
+        wdv[:n_decay] = wd
+    p = params
+    if m in (0, 1):
+        if m == 0:
+            g = g + wdv * p
+        state1.mul_(b1).add_((1 - b1) * g)
+        state2.mul_(b2).add_((1 - b2) * g * g)
+        mh = state1 / bc1
+        vh = state2 / bc2
+        if m == 1:
+            p.mul_(1 - lr * wdv)
+        p.sub_(lr * mh / (vh.sqrt() + eps))
+    elif m == 2:
+        g = g + wdv * p
+        if b1 > 0:
+            state1.mul_(b1).add_(lr * g)
+            p.sub_(state1)
+        else:
+            p.sub_(lr * g)
+    elif m == 3:
+        g = g + wdv * p
+        state1.mul_(b1).add_((1 - b1) * g * g)
+        p.sub_(lr * g / (state1.sqrt() + eps))
+    else:
+        g = g + wdv * p
+        state1.add_(g * g)
+        p.sub_(lr * g / (state1.sqrt() + eps))
+    if params16 is not None:
+        params16.copy_(p)

@@ -1,0 +1,65 @@
+"""Build the scirs_b200 CUDA extension in-tree for sm_100a (B200).
+
+    python setup.py build_ext --inplace
+
+Every kernel is compiled for `-gencode arch=compute_100a,code=sm_100a` only.
+"""
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("scirs_b200", "csrc")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-DNDEBUG",
+    "-U__CUDA_NO_HALF_OPERATORS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
+    "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT162_OPERATORS__",
+]
+if os.environ.get("SCIRS_PTXAS_VERBOSE"):
+    NVCC_FLAGS.append("-Xptxas=-v")
+CXX_FLAGS = ["-O3", "-std=c++17"]
+
+
+def _sources(names):
+    return [os.path.join(CSRC, n) for n in names]
+
+
+ext_modules = [
+    CUDAExtension(
+        name="scirs_b200._C",
+        sources=_sources(
+            [
+                "bindings.cpp",
+                "host_common.cpp",
+                "gemm_sm100.cu",
+                "norm_loss.cu",
+                "optim.cu",
+                "attention.cu",
+            ]
+        ),
+        extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+    ),
+    CUDAExtension(
+        name="scirs_b200._comm",
+        sources=_sources(["comm_bindings.cpp", "host_common.cpp", "comm.cu"]),
+        extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+    ),
+]
+
+setup(
+    name="scirs_b200",
+    version="0.1.0",
+    packages=["scirs_b200"],
+    ext_modules=ext_modules,
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

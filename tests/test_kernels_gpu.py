@@ -1,0 +1,207 @@
+"""Numerics of the sm_100a kernels against PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+from scirs_b200.ops import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-12))
+
+
+def rnd(*s, scale=1.0, dtype=torch.bfloat16, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(*s, generator=g) * scale).to(DEV, dtype)
+
+
+# ---------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K_", [(128, 256, 64), (256, 768, 768), (384, 2304, 768), (200, 136, 72), (1024, 50304, 128)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_layouts(M, N, K_, a_mn, b_mn):
+    a = rnd(K_, M, seed=1) if a_mn else rnd(M, K_, seed=1)
+    b = rnd(K_, N, seed=2) if b_mn else rnd(N, K_, seed=2)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, b, out, a_mn=a_mn, b_mn=b_mn)
+    A = (a.t() if a_mn else a).float()
+    B = (b if b_mn else b.t()).float()
+    ref = A @ B
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_epilogues(bn):
+    M, N, K_ = 512, 768, 256
+    a, w = rnd(M, K_, seed=3), rnd(N, K_, scale=0.1, seed=4)
+    bias, aux = rnd(N, seed=5), rnd(M, N, seed=6)
+    acc = a.float() @ w.float().t()
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, w, out, bias=bias, bn=bn)
+    assert rel_err(out, acc + bias.float()) < 1e-2
+    K.gemm(a, w, out, epi=K.EPI_RESID, bias=bias, aux=aux, bn=bn)
+    assert rel_err(out, acc + bias.float() + aux.float()) < 1e-2
+    pre = torch.empty_like(out)
+    K.gemm(a, w, out, epi=K.EPI_BIAS_GELU, bias=bias, out2=pre, bn=bn)
+    h = acc + bias.float()
+    assert rel_err(pre, h) < 1e-2
+    assert rel_err(out, K.gelu_tanh(h)) < 1e-2
+    K.gemm(a, w, out, epi=K.EPI_DGELU, aux=aux, bn=bn)
+    assert rel_err(out, acc * K.gelu_tanh_grad(aux.float())) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [0, 1, 3])
+def test_gemm_f32_wgrad_accumulate(splits):
+    Mtok, N, K_ = 4096, 768, 384
+    dy, x = rnd(Mtok, N, seed=7), rnd(Mtok, K_, seed=8)
+    out = torch.zeros(N, K_, device=DEV, dtype=torch.float32)
+    K.gemm(dy, x, out, a_mn=True, b_mn=True, epi=K.EPI_F32, splits=splits)
+    ref = dy.float().t() @ x.float()
+    assert rel_err(out, ref) < 5e-3
+    K.gemm(dy, x, out, a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True, splits=splits)
+    assert rel_err(out, 2 * ref) < 5e-3
+
+
+def test_gemm_large_m_persistent():
+    M, N, K_ = 8192, 3072, 768
+    a, b = rnd(M, K_, seed=9), rnd(N, K_, scale=0.05, seed=10)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, b, out)
+    assert rel_err(out, a.float() @ b.float().t()) < 1e-2
+
+
+# ---------------------------------------------------------------------------- LayerNorm
+@pytest.mark.parametrize("D", [256, 768, 1024, 2048, 96])
+def test_layernorm(D):
+    M = 1000
+    x, w, b = rnd(M, D, seed=1), rnd(D, seed=2) * 0.5 + 1, rnd(D, seed=3)
+    y = torch.empty_like(x)
+    mu = torch.empty(M, device=DEV)
+    rs = torch.empty(M, device=DEV)
+    K.layernorm_fwd(x, w, b, y, mu, rs, 1e-5)
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    bf = b.float().requires_grad_(True)
+    ref = torch.nn.functional.layer_norm(xf, (D,), wf, bf, 1e-5)
+    assert rel_err(y, ref) < 1e-2
+    dy, dres = rnd(M, D, seed=4), rnd(M, D, seed=5)
+    ref.backward(dy.float())
+    dx = torch.empty_like(x)
+    dw = torch.zeros(D, device=DEV)
+    db = torch.zeros(D, device=DEV)
+    part = K.ln_partials(M, D, DEV)
+    K.layernorm_bwd(dy, x, w, mu, rs, dx, dw, db, part, dresid=dres)
+    assert rel_err(dx, xf.grad + dres.float()) < 1e-2
+    assert rel_err(dw, wf.grad) < 1e-3
+    assert rel_err(db, bf.grad) < 1e-3
+
+
+# ---------------------------------------------------------------------------- cross entropy
+@pytest.mark.parametrize("V,Vp", [(50257, 50304), (1000, 1024), (10, 16)])
+def test_xent(V, Vp):
+    M = 64
+    logits = rnd(M, Vp, scale=2.0, seed=1)
+    tgt = torch.randint(0, V, (M,), device=DEV)
+    tgt[3] = -100
+    ref_in = logits[:, :V].float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(ref_in, tgt, reduction="none", ignore_index=-100)
+    ref.sum().backward()
+    loss = torch.empty(M, device=DEV)
+    lg = logits.clone()
+    K.xent_fwd_bwd(lg, tgt, loss, V, 1.0)
+    assert torch.allclose(loss, ref, atol=2e-2, rtol=1e-2)
+    assert rel_err(lg[:, :V], ref_in.grad) < 1e-2
+    assert float(lg[:, V:].float().abs().max()) == 0.0
+    loss2 = torch.empty(M, device=DEV)
+    K.xent_fwd(logits, tgt, loss2, V)
+    assert torch.allclose(loss2, ref, atol=2e-2, rtol=1e-2)
+
+
+# ---------------------------------------------------------------------------- embedding / bias grad
+def test_embedding_and_bias_grad():
+    V, D, S, B = 1000, 768, 128, 4
+    wte, wpe = rnd(V, D, seed=1), rnd(S, D, seed=2)
+    tok = torch.randint(0, V, (B * S,), device=DEV)
+    out = torch.empty(B * S, D, device=DEV, dtype=torch.bfloat16)
+    K.embedding_fwd(tok, wte, wpe, out, S)
+    ref = wte.float()[tok] + wpe.float()[torch.arange(B * S, device=DEV) % S]
+    assert rel_err(out, ref) < 1e-2
+    dout = rnd(B * S, D, seed=3)
+    dwte = torch.zeros(V, D, device=DEV)
+    dwpe = torch.zeros(S, D, device=DEV)
+    K.embedding_bwd(tok, dout, dwte, dwpe, S)
+    r1 = torch.zeros(V, D, device=DEV).index_add_(0, tok, dout.float())
+    r2 = torch.zeros(S, D, device=DEV).index_add_(0, torch.arange(B * S, device=DEV) % S, dout.float())
+    assert rel_err(dwte, r1) < 1e-4 and rel_err(dwpe, r2) < 1e-4
+    bg = torch.zeros(D, device=DEV)
+    K.bias_grad(dout, bg)
+    assert rel_err(bg, dout.float().sum(0)) < 1e-4
+
+
+# ---------------------------------------------------------------------------- attention
+@pytest.mark.parametrize("B,S,H,HD,causal", [(2, 256, 4, 64, True), (1, 197, 3, 64, False), (1, 384, 2, 128, True),
+                                             (2, 1024, 2, 64, True)])
+def test_flash_attention(B, S, H, HD, causal):
+    qkv = rnd(B, S, 3, H, HD, seed=11)
+    q, k, v = qkv.unbind(2)
+    out = torch.empty(B, S, H, HD, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(B, H, S, device=DEV)
+    scale = HD ** -0.5
+    K.flash_attn_fwd(q, k, v, out, lse, causal, scale)
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    o_ref, lse_ref = K.attention_reference(qf, kf, vf, causal, scale)
+    assert rel_err(out, o_ref) < 1e-2
+    assert torch.allclose(lse, lse_ref, atol=1e-2)
+    dout = rnd(B, S, H, HD, seed=12)
+    o_ref.backward(dout.float())
+    dqkv = torch.empty_like(qkv)
+    dq, dk, dv = dqkv.unbind(2)
+    dq_acc = torch.empty(B * S * H * HD, device=DEV)
+    delta = torch.empty(B * H * S, device=DEV)
+    K.flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal, scale)
+    assert rel_err(dq, qf.grad) < 2e-2
+    assert rel_err(dk, kf.grad) < 2e-2
+    assert rel_err(dv, vf.grad) < 2e-2
+
+
+# ---------------------------------------------------------------------------- optimizer
+@pytest.mark.parametrize("mode", ["adam", "adamw", "sgd", "rmsprop", "adagrad"])
+def test_fused_optimizer(mode):
+    n = 10000 + 64 * 3
+    p = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV)
+    s1, s2 = torch.rand(n, device=DEV), torch.rand(n, device=DEV)
+    hp = torch.tensor([1e-2, 0.9, 0.99, 1e-8, 0.05, 1 - 0.9**3, 1 - 0.99**3, 0.5, 0.0], device=DEV)
+    ref = [t.cpu().clone() for t in (p, s1, s2)]
+    p16 = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    K.optim_step(mode, p, s1, s2, g, p16, n // 2, hp)
+    rp, r1, r2 = ref
+    K.optim_step(mode, rp, r1, r2, g.cpu(), None, n // 2, hp.cpu())
+    assert torch.allclose(p.cpu(), rp, atol=1e-5, rtol=1e-5)
+    assert torch.allclose(p16.float().cpu(), rp, atol=1e-2, rtol=1e-2)
+
+
+def test_fused_optimizer_clip_and_skip():
+    n = 4096
+    p = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV) * 10
+    s1, s2 = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    hp = torch.tensor([1e-2, 0.9, 0.99, 1e-8, 0.0, 0.1, 0.01, 1.0, 1.0], device=DEV)
+    part = torch.zeros(1024, device=DEV)
+    norm = torch.zeros(1, device=DEV)
+    ref = [t.cpu().clone() for t in (p, s1, s2)]
+    K.optim_step("adamw", p, s1, s2, g, None, n, hp, part=part, norm_out=norm)
+    rn = torch.zeros(1)
+    K.optim_step("adamw", ref[0], ref[1], ref[2], g.cpu(), None, n, hp.cpu(), part=torch.zeros(1), norm_out=rn)
+    assert abs(float(norm) - float(g.norm())) / float(g.norm()) < 1e-4
+    assert torch.allclose(p.cpu(), ref[0], atol=1e-5)
+    g[5] = float("inf")
+    before = p.clone()
+    K.optim_step("adamw", p, s1, s2, g, None, n, hp, part=part, norm_out=norm)
+    assert torch.equal(p, before)
