@@ -4,12 +4,12 @@
 namespace scirs {
 void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
              c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
-             bool accumulate, int64_t splits, int64_t bn_force);
+             bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad);
 void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Tensor y, torch::Tensor mean,
                    torch::Tensor rstd, double eps);
 void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
                    c10::optional<torch::Tensor> dresid, torch::Tensor dx, torch::Tensor dw, torch::Tensor db,
-                   torch::Tensor part);
+                   torch::Tensor part, c10::optional<torch::Tensor> dsum);
 void xent_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss, int64_t V, double grad_scale,
                   int64_t ignore_index);
 void xent_fwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss, int64_t V, int64_t ignore_index);
@@ -33,7 +33,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &scirs::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("a"), py::arg("b"), py::arg("out"),
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("bias") = py::none(), py::arg("aux") = py::none(),
         py::arg("out2") = py::none(), py::arg("accumulate") = false, py::arg("splits") = 0,
-        py::arg("bn_force") = 0);
+        py::arg("bn_force") = 0, py::arg("bias_grad") = py::none());
   m.def("layernorm_fwd", &scirs::layernorm_fwd);
   m.def("layernorm_bwd", &scirs::layernorm_bwd);
   m.def("xent_fwd_bwd", &scirs::xent_fwd_bwd);

@@ -8,10 +8,12 @@
 // so one kernel family serves a Linear layer's forward (x W^T), data
 // gradient (dY W) and weight gradient (dY^T X) without transposes.
 //
-// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+// CTA layout (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      : TMA producer (one thread), fills a STAGES-deep smem ring
 //   warp 1      : owns TMEM; one elected thread issues tcgen05.mma
-//   warps 2..5  : epilogue; tcgen05.ld from TMEM -> fused math -> global
+//   warps 2..9  : epilogue; tcgen05.ld from TMEM -> fused math -> global
+//                 (warp w reads TMEM lane quarter w%4; warps 2-5 take the
+//                 left half of the tile's columns, warps 6-9 the right half)
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -26,7 +28,8 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiWarps = 8;
 
 enum Epi : int {
   EPI_BF16 = 0,       // C = acc (+ bias)
@@ -51,6 +54,7 @@ struct Args {
   const __nv_bfloat16* bias;
   const __nv_bfloat16* aux;
   long ldaux;
+  float* bias_grad;  // EPI_DGELU: += column sums of the output (fp32 [N])
   int atomic_out;
   DevStatus* st;
 };
@@ -105,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -213,6 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // two warps per lane quarter; each takes one half of the tile's columns
+    const int c_begin = (warp < 6) ? 0 : BN / 2;
     int local = 0;
     for (int u = blockIdx.x; u < args.num_units; u += gridDim.x, ++local) {
       int m_blk, n_blk, split;
@@ -225,16 +231,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < args.M;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = c_begin; c < c_begin + BN / 2; c += 32) {
         const int col0 = n_blk * BN + c;
         if (col0 >= args.N) break;  // warp-uniform
         uint32_t r[32];
         tmem_ld_32x32b_x32(trow + c, r);
         tc_wait_ld();
-        if (!row_ok) continue;
+        // the dGELU epilogue keeps invalid rows (as zeros) for its column sums
+        if (EPI != EPI_DGELU && !row_ok) continue;
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        for (int j = 0; j < 32; ++j) v[j] = row_ok ? __uint_as_float(r[j]) : 0.f;
         if (EPI == EPI_F32) {
           float* out = reinterpret_cast<float*>(args.C) + (long)row * args.ldc + col0;
 #pragma unroll
@@ -262,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (EPI == EPI_RESID || EPI == EPI_DGELU) {
+        if ((EPI == EPI_RESID || EPI == EPI_DGELU) && row_ok) {
           const uint4* ap = reinterpret_cast<const uint4*>(args.aux + (long)row * args.ldaux + col0);
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
@@ -297,16 +304,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
         }
-        uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C) + (long)row * args.ldc + col0);
+        if (row_ok) {
+          uint4* op =
+              reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C) + (long)row * args.ldc + col0);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (col0 + g * 8 >= args.N) break;
-          uint4 o;
-          o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-          o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-          o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-          o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-          op[g] = o;
+          for (int g = 0; g < 4; ++g) {
+            if (col0 + g * 8 >= args.N) break;
+            uint4 o;
+            o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+            o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+            o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+            o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+            op[g] = o;
+          }
+        }
+        if (EPI == EPI_DGELU && args.bias_grad != nullptr) {
+          // Column sums over this warp's 32 rows: butterfly reduce-scatter,
+          // after which lane l holds the sum of column col0 + l.
+#pragma unroll
+          for (int s = 16; s >= 1; s >>= 1) {
+            const bool upper = (lane & s) != 0;
+#pragma unroll
+            for (int i = 0; i < s; ++i) {
+              const float send = upper ? v[i] : v[i + s];
+              const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+              v[i] = (upper ? v[i + s] : v[i]) + recv;
+            }
+          }
+          if (col0 + lane < args.N) atomicAdd(args.bias_grad + col0 + lane, v[0]);
         }
       }
       tc_fence_before();
@@ -403,10 +428,11 @@ static void launch_bn(int a_mn, int b_mn, int epi, const CUtensorMap& ta, const 
 //   out2     : bf16 [M,N] pre-activation (epi 1)
 //   aux      : bf16 [M,N] residual (epi 2) / pre-activation (epi 3)
 //   accumulate (epi 4): add into out instead of overwriting
+//   bias_grad (epi 3)  : fp32 [N], accumulates the column sums of out
 //   splits   : split-K factor (0 = automatic; epi 4 only)
 void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
              c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
-             bool accumulate, int64_t splits, int64_t bn_force) {
+             bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad) {
   using namespace gemm;
   CHECK_CUDA_TENSOR(a);
   CHECK_CUDA_TENSOR(b);
@@ -460,6 +486,12 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
     args.ldaux = aux->stride(0);
   }
+  if (bias_grad.has_value() && bias_grad->defined()) {
+    TORCH_CHECK(epi == EPI_DGELU, "fused bias gradient is only available with the dGELU epilogue");
+    CHECK_DTYPE((*bias_grad), at::kFloat);
+    TORCH_CHECK(bias_grad->numel() == N && bias_grad->is_contiguous(), "bias_grad must be fp32 [N]");
+    args.bias_grad = bias_grad->data_ptr<float>();
+  }
   if (epi == EPI_BIAS_GELU) {
     TORCH_CHECK(out2.has_value() && out2->defined(), "gelu epilogue needs out2");
     CHECK_DTYPE((*out2), at::kBFloat16);
@@ -470,6 +502,9 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   }
 
   // Tile width: BN=256 unless BN=128 gives fewer waves for this shape.
+  // Split-K (fp32 outputs only) turns a few large-K tiles into enough work
+  // units to fill every SM.
+  const bool can_split = (epi == EPI_F32);
   int BN = 256;
   {
     auto cost = [&](int bn) {
@@ -477,18 +512,30 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
       long waves = (tiles + sms - 1) / sms;
       return waves * (bn + 48);
     };
-    if (N <= 128 || cost(128) < cost(256)) BN = 128;
+    if (N <= 128 || (!can_split && cost(128) < cost(256))) BN = 128;
   }
   if (bn_force == 128 || bn_force == 256) BN = (int)bn_force;
   args.n_blocks = (int)((N + BN - 1) / BN);
   const long tiles = (long)args.m_blocks * args.n_blocks;
 
   int sp = 1;
-  if (epi == EPI_F32) {
+  if (can_split) {
     if (splits > 0) {
       sp = (int)splits;
     } else if (tiles < 2L * sms) {
-      sp = (int)std::min<long>((2L * sms + tiles - 1) / tiles, std::max(1, args.num_kb / 4));
+      // choose the split that fills whole waves best (mild penalty per split)
+      const int max_sp = std::max(1, std::min(16, args.num_kb / 4));
+      double best = -1e9;
+      for (int s = 1; s <= max_sp; ++s) {
+        const double units = (double)tiles * s;
+        const double waves = std::ceil(units / sms);
+        const double eff = units / (waves * sms);
+        const double score = eff - 0.01 * s - (units < sms ? 0.5 : 0.0);
+        if (score > best) {
+          best = score;
+          sp = s;
+        }
+      }
     }
     sp = std::max(1, std::min(sp, args.num_kb));
   }

@@ -149,9 +149,9 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const bf16* __restrict__ dy
   const int wib = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int sub = (wib % RW) * 32 + lane;
-  float dg[NV * 8], db[NV * 8];
+  float dg[NV * 8], db[NV * 8], ds[NV * 8];
 #pragma unroll
-  for (int i = 0; i < NV * 8; ++i) dg[i] = db[i] = 0.f;
+  for (int i = 0; i < NV * 8; ++i) dg[i] = db[i] = ds[i] = 0.f;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
 
   for (int base = blockIdx.x * RPB; base < M; base += gridDim.x * RPB) {
@@ -201,15 +201,18 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const bf16* __restrict__ dy
 #pragma unroll
           for (int e = 0; e < 8; ++e) o[e] += r8[e];
         }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ds[8 * i + e] += o[e];
         dxr[sub + 32 * RW * i] = pack8(o);
       }
     }
   }
   // Reduce the RPB row groups' partial column sums through shared memory.
   // Columns held by thread `sub`, vector i: (sub + 32*RW*i)*8 + e.
-  __shared__ float sg[8 / RW][RW * 256], sb[8 / RW][RW * 256];
-  float* out_g = part + (long)blockIdx.x * 2 * D;
+  __shared__ float sg[8 / RW][RW * 256], sb[8 / RW][RW * 256], ss[8 / RW][RW * 256];
+  float* out_g = part + (long)blockIdx.x * 3 * D;
   float* out_b = out_g + D;
+  float* out_s = out_b + D;
   const int grp = wib / RW;
 #pragma unroll 1
   for (int i = 0; i < NV; ++i) {
@@ -218,18 +221,21 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const bf16* __restrict__ dy
     for (int e = 0; e < 8; ++e) {
       sg[grp][sub * 8 + e] = dg[8 * i + e];
       sb[grp][sub * 8 + e] = db[8 * i + e];
+      ss[grp][sub * 8 + e] = ds[8 * i + e];
     }
     __syncthreads();
     for (int c = threadIdx.x; c < RW * 256; c += 256) {
-      float a = 0.f, bb = 0.f;
+      float a = 0.f, bb = 0.f, cc = 0.f;
 #pragma unroll
       for (int k = 0; k < 8 / RW; ++k) {
         a += sg[k][c];
         bb += sb[k][c];
+        cc += ss[k][c];
       }
       const int col = ((c >> 3) + 32 * RW * i) * 8 + (c & 7);
       out_g[col] = a;
       out_b[col] = bb;
+      out_s[col] = cc;
     }
   }
 }
@@ -242,9 +248,10 @@ __global__ void __launch_bounds__(256) ln_bwd_generic(const bf16* __restrict__ d
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int nw = gridDim.x * 8;
-  float* out_g = part + (long)blockIdx.x * 2 * D;
+  float* out_g = part + (long)blockIdx.x * 3 * D;
   float* out_b = out_g + D;
-  for (int j = threadIdx.x; j < 2 * D; j += blockDim.x) out_g[j] = 0.f;
+  float* out_s = out_b + D;
+  for (int j = threadIdx.x; j < 3 * D; j += blockDim.x) out_g[j] = 0.f;
   __syncthreads();
   for (int row = gw; row < M; row += nw) {
     const bf16* xr = x + (long)row * D;
@@ -267,20 +274,25 @@ __global__ void __launch_bounds__(256) ln_bwd_generic(const bf16* __restrict__ d
       float g = __bfloat162float(dyr[j]) * __bfloat162float(w[j]);
       float o = rs * (g - s1 - xh * s2);
       if (dresid) o += __bfloat162float(dresid[(long)row * D + j]);
+      atomicAdd(&out_s[j], o);
       dx[(long)row * D + j] = __float2bfloat16(o);
     }
   }
 }
 
-// Sum per-block partials [nb, 2, D] into fp32 gradients (accumulating).
+// Sum per-block partials [nb, 3, D] into fp32 gradients (accumulating):
+// dgamma, dbeta and (optional) the column sum of the produced dx, which is
+// the bias gradient of the projection that wrote the residual stream.
 __global__ void ln_bwd_reduce(const float* __restrict__ part, int nb, int D, float* __restrict__ dw,
-                              float* __restrict__ db) {
+                              float* __restrict__ db, float* __restrict__ dsum) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= 2 * D) return;
+  if (c >= 3 * D) return;
+  if (c >= 2 * D && dsum == nullptr) return;
   float s = 0.f;
-  for (int k = 0; k < nb; ++k) s += part[(long)k * 2 * D + c];
+  for (int k = 0; k < nb; ++k) s += part[(long)k * 3 * D + c];
   if (c < D) dw[c] += s;
-  else db[c - D] += s;
+  else if (c < 2 * D) db[c - D] += s;
+  else dsum[c - 2 * D] += s;
 }
 
 // ===========================================================================
@@ -540,10 +552,10 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
   SCIRS_CHECK_LAUNCH();
 }
 
-// part: scratch fp32 [nblocks, 2, D]; dw/db fp32 [D] accumulated into.
+// part: scratch fp32 [nblocks, 3, D]; dw/db (and optional dsum = colsum(dx)) fp32 [D] accumulated into.
 void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
                    c10::optional<torch::Tensor> dresid, torch::Tensor dx, torch::Tensor dw, torch::Tensor db,
-                   torch::Tensor part) {
+                   torch::Tensor part, c10::optional<torch::Tensor> dsum) {
   CHECK_CONTIG(dy);
   CHECK_CONTIG(x);
   CHECK_CONTIG(dx);
@@ -551,7 +563,7 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   const int M = (int)(x.numel() / D);
   CHECK_DTYPE(dw, at::kFloat);
   CHECK_DTYPE(db, at::kFloat);
-  const int nb = (int)(part.numel() / (2 * D));
+  const int nb = (int)(part.numel() / (3 * D));
   TORCH_CHECK(nb >= 1, "part too small");
   c10::cuda::CUDAGuard g(x.get_device());
   auto s = cur_stream();
@@ -578,7 +590,13 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   }
 #undef LNB
   SCIRS_CHECK_LAUNCH();
-  ln_bwd_reduce<<<(2 * D + 255) / 256, 256, 0, s>>>(pp, nb, D, dw.data_ptr<float>(), db.data_ptr<float>());
+  float* dsp = nullptr;
+  if (dsum.has_value() && dsum->defined()) {
+    CHECK_DTYPE((*dsum), at::kFloat);
+    TORCH_CHECK(dsum->numel() == D, "dsum must have D entries");
+    dsp = dsum->data_ptr<float>();
+  }
+  ln_bwd_reduce<<<(3 * D + 255) / 256, 256, 0, s>>>(pp, nb, D, dw.data_ptr<float>(), db.data_ptr<float>(), dsp);
   SCIRS_CHECK_LAUNCH();
 }
 

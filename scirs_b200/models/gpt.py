@@ -273,27 +273,29 @@ class GPTModel:
         # LM head (tied to wte): dx_f = dlogits @ wte ; dwte += dlogits^T @ lnf
         K.gemm(dlog, fp.w("wte"), A.dln, b_mn=True)
         K.gemm(dlog, A.lnf, fp.g("wte"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
+        # colsum(d x[L]) is the bias gradient of the last block's fc2
         K.layernorm_bwd(A.dln, A.x[L], fp.w("ln_f.weight"), A.muf, A.rsf, A.dres, fp.g("ln_f.weight"),
-                        fp.g("ln_f.bias"), A.ln_part)
+                        fp.g("ln_f.bias"), A.ln_part, dsum=fp.g(f"h{L - 1}.mlp.c_proj.bias"))
         n += 4
         for l in reversed(range(L)):
             p = f"h{l}."
-            # fc2: x[l+1] = xm + g @ W2^T + b2
-            K.gemm(A.dres, fp.w(p + "mlp.c_proj.weight"), A.dh, b_mn=True, epi=K.EPI_DGELU, aux=A.h[l])
+            # fc2: x[l+1] = xm + g @ W2^T + b2  (its bias gradient, colsum(dres),
+            # was produced by the LayerNorm backward that wrote dres)
+            # dh = (dres @ W2) * gelu'(h), with colsum(dh) = fc1 bias gradient fused in
+            K.gemm(A.dres, fp.w(p + "mlp.c_proj.weight"), A.dh, b_mn=True, epi=K.EPI_DGELU, aux=A.h[l],
+                   bias_grad=fp.g(p + "mlp.c_fc.bias"))
             K.gemm(A.dres, A.g[l], fp.g(p + "mlp.c_proj.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
-            K.bias_grad(A.dres, fp.g(p + "mlp.c_proj.bias"))
             # fc1: g = gelu(ln2 @ W1^T + b1)
             K.gemm(A.dh, fp.w(p + "mlp.c_fc.weight"), A.dln, b_mn=True)
             K.gemm(A.dh, A.ln2[l], fp.g(p + "mlp.c_fc.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
-            K.bias_grad(A.dh, fp.g(p + "mlp.c_fc.bias"))
-            # ln2 (+ residual gradient)
+            # ln2 (+ residual gradient); colsum(dres2) = attention proj bias gradient
             K.layernorm_bwd(A.dln, A.xm[l], fp.w(p + "ln_2.weight"), A.mu2[l], A.rs2[l], A.dres2,
-                            fp.g(p + "ln_2.weight"), fp.g(p + "ln_2.bias"), A.ln_part, dresid=A.dres)
+                            fp.g(p + "ln_2.weight"), fp.g(p + "ln_2.bias"), A.ln_part, dresid=A.dres,
+                            dsum=fp.g(p + "attn.c_proj.bias"))
             # proj: xm = x + att @ Wp^T + bp
             K.gemm(A.dres2, fp.w(p + "attn.c_proj.weight"), A.datt, b_mn=True)
             K.gemm(A.dres2, A.att[l], fp.g(p + "attn.c_proj.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32,
                    accumulate=True)
-            K.bias_grad(A.dres2, fp.g(p + "attn.c_proj.bias"))
             # attention
             q, k, v = A.qkv[l].view(B, S, 3, H, hd).unbind(2)
             dq, dk, dv = A.dqkv.view(B, S, 3, H, hd).unbind(2)
@@ -304,10 +306,12 @@ class GPTModel:
             K.gemm(A.dqkv, A.ln1[l], fp.g(p + "attn.c_attn.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32,
                    accumulate=True)
             K.bias_grad(A.dqkv, fp.g(p + "attn.c_attn.bias"))
-            # ln1 (+ residual gradient) -> gradient of x[l]
+            # ln1 (+ residual gradient) -> gradient of x[l]; its column sum is
+            # the fc2 bias gradient of block l-1
             K.layernorm_bwd(A.dln, A.x[l], fp.w(p + "ln_1.weight"), A.mu1[l], A.rs1[l], A.dres,
-                            fp.g(p + "ln_1.weight"), fp.g(p + "ln_1.bias"), A.ln_part, dresid=A.dres2)
-            n += 21
+                            fp.g(p + "ln_1.weight"), fp.g(p + "ln_1.bias"), A.ln_part, dresid=A.dres2,
+                            dsum=fp.g(f"h{l - 1}.mlp.c_proj.bias") if l > 0 else None)
+            n += 18
             if self.grad_sync is not None:
                 self.grad_sync.bucket_ready(l + 1)
         K.embedding_bwd(tokens, A.dres, fp.g("wte"), fp.g("wpe")[:S], S)

@@ -24,48 +24,62 @@ def _aligned(*dims) -> bool:
 
 # ---------------------------------------------------------------------------- linear
 class _LinearFn(torch.autograd.Function):
-    """y = x @ W (+ b) with W stored [in, out] (the reference Dense layout,
-    scirs2-neural/src/layers/dense.rs:82-139), optional fused GELU."""
+    """y = x @ W (+ b), optional fused GELU. W is [in, out] (the reference
+    Dense layout, scirs2-neural/src/layers/dense.rs:82-139) given either as a
+    contiguous [in, out] tensor or as the transpose view of a contiguous
+    [out, in] (torch Linear layout) tensor; both map onto the GEMM without a
+    copy (MN-major or K-major B operand)."""
 
     @staticmethod
     def forward(ctx, x, w, b, gelu):
         shp = x.shape
         x2 = x.reshape(-1, shp[-1]).contiguous()
         M, N = x2.shape[0], w.shape[1]
+        kmaj = not w.is_contiguous()  # w = W_oi.t() with W_oi [out, in] contiguous
+        bw = w.t() if kmaj else w
         out = torch.empty(M, N, device=x.device, dtype=x.dtype)
         pre = None
         if gelu:
             pre = torch.empty_like(out)
-            K.gemm(x2, w, out, b_mn=True, epi=K.EPI_BIAS_GELU, bias=b, out2=pre)
+            K.gemm(x2, bw, out, b_mn=not kmaj, epi=K.EPI_BIAS_GELU, bias=b, out2=pre)
         else:
-            K.gemm(x2, w, out, b_mn=True, bias=b)
-        ctx.save_for_backward(x2, w, pre)
-        ctx.has_b = b is not None
-        ctx.shp = shp
+            K.gemm(x2, bw, out, b_mn=not kmaj, bias=b)
+        ctx.save_for_backward(x2, bw, pre)
+        ctx.has_b, ctx.kmaj, ctx.shp = b is not None, kmaj, shp
         return out.reshape(*shp[:-1], N)
 
     @staticmethod
     def backward(ctx, gy):
-        x2, w, pre = ctx.saved_tensors
-        g2 = gy.reshape(-1, w.shape[1]).contiguous()
+        x2, bw, pre = ctx.saved_tensors
+        kmaj = ctx.kmaj
+        n_out = bw.shape[0] if kmaj else bw.shape[1]
+        g2 = gy.reshape(-1, n_out).contiguous()
         if pre is not None:
             g2 = (g2.float() * K.gelu_tanh_grad(pre.float())).to(g2.dtype)
         dx = torch.empty_like(x2)
-        K.gemm(g2, w, dx, b_mn=False)  # dX = dY W^T ; W [in,out] is [N=in, K=out]
-        dw32 = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
-        K.gemm(x2, g2, dw32, a_mn=True, b_mn=True, epi=K.EPI_F32)
+        # dX = dY W^T: W[in,out] is a K-major [N=in, K=out] operand; W_oi [out,in] an MN-major one.
+        K.gemm(g2, bw, dx, b_mn=kmaj)
+        if kmaj:  # grad w.r.t. W_oi [out, in] = dY^T X
+            dw32 = torch.zeros(bw.shape, device=bw.device, dtype=torch.float32)
+            K.gemm(g2, x2, dw32, a_mn=True, b_mn=True, epi=K.EPI_F32)
+            dw = dw32.to(bw.dtype).t()
+        else:  # grad w.r.t. W [in, out] = X^T dY
+            dw32 = torch.zeros(bw.shape, device=bw.device, dtype=torch.float32)
+            K.gemm(x2, g2, dw32, a_mn=True, b_mn=True, epi=K.EPI_F32)
+            dw = dw32.to(bw.dtype)
         db = None
         if ctx.has_b:
-            db32 = torch.zeros(w.shape[1], device=w.device, dtype=torch.float32)
+            db32 = torch.zeros(n_out, device=bw.device, dtype=torch.float32)
             K.bias_grad(g2, db32)
-            db = db32.to(w.dtype)
-        return dx.reshape(ctx.shp), dw32.to(w.dtype), db, None
+            db = db32.to(bw.dtype)
+        return dx.reshape(ctx.shp), dw, db, None
 
 
 def linear(x, w, b=None, activation: str | None = None):
-    """x @ w (+ b), w is [in, out]."""
+    """x @ w (+ b), w is [in, out] (contiguous, or the .t() view of an [out, in] tensor)."""
     gelu = activation == "gelu"
-    if _native(x, w, b) and _aligned(w.shape[0], w.shape[1]) and x.shape[-1] == w.shape[0]:
+    layout_ok = w.dim() == 2 and (w.is_contiguous() or w.t().is_contiguous())
+    if _native(x, w, b) and layout_ok and _aligned(w.shape[0], w.shape[1]) and x.shape[-1] == w.shape[0]:
         y = _LinearFn.apply(x, w, b, gelu)
         return y if gelu or activation is None else apply_activation(y, activation)
     y = x @ w

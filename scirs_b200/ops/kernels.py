@@ -65,6 +65,7 @@ def gemm(
     accumulate: bool = False,
     splits: int = 0,
     bn: int = 0,
+    bias_grad: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """out[M,N] = op(a) @ op(b) with a fused epilogue.
 
@@ -73,10 +74,12 @@ def gemm(
 
     Epilogues: EPI_BF16 (+bias), EPI_BIAS_GELU (out2 = pre-activation,
     out = gelu(out2)), EPI_RESID (+bias +aux), EPI_DGELU (out = acc *
-    gelu'(aux)), EPI_F32 (fp32 out, optionally accumulated).
+    gelu'(aux)), EPI_F32 (fp32 out, optionally accumulated). With
+    EPI_DGELU, `bias_grad` (fp32 [N]) accumulates the column sums of out.
     """
     if a.is_cuda:
-        _ext.kernels().gemm(a, b, out, int(a_mn), int(b_mn), int(epi), bias, aux, out2, accumulate, splits, bn)
+        _ext.kernels().gemm(a, b, out, int(a_mn), int(b_mn), int(epi), bias, aux, out2, accumulate, splits, bn,
+                            bias_grad)
         _count(1)
         return out
     A = (a.t() if a_mn else a).float()
@@ -94,6 +97,8 @@ def gemm(
         acc = acc + aux.float()
     elif epi == EPI_DGELU:
         acc = acc * gelu_tanh_grad(aux.float())
+        if bias_grad is not None:
+            bias_grad.add_(acc.sum(0))
     elif epi == EPI_BIAS_GELU:
         out2.copy_(acc)
         acc = gelu_tanh(acc)
@@ -119,10 +124,11 @@ def layernorm_fwd(x, w, b, y, mean, rstd, eps=1e-5):
     return y
 
 
-def layernorm_bwd(dy, x, w, mean, rstd, dx, dw, db, part, dresid=None):
-    """dx = LN backward (+ dresid); dw/db (fp32) are accumulated into."""
+def layernorm_bwd(dy, x, w, mean, rstd, dx, dw, db, part, dresid=None, dsum=None):
+    """dx = LN backward (+ dresid); dw/db (fp32) are accumulated into, and
+    so is dsum (fp32 [D], optional) with the column sums of dx."""
     if x.is_cuda:
-        _ext.kernels().layernorm_bwd(dy, x, w, mean, rstd, dresid, dx, dw, db, part)
+        _ext.kernels().layernorm_bwd(dy, x, w, mean, rstd, dresid, dx, dw, db, part, dsum)
         _count(2)
         return dx
     D = x.shape[-1]
@@ -137,6 +143,8 @@ def layernorm_bwd(dy, x, w, mean, rstd, dx, dw, db, part, dresid=None):
     o = rs * (gw - gw.mean(-1, keepdim=True) - xh * (gw * xh).mean(-1, keepdim=True))
     if dresid is not None:
         o = o + dresid.float().reshape(-1, D)
+    if dsum is not None:
+        dsum.add_(o.sum(0))
     dx.copy_(o.reshape(dx.shape))
     return dx
 
@@ -148,7 +156,7 @@ def ln_partials(n_rows: int, D: int, device) -> torch.Tensor:
         nb = max(1, min(2 * sms, (n_rows + 7) // 8))
     else:
         nb = 1
-    return torch.empty(nb * 2 * D, dtype=torch.float32, device=device)
+    return torch.empty(nb * 3 * D, dtype=torch.float32, device=device)
 
 
 # ---------------------------------------------------------------------------
