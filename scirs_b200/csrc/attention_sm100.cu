@@ -1,0 +1,370 @@
+// FlashAttention forward on the 5th-generation tensor cores (tcgen05/TMEM).
+//
+// One CTA = one 128-query tile of one (batch, head). Q, K, V are read with
+// TMA straight out of token-major buffers (e.g. the fused QKV projection
+// [B*S, 3*H*HD]); no transposes.
+//
+//   warp 0     TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 1     owns TMEM; one thread issues  S_j = Q K_j^T  (M=128,N=128,K=HD)
+//              into S[j%2] and  O_j = P_j V_j  (M=128,N=HD,K=128) into O[j%2]
+//   warps 2-5  softmax: thread t owns query row t (TMEM lane t), so row max /
+//              row sum need no cross-thread reduction. Reads S_j from TMEM,
+//              writes P_j = exp2(S_j*scale*log2e - m_j) as bf16 into a
+//              128B-swizzled smem tile (the K-major A operand of the PV MMA),
+//              and folds O_{j-1} into a register accumulator (one block
+//              behind, rescaled by exp2(m_{j-2} - m_{j-1})).
+//
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+HD) O1 [256+HD,256+2HD).
+// Causal masking applies only to the diagonal block (BM == BN == 128); keys
+// >= S are masked, rows >= S are not stored. Every mbarrier wait is bounded.
+//
+// Reference parity: same math as the reference's CPU FlashAttention-2
+// forward (scirs2-neural/src/layers/flash_attention_v2.rs:220,369-482,
+// scirs2-neural/src/attention/flash_v2.rs:96-300); LSE is natural-log.
+#include "host_common.h"
+
+namespace scirs {
+namespace fatc {
+
+using bf16 = __nv_bfloat16;
+constexpr int BM = 128, BN = 128;
+constexpr int kThreads = 192;
+
+struct Params {
+  bf16* out;
+  float* lse;
+  long o_rs;
+  int B, H, S;
+  float scale_log2;
+  DevStatus* st;
+};
+
+template <int HD>
+struct Cfg {
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int KV_BYTES = BN * HD * 2;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;          // 2 stages
+  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;     // 2 stages
+  static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t IDESC_S = umma_idesc_bf16(BM, BN, 0, 0);
+  static constexpr uint32_t IDESC_O = umma_idesc_bf16(BM, HD, 0, 1);
+};
+
+template <int HD, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* v_full = bars + 3;   // [2]
+  uint64_t* kv_empty = bars + 5; // [2]
+  uint64_t* s_full = bars + 7;   // [2]
+  uint64_t* s_free = bars + 9;   // [2]
+  uint64_t* o_full = bars + 11;  // [2]
+  uint64_t* o_free = bars + 13;  // [2]
+  uint64_t* p_full = bars + 15;
+  uint64_t* p_free = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.S, H = p.H;
+  const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal tiles first
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int q0 = qb * BM;
+  const int row_base = b * S;  // token row of position 0 of this sequence
+  const int nkv_all = (S + BN - 1) / BN;
+  const int nkv = CAUSAL ? min(nkv_all, qb + 1) : nkv_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(p_free, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      const int col = h * HD;
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c)
+        tma_load_2d(smem + C::OFF_Q + c * (BM * 128), &tmQ, q_full, col + c * 64, row_base + q0);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, p.st, 20, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + c * (BN * 128), &tmK, &k_full[s], col + c * 64,
+                      row_base + j * BN);
+        mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + c * (BN * 128), &tmV, &v_full[s], col + c * 64,
+                      row_base + j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, p.st, 21, abort_flag);
+      tc_fence_after();
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      const uint32_t p_addr = smem_u32(smem + C::OFF_P);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!mbar_wait(p_full, i & 1, p.st, 22, abort_flag)) return false;
+        if (!mbar_wait(&v_full[s], (i >> 1) & 1, p.st, 23, abort_flag)) return false;
+        if (!mbar_wait(&o_free[s], ((i >> 1) & 1) ^ 1, p.st, 24, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + C::OFF_V + s * C::KV_BYTES);
+        const uint32_t d_tmem = tmem + 256 + s * HD;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          // A = P [128 q][128 keys] K-major in two 64-key column blocks
+          const uint64_t adesc = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          // B = V [keys][HD] MN-major: k-step = 16 key rows = 2048 bytes
+          const uint64_t bdesc = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+          tc_mma_f16_ss(d_tmem, adesc, bdesc, C::IDESC_O, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(p_free);
+        tc_commit(&o_full[s]);
+        tc_commit(&kv_empty[s]);
+        return true;
+      };
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j & 1;
+        ok = mbar_wait(&k_full[s], (j >> 1) & 1, p.st, 25, abort_flag) &&
+             mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, p.st, 26, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + C::OFF_K + s * C::KV_BYTES);
+        const uint32_t d_tmem = tmem + s * BN;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(d_tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + offk, 16, 1024),
+                        C::IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[s]);
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok && nkv >= 1) issue_pv(nkv - 1);
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int q = warp & 3;          // TMEM lane quarter
+    const int r = q * 32 + lane;     // query row within the tile
+    const int qrow = q0 + r;         // position within the sequence
+    const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
+    uint8_t* prow = smem + C::OFF_P + r * 128;
+    float oacc[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) oacc[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_pend = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.st, 30, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const int kv0 = j * BN;
+      const bool mask = (kv0 + BN > S) || (CAUSAL && j == qb);
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + s * BN + c, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x = __uint_as_float(v[e]);
+          const int key = kv0 + c + e;
+          if (mask && (key >= S || (CAUSAL && key > qrow))) x = -INFINITY;
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m, mx * p.scale_log2);
+      const float ref = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2_fast(m - ref);
+      // P may be overwritten once the previous PV MMA has consumed it
+      if (j >= 1 && !mbar_wait(p_free, (j - 1) & 1, p.st, 31, abort_flag)) { ok = false; break; }
+      // pass 2: P = exp2(S*scale_log2 - m_new) -> bf16 swizzled smem tile
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + s * BN + c, v);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
+          const int key = kv0 + c + e;
+          if (mask && (key >= S || (CAUSAL && key > qrow))) x0 = -INFINITY;
+          if (mask && (key + 1 >= S || (CAUSAL && key + 1 > qrow))) x1 = -INFINITY;
+          const float p0 = ex2_fast(fmaf(x0, p.scale_log2, -ref));
+          const float p1 = ex2_fast(fmaf(x1, p.scale_log2, -ref));
+          rs += p0 + p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
+        }
+        // 32 keys = four 16-byte units of the row; key block c/64, unit (c%64)/8 + u
+        uint8_t* blk = prow + (c >> 6) * (BM * 128);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int unit = ((c & 63) >> 3) + u;
+          *reinterpret_cast<uint4*>(blk + ((unit ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_free[s]);
+        mbar_arrive(p_full);
+      }
+      l = l * alpha + rs;
+      m = m_new;
+      // fold O_{j-1} (relative to m_{j-1}) into the accumulator
+      if (j >= 1) {
+        const int so = (j - 1) & 1;
+        if (!mbar_wait(&o_full[so], ((j - 1) >> 1) & 1, p.st, 32, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_base + 256 + so * HD + c, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) oacc[c + e] = fmaf(oacc[c + e], alpha_pend, __uint_as_float(v[e]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[so]);
+      }
+      alpha_pend = alpha;
+    }
+    if (ok && nkv >= 1) {
+      const int so = (nkv - 1) & 1;
+      if (mbar_wait(&o_full[so], ((nkv - 1) >> 1) & 1, p.st, 33, abort_flag)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_base + 256 + so * HD + c, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) oacc[c + e] = fmaf(oacc[c + e], alpha_pend, __uint_as_float(v[e]));
+        }
+        if (qrow < S) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          bf16* orow = p.out + (long)(row_base + qrow) * p.o_rs + h * HD;
+#pragma unroll
+          for (int c = 0; c < HD; c += 8) {
+            uint4 o;
+            o.x = pack_bf16x2(oacc[c] * inv, oacc[c + 1] * inv);
+            o.y = pack_bf16x2(oacc[c + 2] * inv, oacc[c + 3] * inv);
+            o.z = pack_bf16x2(oacc[c + 4] * inv, oacc[c + 5] * inv);
+            o.w = pack_bf16x2(oacc[c + 6] * inv, oacc[c + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c) = o;
+          }
+          p.lse[((long)b * H + h) * S + qrow] = (m + log2f(l)) * 0.6931471805599453f;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fatc
+
+// q/k/v/out: [B, S, H, HD] token-major views with contiguous heads; lse [B,H,S].
+void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       bool causal, double scale) {
+  const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
+  for (auto* t : {&q, &k, &v, &out}) {
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == S &&
+                    t->size(2) == H && t->size(3) == HD,
+                "q/k/v/out must be bf16 [B, S, H, HD]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == S * t->stride(1),
+                "q/k/v/out must be token-major with contiguous heads");
+  }
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * H * S && lse.is_contiguous(), "lse fp32 [B,H,S]");
+  c10::cuda::CUDAGuard guard(q.get_device());
+  auto mk = [&](const torch::Tensor& t) {
+    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * S),
+                        (uint64_t)t.stride(1) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  CUtensorMap tq = mk(q), tk = mk(k), tv = mk(v);
+  fatc::Params p{};
+  p.out = reinterpret_cast<fatc::bf16*>(out.data_ptr());
+  p.lse = lse.data_ptr<float>();
+  p.o_rs = out.stride(1);
+  p.B = (int)B;
+  p.H = (int)H;
+  p.S = (int)S;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.st = status_ptr(q.get_device());
+  dim3 grid((unsigned)((S + 127) / 128), (unsigned)(B * H));
+  auto st = cur_stream();
+#define FATC(HD_, C_)                                                                                      \
+  {                                                                                                        \
+    auto kern = fatc::fa_fwd_tc_kernel<HD_, C_>;                                                           \
+    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,               \
+                                          fatc::Cfg<HD_>::SMEM));                                          \
+    kern<<<grid, fatc::kThreads, fatc::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);                               \
+  }
+  if (HD == 64) {
+    if (causal) FATC(64, true) else FATC(64, false)
+  } else {
+    if (causal) FATC(128, true) else FATC(128, false)
+  }
+#undef FATC
+  SCIRS_CHECK_LAUNCH();
+}
+
+}  // namespace scirs

@@ -26,6 +26,8 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
                     torch::Tensor delta, bool causal, double scale);
+void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       bool causal, double scale);
 }  // namespace scirs
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -44,6 +46,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("optim_step", &scirs::optim_step);
   m.def("flash_attn_fwd", &scirs::flash_attn_fwd);
   m.def("flash_attn_bwd", &scirs::flash_attn_bwd);
+  m.def("flash_attn_fwd_tc", &scirs::flash_attn_fwd_tc);
   m.def("status_read_and_clear", &scirs::status_read_and_clear);
   m.def("num_sms", &scirs::num_sms);
 }

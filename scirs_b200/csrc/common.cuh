@@ -315,6 +315,13 @@ __device__ __forceinline__ float tanh_fast(float x) {
   return y;
 }
 
+// 2^x via the PTX ex2.approx instruction (flush-to-zero; 2^-inf = 0).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // GELU, tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
 // The two constants are the definition of the approximation (Hendrycks &
 // Gimpel 2016), not taken from any library.

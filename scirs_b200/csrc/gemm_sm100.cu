@@ -66,8 +66,26 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // Epilogue staging: per epilogue warp two 2 KB slots (32 rows x 64 bytes,
+  // 64-byte swizzle) that feed TMA stores / reduce-adds.
+  static constexpr int SLOT_BYTES = 2048;
+  static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = STAGING_OFF + kEpiWarps * 2 * SLOT_BYTES;
+  static constexpr int SMEM = BAR_OFF + 256 /*barriers*/ + 1024 /*align*/;
 };
+
+// Write 16 bytes `v` as 16-byte unit `u` (0..3) of row `r` of a 32x64B slot
+// with the TMA 64-byte swizzle (unit index XOR (row/2)%4; slot 512B-aligned).
+__device__ __forceinline__ void slot_st16(uint8_t* slot, int r, int u, uint4 v) {
+  *reinterpret_cast<uint4*>(slot + r * 64 + ((u ^ ((r >> 1) & 3)) << 4)) = v;
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   map),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
 
 __device__ __forceinline__ void decode_unit(const Args& a, int u, int& m_blk, int& n_blk, int& split) {
   split = u % a.splits;
@@ -84,14 +102,15 @@ __device__ __forceinline__ void decode_unit(const Args& a, int u, int& m_blk, in
 
 template <int BN, int A_MN, int B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args args) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const Args args) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -116,6 +135,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+    if (EPI == EPI_BIAS_GELU) prefetch_tmap(&tmC2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -216,9 +237,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // TMEM -> registers -> fused math -> swizzled smem slot -> TMA store
+    // (bf16 outputs) or TMA reduce-add / store (fp32 outputs, 16-col halves).
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     // two warps per lane quarter; each takes one half of the tile's columns
     const int c_begin = (warp < 6) ? 0 : BN / 2;
+    uint8_t* slot0 = smem + C::STAGING_OFF + (warp - 2) * 2 * C::SLOT_BYTES;
+    uint8_t* slot1 = slot0 + C::SLOT_BYTES;
     int local = 0;
     for (int u = blockIdx.x; u < args.num_units; u += gridDim.x, ++local) {
       int m_blk, n_blk, split;
@@ -227,35 +252,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t aph = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], aph, args.st, 4, abort_flag)) break;
       tc_fence_after();
-      const int row = m_blk * BM + q * 32 + lane;
+      const int row0 = m_blk * BM + q * 32;
+      const int row = row0 + lane;
       const bool row_ok = row < args.M;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+      // number of 32-column chunks of this warp's half that lie inside N
+      const int nch = max(0, min(BN / 64, (args.N - (n_blk * BN + c_begin) + 31) / 32));
+      if (nch == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
 #pragma unroll 1
-      for (int c = c_begin; c < c_begin + BN / 2; c += 32) {
+      for (int ci = 0; ci < nch; ++ci) {
+        const int c = c_begin + ci * 32;
         const int col0 = n_blk * BN + c;
-        if (col0 >= args.N) break;  // warp-uniform
         uint32_t r[32];
         tmem_ld_32x32b_x32(trow + c, r);
         tc_wait_ld();
-        // the dGELU epilogue keeps invalid rows (as zeros) for its column sums
-        if (EPI != EPI_DGELU && !row_ok) continue;
+        if (ci == nch - 1) {
+          // last TMEM read of this tile by this warp: release the accumulator
+          // so the MMA warp can start the next tile while we finish the math
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = row_ok ? __uint_as_float(r[j]) : 0.f;
-        if (EPI == EPI_F32) {
-          float* out = reinterpret_cast<float*>(args.C) + (long)row * args.ldc + col0;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            if (col0 + g * 4 >= args.N) break;
-            float4 f = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-            if (args.atomic_out)
-              atomicAdd(reinterpret_cast<float4*>(out + 4 * g), f);
-            else
-              *reinterpret_cast<float4*>(out + 4 * g) = f;
-          }
-          continue;
-        }
-        if (EPI != EPI_DGELU && args.bias != nullptr) {
+        if (EPI != EPI_F32 && EPI != EPI_DGELU && args.bias != nullptr) {
           const uint4* bp = reinterpret_cast<const uint4*>(args.bias + col0);
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
@@ -289,34 +314,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (EPI == EPI_BIAS_GELU) {
-          uint4* hp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C2) + (long)row * args.ldc2 + col0);
+        // slots are free once the previous chunk's stores have read them
+        if (lane == 0) tma_store_wait_read0();
+        __syncwarp();
+        if (EPI == EPI_F32) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (col0 + g * 8 >= args.N) break;
-            uint4 o;
-            o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-            o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-            o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-            o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-            hp[g] = o;
+          for (int hh = 0; hh < 2; ++hh) {
+            uint8_t* sl = hh ? slot1 : slot0;
+#pragma unroll
+            for (int uu = 0; uu < 4; ++uu) {
+              const int j = hh * 16 + uu * 4;
+              slot_st16(sl, lane, uu,
+                        make_uint4(__float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
+                                   __float_as_uint(v[j + 3])));
+            }
+          }
+        } else {
+          if (EPI == EPI_BIAS_GELU) {
+#pragma unroll
+            for (int uu = 0; uu < 4; ++uu) {
+              const int j = uu * 8;
+              slot_st16(slot1, lane, uu,
+                        make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                   pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7])));
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
           }
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+          for (int uu = 0; uu < 4; ++uu) {
+            const int j = uu * 8;
+            slot_st16(slot0, lane, uu,
+                      make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                 pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7])));
+          }
         }
-        if (row_ok) {
-          uint4* op =
-              reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.C) + (long)row * args.ldc + col0);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (col0 + g * 8 >= args.N) break;
-            uint4 o;
-            o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-            o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-            o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-            o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-            op[g] = o;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (EPI == EPI_F32) {
+            if (args.atomic_out) {
+              tma_reduce_add_2d(&tmC, slot0, col0, row0);
+              if (col0 + 16 < args.N) tma_reduce_add_2d(&tmC, slot1, col0 + 16, row0);
+            } else {
+              tma_store_2d(&tmC, slot0, col0, row0);
+              if (col0 + 16 < args.N) tma_store_2d(&tmC, slot1, col0 + 16, row0);
+            }
+          } else {
+            tma_store_2d(&tmC, slot0, col0, row0);
+            if (EPI == EPI_BIAS_GELU) tma_store_2d(&tmC2, slot1, col0, row0);
           }
+          tma_store_commit();
         }
         if (EPI == EPI_DGELU && args.bias_grad != nullptr) {
           // Column sums over this warp's 32 rows: butterfly reduce-scatter,
@@ -334,10 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (col0 + lane < args.N) atomicAdd(args.bias_grad + col0 + lane, v[0]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) tma_store_wait0();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -354,15 +401,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 struct TmapKey {
   const void* p;
   uint64_t inner, outer, stride;
-  uint32_t bi, bo;
+  uint32_t bi, bo, dtype, swz;
   bool operator==(const TmapKey& o) const {
-    return p == o.p && inner == o.inner && outer == o.outer && stride == o.stride && bi == o.bi && bo == o.bo;
+    return p == o.p && inner == o.inner && outer == o.outer && stride == o.stride && bi == o.bi && bo == o.bo &&
+           dtype == o.dtype && swz == o.swz;
   }
 };
 struct TmapHash {
   size_t operator()(const TmapKey& k) const {
     size_t h = std::hash<const void*>()(k.p);
-    h ^= std::hash<uint64_t>()(k.inner * 1315423911ull + k.outer * 2654435761ull + k.stride * 97 + k.bi * 31 + k.bo);
+    h ^= std::hash<uint64_t>()(k.inner * 1315423911ull + k.outer * 2654435761ull + k.stride * 97 + k.bi * 31 +
+                               k.bo * 7 + k.dtype * 3 + k.swz);
     return h;
   }
 };
@@ -370,21 +419,27 @@ struct TmapHash {
 static std::mutex g_tm_mu;
 static std::unordered_map<TmapKey, CUtensorMap, TmapHash> g_tmaps;
 
+// Cached tensor map. Operand maps use bf16 + 128B swizzle; output maps use a
+// 64B swizzle that matches the epilogue staging slots.
 static CUtensorMap get_tmap(const void* p, uint64_t inner, uint64_t outer, uint64_t stride_bytes, uint32_t bi,
-                            uint32_t bo) {
-  TmapKey k{p, inner, outer, stride_bytes, bi, bo};
+                            uint32_t bo, CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                            CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  TmapKey k{p, inner, outer, stride_bytes, bi, bo, (uint32_t)dt, (uint32_t)swz};
   std::lock_guard<std::mutex> lk(g_tm_mu);
   auto it = g_tmaps.find(k);
   if (it != g_tmaps.end()) return it->second;
   if (g_tmaps.size() > 4096) g_tmaps.clear();
-  CUtensorMap m = make_tmap_2d(p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, inner, outer, stride_bytes, bi, bo,
-                               CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap m = make_tmap_2d(p, dt, inner, outer, stride_bytes, bi, bo, swz);
   g_tmaps.emplace(k, m);
   return m;
 }
 
+struct Maps {
+  CUtensorMap a, b, c, c2;
+};
+
 template <int BN, int A_MN, int B_MN, int EPI>
-static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Args& args, int grid, cudaStream_t stream) {
+static void launch_t(const Maps& m, const Args& args, int grid, cudaStream_t stream) {
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -393,30 +448,28 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a
     SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM));
     attr_set[dev] = true;
   }
-  kern<<<grid, kThreads, Cfg<BN>::SMEM, stream>>>(ta, tb, args);
+  kern<<<grid, kThreads, Cfg<BN>::SMEM, stream>>>(m.a, m.b, m.c, m.c2, args);
   SCIRS_CHECK_LAUNCH();
 }
 
 template <int BN, int A_MN, int B_MN>
-static void launch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Args& args, int grid,
-                       cudaStream_t s) {
+static void launch_epi(int epi, const Maps& m, const Args& args, int grid, cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: launch_t<BN, A_MN, B_MN, EPI_BF16>(ta, tb, args, grid, s); break;
-    case EPI_BIAS_GELU: launch_t<BN, A_MN, B_MN, EPI_BIAS_GELU>(ta, tb, args, grid, s); break;
-    case EPI_RESID: launch_t<BN, A_MN, B_MN, EPI_RESID>(ta, tb, args, grid, s); break;
-    case EPI_DGELU: launch_t<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, args, grid, s); break;
-    case EPI_F32: launch_t<BN, A_MN, B_MN, EPI_F32>(ta, tb, args, grid, s); break;
+    case EPI_BF16: launch_t<BN, A_MN, B_MN, EPI_BF16>(m, args, grid, s); break;
+    case EPI_BIAS_GELU: launch_t<BN, A_MN, B_MN, EPI_BIAS_GELU>(m, args, grid, s); break;
+    case EPI_RESID: launch_t<BN, A_MN, B_MN, EPI_RESID>(m, args, grid, s); break;
+    case EPI_DGELU: launch_t<BN, A_MN, B_MN, EPI_DGELU>(m, args, grid, s); break;
+    case EPI_F32: launch_t<BN, A_MN, B_MN, EPI_F32>(m, args, grid, s); break;
     default: TORCH_CHECK(false, "bad epilogue ", epi);
   }
 }
 
 template <int BN>
-static void launch_bn(int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Args& args,
-                      int grid, cudaStream_t s) {
-  if (!a_mn && !b_mn) launch_epi<BN, 0, 0>(epi, ta, tb, args, grid, s);
-  else if (!a_mn && b_mn) launch_epi<BN, 0, 1>(epi, ta, tb, args, grid, s);
-  else if (a_mn && !b_mn) launch_epi<BN, 1, 0>(epi, ta, tb, args, grid, s);
-  else launch_epi<BN, 1, 1>(epi, ta, tb, args, grid, s);
+static void launch_bn(int a_mn, int b_mn, int epi, const Maps& m, const Args& args, int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) launch_epi<BN, 0, 0>(epi, m, args, grid, s);
+  else if (!a_mn && b_mn) launch_epi<BN, 0, 1>(epi, m, args, grid, s);
+  else if (a_mn && !b_mn) launch_epi<BN, 1, 0>(epi, m, args, grid, s);
+  else launch_epi<BN, 1, 1>(epi, m, args, grid, s);
 }
 
 }  // namespace gemm
@@ -547,16 +600,30 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   args.num_units = (int)(tiles * sp);
   const int grid = (int)std::min<long>(args.num_units, sms);
 
-  // Tensor maps (SWIZZLE_128B, 64-element inner boxes).
+  // Operand maps (SWIZZLE_128B, 64-element inner boxes) and output maps
+  // (32x32 bf16 or 32x16 fp32 boxes, SWIZZLE_64B, matching the staging slots).
   const uint64_t lda_b = (uint64_t)a.stride(0) * 2, ldb_b = (uint64_t)b.stride(0) * 2;
-  CUtensorMap ta = a_mn ? get_tmap(a.data_ptr(), (uint64_t)M, (uint64_t)K, lda_b, 64, 64)
-                        : get_tmap(a.data_ptr(), (uint64_t)K, (uint64_t)M, lda_b, 64, BM);
-  CUtensorMap tb = b_mn ? get_tmap(b.data_ptr(), (uint64_t)N, (uint64_t)K, ldb_b, 64, 64)
-                        : get_tmap(b.data_ptr(), (uint64_t)K, (uint64_t)N, ldb_b, 64, (uint32_t)BN);
+  Maps maps;
+  maps.a = a_mn ? get_tmap(a.data_ptr(), (uint64_t)M, (uint64_t)K, lda_b, 64, 64)
+                : get_tmap(a.data_ptr(), (uint64_t)K, (uint64_t)M, lda_b, 64, BM);
+  maps.b = b_mn ? get_tmap(b.data_ptr(), (uint64_t)N, (uint64_t)K, ldb_b, 64, 64)
+                : get_tmap(b.data_ptr(), (uint64_t)K, (uint64_t)N, ldb_b, 64, (uint32_t)BN);
+  if (epi == EPI_F32) {
+    maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)out.stride(0) * 4, 16, 32,
+                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B);
+  } else {
+    maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)out.stride(0) * 2, 32, 32,
+                      CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
+  maps.c2 = maps.c;
+  if (epi == EPI_BIAS_GELU) {
+    maps.c2 = get_tmap(args.C2, (uint64_t)N, (uint64_t)M, (uint64_t)args.ldc2 * 2, 32, 32,
+                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
 
   cudaStream_t s = cur_stream();
-  if (BN == 256) launch_bn<256>((int)a_mn, (int)b_mn, (int)epi, ta, tb, args, grid, s);
-  else launch_bn<128>((int)a_mn, (int)b_mn, (int)epi, ta, tb, args, grid, s);
+  if (BN == 256) launch_bn<256>((int)a_mn, (int)b_mn, (int)epi, maps, args, grid, s);
+  else launch_bn<128>((int)a_mn, (int)b_mn, (int)epi, maps, args, grid, s);
 }
 
 }  // namespace scirs

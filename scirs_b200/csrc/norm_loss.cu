@@ -139,23 +139,30 @@ __global__ void __launch_bounds__(256) ln_fwd_generic(const bf16* __restrict__ x
 // Persistent grid: each row group walks rows with a grid-wide stride.
 // ===========================================================================
 template <int NV, int RW>
-__global__ void __launch_bounds__(256) ln_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
-                                                     const bf16* __restrict__ w, const float* __restrict__ mean,
-                                                     const float* __restrict__ rstd, const bf16* __restrict__ dresid,
-                                                     bf16* __restrict__ dx, float* __restrict__ part, int M) {
+__global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                                        const bf16* __restrict__ w, const float* __restrict__ mean,
+                                                        const float* __restrict__ rstd,
+                                                        const bf16* __restrict__ dresid, bf16* __restrict__ dx,
+                                                        float* __restrict__ part, int M) {
   constexpr int D = RW * 256 * NV;
   constexpr int RPB = 8 / RW;
+  // Per row-group partial column sums (dgamma, dbeta, sum dx) live in shared
+  // memory: each lane owns distinct columns of its group, so no atomics.
+  extern __shared__ float ps[];  // [RPB][3][D]
   __shared__ float red[8];
   const int wib = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int sub = (wib % RW) * 32 + lane;
-  float dg[NV * 8], db[NV * 8], ds[NV * 8];
-#pragma unroll
-  for (int i = 0; i < NV * 8; ++i) dg[i] = db[i] = ds[i] = 0.f;
+  const int grp = wib / RW;
+  for (int i = threadIdx.x; i < RPB * 3 * D; i += 256) ps[i] = 0.f;
+  __syncthreads();
+  float* pg = ps + grp * 3 * D;
+  float* pb = pg + D;
+  float* pd = pb + D;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
 
   for (int base = blockIdx.x * RPB; base < M; base += gridDim.x * RPB) {
-    const int row = base + wib / RW;
+    const int row = base + grp;
     const bool ok = row < M;
     const int rr = ok ? row : 0;
     const uint4* xr = reinterpret_cast<const uint4*>(x + (long)rr * D);
@@ -172,13 +179,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const bf16* __restrict__ dy
     for (int i = 0; i < NV; ++i) {
       float wf[8];
       unpack8(__ldg(wr + sub + 32 * RW * i), wf);
+      const int col = (sub + 32 * RW * i) * 8;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int k = 8 * i + e;
         xh[k] = (xh[k] - mu) * rs;
         if (ok) {
-          dg[k] += g[k] * xh[k];
-          db[k] += g[k];
+          pg[col + e] += g[k] * xh[k];
+          pb[col + e] += g[k];
         }
         g[k] *= wf[e];
         s1 += g[k];
@@ -201,42 +209,20 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const bf16* __restrict__ dy
 #pragma unroll
           for (int e = 0; e < 8; ++e) o[e] += r8[e];
         }
+        const int col = (sub + 32 * RW * i) * 8;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ds[8 * i + e] += o[e];
+        for (int e = 0; e < 8; ++e) pd[col + e] += o[e];
         dxr[sub + 32 * RW * i] = pack8(o);
       }
     }
   }
-  // Reduce the RPB row groups' partial column sums through shared memory.
-  // Columns held by thread `sub`, vector i: (sub + 32*RW*i)*8 + e.
-  __shared__ float sg[8 / RW][RW * 256], sb[8 / RW][RW * 256], ss[8 / RW][RW * 256];
-  float* out_g = part + (long)blockIdx.x * 3 * D;
-  float* out_b = out_g + D;
-  float* out_s = out_b + D;
-  const int grp = wib / RW;
-#pragma unroll 1
-  for (int i = 0; i < NV; ++i) {
-    __syncthreads();
+  __syncthreads();
+  float* out = part + (long)blockIdx.x * 3 * D;
+  for (int c = threadIdx.x; c < 3 * D; c += 256) {
+    float a = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      sg[grp][sub * 8 + e] = dg[8 * i + e];
-      sb[grp][sub * 8 + e] = db[8 * i + e];
-      ss[grp][sub * 8 + e] = ds[8 * i + e];
-    }
-    __syncthreads();
-    for (int c = threadIdx.x; c < RW * 256; c += 256) {
-      float a = 0.f, bb = 0.f, cc = 0.f;
-#pragma unroll
-      for (int k = 0; k < 8 / RW; ++k) {
-        a += sg[k][c];
-        bb += sb[k][c];
-        cc += ss[k][c];
-      }
-      const int col = ((c >> 3) + 32 * RW * i) * 8 + (c & 7);
-      out_g[col] = a;
-      out_b[col] = bb;
-      out_s[col] = cc;
-    }
+    for (int k = 0; k < RPB; ++k) a += ps[k * 3 * D + c];
+    out[c] = a;
   }
 }
 
@@ -576,7 +562,13 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   auto mp = mean.data_ptr<float>(), rp = rstd.data_ptr<float>();
   auto dxp = (bf16*)dx.data_ptr();
   auto pp = part.data_ptr<float>();
-#define LNB(NV, RW) ln_bwd_kernel<NV, RW><<<nb, 256, 0, s>>>(dyp, xp, wp, mp, rp, dr, dxp, pp, M)
+#define LNB(NV, RW)                                                                                 \
+  {                                                                                                 \
+    const int smem_b = (8 / RW) * 3 * (RW * 256 * NV) * (int)sizeof(float);                       \
+    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(ln_bwd_kernel<NV, RW>,                                    \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b));    \
+    ln_bwd_kernel<NV, RW><<<nb, 256, smem_b, s>>>(dyp, xp, wp, mp, rp, dr, dxp, pp, M);             \
+  }
   switch (D) {
     case 256: LNB(1, 1); break;
     case 512: LNB(2, 1); break;

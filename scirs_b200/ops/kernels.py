@@ -7,6 +7,7 @@ CPU tensors. The CPU path is the numerical oracle used by the tests.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -20,6 +21,10 @@ EPI_DGELU = 3
 EPI_F32 = 4
 
 OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
+
+# Attention forward implementation: "tcgen05" (TMEM/TMA kernel) or "mma"
+# (warp-level mma.sync kernel). Both are sm_100a kernels of this library.
+ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "tcgen05")
 
 
 class _Stats:
@@ -256,7 +261,10 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
     """q/k/v/out: [B, S, H, D] token-major views (heads contiguous)."""
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        _ext.kernels().flash_attn_fwd(q, k, v, out, lse, bool(causal), float(scale))
+        if ATTN_FWD_IMPL == "tcgen05":
+            _ext.kernels().flash_attn_fwd_tc(q, k, v, out, lse, bool(causal), float(scale))
+        else:
+            _ext.kernels().flash_attn_fwd(q, k, v, out, lse, bool(causal), float(scale))
         _count(1)
         return out
     o, l = attention_reference(q, k, v, causal, scale)

@@ -45,6 +45,7 @@ ext_modules = [
                 "norm_loss.cu",
                 "optim.cu",
                 "attention.cu",
+                "attention_sm100.cu",
             ]
         ),
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},

@@ -1,0 +1,117 @@
+"""Worker for the multi-GPU tests (run under torchrun, one rank per GPU).
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        tests/dist_worker.py <case> <out_json>
+
+Each case checks the in-kernel NVLink collectives against NCCL / a local
+reference and rank 0 writes a JSON verdict.
+"""
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from scirs_b200 import _ext  # noqa: E402
+from scirs_b200.parallel import dist as sdist  # noqa: E402
+
+
+def case_collectives():
+    from scirs_b200.parallel.nvlink import NVLinkComm
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    comm = NVLinkComm(area_bytes=64 << 20, timeout_s=10.0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = {}
+    for n in [8 * world, 4096, 1 << 20, 3 * (1 << 20) + 64 * world]:
+        g = torch.Generator(device="cpu").manual_seed(100 + rank)
+        x = torch.randn(n, generator=g).to(dev)
+        ref = x.to(torch.bfloat16).float() / world  # each rank's bf16-rounded scaled contribution
+        ref_sum = ref.clone()
+        dist.all_reduce(ref_sum)
+        out = torch.empty_like(x)
+        for _ in range(3):  # repeated calls exercise the epoch protocol
+            comm.allreduce(x, out, 1.0 / world)
+        torch.cuda.synchronize()
+        err = float((out - ref_sum).abs().max() / ref_sum.abs().max())
+        # identical on all ranks
+        o0 = out.clone()
+        dist.broadcast(o0, 0)
+        same = bool(torch.equal(o0, out))
+        res[f"allreduce_{n}"] = {"max_err": err, "identical": same}
+        # reduce-scatter
+        if n % (8 * world) == 0:
+            shard = torch.empty(n // world, device=dev)
+            comm.reduce_scatter(x, shard, 1.0 / world)
+            torch.cuda.synchronize()
+            want = ref_sum[rank * (n // world) : (rank + 1) * (n // world)]
+            res[f"reduce_scatter_{n}"] = {"max_err": float((shard - want).abs().max() / want.abs().max())}
+            # all-gather (bf16)
+            full = torch.empty(n, device=dev, dtype=torch.bfloat16)
+            comm.all_gather(shard.to(torch.bfloat16), full)
+            ag_ref = [torch.empty(n // world, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+            dist.all_gather(ag_ref, shard.to(torch.bfloat16))
+            torch.cuda.synchronize()
+            res[f"allgather_{n}"] = {"equal": bool(torch.equal(full, torch.cat(ag_ref)))}
+    _ext.check_status()
+    comm.close()
+    return res
+
+
+def case_dp_gpt():
+    """DP training with the fused all-reduce == single-process training on the
+    concatenated global batch (same weights, same data)."""
+    from scirs_b200.models.gpt import GPTConfig, GPTModel
+    from scirs_b200.parallel.data_parallel import data_parallel
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = GPTConfig.tiny(vocab=1024, seq=128)
+    g = torch.Generator().manual_seed(7)
+    tok = torch.randint(0, cfg.vocab_size, (4 * world, 129), generator=g)
+    x, y = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
+    lb = 4
+    res = {}
+    for mode in ("fused", "nccl"):
+        m = GPTModel(cfg, device=dev, seed=3)
+        m.configure_adamw(lr=1e-3, weight_decay=0.0, max_grad_norm=0.0)
+        data_parallel(m, mode=mode)
+        losses = []
+        for _ in range(3):
+            l = m.train_step(x[rank * lb : (rank + 1) * lb].to(dev), y[rank * lb : (rank + 1) * lb].to(dev))
+            lt = l.detach().clone()
+            dist.all_reduce(lt)
+            losses.append(float(lt) / world)
+        torch.cuda.synchronize()
+        # replicas must stay identical
+        w = m.fp.master.clone()
+        w0 = w.clone()
+        dist.broadcast(w0, 0)
+        res[mode] = {"losses": losses, "replica_max_diff": float((w - w0).abs().max())}
+        if m.grad_sync is not None and m.grad_sync.comm is not None:
+            m.grad_sync.comm.close()
+    # single-process reference on the full batch
+    if rank == 0:
+        m = GPTModel(cfg, device=dev, seed=3)
+        m.configure_adamw(lr=1e-3, weight_decay=0.0, max_grad_norm=0.0)
+        ref = [float(m.train_step(x.to(dev), y.to(dev))) for _ in range(3)]
+        res["single"] = {"losses": ref}
+    _ext.check_status()
+    return res
+
+
+def main():
+    case, out = sys.argv[1], sys.argv[2]
+    sdist.init(timeout_s=60)
+    res = {"collectives": case_collectives, "dp_gpt": case_dp_gpt}[case]()
+    if dist.get_rank() == 0:
+        json.dump(res, open(out, "w"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

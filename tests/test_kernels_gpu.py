@@ -170,6 +170,25 @@ def test_flash_attention(B, S, H, HD, causal):
     assert rel_err(dv, vf.grad) < 2e-2
 
 
+@pytest.mark.parametrize("impl", ["tcgen05", "mma"])
+@pytest.mark.parametrize("B,S,H,HD,causal", [(2, 256, 4, 64, True), (1, 197, 3, 64, False), (1, 384, 2, 128, True),
+                                             (2, 1024, 2, 64, True), (1, 300, 2, 128, False)])
+def test_flash_attention_fwd_impls(impl, B, S, H, HD, causal, monkeypatch):
+    from scirs_b200 import _ext
+
+    monkeypatch.setattr(K, "ATTN_FWD_IMPL", impl)
+    qkv = rnd(B * S, 3 * H * HD, seed=21).view(B, S, 3, H, HD)  # fused-QKV layout
+    q, k, v = qkv.unbind(2)
+    out = torch.empty(B, S, H, HD, device=DEV, dtype=torch.bfloat16)
+    lse = torch.empty(B, H, S, device=DEV)
+    K.flash_attn_fwd(q, k, v, out, lse, causal, HD**-0.5)
+    torch.cuda.synchronize()
+    _ext.check_status()
+    o_ref, lse_ref = K.attention_reference(q, k, v, causal, HD**-0.5)
+    assert rel_err(out, o_ref) < 1e-2
+    assert torch.allclose(lse, lse_ref, atol=1e-2)
+
+
 # ---------------------------------------------------------------------------- optimizer
 @pytest.mark.parametrize("mode", ["adam", "adamw", "sgd", "rmsprop", "adagrad"])
 def test_fused_optimizer(mode):
