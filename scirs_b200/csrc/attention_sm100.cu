@@ -14,7 +14,8 @@
 //              and folds O_{j-1} into a register accumulator (one block
 //              behind, rescaled by exp2(m_{j-2} - m_{j-1})).
 //
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+HD) O1 [256+HD,256+2HD).
+// TMEM columns: NSB S buffers of 128, then NSB O buffers of HD (NSB = 1 for
+// head_dim 64 -> 256 columns, two CTAs per SM; NSB = 2 for head_dim 128).
 // Causal masking applies only to the diagonal block (BM == BN == 128); keys
 // >= S are masked, rows >= S are not stored. Every mbarrier wait is bounded.
 //
@@ -49,18 +50,31 @@ struct Cfg {
   static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;     // 2 stages
   static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
   static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  // 512 bytes of alignment slack (the kernel checks the base alignment at
+  // run time); with 1024 two 112 KB CTAs would not fit one SM.
+  static constexpr int SLACK = 512;
+  static constexpr int SMEM = OFF_BAR + 256 + SLACK;
+  // TMEM: NSB buffers of S (128 fp32 columns) then NSB buffers of O (HD
+  // columns). head_dim 64 uses one buffer each (256 columns), so two CTAs
+  // share an SM and their softmax / MMA phases interleave.
+  static constexpr int NSB = (HD == 64) ? 1 : 2;
+  static constexpr int TMEM_COLS = (NSB * (128 + HD) <= 256) ? 256 : 512;
+  static constexpr int MIN_BLOCKS = (HD == 64) ? 2 : 1;
   static constexpr uint32_t IDESC_S = umma_idesc_bf16(BM, BN, 0, 0);
   static constexpr uint32_t IDESC_O = umma_idesc_bf16(BM, HD, 0, 1);
 };
 
 template <int HD, bool CAUSAL>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<HD>::MIN_BLOCKS)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem - smem_raw > C::SLACK) {  // dynamic smem less aligned than assumed: refuse, do not overrun
+    if (threadIdx.x == 0) report_status(p.st, kStBadArg, 40, (unsigned)(smem - smem_raw));
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
@@ -106,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmV);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 512);
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -145,13 +159,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t p_addr = smem_u32(smem + C::OFF_P);
       auto issue_pv = [&](int i) -> bool {
-        const int s = i & 1;
+        const int s = i & 1;                  // K/V smem stage
+        const int ob = i % C::NSB;            // O TMEM buffer
         if (!mbar_wait(p_full, i & 1, p.st, 22, abort_flag)) return false;
         if (!mbar_wait(&v_full[s], (i >> 1) & 1, p.st, 23, abort_flag)) return false;
-        if (!mbar_wait(&o_free[s], ((i >> 1) & 1) ^ 1, p.st, 24, abort_flag)) return false;
+        if (!mbar_wait(&o_free[ob], ((i / C::NSB) & 1) ^ 1, p.st, 24, abort_flag)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + C::OFF_V + s * C::KV_BYTES);
-        const uint32_t d_tmem = tmem + 256 + s * HD;
+        const uint32_t d_tmem = tmem + C::NSB * BN + ob * HD;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // A = P [128 q][128 keys] K-major in two 64-key column blocks
@@ -161,18 +176,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_mma_f16_ss(d_tmem, adesc, bdesc, C::IDESC_O, kk > 0 ? 1u : 0u);
         }
         tc_commit(p_free);
-        tc_commit(&o_full[s]);
+        tc_commit(&o_full[ob]);
         tc_commit(&kv_empty[s]);
         return true;
       };
       for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j & 1;
+        const int s = j & 1;        // K/V smem stage
+        const int sb = j % C::NSB;  // S TMEM buffer
         ok = mbar_wait(&k_full[s], (j >> 1) & 1, p.st, 25, abort_flag) &&
-             mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, p.st, 26, abort_flag);
+             mbar_wait(&s_free[sb], ((j / C::NSB) & 1) ^ 1, p.st, 26, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + C::OFF_K + s * C::KV_BYTES);
-        const uint32_t d_tmem = tmem + s * BN;
+        const uint32_t d_tmem = tmem + sb * BN;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
@@ -180,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_mma_f16_ss(d_tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + offk, 16, 1024),
                         C::IDESC_S, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[s]);
+        tc_commit(&s_full[sb]);
         if (j >= 1) ok = issue_pv(j - 1);
       }
       if (ok && nkv >= 1) issue_pv(nkv - 1);
@@ -200,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f, alpha_pend = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv && ok; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.st, 30, abort_flag)) { ok = false; break; }
+      const int s = j % C::NSB;  // S TMEM buffer
+      if (!mbar_wait(&s_full[s], (j / C::NSB) & 1, p.st, 30, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const int kv0 = j * BN;
       const bool mask = (kv0 + BN > S) || (CAUSAL && j == qb);
@@ -264,13 +280,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       m = m_new;
       // fold O_{j-1} (relative to m_{j-1}) into the accumulator
       if (j >= 1) {
-        const int so = (j - 1) & 1;
-        if (!mbar_wait(&o_full[so], ((j - 1) >> 1) & 1, p.st, 32, abort_flag)) { ok = false; break; }
+        const int so = (j - 1) % C::NSB;
+        if (!mbar_wait(&o_full[so], ((j - 1) / C::NSB) & 1, p.st, 32, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_base + 256 + so * HD + c, v);
+          tmem_ld_32x32b_x32(lane_base + C::NSB * BN + so * HD + c, v);
           tc_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) oacc[c + e] = fmaf(oacc[c + e], alpha_pend, __uint_as_float(v[e]));
@@ -282,13 +298,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       alpha_pend = alpha;
     }
     if (ok && nkv >= 1) {
-      const int so = (nkv - 1) & 1;
-      if (mbar_wait(&o_full[so], ((nkv - 1) >> 1) & 1, p.st, 33, abort_flag)) {
+      const int so = (nkv - 1) % C::NSB;
+      if (mbar_wait(&o_full[so], ((nkv - 1) / C::NSB) & 1, p.st, 33, abort_flag)) {
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_base + 256 + so * HD + c, v);
+          tmem_ld_32x32b_x32(lane_base + C::NSB * BN + so * HD + c, v);
           tc_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) oacc[c + e] = fmaf(oacc[c + e], alpha_pend, __uint_as_float(v[e]));
@@ -315,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 

@@ -19,8 +19,11 @@
 //
 // Buffer layout (bytes): [ area0 | area1 | flags ]   area = data_cap / 2.
 //   all-reduce : area0 holds the scaled bf16 inputs, area1 the reduced pieces
-//   reduce-scat: area (epoch & 1) holds the scaled bf16 inputs
-//   all-gather : area (epoch & 1) holds the gathered bf16 payload
+//   reduce-scat: area0 holds the scaled bf16 inputs
+//   all-gather : area0 holds the gathered bf16 payload
+//   Every kernel ends with an exit barrier and all kinds share one epoch
+//   sequence per block, so consecutive collectives of any kind may reuse the
+//   buffer safely.
 //
 // Reference parity: replaces the single-process simulations of the
 // reference's distributed gradient primitives
@@ -36,7 +39,7 @@ namespace comm {
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 128;
-constexpr int kBarriers = 2;
+constexpr int kBarriers = 3;  // phase barriers 0, 1 and the exit barrier 2
 constexpr long kFlagBytes = (long)kBarriers * kMaxBlocks * kMaxRanks * 4;
 
 struct Peers {
@@ -194,6 +197,9 @@ __global__ void __launch_bounds__(512) allreduce_kernel(const Args a) {
     }
   }
   __syncthreads();
+  // exit barrier: every peer is done reading this call's buffers, so the next
+  // collective (of any kind) may overwrite them
+  if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
   if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
 }
 
@@ -205,7 +211,7 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
   const unsigned epoch = a.epochs[blockIdx.x] + 1;
-  const long area = (epoch & 1) ? a.area_bytes : 0;
+  const long area = 0;
   const long shard_vec = a.n / 8 / a.world;
   // Block b handles vectors [b*per, ...) of every shard.
   const long per = (shard_vec + gridDim.x - 1) / gridDim.x;
@@ -234,6 +240,9 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(const Args a) {
     }
   }
   __syncthreads();
+  // exit barrier: every peer is done reading this call's buffers, so the next
+  // collective (of any kind) may overwrite them
+  if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
   if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
 }
 
@@ -245,7 +254,7 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
   const unsigned epoch = a.epochs[blockIdx.x] + 1;
-  const long area = (epoch & 1) ? a.area_bytes : 0;
+  const long area = 0;
   const long shard_vec = a.n / 8 / a.world;
   const long per = (shard_vec + gridDim.x - 1) / gridDim.x;
   const long s0 = min(shard_vec, (long)blockIdx.x * per), s1 = min(shard_vec, s0 + per);
@@ -268,6 +277,9 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Args a) {
     }
   }
   __syncthreads();
+  // exit barrier: every peer is done reading this call's buffers, so the next
+  // collective (of any kind) may overwrite them
+  if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
   if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
 }
 
@@ -436,7 +448,7 @@ void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, do
   a.in32 = in32.data_ptr<float>();
   a.out32 = out32.data_ptr<float>();
   a.scale = (float)scale;
-  a.epochs = cs.epochs_rs;
+  a.epochs = cs.epochs_ar;  // one epoch sequence per block shared by every collective kind
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
   comm::reduce_scatter_kernel<<<nb, 512, 0, cur_stream()>>>(a);
@@ -457,7 +469,7 @@ void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t
   comm::Args a = make_args(cs, n, timeout_s);
   a.in16 = reinterpret_cast<const __nv_bfloat16*>(in16.data_ptr());
   a.out16 = reinterpret_cast<__nv_bfloat16*>(out16.data_ptr());
-  a.epochs = cs.epochs_ag;
+  a.epochs = cs.epochs_ar;
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
   comm::allgather_kernel<<<nb, 512, 0, cur_stream()>>>(a);

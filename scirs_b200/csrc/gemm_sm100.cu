@@ -115,7 +115,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_bar = drain + 1;  // [kEpiWarps]: TMA loads of the epilogue's aux operand
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(aux_bar + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -131,12 +132,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_bar[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmC);
-    if (EPI == EPI_BIAS_GELU) prefetch_tmap(&tmC2);
+    if (EPI == EPI_BIAS_GELU || EPI == EPI_RESID || EPI == EPI_DGELU) prefetch_tmap(&tmC2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -244,20 +246,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c_begin = (warp < 6) ? 0 : BN / 2;
     uint8_t* slot0 = smem + C::STAGING_OFF + (warp - 2) * 2 * C::SLOT_BYTES;
     uint8_t* slot1 = slot0 + C::SLOT_BYTES;
+    // Epilogues with an aux operand (residual / GELU pre-activation) TMA-load
+    // each 32x32 aux chunk into slot1 one chunk ahead; outputs go via slot0.
+    constexpr bool HAS_AUX = (EPI == EPI_RESID || EPI == EPI_DGELU);
+    uint64_t* my_aux_bar = &aux_bar[warp - 2];
+    uint32_t aux_phase = 0;
     int local = 0;
     for (int u = blockIdx.x; u < args.num_units; u += gridDim.x, ++local) {
       int m_blk, n_blk, split;
       decode_unit(args, u, m_blk, n_blk, split);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], aph, args.st, 4, abort_flag)) break;
-      tc_fence_after();
       const int row0 = m_blk * BM + q * 32;
       const int row = row0 + lane;
       const bool row_ok = row < args.M;
-      const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
       // number of 32-column chunks of this warp's half that lie inside N
       const int nch = max(0, min(BN / 64, (args.N - (n_blk * BN + c_begin) + 31) / 32));
+      if (HAS_AUX && nch > 0 && lane == 0) {
+        mbar_arrive_expect_tx(my_aux_bar, C::SLOT_BYTES);
+        tma_load_2d(slot1, &tmC2, my_aux_bar, n_blk * BN + c_begin, row0);
+      }
+      if (!mbar_wait(&tfull[acc], aph, args.st, 4, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
       if (nch == 0) {
         tc_fence_before();
         __syncwarp();
@@ -294,12 +305,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if ((EPI == EPI_RESID || EPI == EPI_DGELU) && row_ok) {
-          const uint4* ap = reinterpret_cast<const uint4*>(args.aux + (long)row * args.ldaux + col0);
+        if (HAS_AUX) {
+          // aux chunk (rows beyond M / cols beyond N arrive zero-filled)
+          mbar_wait(my_aux_bar, aux_phase, args.st, 5, abort_flag);
+          aux_phase ^= 1;
+          uint4 ax[4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+            ax[g] = *reinterpret_cast<const uint4*>(slot1 + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (ci + 1 < nch && lane == 0) {
+            mbar_arrive_expect_tx(my_aux_bar, C::SLOT_BYTES);
+            tma_load_2d(slot1, &tmC2, my_aux_bar, col0 + 32, row0);
+          }
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
-            if (col0 + g * 8 >= args.N) break;
-            uint4 x4 = ap[g];
+            uint4 x4 = ax[g];
             uint32_t xw[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -616,6 +638,10 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
   }
   maps.c2 = maps.c;
+  if (epi == EPI_RESID || epi == EPI_DGELU) {  // aux operand, loaded by the epilogue via TMA
+    maps.c2 = get_tmap(args.aux, (uint64_t)N, (uint64_t)M, (uint64_t)args.ldaux * 2, 32, 32,
+                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
   if (epi == EPI_BIAS_GELU) {
     maps.c2 = get_tmap(args.C2, (uint64_t)N, (uint64_t)M, (uint64_t)args.ldc2 * 2, 32, 32,
                        CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);

@@ -148,7 +148,10 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const bf16* __restrict__
   constexpr int RPB = 8 / RW;
   // Per row-group partial column sums (dgamma, dbeta, sum dx) live in shared
   // memory: each lane owns distinct columns of its group, so no atomics.
-  extern __shared__ float ps[];  // [RPB][3][D]
+  // Layout [RPB][3][NV*8 slots][RW*32 threads]: consecutive lanes touch
+  // consecutive words (bank-conflict free). Slot k of thread `sub` is
+  // column (sub + 32*RW*(k/8))*8 + k%8.
+  extern __shared__ float ps[];
   __shared__ float red[8];
   const int wib = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -179,14 +182,13 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const bf16* __restrict__
     for (int i = 0; i < NV; ++i) {
       float wf[8];
       unpack8(__ldg(wr + sub + 32 * RW * i), wf);
-      const int col = (sub + 32 * RW * i) * 8;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int k = 8 * i + e;
         xh[k] = (xh[k] - mu) * rs;
         if (ok) {
-          pg[col + e] += g[k] * xh[k];
-          pb[col + e] += g[k];
+          pg[k * RW * 32 + sub] += g[k] * xh[k];
+          pb[k * RW * 32 + sub] += g[k];
         }
         g[k] *= wf[e];
         s1 += g[k];
@@ -209,9 +211,8 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const bf16* __restrict__
 #pragma unroll
           for (int e = 0; e < 8; ++e) o[e] += r8[e];
         }
-        const int col = (sub + 32 * RW * i) * 8;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) pd[col + e] += o[e];
+        for (int e = 0; e < 8; ++e) pd[(8 * i + e) * RW * 32 + sub] += o[e];
         dxr[sub + 32 * RW * i] = pack8(o);
       }
     }
@@ -219,10 +220,12 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const bf16* __restrict__
   __syncthreads();
   float* out = part + (long)blockIdx.x * 3 * D;
   for (int c = threadIdx.x; c < 3 * D; c += 256) {
+    // c = arr*D + k*(RW*32) + t  ->  column (t + 32*RW*(k/8))*8 + k%8 of array arr
+    const int arr = c / D, rem = c % D, k = rem / (RW * 32), t = rem % (RW * 32);
     float a = 0.f;
 #pragma unroll
-    for (int k = 0; k < RPB; ++k) a += ps[k * 3 * D + c];
-    out[c] = a;
+    for (int j = 0; j < RPB; ++j) a += ps[j * 3 * D + c];
+    out[arr * D + (t + 32 * RW * (k >> 3)) * 8 + (k & 7)] = a;
   }
 }
 

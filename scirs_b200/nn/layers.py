@@ -157,8 +157,9 @@ class BatchNorm(Layer):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(num_features, dtype=dtype, device=device))
         self.bias = nn.Parameter(torch.zeros(num_features, dtype=dtype, device=device))
-        self.register_buffer("running_mean", torch.zeros(num_features, dtype=torch.float32, device=device))
-        self.register_buffer("running_var", torch.ones(num_features, dtype=torch.float32, device=device))
+        sdt = torch.float32 if dtype in (torch.bfloat16, torch.float16) else dtype
+        self.register_buffer("running_mean", torch.zeros(num_features, dtype=sdt, device=device))
+        self.register_buffer("running_var", torch.ones(num_features, dtype=sdt, device=device))
         self.momentum, self.eps = momentum, eps
 
     def forward(self, x):
