@@ -259,26 +259,34 @@ __global__ void __launch_bounds__(256) fa_fwd_kernel(const Params p) {
   }
 }
 
-// delta[b, h, s] = sum_d dO[s, h, d] * O[s, h, d]
+// delta[b, h, s] = sum_d dO[s, h, d] * O[s, h, d]; HD/8 lanes per (token,
+// head), 16-byte loads, shuffle reduction within the lane group.
 template <int HD>
 __global__ void fa_bwd_delta_kernel(const Params p) {
-  const int idx = blockIdx.x * 8 + (threadIdx.x >> 5);  // (b*S + s)*H + h
-  const int lane = threadIdx.x & 31;
+  constexpr int G = HD / 8;  // lanes per (token, head): 8 or 16
+  const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long idx = gid / G;  // (b*S + s)*H + h
+  const int sub = (int)(gid % G);
   const long total = (long)p.B * p.S * p.H;
-  if (idx >= total) return;
-  const int h = idx % p.H;
-  const long tok = idx / p.H;
-  const int b = (int)(tok / p.S), s = (int)(tok % p.S);
-  const bf16* o = p.o + tok * p.o_rs + h * HD;
-  const bf16* d = p.dout + tok * p.do_rs + h * HD;
+  const bool ok = idx < total;
   float acc = 0.f;
-  for (int i = lane * 2; i < HD; i += 64) {
-    const uint32_t ov = *reinterpret_cast<const uint32_t*>(o + i);
-    const uint32_t dv = *reinterpret_cast<const uint32_t*>(d + i);
-    acc += bf16_lo(ov) * bf16_lo(dv) + bf16_hi(ov) * bf16_hi(dv);
+  long tok = 0;
+  int h = 0;
+  if (ok) {
+    h = (int)(idx % p.H);
+    tok = idx / p.H;
+    const uint4 ov = *reinterpret_cast<const uint4*>(p.o + tok * p.o_rs + h * HD + sub * 8);
+    const uint4 dv = *reinterpret_cast<const uint4*>(p.dout + tok * p.do_rs + h * HD + sub * 8);
+    const uint32_t oa[4] = {ov.x, ov.y, ov.z, ov.w}, da[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc += bf16_lo(oa[e]) * bf16_lo(da[e]) + bf16_hi(oa[e]) * bf16_hi(da[e]);
   }
-  acc = warp_sum(acc);
-  if (lane == 0) p.delta[((long)b * p.H + h) * p.S + s] = acc;
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (ok && sub == 0) {
+    const int b = (int)(tok / p.S), s = (int)(tok % p.S);
+    p.delta[((long)b * p.H + h) * p.S + s] = acc;
+  }
 }
 
 // ===========================================================================
@@ -552,9 +560,14 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 
 // dq/dk/dv: [B, S, H, HD] bf16 views; dq_acc fp32 scratch [B*S*H*HD] (zeroed
 // here); delta fp32 scratch [B*H*S].
+void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
+                       torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
+                       double scale);
+
+// impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernel (head_dim 64).
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
-                    torch::Tensor delta, bool causal, double scale) {
+                    torch::Tensor delta, bool causal, double scale, int64_t impl) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   check_qkv_view(q, "q", B, S, H, HD);
   check_qkv_view(k, "k", B, S, H, HD);
@@ -596,11 +609,14 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   SCIRS_CHECK_CUDA(cudaMemsetAsync(p.dq_acc, 0, sizeof(float) * B * S * H * HD, st));
   {
-    const long rows = B * S * H;
-    if (HD == 64) attn::fa_bwd_delta_kernel<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
-    else attn::fa_bwd_delta_kernel<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
+    const long rows = B * S * H;  // one 8-lane group per (token, head), 16-byte loads
+    if (HD == 64) attn::fa_bwd_delta_kernel<64><<<(unsigned)((rows * 8 + 255) / 256), 256, 0, st>>>(p);
+    else attn::fa_bwd_delta_kernel<128><<<(unsigned)((rows * 16 + 255) / 256), 256, 0, st>>>(p);
     SCIRS_CHECK_LAUNCH();
   }
+  if (impl == 1 && HD == 64) {
+    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale);
+  } else {
   dim3 grid((unsigned)((S + 63) / 64), (unsigned)(B * H));
 #define FA_BWD(HD_, CAUSAL_)                                                                             \
   {                                                                                                      \
@@ -616,6 +632,7 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
   }
 #undef FA_BWD
   SCIRS_CHECK_LAUNCH();
+  }
   {
     const long n4 = B * S * H * HD / 4;
     attn::fa_dq_convert_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(p.dq_acc, p.dq, p.dq_rs, B * S,

@@ -383,4 +383,399 @@ void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   SCIRS_CHECK_LAUNCH();
 }
 
+
+
+// ===========================================================================
+// FlashAttention backward on tcgen05 (head_dim 64).
+//
+// One CTA = one 128-key tile of one (batch, head); it walks the 128-query
+// blocks that can see those keys (all of them, or q >= k for causal).
+//
+//   warp 0     TMA: K, V once; Q_i, dO_i into a 2-stage ring
+//   warp 1     MMA thread, per query block i:
+//                S^T  = K Q_i^T        (TMEM [0,128))
+//                dP^T = V dO_i^T       (TMEM [128,256))
+//                -- dS warps turn them into P^T, dS^T (bf16 smem) --
+//                dV  += P^T dO_i       (TMEM [256,320), accumulated over i)
+//                dK  += dS^T Q_i       (TMEM [320,384), accumulated over i)
+//                dQ_i = dS K           (TMEM [384,448); A = dS^T read MN-major)
+//   warps 2-5  dS warps: thread = key row. P = exp2(S*scale*log2e - LSE*log2e)
+//              (masked to 0), dS = P (dP - delta); both stored as 128B-swizzled
+//              K-major bf16 tiles [key][q].
+//   warps 6-9  dQ warps: TMEM dQ_i -> 128B-swizzled fp32 smem slots -> TMA
+//              reduce-add into the fp32 dQ accumulator [B*S, H*HD]; at the
+//              end they write dK * scale and dV (bf16).
+// dQ is scaled by the softmax scale in the follow-up conversion kernel.
+// ===========================================================================
+namespace fabw {
+
+using bf16 = __nv_bfloat16;
+constexpr int HD = 64, BK = 128, BQ = 128;
+constexpr int kThreads = 320;
+constexpr int T_BYTES = 128 * HD * 2;    // one 128-row x 64-col bf16 tile (16 KB)
+constexpr int P_BYTES = BK * BQ * 2;     // 128 x 128 bf16 (32 KB)
+constexpr int OFF_K = 0;
+constexpr int OFF_V = OFF_K + T_BYTES;
+constexpr int OFF_Q = OFF_V + T_BYTES;      // 2 stages
+constexpr int OFF_DO = OFF_Q + 2 * T_BYTES; // 2 stages
+constexpr int OFF_PT = OFF_DO + 2 * T_BYTES;
+constexpr int OFF_DST = OFF_PT + P_BYTES;
+constexpr int OFF_DQS = OFF_DST + P_BYTES;  // 4 warps x 2 slots x 4 KB
+constexpr int OFF_LD = OFF_DQS + 4 * 2 * 4096;  // lse / delta [2][2][128] fp32
+constexpr int OFF_BAR = OFF_LD + 4 * 128 * 4;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, 0, 0);
+constexpr uint32_t IDESC_KV = umma_idesc_bf16(128, HD, 0, 1);   // dV, dK: A K-major, B MN-major
+constexpr uint32_t IDESC_Q = umma_idesc_bf16(128, HD, 1, 1);    // dQ: A (dS^T) MN-major, B MN-major
+
+struct Params {
+  const float* lse;    // [B, H, S] natural log
+  const float* delta;  // [B, H, S]
+  bf16* dk;
+  bf16* dv;
+  long dk_rs, dv_rs;
+  int B, H, S;
+  float scale, scale_log2;
+  DevStatus* st;
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                     const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pt_free = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_free = bars + 10;
+  uint64_t* dkv_full = bars + 11;
+  uint64_t* drain = bars + 12;
+  uint64_t* ld_bar = bars + 13;  // [2]: the 4 dS warps have staged LSE / delta of a query block
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* sLD = reinterpret_cast<float*>(smem + OFF_LD);  // [buf][0: lse2, 1: delta][128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.S, H = p.H;
+  const int kb = blockIdx.x;
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int k0 = kb * BK;
+  const int row_base = b * S;
+  const int nq = (S + BQ - 1) / BQ;
+  const int i0 = CAUSAL ? kb : 0;
+  const int col = h * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(pt_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(dkv_full, 1);
+    mbar_init(drain, 1);
+    mbar_init(&ld_bar[0], 4);
+    mbar_init(&ld_bar[1], 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmDO);
+    prefetch_tmap(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + HD, T_DQ = 256 + 2 * HD;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * T_BYTES);
+      tma_load_2d(smem + OFF_K, &tmK, kv_full, col, row_base + k0);
+      tma_load_2d(smem + OFF_V, &tmV, kv_full, col, row_base + k0);
+      for (int i = i0, n = 0; i < nq; ++i, ++n) {
+        const int st = n & 1;
+        if (!mbar_wait(&qdo_empty[st], ((n >> 1) & 1) ^ 1, p.st, 50, abort_flag)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * T_BYTES);
+        tma_load_2d(smem + OFF_Q + st * T_BYTES, &tmQ, &qdo_full[st], col, row_base + i * BQ);
+        tma_load_2d(smem + OFF_DO + st * T_BYTES, &tmDO, &qdo_full[st], col, row_base + i * BQ);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane == 0) {
+      bool ok = mbar_wait(kv_full, 0, p.st, 51, abort_flag);
+      tc_fence_after();
+      const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
+      const uint32_t pt_addr = smem_u32(smem + OFF_PT), ds_addr = smem_u32(smem + OFF_DST);
+      for (int i = i0, n = 0; i < nq && ok; ++i, ++n) {
+        const int st = n & 1;
+        ok = mbar_wait(&qdo_full[st], (n >> 1) & 1, p.st, 52, abort_flag) &&
+             mbar_wait(s_free, (n & 1) ^ 1, p.st, 53, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + OFF_Q + st * T_BYTES);
+        const uint32_t do_addr = smem_u32(smem + OFF_DO + st * T_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          tc_mma_f16_ss(tmem + T_S, umma_desc_sw128(k_addr + kk * 32, 16, 1024),
+                        umma_desc_sw128(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          tc_mma_f16_ss(tmem + T_DP, umma_desc_sw128(v_addr + kk * 32, 16, 1024),
+                        umma_desc_sw128(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+        if (!mbar_wait(p_full, n & 1, p.st, 54, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * (BK * 128) + (kk & 3) * 32;  // K-major [key][q] tiles
+          tc_mma_f16_ss(tmem + T_DV, umma_desc_sw128(pt_addr + aoff, 16, 1024),
+                        umma_desc_sw128(do_addr + kk * 2048, 128 * 128, 1024), IDESC_KV,
+                        (n > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_DK, umma_desc_sw128(ds_addr + aoff, 16, 1024),
+                        umma_desc_sw128(q_addr + kk * 2048, 128 * 128, 1024), IDESC_KV,
+                        (n > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (!mbar_wait(dq_free, (n & 1) ^ 1, p.st, 55, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // A = dS [q][key] = dS^T read MN-major: q atoms of 64 (16 KB apart), key rows 8 per 1 KB
+          tc_mma_f16_ss(tmem + T_DQ, umma_desc_sw128(ds_addr + kk * 2048, BK * 128, 1024),
+                        umma_desc_sw128(k_addr + kk * 2048, 128 * 128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(pt_free);
+        tc_commit(dq_full);
+        tc_commit(&qdo_empty[st]);
+      }
+      tc_commit(dkv_full);
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ dS warps
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;   // key row in the tile
+    const int key = k0 + r;
+    const int t128 = (warp - 2) * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    const float* lse_g = p.lse + ((long)b * H + h) * S;
+    const float* del_g = p.delta + ((long)b * H + h) * S;
+    uint8_t* pt_row = smem + OFF_PT + r * 128;
+    uint8_t* ds_row = smem + OFF_DST + r * 128;
+    const float LOG2E = 1.4426950408889634f;
+    for (int i = i0, n = 0; i < nq; ++i, ++n) {
+      const int q0 = i * BQ;
+      float* sL = sLD + (n & 1) * 256;
+      {
+        const int q = q0 + t128;
+        sL[t128] = q < S ? lse_g[q] * LOG2E : 0.f;
+        sL[128 + t128] = q < S ? del_g[q] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ld_bar[n & 1]);
+      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) break;
+      if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) break;
+      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) break;
+      tc_fence_after();
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > S) || (CAUSAL && i == i0);
+#pragma unroll 1
+      for (int c = 0; c < BQ; c += 32) {
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(lane_base + T_S + c, sv);
+        tmem_ld_32x32b_x32(lane_base + T_DP + c, dv);
+        tc_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pr[2], ds[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int ql = c + e + u;
+            const int q = q0 + ql;
+            float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
+            if (need_mask && (q >= S || key >= S || (CAUSAL && key > q))) pv = 0.f;
+            pr[u] = pv;
+            ds[u] = pv * (__uint_as_float(dv[e + u]) - sL[128 + ql]);
+          }
+          pp[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+          dd[e >> 1] = pack_bf16x2(ds[0], ds[1]);
+        }
+        const int blk = (c >> 6) * (BK * 128);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int unit = ((c & 63) >> 3) + u;
+          const int so = blk + ((unit ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(pt_row + so) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+          *reinterpret_cast<uint4*>(ds_row + so) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free);
+        mbar_arrive(p_full);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ warps
+    const int q4 = warp & 3;                 // TMEM lane quarter (query rows of dQ)
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    uint8_t* slot0 = smem + OFF_DQS + (warp - 6) * 8192;
+    uint8_t* slot1 = slot0 + 4096;
+    bool ok = true;
+    for (int i = i0, n = 0; i < nq; ++i, ++n) {
+      if (!mbar_wait(dq_full, n & 1, p.st, 58, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t a0[32], a1[32];
+      tmem_ld_32x32b_x32(lane_base + T_DQ, a0);
+      tmem_ld_32x32b_x32(lane_base + T_DQ + 32, a1);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (lane == 0) tma_store_wait_read0();
+      __syncwarp();
+      // 32 rows x 32 fp32 per slot, 128-byte swizzle: unit u of row r at (u ^ (r & 7)) * 16
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        *reinterpret_cast<uint4*>(slot0 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_uint4(a0[4 * u], a0[4 * u + 1], a0[4 * u + 2], a0[4 * u + 3]);
+        *reinterpret_cast<uint4*>(slot1 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_uint4(a1[4 * u], a1[4 * u + 1], a1[4 * u + 2], a1[4 * u + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int row = row_base + i * BQ + q4 * 32;
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         &tmDQ), "r"(smem_u32(slot0)), "r"(col), "r"(row) : "memory");
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         &tmDQ), "r"(smem_u32(slot1)), "r"(col + 32), "r"(row) : "memory");
+        tma_store_commit();
+      }
+    }
+    if (lane == 0) tma_store_wait0();
+    __syncwarp();
+    // dK, dV (TMEM lane = key row)
+    if (ok && mbar_wait(dkv_full, 0, p.st, 59, abort_flag)) {
+      tc_fence_after();
+      const int r = q4 * 32 + lane;
+      const int key = k0 + r;
+      uint32_t kv[32];
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        bf16* dst = which ? (p.dv + (long)(row_base + key) * p.dv_rs + col)
+                          : (p.dk + (long)(row_base + key) * p.dk_rs + col);
+        const float sc = which ? 1.f : p.scale;
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
+          tc_wait_ld();
+          if (key < S) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
+              uint4 o;
+              o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
+              o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
+              o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
+              o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
+              *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fabw
+
+// Attention backward core on tcgen05 (head_dim 64): writes dK, dV and
+// reduce-adds the unscaled dQ into dq_acc (fp32 [B*S, H*HD], pre-zeroed by
+// the caller). lse / delta fp32 [B, H, S].
+void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
+                       torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
+                       double scale) {
+  const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  TORCH_CHECK(HD == 64, "tcgen05 attention backward supports head_dim 64");
+  for (auto* t : {&q, &k, &v, &dout, &dk, &dv}) {
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == S &&
+                    t->size(2) == H && t->size(3) == HD,
+                "q/k/v/dout/dk/dv must be bf16 [B, S, H, HD]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == S * t->stride(1),
+                "tensors must be token-major with contiguous heads");
+  }
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= B * S * H * HD, "dq_acc fp32 [B*S*H*HD]");
+  c10::cuda::CUDAGuard guard(q.get_device());
+  auto mk = [&](const torch::Tensor& t) {
+    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * S),
+                        (uint64_t)t.stride(1) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  CUtensorMap tq = mk(q), tk = mk(k), tv = mk(v), tdo = mk(dout);
+  CUtensorMap tdq = make_tmap_2d(dq_acc.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)(H * HD),
+                                 (uint64_t)(B * S), (uint64_t)(H * HD) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  fabw::Params p{};
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dk = reinterpret_cast<fabw::bf16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<fabw::bf16*>(dv.data_ptr());
+  p.dk_rs = dk.stride(1);
+  p.dv_rs = dv.stride(1);
+  p.B = (int)B;
+  p.H = (int)H;
+  p.S = (int)S;
+  p.scale = (float)scale;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.st = status_ptr(q.get_device());
+  dim3 grid((unsigned)((S + 127) / 128), (unsigned)(B * H));
+  auto st = cur_stream();
+  if (causal) {
+    auto kern = fabw::fa_bwd_tc_kernel<true>;
+    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fabw::SMEM));
+    kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
+  } else {
+    auto kern = fabw::fa_bwd_tc_kernel<false>;
+    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fabw::SMEM));
+    kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
+  }
+  SCIRS_CHECK_LAUNCH();
+}
+
 }  // namespace scirs

@@ -25,7 +25,7 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
                     bool causal, double scale);
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
-                    torch::Tensor delta, bool causal, double scale);
+                    torch::Tensor delta, bool causal, double scale, int64_t impl);
 void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale);
 }  // namespace scirs
@@ -45,7 +45,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bias_grad", &scirs::bias_grad);
   m.def("optim_step", &scirs::optim_step);
   m.def("flash_attn_fwd", &scirs::flash_attn_fwd);
-  m.def("flash_attn_bwd", &scirs::flash_attn_bwd);
+  m.def("flash_attn_bwd", &scirs::flash_attn_bwd, "attention backward", py::arg("dout"), py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"),
+        py::arg("delta"), py::arg("causal"), py::arg("scale"), py::arg("impl") = 1);
   m.def("flash_attn_fwd_tc", &scirs::flash_attn_fwd_tc);
   m.def("status_read_and_clear", &scirs::status_read_and_clear);
   m.def("num_sms", &scirs::num_sms);

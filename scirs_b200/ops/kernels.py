@@ -25,6 +25,8 @@ OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
 # Attention forward implementation: "tcgen05" (TMEM/TMA kernel) or "mma"
 # (warp-level mma.sync kernel). Both are sm_100a kernels of this library.
 ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "tcgen05")
+# Attention backward: "tcgen05" (head_dim 64; other head dims use mma) or "mma".
+ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05")
 
 
 class _Stats:
@@ -276,7 +278,8 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
 def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=True, scale=None):
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, bool(causal), float(scale))
+        _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, bool(causal), float(scale),
+                                      1 if ATTN_BWD_IMPL == "tcgen05" else 0)
         _count(3)
         return
     with torch.enable_grad():

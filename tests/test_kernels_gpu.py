@@ -145,9 +145,13 @@ def test_embedding_and_bias_grad():
 
 
 # ---------------------------------------------------------------------------- attention
+@pytest.mark.parametrize("bwd_impl", ["tcgen05", "mma"])
 @pytest.mark.parametrize("B,S,H,HD,causal", [(2, 256, 4, 64, True), (1, 197, 3, 64, False), (1, 384, 2, 128, True),
-                                             (2, 1024, 2, 64, True)])
-def test_flash_attention(B, S, H, HD, causal):
+                                             (2, 1024, 2, 64, True), (1, 300, 2, 64, True)])
+def test_flash_attention(B, S, H, HD, causal, bwd_impl, monkeypatch):
+    from scirs_b200 import _ext
+
+    monkeypatch.setattr(K, "ATTN_BWD_IMPL", bwd_impl)
     qkv = rnd(B, S, 3, H, HD, seed=11)
     q, k, v = qkv.unbind(2)
     out = torch.empty(B, S, H, HD, device=DEV, dtype=torch.bfloat16)
@@ -168,6 +172,7 @@ def test_flash_attention(B, S, H, HD, causal):
     assert rel_err(dq, qf.grad) < 2e-2
     assert rel_err(dk, kf.grad) < 2e-2
     assert rel_err(dv, vf.grad) < 2e-2
+    _ext.check_status()
 
 
 @pytest.mark.parametrize("impl", ["tcgen05", "mma"])
