@@ -663,4 +663,127 @@ void bias_grad(torch::Tensor dy, torch::Tensor out) {
   SCIRS_CHECK_LAUNCH();
 }
 
+
+
+// ===========================================================================
+// No-allocation entry point (C ABI). This entry point has no counterpart in
+// the reference; it exists for callers of this library that cannot allocate
+// device memory: code that drives the kernels from C or another language
+// through a fixed device-memory budget with no allocator of its own, and code
+// that must not call cudaMalloc at the point of the call (cudaMalloc may
+// synchronise the device and is not allowed while a stream is being captured
+// into a CUDA graph).
+//
+// scirs_layernorm_bwd_noalloc() computes the same LayerNorm backward as
+// layernorm_bwd() (same kernels), but its per-block partial column sums live
+// in the file-scope array below instead of a caller-provided scratch tensor.
+//   * Limit: kNoAllocScratchFloats fp32 values (4 MiB) per device. A call needs
+//     nblocks * 3 * D of them; nblocks is reduced to fit, and a row width D
+//     whose single block would not fit (D > kNoAllocMaxD) is rejected with a
+//     clear error. Every GPU that loads this library holds the array until
+//     the process exits.
+//   * The first call on a device looks up the array's device address with
+//     cudaGetSymbolAddress (with that device current); make that first call
+//     before any stream capture. Later calls do no set-up.
+//   * All calls share the array. Each call writes every partial it later
+//     reads, so nothing needs clearing between calls, but calls whose
+//     executions overlap on the GPU (different streams without ordering, or
+//     different host threads) race on it; serialise them.
+//   * dw, db and (if given) dsum are accumulated into, exactly like
+//     layernorm_bwd(). No cudaMalloc, cudaFree or allocating library routine
+//     is called.
+// Returns 0 on success, a negative code on invalid arguments (message via
+// scirs_noalloc_last_error()), or a positive cudaError_t.
+// ===========================================================================
+constexpr long kNoAllocScratchFloats = 1L << 20;
+constexpr int kNoAllocMaxD = (int)(kNoAllocScratchFloats / 3);
+static __device__ __align__(256) float g_noalloc_ln_scratch[kNoAllocScratchFloats];
+
+namespace {
+float* g_noalloc_ptr[64] = {nullptr};
+std::mutex g_noalloc_mu;
+thread_local std::string g_noalloc_err;
+
+// Device address of the scratch array for `device` (looked up once).
+cudaError_t noalloc_scratch(int device, float** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_ln_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[device] = reinterpret_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[device];
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* scirs_noalloc_last_error() {
+  return g_noalloc_err.c_str();
+}
+
+extern "C" __attribute__((visibility("default"))) int scirs_layernorm_bwd_noalloc(
+    const void* dy, const void* x, const void* w, const float* mean, const float* rstd, const void* dresid,
+    void* dx, float* dw, float* db, float* dsum, long long rows, int D, void* stream) {
+  g_noalloc_err.clear();
+  if (rows <= 0 || D <= 0 || D % 8 != 0) {
+    g_noalloc_err = "rows must be > 0 and D a positive multiple of 8";
+    return -1;
+  }
+  if (D > kNoAllocMaxD) {
+    g_noalloc_err = "D = " + std::to_string(D) + " exceeds the no-allocation scratch limit (D <= " +
+                    std::to_string(kNoAllocMaxD) + ")";
+    return -2;
+  }
+  if (dy == nullptr || x == nullptr || w == nullptr || mean == nullptr || rstd == nullptr || dx == nullptr ||
+      dw == nullptr || db == nullptr) {
+    g_noalloc_err = "null pointer argument";
+    return -3;
+  }
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return (int)e;
+  if (device < 0 || device >= 64) {
+    g_noalloc_err = "device index out of range";
+    return -4;
+  }
+  float* part = nullptr;
+  e = noalloc_scratch(device, &part);
+  if (e != cudaSuccess) return (int)e;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return (int)e;
+  const int M = (int)rows;
+  long nb = std::min<long>(2L * sms, (rows + 7) / 8);
+  nb = std::max<long>(1, std::min<long>(nb, kNoAllocScratchFloats / (3L * D)));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto dyp = (const bf16*)dy, xp = (const bf16*)x, wp = (const bf16*)w, dr = (const bf16*)dresid;
+  auto dxp = (bf16*)dx;
+  const int inb = (int)nb;
+#define NOALLOC_LNB(NV, RW)                                                                        \
+  {                                                                                                \
+    const int smem_b = (8 / RW) * 3 * (RW * 256 * NV) * (int)sizeof(float);                      \
+    e = cudaFuncSetAttribute(ln_bwd_kernel<NV, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                             smem_b);                                                              \
+    if (e != cudaSuccess) return (int)e;                                                           \
+    ln_bwd_kernel<NV, RW><<<inb, 256, smem_b, s>>>(dyp, xp, wp, mean, rstd, dr, dxp, part, M);     \
+  }
+  switch (D) {
+    case 256: NOALLOC_LNB(1, 1); break;
+    case 512: NOALLOC_LNB(2, 1); break;
+    case 768: NOALLOC_LNB(3, 1); break;
+    case 1024: NOALLOC_LNB(4, 1); break;
+    case 1536: NOALLOC_LNB(3, 2); break;
+    case 2048: NOALLOC_LNB(4, 2); break;
+    case 3072: NOALLOC_LNB(3, 4); break;
+    case 4096: NOALLOC_LNB(4, 4); break;
+    default: ln_bwd_generic<<<inb, 256, 0, s>>>(dyp, xp, wp, mean, rstd, dr, dxp, part, M, D);
+  }
+#undef NOALLOC_LNB
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return (int)e;
+  ln_bwd_reduce<<<(3 * D + 255) / 256, 256, 0, s>>>(part, inb, D, dw, db, dsum);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace scirs
