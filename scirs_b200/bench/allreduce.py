@@ -1,0 +1,76 @@
+"""Fused gradient all-reduce sweep: in-kernel NVLink all-reduce vs NCCL.
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        -m scirs_b200.bench.allreduce [--min 1024] [--max 1073741824] [--iters 20]
+
+Payload sizes are bf16 bytes on the wire (fp32 gradients in, fp32 out; the
+kernel scales by 1/N and casts to bf16 when publishing). NCCL runs
+all_reduce(AVG) on a bf16 tensor of the same element count, i.e. the same
+bytes. Every number is device time from CUDA events, max over ranks.
+Bus bandwidth = 2 (N-1)/N * bytes / time; roofline = the time to move
+2 (N-1)/N * bytes per rank over NVLink at the measured 770 GB/s per
+direction. Rank 0 prints one JSON line per size.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+import torch.distributed as dist
+
+from .. import _ext
+from ..parallel import dist as sdist
+from ..parallel.nvlink import NVLinkComm
+
+LINK_GBS = 770.0
+
+
+def _time(fn, iters, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return sdist.max_over_ranks(e0.elapsed_time(e1) / iters)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--min", type=int, default=1024)
+    ap.add_argument("--max", type=int, default=1 << 30)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    rank, world, local = sdist.init(timeout_s=120)
+    dev = torch.device("cuda", local)
+    comm = NVLinkComm(area_bytes=max(args.max, 1 << 20) + (1 << 20), timeout_s=10.0)
+    size = args.min
+    while size <= args.max:
+        n = max(8 * world, (size // 2) // (8 * world) * (8 * world))
+        x = torch.randn(n, device=dev)
+        y = torch.empty_like(x)
+        xb = x.to(torch.bfloat16)
+        t_ours = _time(lambda: comm.allreduce(x, y, 1.0 / world), args.iters)
+        t_nccl = _time(lambda: dist.all_reduce(xb, op=dist.ReduceOp.AVG), args.iters)
+        nbytes = 2 * n
+        bus = lambda t: 2 * (world - 1) / world * nbytes / (t * 1e-3) / 1e9  # noqa: E731
+        roof_ms = 2 * (world - 1) / world * nbytes / (LINK_GBS * 1e9) * 1e3
+        if rank == 0:
+            print(json.dumps({
+                "bytes": nbytes, "n_gpus": world, "ours_ms": round(t_ours, 4), "nccl_ms": round(t_nccl, 4),
+                "ours_busbw_GBs": round(bus(t_ours), 1), "nccl_busbw_GBs": round(bus(t_nccl), 1),
+                "speedup_vs_nccl": round(t_nccl / t_ours, 3), "roofline_frac": round(roof_ms / t_ours, 3),
+            }), flush=True)
+        size *= 4
+    _ext.check_status(local)
+    comm.close()
+    sdist.shutdown()
+
+
+if __name__ == "__main__":
+    main()
