@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--dp-mode", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--layers", type=int, default=12)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="run the step eagerly instead of as a CUDA graph")
     return ap.parse_args()
 
 
@@ -176,6 +177,8 @@ def main():
         model.configure_adamw(lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
         if world > 1:
             data_parallel(model, mode=args.dp_mode)
+        if not args.no_graph:
+            model.enable_cuda_graph()
 
         def step(tok, tgt):
             return model.train_step(tok, tgt)
@@ -303,6 +306,7 @@ def main():
                 if N > 1
                 else None,
                 "optimizer": "AdamW (fp32 master, wd 0.1, clip 1.0)",
+                "cuda_graph": (not args.no_graph) if args.impl == "ours" else False,
                 "l2": "no flush: per-step working set (activations, logits, optimizer state) is many GB >> 126 MB L2",
                 "model_flops_per_token": flops_tok,
                 "mfu_vs_measured_sustained_bf16": round(mfu, 4),

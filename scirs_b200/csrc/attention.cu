@@ -545,8 +545,7 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 #define FA_FWD(HD_, CAUSAL_)                                                                             \
   {                                                                                                      \
     auto kern = attn::fa_fwd_kernel<HD_, CAUSAL_>;                                                       \
-    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,             \
-                                          attn::FwdCfg<HD_>::SMEM));                                     \
+    set_max_smem((const void*)kern, attn::FwdCfg<HD_>::SMEM);                                     \
     kern<<<grid, 256, attn::FwdCfg<HD_>::SMEM, st>>>(p);                                                 \
   }
   if (HD == 64) {
@@ -621,8 +620,7 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
 #define FA_BWD(HD_, CAUSAL_)                                                                             \
   {                                                                                                      \
     auto kern = attn::fa_bwd_kernel<HD_, CAUSAL_>;                                                       \
-    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,             \
-                                          attn::BwdCfg<HD_>::SMEM));                                     \
+    set_max_smem((const void*)kern, attn::BwdCfg<HD_>::SMEM);                                     \
     kern<<<grid, 128, attn::BwdCfg<HD_>::SMEM, st>>>(p);                                                 \
   }
   if (HD == 64) {

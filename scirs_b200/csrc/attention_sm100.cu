@@ -370,8 +370,7 @@ void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
 #define FATC(HD_, C_)                                                                                      \
   {                                                                                                        \
     auto kern = fatc::fa_fwd_tc_kernel<HD_, C_>;                                                           \
-    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,               \
-                                          fatc::Cfg<HD_>::SMEM));                                          \
+    set_max_smem((const void*)kern, fatc::Cfg<HD_>::SMEM);                                          \
     kern<<<grid, fatc::kThreads, fatc::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);                               \
   }
   if (HD == 64) {
@@ -768,11 +767,11 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   auto st = cur_stream();
   if (causal) {
     auto kern = fabw::fa_bwd_tc_kernel<true>;
-    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fabw::SMEM));
+    set_max_smem((const void*)kern, fabw::SMEM);
     kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
   } else {
     auto kern = fabw::fa_bwd_tc_kernel<false>;
-    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fabw::SMEM));
+    set_max_smem((const void*)kern, fabw::SMEM);
     kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
   }
   SCIRS_CHECK_LAUNCH();

@@ -38,7 +38,7 @@ namespace scirs {
 namespace comm {
 
 constexpr int kMaxRanks = 8;
-constexpr int kMaxBlocks = 128;
+constexpr int kMaxBlocks = 256;
 constexpr int kBarriers = 3;  // phase barriers 0, 1 and the exit barrier 2
 constexpr long kFlagBytes = (long)kBarriers * kMaxBlocks * kMaxRanks * 4;
 
@@ -143,56 +143,82 @@ __device__ __forceinline__ void piece(long v0, long v1, int world, int r, long& 
   p1 = min(v1, p0 + per);
 }
 
+// Memory-level parallelism: every thread keeps kU independent 16-byte vectors
+// in flight per step (phase 2 keeps one vector per peer in flight instead),
+// and blocks are kept small in registers (<= 64) so they can co-reside with
+// a persistent GEMM CTA while overlapping the backward pass.
+constexpr int kU = 4;
+constexpr int kCommThreads = 256;
+
 // ---------------------------------------------------------------------------
 // All-reduce (sum * scale), fp32 in -> fp32 out, bf16 on the wire.
 // Two-shot: publish scaled bf16 copy; reduce own piece from all peers into
 // area1; gather every reduced piece. Every rank ends with bit-identical output.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) allreduce_kernel(const Args a) {
+__global__ void __launch_bounds__(kCommThreads, 4) allreduce_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
   const unsigned epoch = a.epochs[blockIdx.x] + 1;
   const long nvec = a.n / 8;
+  const long bd = blockDim.x;
   long v0, v1;
   block_slice(nvec, a.world, v0, v1);
   uint4* my_in = reinterpret_cast<uint4*>(a.peers.base[a.rank]);
   // phase 1: scale + cast + publish
-  for (long v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
-    float f[8];
-    load8f(a.in32 + v * 8, f);
+  for (long base = v0 + threadIdx.x; base < v1; base += bd * kU) {
+    float f[kU][8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] *= a.scale;
-    my_in[v] = pack8(f);
+    for (int u = 0; u < kU; ++u)
+      if (base + u * bd < v1) load8f(a.in32 + (base + u * bd) * 8, f[u]);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (base + u * bd < v1) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
+        my_in[base + u * bd] = pack8(f[u]);
+      }
+    }
   }
   bool ok = block_barrier(a, 0, epoch, &sfail);
-  // phase 2: reduce my piece
+  // phase 2: reduce my piece (one load per peer in flight per vector)
   long p0, p1;
   piece(v0, v1, a.world, a.rank, p0, p1);
   if (ok) {
     uint4* my_out = reinterpret_cast<uint4*>(a.peers.base[a.rank] + a.area_bytes);
-    for (long v = p0 + threadIdx.x; v < p1; v += blockDim.x) {
+    for (long v = p0 + threadIdx.x; v < p1; v += bd) {
+      uint4 x[kMaxRanks];
+#pragma unroll
+      for (int k = 0; k < kMaxRanks; ++k)
+        if (k < a.world) x[k] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[(a.rank + k) % a.world]) + v);
       float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-      for (int k = 0; k < kMaxRanks; ++k) {
-        if (k >= a.world) break;
-        const int src = (a.rank + k) % a.world;  // stagger peers
-        acc8(__ldcg(reinterpret_cast<const uint4*>(a.peers.base[src]) + v), f);
-      }
+      for (int k = 0; k < kMaxRanks; ++k)
+        if (k < a.world) acc8(x[k], f);
       my_out[v] = pack8(f);
     }
     ok = block_barrier(a, 1, epoch, &sfail);
   }
   // phase 3: gather every reduced piece (own included, for bit-identical results)
   if (ok) {
-    for (int k = 0; k < a.world; ++k) {
-      const int src = (a.rank + k) % a.world;
-      long q0, q1;
-      piece(v0, v1, a.world, src, q0, q1);
-      const uint4* o = reinterpret_cast<const uint4*>(a.peers.base[src] + a.area_bytes);
-      for (long v = q0 + threadIdx.x; v < q1; v += blockDim.x) {
-        float f[8];
-        unpack8(__ldcg(o + v), f);
-        store8f(a.out32 + v * 8, f);
+    const long per = (v1 - v0 + a.world - 1) / a.world;
+    for (long base = v0 + threadIdx.x; base < v1; base += bd * kU) {
+      uint4 x[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long v = base + u * bd;
+        if (v < v1) {
+          const int src = (int)((v - v0) / per);
+          x[u] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[src] + a.area_bytes) + v);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long v = base + u * bd;
+        if (v < v1) {
+          float f[8];
+          unpack8(x[u], f);
+          store8f(a.out32 + v * 8, f);
+        }
       }
     }
   }
@@ -207,41 +233,53 @@ __global__ void __launch_bounds__(512) allreduce_kernel(const Args a) {
 // Reduce-scatter (sum * scale): fp32 full input -> fp32 shard output.
 // Rank r's shard is elements [r*n/world, (r+1)*n/world).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) reduce_scatter_kernel(const Args a) {
+__global__ void __launch_bounds__(kCommThreads, 4) reduce_scatter_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
   const unsigned epoch = a.epochs[blockIdx.x] + 1;
   const long area = 0;
+  const long bd = blockDim.x;
   const long shard_vec = a.n / 8 / a.world;
   // Block b handles vectors [b*per, ...) of every shard.
   const long per = (shard_vec + gridDim.x - 1) / gridDim.x;
   const long s0 = min(shard_vec, (long)blockIdx.x * per), s1 = min(shard_vec, s0 + per);
   uint4* my_in = reinterpret_cast<uint4*>(a.peers.base[a.rank] + area);
-  for (int r = 0; r < a.world; ++r) {
-    const long off = (long)r * shard_vec;
-    for (long v = s0 + threadIdx.x; v < s1; v += blockDim.x) {
-      float f[8];
-      load8f(a.in32 + (off + v) * 8, f);
+  const long span = s1 - s0;
+  // phase 1: publish the block's slice of every shard (scaled, bf16)
+  for (long base = threadIdx.x; base < span * a.world; base += bd * kU) {
+    float f[kU][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] *= a.scale;
-      my_in[off + v] = pack8(f);
+    for (int u = 0; u < kU; ++u) {
+      const long t = base + u * bd;
+      if (t < span * a.world) load8f(a.in32 + ((t / span) * shard_vec + s0 + t % span) * 8, f[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long t = base + u * bd;
+      if (t < span * a.world) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
+        my_in[(t / span) * shard_vec + s0 + t % span] = pack8(f[u]);
+      }
     }
   }
   const bool ok = block_barrier(a, 0, epoch, &sfail);
   if (ok) {
     const long off = (long)a.rank * shard_vec;
-    for (long v = s0 + threadIdx.x; v < s1; v += blockDim.x) {
+    for (long v = s0 + threadIdx.x; v < s1; v += bd) {
+      uint4 x[kMaxRanks];
+#pragma unroll
+      for (int k = 0; k < kMaxRanks; ++k)
+        if (k < a.world)
+          x[k] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[(a.rank + k) % a.world] + area) + off + v);
       float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int k = 0; k < a.world; ++k) {
-        const int src = (a.rank + k) % a.world;
-        acc8(__ldcg(reinterpret_cast<const uint4*>(a.peers.base[src] + area) + off + v), f);
-      }
+#pragma unroll
+      for (int k = 0; k < kMaxRanks; ++k)
+        if (k < a.world) acc8(x[k], f);
       store8f(a.out32 + v * 8, f);
     }
   }
   __syncthreads();
-  // exit barrier: every peer is done reading this call's buffers, so the next
-  // collective (of any kind) may overwrite them
   if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
   if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
 }
@@ -250,35 +288,49 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(const Args a) {
 // All-gather: bf16 shard in -> bf16 full output. Push model: every rank
 // stores its shard straight into every peer's buffer, then one barrier.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) allgather_kernel(const Args a) {
+__global__ void __launch_bounds__(kCommThreads, 4) allgather_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
   const unsigned epoch = a.epochs[blockIdx.x] + 1;
   const long area = 0;
+  const long bd = blockDim.x;
   const long shard_vec = a.n / 8 / a.world;
   const long per = (shard_vec + gridDim.x - 1) / gridDim.x;
   const long s0 = min(shard_vec, (long)blockIdx.x * per), s1 = min(shard_vec, s0 + per);
   const long off = (long)a.rank * shard_vec;
   const uint4* src = reinterpret_cast<const uint4*>(a.in16);
-  for (long v = s0 + threadIdx.x; v < s1; v += blockDim.x) {
-    const uint4 q = src[v];
+  for (long base = s0 + threadIdx.x; base < s1; base += bd * kU) {
+    uint4 q[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (base + u * bd < s1) q[u] = src[base + u * bd];
     for (int k = 0; k < a.world; ++k) {
-      const int dst = (a.rank + k) % a.world;
-      reinterpret_cast<uint4*>(a.peers.base[dst] + area)[off + v] = q;
+      uint4* dst = reinterpret_cast<uint4*>(a.peers.base[(a.rank + k) % a.world] + area) + off;
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (base + u * bd < s1) dst[base + u * bd] = q[u];
     }
   }
   const bool ok = block_barrier(a, 0, epoch, &sfail);
   if (ok && a.out16 != nullptr) {
     const uint4* full = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + area);
     uint4* out = reinterpret_cast<uint4*>(a.out16);
-    for (int r = 0; r < a.world; ++r) {
-      const long o = (long)r * shard_vec;
-      for (long v = s0 + threadIdx.x; v < s1; v += blockDim.x) out[o + v] = __ldcg(full + o + v);
+    const long span = s1 - s0;
+    for (long base = threadIdx.x; base < span * a.world; base += bd * kU) {
+      uint4 x[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long t = base + u * bd;
+        if (t < span * a.world) x[u] = __ldcg(full + (t / span) * shard_vec + s0 + t % span);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long t = base + u * bd;
+        if (t < span * a.world) out[(t / span) * shard_vec + s0 + t % span] = x[u];
+      }
     }
   }
   __syncthreads();
-  // exit barrier: every peer is done reading this call's buffers, so the next
-  // collective (of any kind) may overwrite them
   if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
   if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
 }
@@ -404,9 +456,10 @@ static CommState& get_cs(int64_t id) {
 
 static int pick_blocks(long nvec_total, int world, int64_t blocks) {
   if (blocks > 0) return (int)std::min<int64_t>(blocks, comm::kMaxBlocks);
-  // ~8 vectors per thread per block at least; few SMs so comm overlaps compute
-  long b = (nvec_total + 512L * 8 - 1) / (512L * 8);
-  return (int)std::max<long>(1, std::min<long>(b, 32));
+  // at least kU vectors per thread per block; up to two blocks per SM for
+  // large payloads (the blocks are small enough to co-reside with a GEMM CTA)
+  long b = (nvec_total + (long)comm::kCommThreads * comm::kU - 1) / ((long)comm::kCommThreads * comm::kU);
+  return (int)std::max<long>(1, std::min<long>(b, comm::kMaxBlocks));
 }
 
 // out32 = scale * sum_over_ranks(in32); in/out fp32 contiguous, may alias.
@@ -428,7 +481,7 @@ void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double 
   a.epochs = cs.epochs_ar;
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8, cs.world, blocks);
-  comm::allreduce_kernel<<<nb, 512, 0, cur_stream()>>>(a);
+  comm::allreduce_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   SCIRS_CHECK_LAUNCH();
 }
 
@@ -451,7 +504,7 @@ void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, do
   a.epochs = cs.epochs_ar;  // one epoch sequence per block shared by every collective kind
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
-  comm::reduce_scatter_kernel<<<nb, 512, 0, cur_stream()>>>(a);
+  comm::reduce_scatter_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   SCIRS_CHECK_LAUNCH();
 }
 
@@ -472,7 +525,7 @@ void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t
   a.epochs = cs.epochs_ar;
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
-  comm::allgather_kernel<<<nb, 512, 0, cur_stream()>>>(a);
+  comm::allgather_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   SCIRS_CHECK_LAUNCH();
 }
 

@@ -45,3 +45,20 @@ CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, uint64_t i
 inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 }  // namespace scirs
+
+#include <set>
+
+namespace scirs {
+// Set a kernel's max dynamic shared memory once per device (keeps the call
+// out of later launches, e.g. while a CUDA graph is being captured).
+inline void set_max_smem(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  SCIRS_CHECK_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kern, dev})) return;
+  SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({kern, dev});
+}
+}  // namespace scirs

@@ -568,8 +568,7 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
 #define LNB(NV, RW)                                                                                 \
   {                                                                                                 \
     const int smem_b = (8 / RW) * 3 * (RW * 256 * NV) * (int)sizeof(float);                       \
-    SCIRS_CHECK_CUDA(cudaFuncSetAttribute(ln_bwd_kernel<NV, RW>,                                    \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b));    \
+    set_max_smem((const void*)ln_bwd_kernel<NV, RW>, smem_b);    \
     ln_bwd_kernel<NV, RW><<<nb, 256, smem_b, s>>>(dyp, xp, wp, mp, rp, dr, dxp, pp, M);             \
   }
   switch (D) {

@@ -24,9 +24,13 @@ enum OptMode : int { OPT_ADAM = 0, OPT_ADAMW = 1, OPT_SGD = 2, OPT_RMSPROP = 3, 
 
 // hp layout (fp32, device):
 //  0 lr, 1 beta1 | momentum | rho, 2 beta2, 3 eps, 4 weight_decay,
-//  5 bias_correction1, 6 bias_correction2, 7 grad multiplier, 8 max_norm (<=0: off)
+//  5 bias_correction1, 6 bias_correction2, 7 grad multiplier, 8 max_norm (<=0: off),
+//  9 step counter, 10 device-managed bias correction flag. When the flag is
+//  set, the norm kernel increments the step counter and the update kernel
+//  derives the bias corrections from it, so a captured step replays without
+//  any host writes.
 struct HP {
-  float lr, b1, b2, eps, wd, bc1, bc2, gmul, max_norm;
+  float lr, b1, b2, eps, wd, bc1, bc2, gmul, max_norm, step, dev_step;
 };
 
 template <typename G>
@@ -41,7 +45,9 @@ __device__ __forceinline__ float gload<__nv_bfloat16>(const __nv_bfloat16* g, lo
 }
 
 template <typename G>
-__global__ void __launch_bounds__(256) sumsq_kernel(const G* __restrict__ g, long n, float* __restrict__ part) {
+__global__ void __launch_bounds__(256) sumsq_kernel(const G* __restrict__ g, long n, float* __restrict__ part,
+                                                    float* __restrict__ hp_dev) {
+  if (blockIdx.x == 0 && threadIdx.x == 0 && hp_dev[10] != 0.f) hp_dev[9] += 1.f;
   float s = 0.f;
   for (long i = blockIdx.x * 256L + threadIdx.x; i < n; i += (long)gridDim.x * 256) {
     float x = gload(g, i);
@@ -81,7 +87,11 @@ __global__ void __launch_bounds__(256)
                  __nv_bfloat16* __restrict__ p16, long n, long n_decay, const uint8_t* __restrict__ decay_mask,
                  const float* __restrict__ hp_dev, const float* __restrict__ part, int nparts,
                  float* __restrict__ norm_out) {
-  const HP h = *reinterpret_cast<const HP*>(hp_dev);
+  HP h = *reinterpret_cast<const HP*>(hp_dev);
+  if (h.dev_step != 0.f) {
+    h.bc1 = 1.f - powf(h.b1, h.step);
+    h.bc2 = 1.f - powf(h.b2, h.step);
+  }
   float gmul = h.gmul;
   if (part != nullptr) {
     // global gradient norm (of the unscaled gradient)
@@ -145,7 +155,7 @@ void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch:
   CHECK_CONTIG(params);
   CHECK_CONTIG(grads);
   CHECK_DTYPE(hp, at::kFloat);
-  TORCH_CHECK(hp.numel() >= 9 && hp.is_cuda(), "hp must be a device fp32 tensor with 9 entries");
+  TORCH_CHECK(hp.numel() >= 11 && hp.is_cuda(), "hp must be a device fp32 tensor with 11 entries");
   const long n = params.numel();
   TORCH_CHECK(grads.numel() == n, "grads size mismatch");
   c10::cuda::CUDAGuard guard(params.get_device());
@@ -174,9 +184,9 @@ void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch:
     partp = part->data_ptr<float>();
     if (bf)
       sumsq_kernel<__nv_bfloat16><<<nparts, 256, 0, st>>>(
-          reinterpret_cast<const __nv_bfloat16*>(grads.data_ptr()), n, partp);
+          reinterpret_cast<const __nv_bfloat16*>(grads.data_ptr()), n, partp, hp.data_ptr<float>());
     else
-      sumsq_kernel<float><<<nparts, 256, 0, st>>>(grads.data_ptr<float>(), n, partp);
+      sumsq_kernel<float><<<nparts, 256, 0, st>>>(grads.data_ptr<float>(), n, partp, hp.data_ptr<float>());
     SCIRS_CHECK_LAUNCH();
   }
   const uint8_t* mk = nullptr;

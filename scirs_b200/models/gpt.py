@@ -38,6 +38,7 @@ import torch
 
 from ..ops import kernels as K
 from ..utils.flat import FlatParams
+from .transformer import BlockActs, FusedTrainerMixin, add_block_params, block_backward, block_forward
 
 
 @dataclass
@@ -102,46 +103,21 @@ class GPTConfig:
         return 3.0 * (mm + attn)
 
 
-class _Acts:
+class _Acts(BlockActs):
     """Preallocated activations for one micro-batch shape."""
 
     def __init__(self, cfg: GPTConfig, B: int, S: int, device):
-        M, D, F, L = B * S, cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
-        H = cfg.num_attention_heads
-        bf, f32 = torch.bfloat16, torch.float32
-        e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=device)  # noqa: E731
-        self.B, self.S, self.M = B, S, M
-        self.x = [e(M, D) for _ in range(L + 1)]  # residual stream entering block l
-        self.ln1 = [e(M, D) for _ in range(L)]
-        self.mu1 = [e(M, dt=f32) for _ in range(L)]
-        self.rs1 = [e(M, dt=f32) for _ in range(L)]
-        self.qkv = [e(M, 3 * D) for _ in range(L)]
-        self.att = [e(M, D) for _ in range(L)]
-        self.lse = [e(B, H, S, dt=f32) for _ in range(L)]
-        self.xm = [e(M, D) for _ in range(L)]
-        self.ln2 = [e(M, D) for _ in range(L)]
-        self.mu2 = [e(M, dt=f32) for _ in range(L)]
-        self.rs2 = [e(M, dt=f32) for _ in range(L)]
-        self.h = [e(M, F) for _ in range(L)]
-        self.g = [e(M, F) for _ in range(L)]
-        self.lnf = e(M, D)
-        self.muf = e(M, dt=f32)
-        self.rsf = e(M, dt=f32)
-        self.logits = e(M, cfg.vocab_padded)
-        self.losses = e(M, dt=f32)
-        # backward scratch (shared by all blocks)
-        self.dres = e(M, D)
-        self.dres2 = e(M, D)
-        self.dln = e(M, D)
-        self.datt = e(M, D)
-        self.dqkv = e(M, 3 * D)
-        self.dh = e(M, F)
-        self.dq_acc = e(M * D, dt=f32)
-        self.delta = e(B * H * S, dt=f32)
-        self.ln_part = K.ln_partials(M, D, device)
+        D, F, L, H = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers, cfg.num_attention_heads
+        super().__init__(L, B, S, D, F, H, device)
+        M = B * S
+        self.lnf = torch.empty(M, D, dtype=torch.bfloat16, device=device)
+        self.muf = torch.empty(M, dtype=torch.float32, device=device)
+        self.rsf = torch.empty(M, dtype=torch.float32, device=device)
+        self.logits = torch.empty(M, cfg.vocab_padded, dtype=torch.bfloat16, device=device)
+        self.losses = torch.empty(M, dtype=torch.float32, device=device)
 
 
-class GPTModel:
+class GPTModel(FusedTrainerMixin):
     """GPT decoder trained with fused sm_100a kernels (see module docstring).
 
     Usage::
@@ -165,19 +141,7 @@ class GPTModel:
         self.bucket_bounds = [(0, fp.mark())]
         for l in range(cfg.num_hidden_layers):
             s = fp.mark()
-            p = f"h{l}."
-            fp.add(p + "attn.c_attn.weight", (3 * D, D), True)
-            fp.add(p + "attn.c_proj.weight", (D, D), True)
-            fp.add(p + "mlp.c_fc.weight", (F, D), True)
-            fp.add(p + "mlp.c_proj.weight", (D, F), True)
-            fp.add(p + "attn.c_attn.bias", (3 * D,), False)
-            fp.add(p + "attn.c_proj.bias", (D,), False)
-            fp.add(p + "mlp.c_fc.bias", (F,), False)
-            fp.add(p + "mlp.c_proj.bias", (D,), False)
-            fp.add(p + "ln_1.weight", (D,), False)
-            fp.add(p + "ln_1.bias", (D,), False)
-            fp.add(p + "ln_2.weight", (D,), False)
-            fp.add(p + "ln_2.bias", (D,), False)
+            add_block_params(fp, f"h{l}.", D, F)
             if l == cfg.num_hidden_layers - 1:
                 fp.add("ln_f.weight", (D,), False)
                 fp.add("ln_f.bias", (D,), False)
@@ -236,26 +200,12 @@ class GPTModel:
     # --------------------------------------------------------------- forward
     def _forward(self, tokens: torch.Tensor, A: _Acts):
         cfg, fp = self.cfg, self.fp
-        B, S, M = A.B, A.S, A.M
-        D, H, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.head_dim
-        eps = cfg.layer_norm_eps
+        S, H, hd, eps = A.S, cfg.num_attention_heads, cfg.head_dim, cfg.layer_norm_eps
         n = 0
         K.embedding_fwd(tokens, fp.w("wte"), fp.w("wpe")[:S], A.x[0], S)
         n += 1
         for l in range(cfg.num_hidden_layers):
-            p = f"h{l}."
-            K.layernorm_fwd(A.x[l], fp.w(p + "ln_1.weight"), fp.w(p + "ln_1.bias"), A.ln1[l], A.mu1[l], A.rs1[l], eps)
-            K.gemm(A.ln1[l], fp.w(p + "attn.c_attn.weight"), A.qkv[l], bias=fp.w(p + "attn.c_attn.bias"))
-            q, k, v = A.qkv[l].view(B, S, 3, H, hd).unbind(2)
-            K.flash_attn_fwd(q, k, v, A.att[l].view(B, S, H, hd), A.lse[l], causal=True)
-            K.gemm(A.att[l], fp.w(p + "attn.c_proj.weight"), A.xm[l], epi=K.EPI_RESID,
-                   bias=fp.w(p + "attn.c_proj.bias"), aux=A.x[l])
-            K.layernorm_fwd(A.xm[l], fp.w(p + "ln_2.weight"), fp.w(p + "ln_2.bias"), A.ln2[l], A.mu2[l], A.rs2[l], eps)
-            K.gemm(A.ln2[l], fp.w(p + "mlp.c_fc.weight"), A.g[l], epi=K.EPI_BIAS_GELU,
-                   bias=fp.w(p + "mlp.c_fc.bias"), out2=A.h[l])
-            K.gemm(A.g[l], fp.w(p + "mlp.c_proj.weight"), A.x[l + 1], epi=K.EPI_RESID,
-                   bias=fp.w(p + "mlp.c_proj.bias"), aux=A.xm[l])
-            n += 7
+            n += block_forward(fp, f"h{l}.", A, l, H, hd, eps, causal=True)
         L = cfg.num_hidden_layers
         K.layernorm_fwd(A.x[L], fp.w("ln_f.weight"), fp.w("ln_f.bias"), A.lnf, A.muf, A.rsf, eps)
         K.gemm(A.lnf, fp.w("wte"), A.logits)
@@ -265,9 +215,7 @@ class GPTModel:
     # -------------------------------------------------------------- backward
     def _backward(self, tokens: torch.Tensor, A: _Acts):
         cfg, fp = self.cfg, self.fp
-        B, S, M = A.B, A.S, A.M
-        D, H, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.head_dim
-        L = cfg.num_hidden_layers
+        S, H, hd, L = A.S, cfg.num_attention_heads, cfg.head_dim, cfg.num_hidden_layers
         n = 0
         dlog = A.logits  # now holds dloss/dlogits
         # LM head (tied to wte): dx_f = dlogits @ wte ; dwte += dlogits^T @ lnf
@@ -278,40 +226,10 @@ class GPTModel:
                         fp.g("ln_f.bias"), A.ln_part, dsum=fp.g(f"h{L - 1}.mlp.c_proj.bias"))
         n += 4
         for l in reversed(range(L)):
-            p = f"h{l}."
-            # fc2: x[l+1] = xm + g @ W2^T + b2  (its bias gradient, colsum(dres),
-            # was produced by the LayerNorm backward that wrote dres)
-            # dh = (dres @ W2) * gelu'(h), with colsum(dh) = fc1 bias gradient fused in
-            K.gemm(A.dres, fp.w(p + "mlp.c_proj.weight"), A.dh, b_mn=True, epi=K.EPI_DGELU, aux=A.h[l],
-                   bias_grad=fp.g(p + "mlp.c_fc.bias"))
-            K.gemm(A.dres, A.g[l], fp.g(p + "mlp.c_proj.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
-            # fc1: g = gelu(ln2 @ W1^T + b1)
-            K.gemm(A.dh, fp.w(p + "mlp.c_fc.weight"), A.dln, b_mn=True)
-            K.gemm(A.dh, A.ln2[l], fp.g(p + "mlp.c_fc.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
-            # ln2 (+ residual gradient); colsum(dres2) = attention proj bias gradient
-            K.layernorm_bwd(A.dln, A.xm[l], fp.w(p + "ln_2.weight"), A.mu2[l], A.rs2[l], A.dres2,
-                            fp.g(p + "ln_2.weight"), fp.g(p + "ln_2.bias"), A.ln_part, dresid=A.dres,
-                            dsum=fp.g(p + "attn.c_proj.bias"))
-            # proj: xm = x + att @ Wp^T + bp
-            K.gemm(A.dres2, fp.w(p + "attn.c_proj.weight"), A.datt, b_mn=True)
-            K.gemm(A.dres2, A.att[l], fp.g(p + "attn.c_proj.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32,
-                   accumulate=True)
-            # attention
-            q, k, v = A.qkv[l].view(B, S, 3, H, hd).unbind(2)
-            dq, dk, dv = A.dqkv.view(B, S, 3, H, hd).unbind(2)
-            K.flash_attn_bwd(A.datt.view(B, S, H, hd), q, k, v, A.att[l].view(B, S, H, hd), A.lse[l], dq, dk, dv,
-                             A.dq_acc, A.delta, causal=True)
-            # qkv
-            K.gemm(A.dqkv, fp.w(p + "attn.c_attn.weight"), A.dln, b_mn=True)
-            K.gemm(A.dqkv, A.ln1[l], fp.g(p + "attn.c_attn.weight"), a_mn=True, b_mn=True, epi=K.EPI_F32,
-                   accumulate=True)
-            K.bias_grad(A.dqkv, fp.g(p + "attn.c_attn.bias"))
-            # ln1 (+ residual gradient) -> gradient of x[l]; its column sum is
-            # the fc2 bias gradient of block l-1
-            K.layernorm_bwd(A.dln, A.x[l], fp.w(p + "ln_1.weight"), A.mu1[l], A.rs1[l], A.dres,
-                            fp.g(p + "ln_1.weight"), fp.g(p + "ln_1.bias"), A.ln_part, dresid=A.dres2,
-                            dsum=fp.g(f"h{l - 1}.mlp.c_proj.bias") if l > 0 else None)
-            n += 18
+            # d x[l+1] is in A.dres and its column sum (the fc2 bias gradient)
+            # was produced by the LayerNorm backward that wrote it
+            n += block_backward(fp, f"h{l}.", A, l, H, hd, causal=True,
+                                prev_fc2_bias=f"h{l - 1}.mlp.c_proj.bias" if l > 0 else None)
             if self.grad_sync is not None:
                 self.grad_sync.bucket_ready(l + 1)
         K.embedding_bwd(tokens, A.dres, fp.g("wte"), fp.g("wpe")[:S], S)
@@ -333,29 +251,6 @@ class GPTModel:
         n += self._backward(tok, A)
         self.kernel_launches += n
         return A.losses.mean()
-
-    def zero_grad(self):
-        self.fp.grad.zero_()
-
-    def configure_adamw(self, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_grad_norm=1.0):
-        from ..optim.fused import FusedFlatOptimizer
-
-        self.optimizer = FusedFlatOptimizer(
-            self.fp, "adamw", lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, max_grad_norm=max_grad_norm
-        )
-        return self.optimizer
-
-    def train_step(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
-        """zero_grad -> forward/backward -> gradient sync -> fused optimizer step."""
-        if self.optimizer is None:
-            self.configure_adamw()
-        self.zero_grad()
-        loss = self.forward_backward(tokens, targets)
-        if self.grad_sync is not None:
-            self.grad_sync.finish()
-        self.optimizer.step()
-        self.kernel_launches += self.optimizer.launches_per_step
-        return loss
 
     @torch.no_grad()
     def logits(self, tokens: torch.Tensor) -> torch.Tensor:

@@ -295,9 +295,13 @@ def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=Tr
 # Fused optimizer step over flat buffers
 # ---------------------------------------------------------------------------
 def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=None, norm_out=None, decay_mask=None):
-    """One fused step; hp (fp32 [9]) = lr, beta1|momentum|rho, beta2, eps, wd,
-    bias_corr1, bias_corr2, grad multiplier, max_norm."""
+    """One fused step; hp (fp32, >= 11 entries) = lr, beta1|momentum|rho, beta2,
+    eps, wd, bias_corr1, bias_corr2, grad multiplier, max_norm, step counter,
+    device-managed flag. With the flag set (and `part` given) the step counter
+    is incremented on the device and the bias corrections derived from it."""
     m = OPT_MODES[mode] if isinstance(mode, str) else int(mode)
+    if hp.numel() < 11:
+        hp = torch.cat([hp.reshape(-1), torch.zeros(11 - hp.numel(), dtype=hp.dtype, device=hp.device)])
     if params.is_cuda:
         _ext.kernels().optim_step(
             m, params, state1, state2, grads, params16, int(n_decay), decay_mask, hp, part, norm_out
@@ -306,6 +310,9 @@ def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=
         return
     h = hp.tolist()
     lr, b1, b2, eps, wd, bc1, bc2, gmul, max_norm = h[:9]
+    if h[10] != 0 and part is not None:
+        hp[9] += 1
+        bc1, bc2 = 1 - b1 ** float(hp[9]), 1 - b2 ** float(hp[9])
     g = grads.float() * gmul
     if part is not None:
         norm = float(grads.float().norm()) * abs(gmul)

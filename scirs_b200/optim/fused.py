@@ -58,18 +58,33 @@ class FusedFlatOptimizer:
         self.grad_norm = torch.zeros(1, dtype=torch.float32, device=dev)
         self.launches_per_step = 2
 
-    def _hyper(self):
-        self.t += 1
+    def _hp_values(self):
         b1, b2 = self.betas
         if self.mode == "sgd":
             b1 = self.momentum
         elif self.mode == "rmsprop":
             b1 = self.rho
-        bc1 = 1.0 - self.betas[0] ** self.t
-        bc2 = 1.0 - self.betas[1] ** self.t
-        vals = [self.lr, b1, b2, self.eps, self.weight_decay, bc1, bc2, self.grad_multiplier, self.max_grad_norm]
-        self._hp_host[: len(vals)] = torch.tensor(vals, dtype=torch.float32)
-        self.hp.copy_(self._hp_host, non_blocking=True)
+        return [self.lr, b1, b2, self.eps, self.weight_decay, 1.0, 1.0, self.grad_multiplier, self.max_grad_norm]
+
+    def _hyper(self):
+        """Upload hyperparameters when they changed. The step counter and the
+        bias corrections are maintained on the device (hp[9], hp[10] = 1), so a
+        step captured in a CUDA graph replays correctly without host writes."""
+        self.t += 1
+        vals = self._hp_values()
+        if getattr(self, "_uploaded", None) != vals:
+            self._hp_host[: len(vals)] = torch.tensor(vals, dtype=torch.float32)
+            self._hp_host[9] = float(self.t - 1)  # incremented on the device before use
+            self._hp_host[10] = 1.0
+            if getattr(self, "_uploaded", None) is not None:
+                # keep the device step counter: only the first upload sets it
+                torch.cuda.current_stream().synchronize() if self.hp.is_cuda else None
+                self._hp_host[9] = float(self.hp[9].item())
+            self.hp.copy_(self._hp_host, non_blocking=False)
+            self._uploaded = vals
+
+    def set_lr(self, lr: float):
+        self.lr = lr
 
     def step(self):
         self._hyper()
@@ -96,3 +111,5 @@ class FusedFlatOptimizer:
         self.state1.copy_(sd["state1"])
         self.state2.copy_(sd["state2"])
         self.lr = sd.get("lr", self.lr)
+        self.hp[9] = float(self.t)
+        self._uploaded = None

@@ -55,3 +55,23 @@ def test_gpt_engine_trains_gpu():
         l = float(m.train_step(x, y))
     _ext.check_status(0)
     assert l < l0 - 1.0
+
+
+def test_cuda_graph_step_matches_eager():
+    cfg = _cfg()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(5)
+    toks = [torch.randint(0, cfg.vocab_size, (4, 257), generator=g).to(dev) for _ in range(5)]
+    runs = []
+    for graphed in (False, True):
+        m = GPTModel(cfg, device=dev, seed=4)
+        m.configure_adamw(lr=1e-3, weight_decay=0.1, max_grad_norm=1.0)
+        if graphed:
+            m.enable_cuda_graph()
+        losses = [float(m.train_step(t[:, :-1].contiguous(), t[:, 1:].contiguous())) for t in toks]
+        torch.cuda.synchronize()
+        runs.append((losses, m.fp.master.clone()))
+    _ext.check_status(0)
+    (l0, w0), (l1, w1) = runs
+    assert all(abs(a - b) < 2e-3 for a, b in zip(l0, l1)), (l0, l1)
+    assert float((w0 - w1).abs().max()) < 1e-3
