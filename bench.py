@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=12)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="run the step eagerly instead of as a CUDA graph")
+    ap.add_argument("--model", default="gpt2", choices=["gpt2", "vit"],
+                    help="gpt2: GPT-2-small decoder, data parallel (headline); "
+                    "vit: ViT-B/16 encoder, ZeRO (sharded AdamW, grad reduce-scatter, param all-gather)")
+    ap.add_argument("--images", type=int, default=256, help="global batch of the ViT workload")
     return ap.parse_args()
 
 
@@ -134,41 +138,19 @@ def synthetic_batches(n, local_batch, seq, vocab, seed):
         out.append((t[:, :-1].contiguous().pin_memory(), t[:, 1:].contiguous().pin_memory()))
     return out
 
-
-def main():
-    args = parse()
-    if args.impl == "reference":
-        reference_unavailable()
-        return 0
-
+def build_gpt(args, rank, world, local, dev):
+    """GPT-2-small decoder, data parallel (fused in-kernel all-reduce or NCCL)."""
     import torch
-
-    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
-    from scirs_b200.parallel import dist as sdist
-
-    rank, world, local = sdist.init(timeout_s=300)
-    N = args.gpus
-    if N != world:
-        raise SystemExit(f"--gpus {N} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    dev = torch.device("cuda", local)
-    torch.manual_seed(0)
-    assert args.global_batch % world == 0
-    lb = args.global_batch // world
-    S = args.seq
 
     from scirs_b200.models.gpt import GPTConfig
 
+    S, lb = args.seq, args.global_batch // world
     cfg = GPTConfig.gpt2_small()
     cfg.num_hidden_layers = args.layers
     cfg.max_position_embeddings = max(cfg.max_position_embeddings, S)
-
     n_batches = max(args.warmup, 1) + args.steps
     batches = synthetic_batches(n_batches, lb, S, VOCAB, seed=1234 + rank)
-    dev_batches = [(a.to(dev), b.to(dev)) for a, b in batches]
-
-    launches_before = None
     if args.impl == "ours":
-        from scirs_b200 import _ext
         from scirs_b200.models.gpt import GPTModel
         from scirs_b200.ops import kernels as K
         from scirs_b200.parallel.data_parallel import data_parallel
@@ -188,6 +170,9 @@ def main():
             if model.grad_sync is not None and args.dp_mode == "fused":
                 n += model.grad_sync.launches
             return n
+
+        def cleanup():
+            model.release_cuda_graph()
 
     else:
         from torch.distributed.algorithms.ddp_comm_hooks import default_hooks
@@ -212,6 +197,165 @@ def main():
 
         def launches():
             return 0
+
+        def cleanup():
+            pass
+
+    return {
+        "step": step,
+        "launches": launches,
+        "cleanup": cleanup,
+        "batches": batches,
+        "tokens_per_step": args.global_batch * S,
+        "flops_per_token": cfg.flops_per_token(S),
+        "h2d_bytes_per_step": 2 * lb * S * 8,
+        "api": "GPTModel.train_step" if args.impl == "ours" else "torch DDP module + torch.optim.AdamW",
+        "data": "synthetic (tokens uniform in [0, 50257) from a fixed seed; random-init weights)",
+        "config": {
+            "model": "GPT-2-small-shaped decoder: 12 layers, d=768, 12 heads, MLP 3072 GELU, vocab 50257",
+            "layers": cfg.num_hidden_layers,
+            "global_batch": args.global_batch,
+            "seq_len": S,
+            "parallelism": f"dp{world}",
+            "dp_allreduce": (args.dp_mode if args.impl == "ours" else "nccl (DDP, bf16 compress hook)")
+            if world > 1
+            else None,
+            "optimizer": "AdamW (fp32 master, wd 0.1, clip 1.0)",
+        },
+    }
+
+
+def synthetic_images(n, local_batch, classes, seed):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        img = torch.randn(local_batch, 3, 224, 224, generator=g).to(torch.bfloat16)
+        lab = torch.randint(0, classes, (local_batch,), generator=g)
+        out.append((img.pin_memory(), lab.pin_memory()))
+    return out
+
+
+def build_vit(args, rank, world, local, dev):
+    """ViT-B/16 encoder with ZeRO: sharded fp32 master + AdamW moments,
+    per-bucket gradient reduce-scatter overlapped with backward, per-bucket
+    bf16 parameter all-gather prefetched ahead of each block's forward."""
+    import torch
+
+    from scirs_b200.models.vit import ViTConfig
+
+    cfg = ViTConfig.vit_base()
+    cfg.num_layers = args.layers
+    assert args.images % world == 0
+    lb = args.images // world
+    T = cfg.seq_len
+    n_batches = max(args.warmup, 1) + args.steps
+    batches = synthetic_images(n_batches, lb, cfg.num_classes, seed=4321 + rank)
+    hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.05, max_grad_norm=1.0)
+    if args.impl == "ours":
+        from scirs_b200.models.vit import ViTModel
+        from scirs_b200.ops import kernels as K
+        from scirs_b200.parallel.zero import zero_data_parallel
+
+        model = ViTModel(cfg, device=dev, seed=0, bucket_align=64 * world)
+        if world > 1:
+            zero_data_parallel(model, mode=args.dp_mode, **hp)
+        else:
+            model.configure_adamw(**hp)
+        if not args.no_graph:
+            model.enable_cuda_graph()
+
+        def step(img, lab):
+            return model.train_step(img, lab)
+
+        def launches():
+            n = K.STATS.launches
+            if model.grad_sync is not None and args.dp_mode == "fused":
+                n += model.grad_sync.launches
+            return n
+
+        def cleanup():
+            model.release_cuda_graph()
+
+    else:
+        from torch.distributed.optim import ZeroRedundancyOptimizer
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        from scirs_b200.models.torch_vit import TorchViT
+
+        net = TorchViT(cfg).to(dev)
+        if world > 1:
+            net = DDP(net, device_ids=[local], bucket_cap_mb=25, gradient_as_bucket_view=True)
+            opt = ZeroRedundancyOptimizer(net.parameters(), optimizer_class=torch.optim.AdamW, lr=hp["lr"],
+                                          betas=hp["betas"], weight_decay=hp["weight_decay"], fused=True)
+        else:
+            opt = torch.optim.AdamW(net.parameters(), lr=hp["lr"], betas=hp["betas"],
+                                    weight_decay=hp["weight_decay"], fused=True)
+
+        def step(img, lab):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = net(img, lab)
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(net.parameters(), 1.0)
+            opt.step()
+            return loss
+
+        def launches():
+            return 0
+
+        def cleanup():
+            pass
+
+    return {
+        "step": step,
+        "launches": launches,
+        "cleanup": cleanup,
+        "batches": batches,
+        "tokens_per_step": args.images * T,
+        "flops_per_token": cfg.flops_per_image() / T,
+        "h2d_bytes_per_step": lb * (3 * 224 * 224 * 2 + 8),
+        "api": "ViTModel.train_step" if args.impl == "ours" else "torch DDP module + ZeroRedundancyOptimizer(AdamW)",
+        "data": "synthetic (images N(0,1) in bf16, labels uniform in [0, 1000) from a fixed seed; random-init weights)",
+        "config": {
+            "model": "ViT-B/16-shaped encoder: 224x224x3, patch 16, 12 layers, d=768, 12 heads, MLP 3072, "
+            "1000 classes",
+            "layers": cfg.num_layers,
+            "global_batch": args.images,
+            "seq_len": T,
+            "tokens_per_image": T,
+            "parallelism": f"zero-dp{world}" if world > 1 else "dp1",
+            "zero_collectives": (args.dp_mode if args.impl == "ours" else "nccl (DDP + ZeroRedundancyOptimizer)")
+            if world > 1
+            else None,
+            "optimizer": "AdamW (fp32 master, wd 0.05, clip 1.0)",
+        },
+    }
+
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable()
+        return 0
+
+    import torch
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from scirs_b200.parallel import dist as sdist
+
+    rank, world, local = sdist.init(timeout_s=300)
+    N = args.gpus
+    if N != world:
+        raise SystemExit(f"--gpus {N} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    assert args.global_batch % world == 0
+    W = build_vit(args, rank, world, local, dev) if args.model == "vit" else build_gpt(args, rank, world, local, dev)
+    step, launches, batches = W["step"], W["launches"], W["batches"]
+    dev_batches = [(a.to(dev), b.to(dev)) for a, b in batches]
 
     # ---- warm-up
     for i in range(args.warmup):
@@ -240,7 +384,7 @@ def main():
     clk = clocks.stop(N) if rank == 0 else None
     ms = sdist.max_over_ranks(ms_local)
     ms_step = ms / args.steps
-    tokens_per_step = args.global_batch * S
+    tokens_per_step = W["tokens_per_step"]
     value = tokens_per_step / (ms_step / 1e3)
     final_loss = float(loss.item())
 
@@ -249,40 +393,48 @@ def main():
     if not args.no_e2e:
         sdist.barrier()
         torch.cuda.synchronize()
-        tok_d = torch.empty((lb, S), dtype=torch.long, device=dev)
-        tgt_d = torch.empty((lb, S), dtype=torch.long, device=dev)
+        a0, b0 = batches[0]
+        in_d = torch.empty(a0.shape, dtype=a0.dtype, device=dev)
+        tg_d = torch.empty(b0.shape, dtype=b0.dtype, device=dev)
         h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         h0.record()
         for i in range(args.steps):
             a, b = batches[(args.warmup + i) % len(batches)]
-            tok_d.copy_(a, non_blocking=True)
-            tgt_d.copy_(b, non_blocking=True)
-            l = step(tok_d, tgt_d)
+            in_d.copy_(a, non_blocking=True)
+            tg_d.copy_(b, non_blocking=True)
+            l = step(in_d, tg_d)
             _ = float(l.item())
         h1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         e2e_ms = sdist.max_over_ranks(max(h0.elapsed_time(h1), wall * 1e3))
-        bi = 2 * lb * S * 8
         e2e = {
             "value": round(tokens_per_step / (e2e_ms / args.steps / 1e3), 1),
             "unit": "tokens/s",
-            "h2d_bytes_per_step": bi,
+            "h2d_bytes_per_step": W["h2d_bytes_per_step"],
             "d2h_bytes_per_step": 4,
-            "api": "GPTModel.train_step" if args.impl == "ours" else "torch DDP module + torch.optim.AdamW",
+            "api": W["api"],
         }
+    W["cleanup"]()
 
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")))
     except Exception:
         pass
-    flops_tok = cfg.flops_per_token(S)
+    flops_tok = W["flops_per_token"]
     peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
     mfu = value * flops_tok / (peak_tf * 1e12 * N)
 
     if rank == 0:
+        cfg_out = dict(W["config"])
+        cfg_out.update({
+            "cuda_graph": (not args.no_graph) if args.impl == "ours" else False,
+            "l2": "no flush: per-step working set (activations, logits, optimizer state) is many GB >> 126 MB L2",
+            "model_flops_per_token": flops_tok,
+            "mfu_vs_measured_sustained_bf16": round(mfu, 4),
+        })
         out = {
             "metric": METRIC,
             "value": round(value, 1),
@@ -295,22 +447,8 @@ def main():
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic (tokens uniform in [0, 50257) from a fixed seed; random-init weights)",
-            "config": {
-                "model": "GPT-2-small-shaped decoder: 12 layers, d=768, 12 heads, MLP 3072 GELU, vocab 50257",
-                "layers": cfg.num_hidden_layers,
-                "global_batch": args.global_batch,
-                "seq_len": S,
-                "parallelism": f"dp{N}",
-                "dp_allreduce": (args.dp_mode if args.impl == "ours" else "nccl (DDP, bf16 compress hook)")
-                if N > 1
-                else None,
-                "optimizer": "AdamW (fp32 master, wd 0.1, clip 1.0)",
-                "cuda_graph": (not args.no_graph) if args.impl == "ours" else False,
-                "l2": "no flush: per-step working set (activations, logits, optimizer state) is many GB >> 126 MB L2",
-                "model_flops_per_token": flops_tok,
-                "mfu_vs_measured_sustained_bf16": round(mfu, 4),
-            },
+            "data": W["data"],
+            "config": cfg_out,
             "clocks": clk,
             "e2e": e2e,
             "gpu_launches": n_launch if args.impl == "ours" else 0,
@@ -320,6 +458,8 @@ def main():
             out["impl"] = args.impl
         print(json.dumps(out), flush=True)
     if args.impl == "ours":
+        from scirs_b200 import _ext
+
         _ext.check_status(local)
     sdist.shutdown()
     return 0

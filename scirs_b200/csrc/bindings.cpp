@@ -20,7 +20,12 @@ void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor dwte, c1
 void bias_grad(torch::Tensor dy, torch::Tensor out);
 void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch::Tensor state2, torch::Tensor grads,
                 c10::optional<torch::Tensor> params16, int64_t n_decay, c10::optional<torch::Tensor> decay_mask,
-                torch::Tensor hp, c10::optional<torch::Tensor> part, c10::optional<torch::Tensor> norm_out);
+                torch::Tensor hp, c10::optional<torch::Tensor> part, c10::optional<torch::Tensor> norm_out,
+                int64_t parts_ready);
+int64_t grad_sumsq(torch::Tensor grads, torch::Tensor part, torch::Tensor hp);
+void patchify(torch::Tensor img, torch::Tensor out, int64_t patch);
+void vit_embed_fwd(torch::Tensor pe, torch::Tensor cls, torch::Tensor pos, torch::Tensor x, int64_t B);
+void vit_embed_bwd(torch::Tensor dx, torch::Tensor dpe, torch::Tensor dpos, torch::Tensor dcls, int64_t B);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     bool causal, double scale);
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
@@ -43,7 +48,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &scirs::embedding_fwd);
   m.def("embedding_bwd", &scirs::embedding_bwd);
   m.def("bias_grad", &scirs::bias_grad);
-  m.def("optim_step", &scirs::optim_step);
+  m.def("optim_step", &scirs::optim_step, py::arg("mode"), py::arg("params"), py::arg("state1"), py::arg("state2"),
+        py::arg("grads"), py::arg("params16"), py::arg("n_decay"), py::arg("decay_mask"), py::arg("hp"),
+        py::arg("part"), py::arg("norm_out"), py::arg("parts_ready") = 0);
+  m.def("grad_sumsq", &scirs::grad_sumsq);
+  m.def("patchify", &scirs::patchify);
+  m.def("vit_embed_fwd", &scirs::vit_embed_fwd);
+  m.def("vit_embed_bwd", &scirs::vit_embed_bwd);
   m.def("flash_attn_fwd", &scirs::flash_attn_fwd);
   m.def("flash_attn_bwd", &scirs::flash_attn_bwd, "attention backward", py::arg("dout"), py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"),

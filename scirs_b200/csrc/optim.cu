@@ -150,7 +150,8 @@ static void launch_optim(float* p, float* s1, float* s2, const G* g, __nv_bfloat
 // non-finite detection is wanted; norm_out fp32 [1] optional.
 void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch::Tensor state2, torch::Tensor grads,
                 c10::optional<torch::Tensor> params16, int64_t n_decay, c10::optional<torch::Tensor> decay_mask,
-                torch::Tensor hp, c10::optional<torch::Tensor> part, c10::optional<torch::Tensor> norm_out) {
+                torch::Tensor hp, c10::optional<torch::Tensor> part, c10::optional<torch::Tensor> norm_out,
+                int64_t parts_ready) {
   CHECK_DTYPE(params, at::kFloat);
   CHECK_CONTIG(params);
   CHECK_CONTIG(grads);
@@ -179,7 +180,13 @@ void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch:
   float* partp = nullptr;
   int nparts = 0;
   const bool bf = grads.scalar_type() == at::kBFloat16;
-  if (part.has_value() && part->defined()) {
+  if (part.has_value() && part->defined() && parts_ready > 0) {
+    // partial sums of squares already in `part` (e.g. summed over the ranks
+    // that each hold one shard of the gradient)
+    TORCH_CHECK(parts_ready <= part->numel(), "parts_ready exceeds part");
+    nparts = (int)parts_ready;
+    partp = part->data_ptr<float>();
+  } else if (part.has_value() && part->defined()) {
     nparts = (int)std::min<long>(part->numel(), 2L * sms);
     partp = part->data_ptr<float>();
     if (bf)
@@ -215,6 +222,27 @@ void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch:
     default: TORCH_CHECK(false, "unknown optimizer mode ", mode);
   }
 #undef SCIRS_OPT_CASE
+}
+
+// Partial sums of squares of `grads` into part[0 .. nparts) (and the device
+// step counter update of the optimizer). Returns nparts. Used when the global
+// gradient norm needs a reduction across ranks before the update.
+int64_t grad_sumsq(torch::Tensor grads, torch::Tensor part, torch::Tensor hp) {
+  CHECK_CONTIG(grads);
+  CHECK_DTYPE(part, at::kFloat);
+  CHECK_DTYPE(hp, at::kFloat);
+  TORCH_CHECK(hp.numel() >= 11 && hp.is_cuda(), "hp must be a device fp32 tensor with 11 entries");
+  c10::cuda::CUDAGuard guard(grads.get_device());
+  cudaStream_t st = cur_stream();
+  const int nparts = (int)std::min<long>(part.numel(), 2L * num_sms(grads.get_device()));
+  if (grads.scalar_type() == at::kBFloat16)
+    sumsq_kernel<__nv_bfloat16><<<nparts, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(grads.data_ptr()),
+                                                        grads.numel(), part.data_ptr<float>(), hp.data_ptr<float>());
+  else
+    sumsq_kernel<float><<<nparts, 256, 0, st>>>(grads.data_ptr<float>(), grads.numel(), part.data_ptr<float>(),
+                                                hp.data_ptr<float>());
+  SCIRS_CHECK_LAUNCH();
+  return nparts;
 }
 
 }  // namespace scirs

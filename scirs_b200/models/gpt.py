@@ -127,7 +127,7 @@ class GPTModel(FusedTrainerMixin):
         loss = model.train_step(tokens, targets)        # tokens/targets [B, S] int64
     """
 
-    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0):
+    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, bucket_align: int = 64):
         assert cfg.hidden_dropout_prob == 0 and cfg.attention_probs_dropout_prob == 0, "dropout must be 0"
         assert cfg.head_dim in (64, 128), "head_dim must be 64 or 128"
         self.cfg = cfg
@@ -138,6 +138,7 @@ class GPTModel(FusedTrainerMixin):
         # contiguous gradient bucket (ln_f rides with the last block).
         fp.add("wte", (Vp, D), decay=True)
         fp.add("wpe", (cfg.max_position_embeddings, D), decay=True)
+        fp.pad_to(bucket_align)  # buckets split evenly into per-rank shards (ZeRO)
         self.bucket_bounds = [(0, fp.mark())]
         for l in range(cfg.num_hidden_layers):
             s = fp.mark()
@@ -145,6 +146,7 @@ class GPTModel(FusedTrainerMixin):
             if l == cfg.num_hidden_layers - 1:
                 fp.add("ln_f.weight", (D,), False)
                 fp.add("ln_f.bias", (D,), False)
+            fp.pad_to(bucket_align)
             self.bucket_bounds.append((s, fp.mark()))
         fp.allocate(self.device)
         self.fp = fp
@@ -202,13 +204,17 @@ class GPTModel(FusedTrainerMixin):
         cfg, fp = self.cfg, self.fp
         S, H, hd, eps = A.S, cfg.num_attention_heads, cfg.head_dim, cfg.layer_norm_eps
         n = 0
+        self._params_begin()
+        self._wait_params(0)
         K.embedding_fwd(tokens, fp.w("wte"), fp.w("wpe")[:S], A.x[0], S)
         n += 1
         for l in range(cfg.num_hidden_layers):
+            self._wait_params(l + 1)
             n += block_forward(fp, f"h{l}.", A, l, H, hd, eps, causal=True)
         L = cfg.num_hidden_layers
         K.layernorm_fwd(A.x[L], fp.w("ln_f.weight"), fp.w("ln_f.bias"), A.lnf, A.muf, A.rsf, eps)
         K.gemm(A.lnf, fp.w("wte"), A.logits)
+        self._params_end()
         n += 2
         return n
 

@@ -18,29 +18,36 @@ import torch.nn.functional as F
 from .gpt import GPTConfig
 
 
-class Block(nn.Module):
-    def __init__(self, cfg: GPTConfig):
+class TorchBlock(nn.Module):
+    """Pre-LN transformer block (GPT-2 parameter names)."""
+
+    def __init__(self, D: int, H: int, Fd: int, eps: float, causal: bool = True):
         super().__init__()
-        D, Fd = cfg.hidden_size, cfg.intermediate_size
-        self.ln_1 = nn.LayerNorm(D, eps=cfg.layer_norm_eps)
+        self.ln_1 = nn.LayerNorm(D, eps=eps)
         self.attn = nn.Module()
         self.attn.c_attn = nn.Linear(D, 3 * D)
         self.attn.c_proj = nn.Linear(D, D)
-        self.ln_2 = nn.LayerNorm(D, eps=cfg.layer_norm_eps)
+        self.ln_2 = nn.LayerNorm(D, eps=eps)
         self.mlp = nn.Module()
         self.mlp.c_fc = nn.Linear(D, Fd)
         self.mlp.c_proj = nn.Linear(Fd, D)
-        self.H = cfg.num_attention_heads
+        self.H = H
+        self.causal = causal
 
     def forward(self, x):
         B, S, D = x.shape
         h = self.ln_1(x)
         qkv = self.attn.c_attn(h).view(B, S, 3, self.H, D // self.H)
         q, k, v = qkv.unbind(2)
-        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
+        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           is_causal=self.causal)
         x = x + self.attn.c_proj(a.transpose(1, 2).reshape(B, S, D))
         x = x + self.mlp.c_proj(F.gelu(self.mlp.c_fc(self.ln_2(x)), approximate="tanh"))
         return x
+
+
+def Block(cfg: GPTConfig) -> TorchBlock:
+    return TorchBlock(cfg.hidden_size, cfg.num_attention_heads, cfg.intermediate_size, cfg.layer_norm_eps, True)
 
 
 class TorchGPT(nn.Module):

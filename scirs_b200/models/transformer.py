@@ -135,6 +135,20 @@ class FusedTrainerMixin:
     `forward_backward(inputs, targets)`, `optimizer` and `grad_sync`."""
 
     kernel_launches = 0
+    param_sync = None
+
+    def _params_begin(self):
+        """Start the (ZeRO) parameter all-gather for this forward, if any."""
+        if self.param_sync is not None:
+            self.param_sync.begin_forward()
+
+    def _wait_params(self, i: int):
+        if self.param_sync is not None:
+            self.param_sync.wait_bucket(i)
+
+    def _params_end(self):
+        if self.param_sync is not None:
+            self.param_sync.end_forward()
 
     def zero_grad(self):
         self.fp.grad.zero_()

@@ -294,7 +294,22 @@ def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=Tr
 # ---------------------------------------------------------------------------
 # Fused optimizer step over flat buffers
 # ---------------------------------------------------------------------------
-def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=None, norm_out=None, decay_mask=None):
+def grad_sumsq(grads, part, hp) -> int:
+    """Partial sums of squares of `grads` into part[:n]; returns n. Also
+    advances the device-managed step counter (hp[9] when hp[10] != 0), as
+    the fused optimizer's own norm pass would."""
+    if grads.is_cuda:
+        n = _ext.kernels().grad_sumsq(grads, part, hp)
+        _count(1)
+        return int(n)
+    if float(hp[10]) != 0:
+        hp[9] += 1
+    part[0] = grads.float().pow(2).sum()
+    return 1
+
+
+def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=None, norm_out=None, decay_mask=None,
+               parts_ready: int = 0):
     """One fused step; hp (fp32, >= 11 entries) = lr, beta1|momentum|rho, beta2,
     eps, wd, bias_corr1, bias_corr2, grad multiplier, max_norm, step counter,
     device-managed flag. With the flag set (and `part` given) the step counter
@@ -304,18 +319,22 @@ def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=
         hp = torch.cat([hp.reshape(-1), torch.zeros(11 - hp.numel(), dtype=hp.dtype, device=hp.device)])
     if params.is_cuda:
         _ext.kernels().optim_step(
-            m, params, state1, state2, grads, params16, int(n_decay), decay_mask, hp, part, norm_out
+            m, params, state1, state2, grads, params16, int(n_decay), decay_mask, hp, part, norm_out, int(parts_ready)
         )
-        _count(2 if part is not None else 1)
+        _count(2 if part is not None and not parts_ready else 1)
         return
     h = hp.tolist()
     lr, b1, b2, eps, wd, bc1, bc2, gmul, max_norm = h[:9]
     if h[10] != 0 and part is not None:
-        hp[9] += 1
+        if not parts_ready:
+            hp[9] += 1
         bc1, bc2 = 1 - b1 ** float(hp[9]), 1 - b2 ** float(hp[9])
     g = grads.float() * gmul
     if part is not None:
-        norm = float(grads.float().norm()) * abs(gmul)
+        if parts_ready:
+            norm = math.sqrt(max(float(part[:parts_ready].sum()), 0.0)) * abs(gmul)
+        else:
+            norm = float(grads.float().norm()) * abs(gmul)
         if norm_out is not None:
             norm_out.fill_(norm)
         if not math.isfinite(norm):
@@ -356,3 +375,46 @@ def optim_step(mode, params, state1, state2, grads, params16, n_decay, hp, part=
         p.sub_(lr * g / (state1.sqrt() + eps))
     if params16 is not None:
         params16.copy_(p)
+
+
+# ---------------------------------------------------------------------------
+# Vision transformer input
+# ---------------------------------------------------------------------------
+def patchify(images: torch.Tensor, out: torch.Tensor, patch: int) -> torch.Tensor:
+    """images [B, C, H, W] (fp32/bf16) -> out [B*(H/P)*(W/P), C*P*P] bf16,
+    columns ordered (c, ky, kx) like a flattened conv weight [E, C, P, P]."""
+    if images.is_cuda:
+        _ext.kernels().patchify(images, out, int(patch))
+        _count(1)
+        return out
+    B, C, H, W = images.shape
+    P = patch
+    t = images.reshape(B, C, H // P, P, W // P, P).permute(0, 2, 4, 1, 3, 5)
+    out.copy_(t.reshape(out.shape))
+    return out
+
+
+def vit_embed_fwd(pe, cls, pos, x, B: int):
+    """x[b, 0] = cls + pos[0]; x[b, 1 + i] = pe[b, i] + pos[1 + i]."""
+    if x.is_cuda:
+        _ext.kernels().vit_embed_fwd(pe, cls, pos, x, int(B))
+        _count(1)
+        return x
+    T, D = pos.shape
+    xv = x.view(B, T, D)
+    xv[:, 0] = (cls.float() + pos[0].float()).to(x.dtype)
+    xv[:, 1:] = (pe.view(B, T - 1, D).float() + pos[1:].float()).to(x.dtype)
+    return x
+
+
+def vit_embed_bwd(dx, dpe, dpos, dcls, B: int):
+    """dpe = dx[:, 1:]; dpos += sum_b dx; dcls += sum_b dx[:, 0]."""
+    if dx.is_cuda:
+        _ext.kernels().vit_embed_bwd(dx, dpe, dpos, dcls, int(B))
+        _count(1)
+        return
+    T, D = dpos.shape
+    d = dx.view(B, T, D).float()
+    dpe.copy_(d[:, 1:].reshape(dpe.shape))
+    dpos.add_(d.sum(0))
+    dcls.add_(d[:, 0].sum(0))

@@ -51,6 +51,12 @@ class FlatParams:
         self.total += _round_up(n)
         return slot
 
+    def pad_to(self, multiple: int) -> int:
+        """Advance the end offset to a multiple of `multiple` elements (e.g.
+        so that gradient buckets split evenly into per-rank shards)."""
+        self.total = _round_up(self.total, int(multiple))
+        return self.total
+
     def mark(self) -> int:
         """Current end offset (use to delimit gradient buckets)."""
         return self.total

@@ -46,6 +46,7 @@ ext_modules = [
                 "optim.cu",
                 "attention.cu",
                 "attention_sm100.cu",
+                "vision.cu",
             ]
         ),
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
@@ -57,10 +58,23 @@ ext_modules = [
     ),
 ]
 
+class _BuildExt(BuildExtension):
+    """One build directory per extension, so each keeps its own ninja log and
+    dependency state (incremental rebuilds recompile only what changed)."""
+
+    def build_extension(self, ext):
+        old = self.build_temp
+        self.build_temp = os.path.join(old, ext.name.rsplit(".", 1)[-1])
+        try:
+            super().build_extension(ext)
+        finally:
+            self.build_temp = old
+
+
 setup(
     name="scirs_b200",
     version="0.1.0",
     packages=["scirs_b200"],
     ext_modules=ext_modules,
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": _BuildExt.with_options(use_ninja=True)},
 )

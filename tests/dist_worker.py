@@ -103,10 +103,53 @@ def case_dp_gpt():
     return res
 
 
+def case_zero_vit():
+    """ZeRO (sharded AdamW, reduce-scatter of gradients, all-gather of bf16
+    parameters) with the fused collectives and with NCCL == single-process
+    training on the full batch."""
+    from scirs_b200.models.vit import ViTConfig, ViTModel
+    from scirs_b200.parallel.zero import zero_data_parallel
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = ViTConfig.tiny(num_classes=10)
+    g = torch.Generator().manual_seed(9)
+    lb = 4
+    img = torch.randn(lb * world, 3, 32, 32, generator=g)
+    lab = torch.randint(0, 10, (lb * world,), generator=g)
+    hp = dict(lr=1e-3, weight_decay=0.05, max_grad_norm=1.0)
+    res = {}
+    for mode in ("fused", "nccl"):
+        m = ViTModel(cfg, device=dev, seed=3, bucket_align=64 * world)
+        zero_data_parallel(m, mode=mode, **hp)
+        losses = []
+        sl = slice(rank * lb, (rank + 1) * lb)
+        for it in range(4):
+            if it == 2:
+                m.enable_cuda_graph()
+            l = m.train_step(img[sl].to(dev), lab[sl].to(dev))
+            lt = l.detach().clone()
+            dist.all_reduce(lt)
+            losses.append(float(lt) / world)
+        torch.cuda.synchronize()
+        m.release_cuda_graph()
+        full = m.param_sync.consolidated_master()
+        res[mode] = {"losses": losses, "master_sum": float(full.double().sum())}
+        if mode == "fused":
+            m.param_sync.comm.close()
+    if rank == 0:
+        m = ViTModel(cfg, device=dev, seed=3, bucket_align=64 * world)
+        m.configure_adamw(betas=(0.9, 0.999), **hp)
+        ref = [float(m.train_step(img.to(dev), lab.to(dev))) for _ in range(4)]
+        res["single"] = {"losses": ref, "master_sum": float(m.fp.master.double().sum())}
+    _ext.check_status()
+    return res
+
+
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
-    res = {"collectives": case_collectives, "dp_gpt": case_dp_gpt}[case]()
+    res = {"collectives": case_collectives, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))
     dist.barrier()

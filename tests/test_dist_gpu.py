@@ -49,3 +49,11 @@ def test_data_parallel_gpt_2gpu(tmp_path):
         assert res[mode]["replica_max_diff"] == 0.0, mode
         for a, b in zip(res[mode]["losses"], ref):
             assert abs(a - b) < 2e-2, (mode, res[mode]["losses"], ref)
+
+
+def test_zero_vit_2gpu(tmp_path):
+    res = _run("zero_vit", tmp_path, port=29613)
+    ref = res["single"]["losses"]
+    for mode in ("fused", "nccl"):
+        for a, b in zip(res[mode]["losses"], ref):
+            assert abs(a - b) < 3e-2, (mode, res[mode]["losses"], ref)

@@ -1,0 +1,108 @@
+"""ViT engine on the native kernels vs the fp32 PyTorch oracle, and the
+patch / [CLS]+position kernels vs their PyTorch definitions."""
+import pytest
+import torch
+
+from scirs_b200 import _ext
+from scirs_b200.ops import kernels as K
+from scirs_b200.models.torch_vit import TorchViT
+from scirs_b200.models.vit import ViTConfig, ViTModel
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg(hd=64):
+    c = ViTConfig.vit_base(num_classes=100)
+    c.embed_dim, c.num_heads, c.mlp_dim, c.num_layers = 256, 256 // hd, 1024, 2
+    return c
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_patchify_and_embed_kernels(dtype):
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(1)
+    B, C, Hh, W, P, D = 3, 3, 64, 48, 16, 128
+    img = torch.randn(B, C, Hh, W, generator=g).to(dtype)
+    out = torch.empty(B * (Hh // P) * (W // P), C * P * P, dtype=torch.bfloat16, device=dev)
+    K.patchify(img.to(dev), out, P)
+    ref = torch.empty(out.shape, dtype=torch.bfloat16)
+    K.patchify(img, ref, P)
+    assert torch.equal(out.cpu(), ref)
+    # conv equivalence: patches @ W^T == conv2d(stride=P)
+    w = torch.randn(D, C, P, P, generator=g)
+    conv = torch.nn.functional.conv2d(img.float(), w, stride=P).flatten(2).transpose(1, 2).reshape(-1, D)
+    assert torch.allclose(ref.float() @ w.reshape(D, -1).t(), conv, atol=0.3, rtol=2e-2)
+    T = (Hh // P) * (W // P) + 1
+    pe = torch.randn(B * (T - 1), D, generator=g).to(torch.bfloat16)
+    cls = torch.randn(D, generator=g).to(torch.bfloat16)
+    pos = torch.randn(T, D, generator=g).to(torch.bfloat16)
+    x = torch.empty(B * T, D, dtype=torch.bfloat16, device=dev)
+    K.vit_embed_fwd(pe.to(dev), cls.to(dev), pos.to(dev), x, B)
+    xr = torch.empty(B * T, D, dtype=torch.bfloat16)
+    K.vit_embed_fwd(pe, cls, pos, xr, B)
+    assert torch.equal(x.cpu(), xr)
+    dx = torch.randn(B * T, D, generator=g).to(torch.bfloat16)
+    dpe = torch.empty(B * (T - 1), D, dtype=torch.bfloat16, device=dev)
+    dpos = torch.ones(T, D, device=dev)
+    dcls = torch.ones(D, device=dev)
+    K.vit_embed_bwd(dx.to(dev), dpe, dpos, dcls, B)
+    dpe_r, dpos_r, dcls_r = torch.empty(dpe.shape, dtype=torch.bfloat16), torch.ones(T, D), torch.ones(D)
+    K.vit_embed_bwd(dx, dpe_r, dpos_r, dcls_r, B)
+    torch.cuda.synchronize()
+    _ext.check_status(0)
+    assert torch.equal(dpe.cpu(), dpe_r)
+    assert torch.allclose(dpos.cpu(), dpos_r, atol=1e-4)
+    assert torch.allclose(dcls.cpu(), dcls_r, atol=1e-4)
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_vit_engine_matches_oracle_gpu(hd):
+    cfg = _cfg(hd)
+    dev = torch.device("cuda", 0)
+    m = ViTModel(cfg, device=dev, seed=1)
+    sd = {k: v.to(torch.bfloat16).float() for k, v in m.state_dict().items()}
+    m.load_state_dict(sd)
+    ref = TorchViT(cfg).to(dev)
+    ref.load_flat_state(sd)
+    g = torch.Generator().manual_seed(0)
+    img = torch.randn(4, 3, 224, 224, generator=g).to(dev)
+    lab = torch.randint(0, cfg.num_classes, (4,), generator=g).to(dev)
+    m.zero_grad()
+    loss = m.forward_backward(img, lab)
+    lref = ref(img, lab)
+    lref.backward()
+    torch.cuda.synchronize()
+    _ext.check_status(0)
+    assert abs(float(loss) - float(lref)) < 3e-2
+    for name, gr in ref.flat_grads().items():
+        mine = m.fp.g(name)
+        if name.startswith("classifier"):
+            mine = mine[: cfg.num_classes]
+        if name.endswith("c_attn.bias"):
+            # the key bias gradient is exactly zero in exact arithmetic
+            D = cfg.embed_dim
+            mine, gr = torch.cat([mine[:D], mine[2 * D :]]), torch.cat([gr[:D], gr[2 * D :]])
+        err = float((mine - gr).norm() / (gr.norm() + 1e-8))
+        assert err < 6e-2, (name, err)
+
+
+def test_vit_graph_step_matches_eager_and_trains():
+    cfg = _cfg()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(5)
+    img = torch.randn(8, 3, 224, 224, generator=g).to(dev)
+    lab = torch.randint(0, cfg.num_classes, (8,), generator=g).to(dev)
+    runs = []
+    for graphed in (False, True):
+        m = ViTModel(cfg, device=dev, seed=4)
+        m.configure_adamw(lr=1e-3, weight_decay=0.05, max_grad_norm=1.0)
+        if graphed:
+            m.enable_cuda_graph()
+        losses = [float(m.train_step(img, lab)) for _ in range(12)]
+        torch.cuda.synchronize()
+        runs.append((losses, m.fp.master.clone()))
+    _ext.check_status(0)
+    (l0, w0), (l1, w1) = runs
+    assert all(abs(a - b) < 2e-3 for a, b in zip(l0, l1)), (l0, l1)
+    assert float((w0 - w1).norm() / w0.norm()) < 1e-3
+    assert l0[-1] < l0[0] - 1.0
