@@ -13,7 +13,7 @@ profiler can skip the first round(s) and capture one launch per op, e.g.
 
 Shapes: M = 16384 tokens (16 sequences of 1024; a quarter of the 1-GPU
 step), d=768, MLP 3072, 12 heads of 64, vocabulary 50304 (padded) over 4096
-rows, AdamW over the 124M-parameter flat buffer. Each op's working set is
+rows, AdamW over a 32M-element flat buffer. Each op's working set is
 larger than the 126 MB L2.
 
 Without a profiler it prints one line per op with the CUDA-event time of the
@@ -32,6 +32,7 @@ from .. import _ext
 from ..ops import kernels as K
 
 M, D, F, H, HD, S = 16384, 768, 3072, 12, 64, 1024
+NOPT = 32 << 20  # optimizer elements (a quarter of GPT-2 small; 640 MB of state)
 B = M // S
 
 
@@ -76,7 +77,7 @@ def build(dev):
     t["logits"] = r(M // 4, V)  # 4096 rows x 50304 = 412 MB
     t["tgt"] = torch.randint(0, 50257, (M // 4,), device=dev)
     t["losses"] = torch.empty(M // 4, device=dev, dtype=f32)
-    n = 124_475_904
+    n = NOPT
     t["p"] = torch.randn(n, device=dev) * 0.02
     t["m1"] = torch.zeros(n, device=dev)
     t["m2"] = torch.zeros(n, device=dev)
@@ -146,7 +147,7 @@ OPS = {
     "ln_fwd": (op_ln_fwd, 0, 2 * M * D * 2),
     "ln_bwd": (op_ln_bwd, 0, 4 * M * D * 2),
     "xent": (op_xent, 0, 2 * (M // 4) * 50304 * 2),
-    "adamw": (op_adamw, 0, 124_475_904 * (4 * 2 + 8 * 2 + 4 + 2) + 124_475_904 * 4),
+    "adamw": (op_adamw, 0, NOPT * (4 * 2 + 8 * 2 + 4 + 2) + NOPT * 4),
 }
 
 
