@@ -2,28 +2,42 @@
 //
 // Every rank owns one "symmetric" device buffer of the same size, mapped into
 // every other rank's address space with CUDA IPC (handles exchanged over the
-// process group by the Python side). Kernels here read and write peers'
-// buffers directly (P2P loads/stores over NVLink 5 / NVSwitch) and
-// synchronise with per-block epoch flags:
+// process group by the Python side). All data crosses NVLink as STORES into
+// the owner's buffer (push): a remote store is fire-and-forget, so a block
+// keeps many 16-byte vectors in flight without waiting for NVLink round
+// trips, and every read in these kernels is a read of local memory.
+// Ranks synchronise with per-block epoch flags:
 //
 //   signal: __syncthreads; thread i < world stores `epoch` into peer i's flag
 //           slot [barrier][block][my_rank] with st.release.sys
 //   wait  : thread i < world spins (bounded by a globaltimer budget) with
 //           ld.acquire.sys on my flag slot [barrier][block][i]; __syncthreads
 //
-// Block b of every rank works on the same slice of the payload, so the
-// barriers are per block and no grid-wide synchronisation is needed. A wait
-// that runs out of budget records kStPeerTimeout in the status word and the
-// kernel finishes without hanging (its output is then invalid; the host
-// raises when it reads the status word).
+// Block b of every rank works on the same sub-slice of every rank's shard,
+// so barriers are per block; no grid-wide synchronisation. A wait that runs
+// out of budget records kStPeerTimeout in the status word and the kernel
+// finishes without hanging (its output is then invalid; the host raises when
+// it reads the status word).
 //
-// Buffer layout (bytes): [ area0 | area1 | flags ]   area = data_cap / 2.
-//   all-reduce : area0 holds the scaled bf16 inputs, area1 the reduced pieces
-//   reduce-scat: area0 holds the scaled bf16 inputs
-//   all-gather : area0 holds the gathered bf16 payload
-//   Every kernel ends with an exit barrier and all kinds share one epoch
-//   sequence per block, so consecutive collectives of any kind may reuse the
-//   buffer safely.
+// Buffer layout (bytes): [ set0: A | B ][ set1: A | B ][ flags ], each area
+// `area_bytes`. Consecutive calls alternate between the two sets (a call
+// counter kept on the device, advanced by the last block to finish), which
+// replaces an exit barrier: a rank can only start call c+2 (which writes set
+// c%2 again) after every peer has started call c+1, i.e. finished call c.
+// All collectives of one communicator must therefore run on one stream.
+//
+//   all-reduce, two-shot (payload split into `world` shards, owner k):
+//     1. push: scale, cast to bf16, store my copy of shard k into owner k's
+//        A[my_rank][.]                                       -- barrier 0 --
+//     2. owner sums A[0..world-1][.] in fp32 in a fixed rank order, casts to
+//        bf16 and stores the reduced shard into every rank's B  -- barrier 1 --
+//     3. every rank expands its local B to fp32 (bit-identical on all ranks)
+//   all-reduce, one-shot (small payloads): push the whole scaled bf16 vector
+//     into every rank's A[my_rank]; -- barrier 0 --; each rank sums locally.
+//   reduce-scatter: step 1 of the two-shot all-reduce, then the owner sums
+//     into its fp32 shard.
+//   all-gather: push my bf16 shard into every rank's A; -- barrier 0 --;
+//     copy A to the output.
 //
 // Reference parity: replaces the single-process simulations of the
 // reference's distributed gradient primitives
@@ -57,12 +71,13 @@ struct Args {
   __nv_bfloat16* out16;       // bf16 output (all-gather full)
   float scale;
   unsigned* epochs;  // local per-block counters [kMaxBlocks]
+  unsigned* ctl;     // local [call counter, finished-block counter]
   DevStatus* st;
   long long timeout_ns;
 };
 
 __device__ __forceinline__ unsigned* flag_ptr(char* base, long area_bytes, int barrier, int block, int src) {
-  return reinterpret_cast<unsigned*>(base + 2 * area_bytes) + ((barrier * kMaxBlocks + block) * kMaxRanks + src);
+  return reinterpret_cast<unsigned*>(base + 4 * area_bytes) + ((barrier * kMaxBlocks + block) * kMaxRanks + src);
 }
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -130,41 +145,168 @@ __device__ __forceinline__ void unpack8(const uint4& q, float* f) {
   f[6] = bf16_lo(q.w); f[7] = bf16_hi(q.w);
 }
 
-// Slice of the payload (in 8-element vectors) owned by this block, and the
-// piece of that slice owned by rank r.
-__device__ __forceinline__ void block_slice(long nvec, int world, long& v0, long& v1) {
-  const long per = ((nvec + gridDim.x - 1) / gridDim.x + world - 1) / world * world;
-  v0 = min(nvec, (long)blockIdx.x * per);
-  v1 = min(nvec, v0 + per);
-}
-__device__ __forceinline__ void piece(long v0, long v1, int world, int r, long& p0, long& p1) {
-  const long per = (v1 - v0 + world - 1) / world;
-  p0 = min(v1, v0 + r * per);
-  p1 = min(v1, p0 + per);
-}
-
 // Memory-level parallelism: every thread keeps kU independent 16-byte vectors
-// in flight per step (phase 2 keeps one vector per peer in flight instead),
-// and blocks are kept small in registers (<= 64) so they can co-reside with
-// a persistent GEMM CTA while overlapping the backward pass.
+// in flight per step, and blocks stay small in registers (<= 64) so they can
+// co-reside with a persistent GEMM CTA while overlapping the backward pass.
 constexpr int kU = 4;
 constexpr int kCommThreads = 256;
 
+// Call bookkeeping shared by every kernel: the data set (parity) of this
+// call, and the hand-over to the next call.
+struct CallCtx {
+  unsigned epoch;
+  long set_off;  // byte offset of this call's [A | B] set
+};
+__device__ __forceinline__ CallCtx call_begin(const Args& a) {
+  CallCtx c;
+  c.epoch = a.epochs[blockIdx.x] + 1;
+  const unsigned calls = *reinterpret_cast<volatile unsigned*>(a.ctl);
+  c.set_off = (long)(calls & 1u) * 2 * a.area_bytes;
+  return c;
+}
+__device__ __forceinline__ void call_end(const Args& a, const CallCtx& c) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    a.epochs[blockIdx.x] = c.epoch;
+    __threadfence();
+    // the last block to finish advances the call counter; every block read it
+    // at its start, before arriving here
+    if (atomicAdd(a.ctl + 1, 1u) == gridDim.x - 1) {
+      a.ctl[1] = 0u;
+      a.ctl[0] = a.ctl[0] + 1u;
+      __threadfence();
+    }
+  }
+}
+
+__device__ __forceinline__ uint4* areaA(const Args& a, int r, const CallCtx& c) {
+  return reinterpret_cast<uint4*>(a.peers.base[r] + c.set_off);
+}
+__device__ __forceinline__ uint4* areaB(const Args& a, int r, const CallCtx& c) {
+  return reinterpret_cast<uint4*>(a.peers.base[r] + c.set_off + a.area_bytes);
+}
+
+// Sub-slice [s0, s1) of every shard (of `sv` vectors) handled by this block.
+__device__ __forceinline__ void sub_slice(long sv, long& s0, long& s1) {
+  const long per = (sv + gridDim.x - 1) / gridDim.x;
+  s0 = min(sv, (long)blockIdx.x * per);
+  s1 = min(sv, s0 + per);
+}
+
+// Step 1 of reduce-scatter / two-shot all-reduce: scale + cast my copy of
+// every shard's sub-slice and store it into the owner's A[my_rank][.].
+__device__ __forceinline__ void push_scaled_shards(const Args& a, const CallCtx& c, long nvec, long sv, long s0,
+                                                   long s1) {
+  const long span = s1 - s0, tot = span * a.world, bd = blockDim.x;
+  for (long base = threadIdx.x; base < tot; base += bd * kU) {
+    float f[kU][8];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long t = base + u * bd;
+      const int k = (int)(t / max(span, 1L));
+      const long g = (long)((k + a.rank + 1) % a.world) * sv + s0 + t % max(span, 1L);
+      if (t < tot && g < nvec) load8f(a.in32 + g * 8, f[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long t = base + u * bd;
+      const int k = (a.rank + 1 + (int)(t / max(span, 1L))) % a.world;
+      const long s = s0 + t % max(span, 1L);
+      if (t < tot && (long)k * sv + s < nvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
+        areaA(a, k, c)[(long)a.rank * sv + s] = pack8(f[u]);
+      }
+    }
+  }
+}
+
+// Sum A[0..world-1][s] (local) for kU consecutive s of this thread, in a
+// fixed rank order (so every owner produces the same bits).
+__device__ __forceinline__ void sum_slots(const Args& a, const CallCtx& c, long sv, long s, long s1, long bd,
+                                          float (&acc)[kU][8]) {
+  const uint4* A = areaA(a, a.rank, c);
+#pragma unroll
+  for (int u = 0; u < kU; ++u)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[u][e] = 0.f;
+  for (int src = 0; src < a.world; ++src) {
+    uint4 x[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (s + u * bd < s1) x[u] = __ldcg(A + (long)src * sv + s + u * bd);
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (s + u * bd < s1) acc8(x[u], acc[u]);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// All-reduce (sum * scale), fp32 in -> fp32 out, bf16 on the wire.
-// Two-shot: publish scaled bf16 copy; reduce own piece from all peers into
-// area1; gather every reduced piece. Every rank ends with bit-identical output.
+// All-reduce (sum * scale), fp32 in -> fp32 out (may alias), bf16 on the wire,
+// fp32 accumulation; every rank ends with bit-identical output.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kCommThreads, 4) allreduce_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
-  const unsigned epoch = a.epochs[blockIdx.x] + 1;
-  const long nvec = a.n / 8;
-  const long bd = blockDim.x;
+  const CallCtx c = call_begin(a);
+  const long nvec = a.n / 8, bd = blockDim.x;
+  const long sv = (nvec + a.world - 1) / a.world;
+  long s0, s1;
+  sub_slice(sv, s0, s1);
+  push_scaled_shards(a, c, nvec, sv, s0, s1);
+  bool ok = block_barrier(a, 0, c.epoch, &sfail);
+  // owner: reduce my shard's sub-slice and push it into every rank's B
+  const long mine_end = min(s1, nvec - (long)a.rank * sv);
+  if (ok) {
+    for (long s = s0 + threadIdx.x; s < mine_end; s += bd * kU) {
+      float acc[kU][8];
+      sum_slots(a, c, sv, s, mine_end, bd, acc);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (s + u * bd < mine_end) {
+          const uint4 q = pack8(acc[u]);
+          for (int j = 0; j < a.world; ++j)
+            areaB(a, (a.rank + 1 + j) % a.world, c)[(long)a.rank * sv + s + u * bd] = q;
+        }
+      }
+    }
+    ok = block_barrier(a, 1, c.epoch, &sfail);
+  }
+  // expand the gathered bf16 result (local reads only)
+  if (ok) {
+    const uint4* Bl = areaB(a, a.rank, c);
+    const long span = s1 - s0, tot = span * a.world;
+    for (long base = threadIdx.x; base < tot; base += bd * kU) {
+      uint4 x[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long t = base + u * bd;
+        const long g = (t / max(span, 1L)) * sv + s0 + t % max(span, 1L);
+        if (t < tot && g < nvec) x[u] = __ldcg(Bl + g);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long t = base + u * bd;
+        const long g = (t / max(span, 1L)) * sv + s0 + t % max(span, 1L);
+        if (t < tot && g < nvec) {
+          float f[8];
+          unpack8(x[u], f);
+          store8f(a.out32 + g * 8, f);
+        }
+      }
+    }
+  }
+  call_end(a, c);
+}
+
+// One-shot all-reduce for small payloads: one barrier.
+__global__ void __launch_bounds__(kCommThreads, 4) allreduce_oneshot_kernel(const Args a) {
+  __shared__ volatile int sfail;
+  if (threadIdx.x == 0) sfail = 0;
+  const CallCtx c = call_begin(a);
+  const long nvec = a.n / 8, bd = blockDim.x;
   long v0, v1;
-  block_slice(nvec, a.world, v0, v1);
-  uint4* my_in = reinterpret_cast<uint4*>(a.peers.base[a.rank]);
-  // phase 1: scale + cast + publish
+  sub_slice(nvec, v0, v1);
   for (long base = v0 + threadIdx.x; base < v1; base += bd * kU) {
     float f[kU][8];
 #pragma unroll
@@ -175,58 +317,22 @@ __global__ void __launch_bounds__(kCommThreads, 4) allreduce_kernel(const Args a
       if (base + u * bd < v1) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
-        my_in[base + u * bd] = pack8(f[u]);
+        const uint4 q = pack8(f[u]);
+        for (int j = 0; j < a.world; ++j) areaA(a, (a.rank + 1 + j) % a.world, c)[(long)a.rank * nvec + base + u * bd] = q;
       }
     }
   }
-  bool ok = block_barrier(a, 0, epoch, &sfail);
-  // phase 2: reduce my piece (one load per peer in flight per vector)
-  long p0, p1;
-  piece(v0, v1, a.world, a.rank, p0, p1);
+  const bool ok = block_barrier(a, 0, c.epoch, &sfail);
   if (ok) {
-    uint4* my_out = reinterpret_cast<uint4*>(a.peers.base[a.rank] + a.area_bytes);
-    for (long v = p0 + threadIdx.x; v < p1; v += bd) {
-      uint4 x[kMaxRanks];
+    for (long s = v0 + threadIdx.x; s < v1; s += bd * kU) {
+      float acc[kU][8];
+      sum_slots(a, c, nvec, s, v1, bd, acc);
 #pragma unroll
-      for (int k = 0; k < kMaxRanks; ++k)
-        if (k < a.world) x[k] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[(a.rank + k) % a.world]) + v);
-      float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-      for (int k = 0; k < kMaxRanks; ++k)
-        if (k < a.world) acc8(x[k], f);
-      my_out[v] = pack8(f);
-    }
-    ok = block_barrier(a, 1, epoch, &sfail);
-  }
-  // phase 3: gather every reduced piece (own included, for bit-identical results)
-  if (ok) {
-    const long per = (v1 - v0 + a.world - 1) / a.world;
-    for (long base = v0 + threadIdx.x; base < v1; base += bd * kU) {
-      uint4 x[kU];
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const long v = base + u * bd;
-        if (v < v1) {
-          const int src = (int)((v - v0) / per);
-          x[u] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[src] + a.area_bytes) + v);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const long v = base + u * bd;
-        if (v < v1) {
-          float f[8];
-          unpack8(x[u], f);
-          store8f(a.out32 + v * 8, f);
-        }
-      }
+      for (int u = 0; u < kU; ++u)
+        if (s + u * bd < v1) store8f(a.out32 + (s + u * bd) * 8, acc[u]);
     }
   }
-  __syncthreads();
-  // exit barrier: every peer is done reading this call's buffers, so the next
-  // collective (of any kind) may overwrite them
-  if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
-  if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
+  call_end(a, c);
 }
 
 // ---------------------------------------------------------------------------
@@ -236,103 +342,69 @@ __global__ void __launch_bounds__(kCommThreads, 4) allreduce_kernel(const Args a
 __global__ void __launch_bounds__(kCommThreads, 4) reduce_scatter_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
-  const unsigned epoch = a.epochs[blockIdx.x] + 1;
-  const long area = 0;
-  const long bd = blockDim.x;
-  const long shard_vec = a.n / 8 / a.world;
-  // Block b handles vectors [b*per, ...) of every shard.
-  const long per = (shard_vec + gridDim.x - 1) / gridDim.x;
-  const long s0 = min(shard_vec, (long)blockIdx.x * per), s1 = min(shard_vec, s0 + per);
-  uint4* my_in = reinterpret_cast<uint4*>(a.peers.base[a.rank] + area);
-  const long span = s1 - s0;
-  // phase 1: publish the block's slice of every shard (scaled, bf16)
-  for (long base = threadIdx.x; base < span * a.world; base += bd * kU) {
-    float f[kU][8];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const long t = base + u * bd;
-      if (t < span * a.world) load8f(a.in32 + ((t / span) * shard_vec + s0 + t % span) * 8, f[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const long t = base + u * bd;
-      if (t < span * a.world) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
-        my_in[(t / span) * shard_vec + s0 + t % span] = pack8(f[u]);
-      }
-    }
-  }
-  const bool ok = block_barrier(a, 0, epoch, &sfail);
+  const CallCtx c = call_begin(a);
+  const long nvec = a.n / 8, bd = blockDim.x;
+  const long sv = nvec / a.world;
+  long s0, s1;
+  sub_slice(sv, s0, s1);
+  push_scaled_shards(a, c, nvec, sv, s0, s1);
+  const bool ok = block_barrier(a, 0, c.epoch, &sfail);
   if (ok) {
-    const long off = (long)a.rank * shard_vec;
-    for (long v = s0 + threadIdx.x; v < s1; v += bd) {
-      uint4 x[kMaxRanks];
+    for (long s = s0 + threadIdx.x; s < s1; s += bd * kU) {
+      float acc[kU][8];
+      sum_slots(a, c, sv, s, s1, bd, acc);
 #pragma unroll
-      for (int k = 0; k < kMaxRanks; ++k)
-        if (k < a.world)
-          x[k] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[(a.rank + k) % a.world] + area) + off + v);
-      float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-      for (int k = 0; k < kMaxRanks; ++k)
-        if (k < a.world) acc8(x[k], f);
-      store8f(a.out32 + v * 8, f);
+      for (int u = 0; u < kU; ++u)
+        if (s + u * bd < s1) store8f(a.out32 + (s + u * bd) * 8, acc[u]);
     }
   }
-  __syncthreads();
-  if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
-  if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
+  call_end(a, c);
 }
 
 // ---------------------------------------------------------------------------
-// All-gather: bf16 shard in -> bf16 full output. Push model: every rank
-// stores its shard straight into every peer's buffer, then one barrier.
+// All-gather: bf16 shard in -> bf16 full output.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kCommThreads, 4) allgather_kernel(const Args a) {
   __shared__ volatile int sfail;
   if (threadIdx.x == 0) sfail = 0;
-  const unsigned epoch = a.epochs[blockIdx.x] + 1;
-  const long area = 0;
+  const CallCtx c = call_begin(a);
   const long bd = blockDim.x;
-  const long shard_vec = a.n / 8 / a.world;
-  const long per = (shard_vec + gridDim.x - 1) / gridDim.x;
-  const long s0 = min(shard_vec, (long)blockIdx.x * per), s1 = min(shard_vec, s0 + per);
-  const long off = (long)a.rank * shard_vec;
+  const long sv = a.n / 8 / a.world;
+  long s0, s1;
+  sub_slice(sv, s0, s1);
   const uint4* src = reinterpret_cast<const uint4*>(a.in16);
   for (long base = s0 + threadIdx.x; base < s1; base += bd * kU) {
     uint4 q[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u)
       if (base + u * bd < s1) q[u] = src[base + u * bd];
-    for (int k = 0; k < a.world; ++k) {
-      uint4* dst = reinterpret_cast<uint4*>(a.peers.base[(a.rank + k) % a.world] + area) + off;
+    for (int j = 0; j < a.world; ++j) {
+      uint4* dst = areaA(a, (a.rank + 1 + j) % a.world, c) + (long)a.rank * sv;
 #pragma unroll
       for (int u = 0; u < kU; ++u)
         if (base + u * bd < s1) dst[base + u * bd] = q[u];
     }
   }
-  const bool ok = block_barrier(a, 0, epoch, &sfail);
+  const bool ok = block_barrier(a, 0, c.epoch, &sfail);
   if (ok && a.out16 != nullptr) {
-    const uint4* full = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + area);
+    const uint4* full = areaA(a, a.rank, c);
     uint4* out = reinterpret_cast<uint4*>(a.out16);
-    const long span = s1 - s0;
-    for (long base = threadIdx.x; base < span * a.world; base += bd * kU) {
+    const long span = s1 - s0, tot = span * a.world;
+    for (long base = threadIdx.x; base < tot; base += bd * kU) {
       uint4 x[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const long t = base + u * bd;
-        if (t < span * a.world) x[u] = __ldcg(full + (t / span) * shard_vec + s0 + t % span);
+        if (t < tot) x[u] = __ldcg(full + (t / span) * sv + s0 + t % span);
       }
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const long t = base + u * bd;
-        if (t < span * a.world) out[(t / span) * shard_vec + s0 + t % span] = x[u];
+        if (t < tot) out[(t / span) * sv + s0 + t % span] = x[u];
       }
     }
   }
-  __syncthreads();
-  if (sfail == 0) block_barrier(a, 2, epoch, &sfail);
-  if (threadIdx.x == 0) a.epochs[blockIdx.x] = epoch;
+  call_end(a, c);
 }
 
 // Fault-injection helper for tests: waits on a flag nothing ever sets, with
@@ -363,9 +435,8 @@ struct CommState {
   long area_bytes = 0;
   char* local = nullptr;
   comm::Peers peers{};
-  unsigned* epochs_ar = nullptr;
-  unsigned* epochs_rs = nullptr;
-  unsigned* epochs_ag = nullptr;
+  unsigned* epochs_ar = nullptr;  // per-block epochs [kMaxBlocks] + call control [2]
+  unsigned* ctl = nullptr;
   std::vector<char*> opened;
 };
 std::unordered_map<int64_t, CommState> g_comms;
@@ -373,8 +444,8 @@ int64_t g_next_id = 1;
 std::mutex g_mu;
 }  // namespace
 
-// Allocate this rank's symmetric buffer (2 data areas of area_bytes + flags)
-// and return (comm id, IPC handle bytes).
+// Allocate this rank's symmetric buffer (2 sets of 2 data areas of area_bytes,
+// plus flags) and return (comm id, IPC handle bytes).
 std::tuple<int64_t, py::bytes> comm_create(int64_t device, int64_t rank, int64_t world, int64_t area_bytes) {
   TORCH_CHECK(world >= 1 && world <= comm::kMaxRanks, "world size must be 1..8");
   TORCH_CHECK(area_bytes % 256 == 0, "area_bytes must be a multiple of 256");
@@ -384,13 +455,12 @@ std::tuple<int64_t, py::bytes> comm_create(int64_t device, int64_t rank, int64_t
   cs.world = (int)world;
   cs.device = (int)device;
   cs.area_bytes = area_bytes;
-  const size_t total = 2 * area_bytes + comm::kFlagBytes;
+  const size_t total = 4 * area_bytes + comm::kFlagBytes;
   SCIRS_CHECK_CUDA(cudaMalloc(&cs.local, total));
   SCIRS_CHECK_CUDA(cudaMemset(cs.local, 0, total));
-  SCIRS_CHECK_CUDA(cudaMalloc(&cs.epochs_ar, 3 * comm::kMaxBlocks * sizeof(unsigned)));
-  SCIRS_CHECK_CUDA(cudaMemset(cs.epochs_ar, 0, 3 * comm::kMaxBlocks * sizeof(unsigned)));
-  cs.epochs_rs = cs.epochs_ar + comm::kMaxBlocks;
-  cs.epochs_ag = cs.epochs_rs + comm::kMaxBlocks;
+  SCIRS_CHECK_CUDA(cudaMalloc(&cs.epochs_ar, (comm::kMaxBlocks + 2) * sizeof(unsigned)));
+  SCIRS_CHECK_CUDA(cudaMemset(cs.epochs_ar, 0, (comm::kMaxBlocks + 2) * sizeof(unsigned)));
+  cs.ctl = cs.epochs_ar + comm::kMaxBlocks;
   SCIRS_CHECK_CUDA(cudaDeviceSynchronize());
   cudaIpcMemHandle_t h;
   SCIRS_CHECK_CUDA(cudaIpcGetMemHandle(&h, cs.local));
@@ -444,6 +514,8 @@ static comm::Args make_args(const CommState& cs, long n, double timeout_s) {
   a.n = n;
   a.st = status_ptr(cs.device);
   a.timeout_ns = (long long)(timeout_s * 1e9);
+  a.epochs = cs.epochs_ar;  // one epoch sequence per block shared by every collective kind
+  a.ctl = cs.ctl;
   return a;
 }
 
@@ -454,6 +526,10 @@ static CommState& get_cs(int64_t id) {
   return it->second;
 }
 
+// Payloads up to this many elements use the one-shot all-reduce (one barrier;
+// every rank pushes its whole bf16 vector to every peer).
+constexpr long kOneShotMaxElems = 256L * 1024;
+
 static int pick_blocks(long nvec_total, int world, int64_t blocks) {
   if (blocks > 0) return (int)std::min<int64_t>(blocks, comm::kMaxBlocks);
   // at least kU vectors per thread per block; up to two blocks per SM for
@@ -463,8 +539,9 @@ static int pick_blocks(long nvec_total, int world, int64_t blocks) {
 }
 
 // out32 = scale * sum_over_ranks(in32); in/out fp32 contiguous, may alias.
+// algo: 0 = choose (one-shot for small payloads), 1 = one-shot, 2 = two-shot.
 void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double scale, int64_t blocks,
-                    double timeout_s) {
+                    double timeout_s, int64_t algo) {
   CommState& cs = get_cs(id);
   CHECK_DTYPE(in32, at::kFloat);
   CHECK_DTYPE(out32, at::kFloat);
@@ -473,15 +550,23 @@ void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double 
   const long n = in32.numel();
   TORCH_CHECK(out32.numel() == n, "size mismatch");
   TORCH_CHECK(n % 8 == 0, "all-reduce payload must be a multiple of 8 elements");
-  TORCH_CHECK(n * 2 <= cs.area_bytes, "payload larger than the symmetric buffer area");
+  const long nvec = n / 8;
+  const bool fits1 = (long)cs.world * nvec * 16 <= cs.area_bytes;
+  const bool fits2 = (nvec + cs.world) * 16 <= cs.area_bytes;
+  if (algo == 0) algo = (fits1 && n <= kOneShotMaxElems) ? 1 : 2;
+  TORCH_CHECK(algo == 1 ? fits1 : fits2, "payload larger than the symmetric buffer area");
   comm::Args a = make_args(cs, n, timeout_s);
   a.in32 = in32.data_ptr<float>();
   a.out32 = out32.data_ptr<float>();
   a.scale = (float)scale;
-  a.epochs = cs.epochs_ar;
   c10::cuda::CUDAGuard guard(cs.device);
-  const int nb = pick_blocks(n / 8, cs.world, blocks);
-  comm::allreduce_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
+  if (algo == 1) {
+    const int nb = pick_blocks(nvec, cs.world, blocks);
+    comm::allreduce_oneshot_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
+  } else {
+    const int nb = pick_blocks((nvec + cs.world - 1) / cs.world, cs.world, blocks);
+    comm::allreduce_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
+  }
   SCIRS_CHECK_LAUNCH();
 }
 
@@ -501,7 +586,6 @@ void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, do
   a.in32 = in32.data_ptr<float>();
   a.out32 = out32.data_ptr<float>();
   a.scale = (float)scale;
-  a.epochs = cs.epochs_ar;  // one epoch sequence per block shared by every collective kind
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
   comm::reduce_scatter_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
@@ -522,7 +606,6 @@ void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t
   comm::Args a = make_args(cs, n, timeout_s);
   a.in16 = reinterpret_cast<const __nv_bfloat16*>(in16.data_ptr());
   a.out16 = reinterpret_cast<__nv_bfloat16*>(out16.data_ptr());
-  a.epochs = cs.epochs_ar;
   c10::cuda::CUDAGuard guard(cs.device);
   const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
   comm::allgather_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);

@@ -1,14 +1,15 @@
 """Symmetric peer buffers and the in-kernel NVLink collectives.
 
-`NVLinkComm` allocates one device buffer per rank, exchanges CUDA IPC
-handles over the process group and maps every peer's buffer, after which the
-kernels in scirs_b200/csrc/comm.cu move data with plain P2P loads/stores
-over NVLink 5 / NVSwitch (no NCCL on the data path). Every wait inside
+`NVLinkComm` allocates one device buffer per rank (4 x `area_bytes`: two
+alternating sets of two data areas, plus flags), exchanges CUDA IPC handles
+over the process group and maps every peer's buffer, after which the kernels
+in scirs_b200/csrc/comm.cu move data with P2P stores over NVLink 5 / NVSwitch
+(no NCCL on the data path). Every wait inside
 those kernels is bounded; a timed-out wait is reported through the status
 word (see :func:`scirs_b200._ext.check_status`).
 
 All ranks must issue the same collectives with the same sizes in the same
-order.
+order, and all collectives of one NVLinkComm must run on one CUDA stream.
 """
 from __future__ import annotations
 
@@ -36,15 +37,17 @@ class NVLinkComm:
 
     @property
     def max_elems(self) -> int:
-        return self.area_bytes // 2
+        """Largest payload (elements) of any collective on this buffer."""
+        return self.area_bytes // 2 - 8 * self.world
 
-    def allreduce_(self, t: torch.Tensor, scale: float = 1.0, blocks: int = 0) -> torch.Tensor:
-        """In place: t <- scale * sum over ranks (fp32 tensor, bf16 on the wire)."""
-        self.mod.allreduce(self.id, t, t, float(scale), int(blocks), self.timeout_s)
+    def allreduce_(self, t: torch.Tensor, scale: float = 1.0, blocks: int = 0, algo: int = 0) -> torch.Tensor:
+        """In place: t <- scale * sum over ranks (fp32 tensor, bf16 on the wire).
+        algo: 0 automatic, 1 one-shot, 2 two-shot."""
+        self.mod.allreduce(self.id, t, t, float(scale), int(blocks), self.timeout_s, int(algo))
         return t
 
-    def allreduce(self, src: torch.Tensor, dst: torch.Tensor, scale: float = 1.0, blocks: int = 0):
-        self.mod.allreduce(self.id, src, dst, float(scale), int(blocks), self.timeout_s)
+    def allreduce(self, src: torch.Tensor, dst: torch.Tensor, scale: float = 1.0, blocks: int = 0, algo: int = 0):
+        self.mod.allreduce(self.id, src, dst, float(scale), int(blocks), self.timeout_s, int(algo))
         return dst
 
     def reduce_scatter(self, src: torch.Tensor, dst: torch.Tensor, scale: float = 1.0, blocks: int = 0):

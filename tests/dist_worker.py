@@ -32,16 +32,17 @@ def case_collectives():
         ref = x.to(torch.bfloat16).float() / world  # each rank's bf16-rounded scaled contribution
         ref_sum = ref.clone()
         dist.all_reduce(ref_sum)
-        out = torch.empty_like(x)
-        for _ in range(3):  # repeated calls exercise the epoch protocol
-            comm.allreduce(x, out, 1.0 / world)
-        torch.cuda.synchronize()
-        err = float((out - ref_sum).abs().max() / ref_sum.abs().max())
-        # identical on all ranks
-        o0 = out.clone()
-        dist.broadcast(o0, 0)
-        same = bool(torch.equal(o0, out))
-        res[f"allreduce_{n}"] = {"max_err": err, "identical": same}
+        for algo in (1, 2):  # one-shot and two-shot
+            out = torch.empty_like(x)
+            for _ in range(3):  # repeated calls exercise the epoch and buffer-set protocol
+                comm.allreduce(x, out, 1.0 / world, algo=algo)
+            torch.cuda.synchronize()
+            err = float((out - ref_sum).abs().max() / ref_sum.abs().max())
+            # identical on all ranks
+            o0 = out.clone()
+            dist.broadcast(o0, 0)
+            same = bool(torch.equal(o0, out))
+            res[f"allreduce{algo}_{n}"] = {"max_err": err, "identical": same}
         # reduce-scatter
         if n % (8 * world) == 0:
             shard = torch.empty(n // world, device=dev)
