@@ -30,6 +30,8 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kEpiWarps = 8;
+constexpr int kMaxPeers = 8;
+constexpr unsigned kSigStride = 4096;  // signals per step (flag values are epoch * kSigStride + idx)
 
 enum Epi : int {
   EPI_BF16 = 0,       // C = acc (+ bias)
@@ -57,6 +59,28 @@ struct Args {
   float* bias_grad;  // EPI_DGELU: += column sums of the output (fp32 [N])
   int atomic_out;
   DevStatus* st;
+  int m_rot;   // rotation of the m-block order (tensor parallel: start with local rows)
+  int kb_rot;  // rotation of the k-block order (tensor parallel: start with local K rows)
+  // ---- tensor-parallel extensions (gemm_tp_kernel only) ----
+  int rank, world;
+  int a_seg, b_seg;            // >0: the operand's split dimension (A: M rows if K-major, K rows if
+                               // MN-major; B: K rows, MN-major) is split over the ranks in segments of
+                               // this many elements, rank r's segment read through peer map r
+  const unsigned* wait_flags;  // [world] local flag words written by the peers
+  const unsigned* epoch_ptr;   // device step counter; flag value = epoch * kSigStride + idx
+  unsigned wait_idx;
+  long long timeout_ns;
+  __nv_bfloat16* rs_dst[kMaxPeers];  // GEMM->RS: owner r's receive slot for this rank's partial
+  int rs_seg;                        // output rows per owner (0: plain output)
+  long rs_ld;
+  unsigned* sig_flags[kMaxPeers];    // flag words [peer r][this rank] set when the kernel is done
+  unsigned sig_idx;
+  unsigned* done_ctr;                // local counter for the last-CTA signal
+};
+
+struct PeerMaps {
+  CUtensorMap a[kMaxPeers];
+  CUtensorMap b[kMaxPeers];
 };
 
 template <int BN>
@@ -98,13 +122,64 @@ __device__ __forceinline__ void decode_unit(const Args& a, int u, int& m_blk, in
   int r = t % per_group;
   m_blk = first_m + r % gsize;
   n_blk = r / gsize;
+  if (a.m_rot) m_blk = (m_blk + a.m_rot) % a.m_blocks;
 }
 
-template <int BN, int A_MN, int B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const Args args) {
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait (bounded) until peer r's flag reaches this kernel's expected value;
+// afterwards the peer's data may be read, also by TMA (async proxy).
+__device__ __forceinline__ bool wait_peer(const Args& a, int r, volatile int* abort_flag) {
+  const unsigned want = *a.epoch_ptr * kSigStride + a.wait_idx;
+  const unsigned* f = a.wait_flags + r;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while ((int)(ld_acquire_sys_u32(f) - want) < 0) {
+    if ((++spins & 255u) == 0) {
+      if (*abort_flag) return false;
+      if ((long long)(globaltimer_ns() - t0) > a.timeout_ns) {
+        report_status(a.st, kStPeerTimeout, 60, (unsigned)r);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
+// Tensor map and coordinate for a tile of an operand whose split dimension
+// may live on the peers (coordinate `c` along that dimension is rewritten to
+// the owner's local coordinate).
+template <bool PEER>
+__device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap* local, const CUtensorMap* peers, int seg,
+                                                        int& c, const Args& a, uint32_t& ready, bool& ok,
+                                                        volatile int* abort_flag) {
+  if (!PEER || seg == 0) return local;
+  const int r = c / seg;
+  c -= r * seg;
+  if (r != a.rank && a.wait_flags != nullptr && !(ready & (1u << r))) {
+    if (!wait_peer(a, r, abort_flag)) ok = false;
+    ready |= 1u << r;
+  }
+  return peers + r;
+}
+
+template <int BN, int A_MN, int B_MN, int EPI, bool PEER>
+__device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorMap* pB, const CUtensorMap* pC,
+                                          const CUtensorMap* pC2, const PeerMaps* pm, const Args& args) {
   using C = Cfg<BN>;
+  const CUtensorMap& tmA = *pA;
+  const CUtensorMap& tmB = *pB;
+  const CUtensorMap& tmC = *pC;
+  const CUtensorMap& tmC2 = *pC2;
   constexpr int STAGES = C::STAGES;
   constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
 
@@ -154,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      uint32_t ready = 0;  // peers whose data is known to be ready
       for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
         int m_blk, n_blk, split;
         decode_unit(args, u, m_blk, n_blk, split);
@@ -168,22 +244,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sA = smem + s * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
+          const int kbp = args.kb_rot ? (kb + args.kb_rot) % args.num_kb : kb;
+          // split coordinates (rewritten to the owner's local coordinate for peer operands)
+          int ca = A_MN ? kbp * BK : m_blk * BM;
+          int cb = kbp * BK;
+          const CUtensorMap* mA =
+              pick_map<PEER>(&tmA, PEER ? pm->a : nullptr, args.a_seg, ca, args, ready, ok, abort_flag);
+          const CUtensorMap* mB =
+              pick_map<PEER>(&tmB, PEER ? pm->b : nullptr, B_MN ? args.b_seg : 0, cb, args, ready, ok, abort_flag);
+          if (!ok) break;
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
           if (A_MN) {
-            tma_load_2d(sA, &tmA, &full[s], m_blk * BM, kb * BK);
-            tma_load_2d(sA + 8192, &tmA, &full[s], m_blk * BM + 64, kb * BK);
+            tma_load_2d(sA, mA, &full[s], m_blk * BM, ca);
+            tma_load_2d(sA + 8192, mA, &full[s], m_blk * BM + 64, ca);
           } else {
-            tma_load_2d(sA, &tmA, &full[s], kb * BK, m_blk * BM);
+            tma_load_2d(sA, mA, &full[s], kbp * BK, ca);
           }
           if (B_MN) {
 #pragma unroll
-            for (int h = 0; h < BN / 64; ++h) tma_load_2d(sB + h * 8192, &tmB, &full[s], n_blk * BN + h * 64, kb * BK);
+            for (int h = 0; h < BN / 64; ++h) tma_load_2d(sB + h * 8192, mB, &full[s], n_blk * BN + h * 64, cb);
           } else {
-            tma_load_2d(sB, &tmB, &full[s], kb * BK, n_blk * BN);
+            tma_load_2d(sB, mB, &full[s], kbp * BK, n_blk * BN);
           }
         }
       }
       if (!ok) {
+        *abort_flag = 1;
         // Let copies already in flight land before the CTA exits.
         for (int j = 1; j <= STAGES && it - j >= 0; ++j) {
           const int i2 = it - j;
@@ -336,6 +422,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        if (PEER && args.rs_seg > 0) {
+          // GEMM -> reduce-scatter: push this row's 32 partial sums (bf16)
+          // straight into the owner's receive slot over NVLink
+          if (row_ok) {
+            const int owner = row / args.rs_seg;
+            uint4* dst = reinterpret_cast<uint4*>(args.rs_dst[owner] + (long)(row - owner * args.rs_seg) * args.rs_ld +
+                                                  col0);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              if (col0 + g * 8 < args.N) {
+                const int j = g * 8;
+                dst[g] = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                    pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+              }
+            }
+          }
+          continue;
+        }
         // slots are free once the previous chunk's stores have read them
         if (lane == 0) tma_store_wait_read0();
         __syncwarp();
@@ -415,6 +519,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (PEER && args.sig_flags[0] != nullptr && threadIdx.x == 0) {
+    // last CTA to finish tells every peer that this rank's output is complete
+    __threadfence_system();
+    if (atomicAdd(args.done_ctr, 1u) == gridDim.x - 1) {
+      *args.done_ctr = 0u;
+      const unsigned v = *args.epoch_ptr * kSigStride + args.sig_idx;
+      __threadfence_system();
+      for (int r = 0; r < args.world; ++r) st_release_sys_u32(args.sig_flags[r], v);
+    }
+  }
+}
+
+template <int BN, int A_MN, int B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const Args args) {
+  gemm_body<BN, A_MN, B_MN, EPI, false>(&tmA, &tmB, &tmC, &tmC2, nullptr, args);
+}
+
+// Tensor-parallel variant: operands may be split over the ranks' symmetric
+// buffers (one TMA map per rank, plain TMA loads, no multicast), the output
+// may be pushed to the owners of its rows, and the kernel can signal peers.
+template <int BN, int A_MN, int B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
+                   const __grid_constant__ PeerMaps pm, const Args args) {
+  gemm_body<BN, A_MN, B_MN, EPI, true>(&tmA, &tmB, &tmC, &tmC2, &pm, args);
 }
 
 // ---------------------------------------------------------------------------
@@ -494,7 +626,196 @@ static void launch_bn(int a_mn, int b_mn, int epi, const Maps& m, const Args& ar
   else launch_epi<BN, 1, 1>(epi, m, args, grid, s);
 }
 
+template <int A_MN, int B_MN, int EPI>
+static void launch_tp_t(const Maps& m, const PeerMaps& pm, const Args& args, int grid, cudaStream_t stream) {
+  constexpr int BN = 256;
+  auto kern = gemm_tp_kernel<BN, A_MN, B_MN, EPI>;
+  set_max_smem(reinterpret_cast<const void*>(kern), Cfg<BN>::SMEM);
+  kern<<<grid, kThreads, Cfg<BN>::SMEM, stream>>>(m.a, m.b, m.c, m.c2, pm, args);
+  SCIRS_CHECK_LAUNCH();
+}
+
+// Operand forms used by the tensor-parallel layers (BN = 256):
+//   (K, K, BF16/BIAS_GELU) forward column-parallel (A rows gathered from the
+//   peers) and row-parallel (output rows pushed to their owners);
+//   (K, MN, BF16/DGELU) data gradients; (MN, MN, F32) weight gradients with
+//   the K (token) dimension of one operand gathered from the peers.
+static void launch_tp(int a_mn, int b_mn, int epi, const Maps& m, const PeerMaps& pm, const Args& args, int grid,
+                      cudaStream_t s) {
+  if (!a_mn && !b_mn && epi == EPI_BF16) launch_tp_t<0, 0, EPI_BF16>(m, pm, args, grid, s);
+  else if (!a_mn && !b_mn && epi == EPI_BIAS_GELU) launch_tp_t<0, 0, EPI_BIAS_GELU>(m, pm, args, grid, s);
+  else if (!a_mn && b_mn && epi == EPI_BF16) launch_tp_t<0, 1, EPI_BF16>(m, pm, args, grid, s);
+  else if (!a_mn && b_mn && epi == EPI_DGELU) launch_tp_t<0, 1, EPI_DGELU>(m, pm, args, grid, s);
+  else if (a_mn && b_mn && epi == EPI_F32) launch_tp_t<1, 1, EPI_F32>(m, pm, args, grid, s);
+  else TORCH_CHECK(false, "tensor-parallel GEMM form not supported: a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+static unsigned* done_counter(int dev) {
+  static unsigned* ctr[64] = {nullptr};
+  if (ctr[dev] == nullptr) {
+    SCIRS_CHECK_CUDA(cudaMalloc(&ctr[dev], sizeof(unsigned)));
+    SCIRS_CHECK_CUDA(cudaMemset(ctr[dev], 0, sizeof(unsigned)));
+  }
+  return ctr[dev];
+}
+
 }  // namespace gemm
+
+// Tensor-parallel GEMM (fused all-gather -> GEMM and GEMM -> reduce-scatter).
+//   a_peers (optional): base address of A's segment on every rank (symmetric
+//     buffers; `a` is this rank's segment): A K-major [Mr, K] -> rows
+//     gathered, M = world * Mr; A MN-major [Kr, M] -> K gathered, K = world*Kr.
+//   b_peers (optional, B MN-major [Kr, N]): K gathered, K = world * Kr.
+//   rs_dst (optional): owner r's receive-slot address for this rank's rows;
+//     `out` is then this rank's receive buffer [world, Mr, N] (shape check
+//     only) and output rows [r*Mr, (r+1)*Mr) are pushed to owner r.
+//   flags / epoch / wait_idx: before reading a peer's segment the producer
+//     waits (bounded) until flags[peer] >= epoch * 4096 + wait_idx.
+//   sig_flags / sig_idx (optional): when every CTA is done, each peer's flag
+//     word for this rank is set to epoch * 4096 + sig_idx.
+void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
+             c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
+             bool accumulate, int64_t splits, int64_t rank, int64_t world, std::vector<int64_t> a_peers,
+             std::vector<int64_t> b_peers, std::vector<int64_t> rs_dst, c10::optional<torch::Tensor> flags,
+             c10::optional<torch::Tensor> epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
+             double timeout_s) {
+  using namespace gemm;
+  CHECK_DTYPE(a, at::kBFloat16);
+  CHECK_DTYPE(b, at::kBFloat16);
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "bad rank/world");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "gemm operands must be 2-D");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm operands need unit inner stride");
+  const bool ap = !a_peers.empty(), bp = !b_peers.empty(), rs = !rs_dst.empty();
+  TORCH_CHECK(!ap || (int64_t)a_peers.size() == world, "a_peers needs one address per rank");
+  TORCH_CHECK(!bp || ((int64_t)b_peers.size() == world && b_mn), "b_peers: one address per rank, B MN-major");
+  TORCH_CHECK(!rs || ((int64_t)rs_dst.size() == world && epi == EPI_BF16 && !a_mn), "rs_dst: one per rank, bf16");
+  const int64_t Ml = a_mn ? a.size(1) : a.size(0);
+  const int64_t Kl = a_mn ? a.size(0) : a.size(1);
+  const int64_t M = (ap && !a_mn) ? Ml * world : Ml;
+  const int64_t K = (ap && a_mn) ? Kl * world : Kl;
+  const int64_t Kb = b_mn ? b.size(0) * (bp ? world : 1) : b.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK(K == Kb, "gemm K mismatch: ", K, " vs ", Kb);
+  TORCH_CHECK(N % 8 == 0 && K % BK == 0 && M % BM == 0, "tensor-parallel gemm needs M % 128, K % 64, N % 8 == 0");
+  if (ap) TORCH_CHECK(a_mn ? (a.size(0) % BK == 0) : (a.size(0) % BM == 0), "segment not tile aligned");
+  if (bp) TORCH_CHECK(b.size(0) % BK == 0, "B segment not tile aligned");
+  const int dev = a.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  const int sms = num_sms(dev);
+  Args args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.num_kb = (int)(K / BK);
+  args.m_blocks = (int)(M / BM);
+  args.st = status_ptr(dev);
+  args.group_m = 16;
+  args.rank = (int)rank;
+  args.world = (int)world;
+  args.timeout_ns = (long long)(timeout_s * 1e9);
+  if (flags.has_value() && flags->defined()) {
+    TORCH_CHECK(flags->numel() >= world && flags->element_size() == 4, "flags: 32-bit [world]");
+    TORCH_CHECK(epoch.has_value() && epoch->defined() && epoch->element_size() == 4, "epoch: 32-bit device scalar");
+    args.wait_flags = reinterpret_cast<const unsigned*>(flags->data_ptr());
+    args.epoch_ptr = reinterpret_cast<const unsigned*>(epoch->data_ptr());
+    args.wait_idx = (unsigned)wait_idx;
+  }
+  if (!sig_flags.empty()) {
+    TORCH_CHECK((int64_t)sig_flags.size() == world && args.epoch_ptr != nullptr, "sig_flags: one per rank + epoch");
+    for (int r = 0; r < world; ++r) args.sig_flags[r] = reinterpret_cast<unsigned*>(sig_flags[r]);
+    args.sig_idx = (unsigned)sig_idx;
+    args.done_ctr = done_counter(dev);
+  }
+  if (bias.has_value() && bias->defined()) {
+    CHECK_DTYPE((*bias), at::kBFloat16);
+    TORCH_CHECK(bias->numel() >= N && bias->is_contiguous(), "bias must hold N contiguous values");
+    args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (epi == EPI_DGELU) {
+    TORCH_CHECK(aux.has_value() && aux->defined() && aux->size(0) == M && aux->size(1) == N, "dgelu needs aux [M,N]");
+    args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+    args.ldaux = aux->stride(0);
+  }
+  Maps maps;
+  if (rs) {
+    TORCH_CHECK(out.dim() == 3 && out.size(0) == world && out.size(1) * world == M && out.size(2) == N &&
+                    out.is_contiguous(), "out must be this rank's receive buffer [world, M/world, N]");
+    CHECK_DTYPE(out, at::kBFloat16);
+    args.rs_seg = (int)(M / world);
+    args.rs_ld = N;
+    for (int r = 0; r < world; ++r) args.rs_dst[r] = reinterpret_cast<__nv_bfloat16*>(rs_dst[r]);
+    // start with the next rank's rows so that every rank pushes to a different owner
+    args.m_rot = (int)(((rank + 1) % world) * (args.rs_seg / BM));
+    maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)N * 2, 32, 32,
+                      CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+  } else {
+    TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "out must be [M, N]");
+    if (epi == EPI_F32) CHECK_DTYPE(out, at::kFloat);
+    else CHECK_DTYPE(out, at::kBFloat16);
+    args.C = out.data_ptr();
+    args.ldc = out.stride(0);
+    if (epi == EPI_F32)
+      maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)out.stride(0) * 4, 16, 32,
+                        CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B);
+    else
+      maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)out.stride(0) * 2, 32, 32,
+                        CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (ap && !a_mn) args.m_rot = (int)(rank * (Ml / BM));  // local rows first
+  }
+  maps.c2 = maps.c;
+  if (epi == EPI_DGELU)
+    maps.c2 = get_tmap(args.aux, (uint64_t)N, (uint64_t)M, (uint64_t)args.ldaux * 2, 32, 32,
+                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (epi == EPI_BIAS_GELU) {
+    TORCH_CHECK(out2.has_value() && out2->defined() && out2->size(0) == M && out2->size(1) == N, "gelu needs out2");
+    args.C2 = out2->data_ptr();
+    args.ldc2 = out2->stride(0);
+    maps.c2 = get_tmap(args.C2, (uint64_t)N, (uint64_t)M, (uint64_t)args.ldc2 * 2, 32, 32,
+                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
+  const uint64_t lda_b = (uint64_t)a.stride(0) * 2, ldb_b = (uint64_t)b.stride(0) * 2;
+  PeerMaps pm;
+  memset(&pm, 0, sizeof(pm));
+  // local maps (own segment) and one map per rank for peer operands
+  maps.a = a_mn ? get_tmap(a.data_ptr(), (uint64_t)Ml, (uint64_t)a.size(0), lda_b, 64, 64)
+                : get_tmap(a.data_ptr(), (uint64_t)Kl, (uint64_t)a.size(0), lda_b, 64, BM);
+  maps.b = b_mn ? get_tmap(b.data_ptr(), (uint64_t)N, (uint64_t)b.size(0), ldb_b, 64, 64)
+                : get_tmap(b.data_ptr(), (uint64_t)b.size(1), (uint64_t)N, ldb_b, 64, 256);
+  if (ap) {
+    args.a_seg = (int)a.size(0);
+    for (int r = 0; r < world; ++r) {
+      const void* p = reinterpret_cast<const void*>(a_peers[r]);
+      TORCH_CHECK((a_peers[r] & 15) == 0, "peer operand must be 16-byte aligned");
+      pm.a[r] = a_mn ? get_tmap(p, (uint64_t)Ml, (uint64_t)a.size(0), lda_b, 64, 64)
+                     : get_tmap(p, (uint64_t)Kl, (uint64_t)a.size(0), lda_b, 64, BM);
+    }
+    if (a_mn) args.kb_rot = (int)(rank * (a.size(0) / BK));
+  }
+  if (bp) {
+    args.b_seg = (int)b.size(0);
+    for (int r = 0; r < world; ++r) {
+      TORCH_CHECK((b_peers[r] & 15) == 0, "peer operand must be 16-byte aligned");
+      pm.b[r] = get_tmap(reinterpret_cast<const void*>(b_peers[r]), (uint64_t)N, (uint64_t)b.size(0), ldb_b, 64, 64);
+    }
+    args.kb_rot = (int)(rank * (b.size(0) / BK));
+  }
+  args.n_blocks = (int)((N + 255) / 256);
+  const long tiles = (long)args.m_blocks * args.n_blocks;
+  int sp = 1;
+  if (epi == EPI_F32) {
+    if (splits > 0) sp = (int)splits;
+    else if (tiles < 2L * sms) sp = (int)std::max<long>(1, std::min<long>(16, (2L * sms + tiles - 1) / tiles));
+    sp = std::max(1, std::min(sp, args.num_kb));
+  }
+  args.kb_per_split = (args.num_kb + sp - 1) / sp;
+  sp = (args.num_kb + args.kb_per_split - 1) / args.kb_per_split;
+  args.splits = sp;
+  args.atomic_out = (epi == EPI_F32 && (accumulate || sp > 1)) ? 1 : 0;
+  if (epi == EPI_F32 && sp > 1 && !accumulate) out.zero_();
+  args.num_units = (int)(tiles * sp);
+  const int grid = (int)std::min<long>(args.num_units, sms);
+  launch_tp((int)a_mn, (int)b_mn, (int)epi, maps, pm, args, grid, cur_stream());
+}
 
 // Python entry: see scirs_b200/ops/gemm.py for the calling convention.
 //   a        : bf16 2-D, [M,K] (a_mn=0) or [K,M] (a_mn=1)
@@ -522,8 +843,11 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   const int64_t Kb = b_mn ? b.size(0) : b.size(1);
   TORCH_CHECK(K == Kb, "gemm K mismatch: ", K, " vs ", Kb);
   TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm out shape mismatch");
+  // TMA: the contiguous dimension of every operand must span a multiple of
+  // 16 bytes (N is the output's contiguous dimension)
   TORCH_CHECK(N % 8 == 0, "gemm N must be a multiple of 8");
-  TORCH_CHECK(K % 8 == 0 && M % 8 == 0, "gemm M and K must be multiples of 8");
+  TORCH_CHECK((a_mn ? M : K) % 8 == 0, "gemm: A's contiguous dimension must be a multiple of 8");
+  TORCH_CHECK((b_mn || K % 8 == 0), "gemm: B's contiguous dimension (K) must be a multiple of 8");
   if (epi == EPI_F32) {
     CHECK_DTYPE(out, at::kFloat);
   } else {
