@@ -42,17 +42,28 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
-    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
-    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="sequences per step (default 64 for gpt2, 32 for gpt1.3b)")
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default 1024 gpt2, 2048 gpt1.3b)")
     ap.add_argument("--dp-mode", default="fused", choices=["fused", "nccl"])
-    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--layers", type=int, default=None, help="layers (default: the model's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="run the step eagerly instead of as a CUDA graph")
-    ap.add_argument("--model", default="gpt2", choices=["gpt2", "vit"],
+    ap.add_argument("--model", default="gpt2", choices=["gpt2", "vit", "gpt1.3b"],
                     help="gpt2: GPT-2-small decoder, data parallel (headline); "
-                    "vit: ViT-B/16 encoder, ZeRO (sharded AdamW, grad reduce-scatter, param all-gather)")
+                    "vit: ViT-B/16 encoder, ZeRO (sharded AdamW, grad reduce-scatter, param all-gather); "
+                    "gpt1.3b: 1.3B rotary decoder, tensor parallel over all GPUs (fused AG->GEMM, GEMM->RS)")
+    ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
+                    help="gpt1.3b: fused collective GEMMs, or NCCL all-gather/reduce-scatter + separate GEMMs")
     ap.add_argument("--images", type=int, default=256, help="global batch of the ViT workload")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.global_batch is None:
+        a.global_batch = 32 if a.model == "gpt1.3b" else GLOBAL_BATCH
+    if a.seq is None:
+        a.seq = 2048 if a.model == "gpt1.3b" else SEQ
+    if a.layers is None:
+        a.layers = 24 if a.model == "gpt1.3b" else 12
+    return a
 
 
 def reference_unavailable():
@@ -140,6 +151,7 @@ def synthetic_batches(n, local_batch, seq, vocab, seed):
 
 def build_gpt(args, rank, world, local, dev):
     """GPT-2-small decoder, data parallel (fused in-kernel all-reduce or NCCL)."""
+    assert args.global_batch % world == 0, "global batch must split over the GPUs"
     import torch
 
     from scirs_b200.models.gpt import GPTConfig
@@ -335,6 +347,91 @@ def build_vit(args, rank, world, local, dev):
 
 
 
+def build_tp(args, rank, world, local, dev):
+    """1.3B rotary decoder, tensor parallel over all ranks (sequence-parallel
+    activations, vocabulary-parallel head and cross-entropy). Every rank sees
+    the full batch; the step's tokens are global_batch x seq."""
+    import torch
+
+    from scirs_b200.models.tp_gpt import DecoderConfig, TPDecoder
+
+    cfg = DecoderConfig.decoder_1_3b()
+    cfg.num_hidden_layers = args.layers
+    B, S = args.global_batch, args.seq
+    cfg.max_position_embeddings = max(cfg.max_position_embeddings, S)
+    n_batches = max(args.warmup, 1) + args.steps
+    batches = synthetic_batches(n_batches, B, S, cfg.vocab_size, seed=999)
+    hp = dict(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
+    if args.impl == "ours":
+        from scirs_b200.ops import kernels as K
+        from scirs_b200.parallel.tensor_parallel import TPContext
+
+        ctx = TPContext(TPDecoder.heap_bytes(cfg, B, S, world), mode=args.tp_mode)
+        model = TPDecoder(cfg, ctx, batch=B, seq=S, seed=0)
+        model.configure_adamw(**hp)
+        if not args.no_graph:
+            model.enable_cuda_graph()
+
+        def step(tok, tgt):
+            return model.train_step(tok, tgt)
+
+        def launches():
+            return K.STATS.launches + ctx.launches
+
+        def cleanup():
+            model.close()
+            ctx.close()
+
+    else:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        from scirs_b200.models.torch_gpt import TorchDecoder
+
+        assert B % world == 0
+        lb = B // world
+        net = TorchDecoder(cfg, seq=S).to(dev)
+        if world > 1:
+            net = DDP(net, device_ids=[local], bucket_cap_mb=25, gradient_as_bucket_view=True)
+        opt = torch.optim.AdamW(net.parameters(), lr=hp["lr"], betas=hp["betas"], weight_decay=hp["weight_decay"],
+                                fused=True)
+
+        def step(tok, tgt):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = net(tok[rank * lb : (rank + 1) * lb], tgt[rank * lb : (rank + 1) * lb])
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(net.parameters(), 1.0)
+            opt.step()
+            return loss
+
+        def launches():
+            return 0
+
+        def cleanup():
+            pass
+
+    return {
+        "step": step,
+        "launches": launches,
+        "cleanup": cleanup,
+        "batches": batches,
+        "tokens_per_step": B * S,
+        "flops_per_token": cfg.flops_per_token(S),
+        "h2d_bytes_per_step": 2 * B * S * 8,
+        "api": "TPDecoder.train_step" if args.impl == "ours" else "torch DDP module + torch.optim.AdamW",
+        "data": "synthetic (tokens uniform in [0, 32000) from a fixed seed; random-init weights)",
+        "config": {
+            "model": "1.3B rotary decoder: 24 layers, d=2048, 16 heads, MLP 8192 GELU, vocab 32000",
+            "layers": cfg.num_hidden_layers,
+            "global_batch": B,
+            "seq_len": S,
+            "parallelism": f"tp{world}" if args.impl == "ours" else f"dp{world}",
+            "tp_collectives": args.tp_mode if args.impl == "ours" else None,
+            "optimizer": "AdamW (fp32 master, wd 0.1, clip 1.0)",
+        },
+    }
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -352,8 +449,8 @@ def main():
         raise SystemExit(f"--gpus {N} but WORLD_SIZE={world}; launch N>1 with torchrun")
     dev = torch.device("cuda", local)
     torch.manual_seed(0)
-    assert args.global_batch % world == 0
-    W = build_vit(args, rank, world, local, dev) if args.model == "vit" else build_gpt(args, rank, world, local, dev)
+    builders = {"gpt2": build_gpt, "vit": build_vit, "gpt1.3b": build_tp}
+    W = builders[args.model](args, rank, world, local, dev)
     step, launches, batches = W["step"], W["launches"], W["batches"]
     dev_batches = [(a.to(dev), b.to(dev)) for a, b in batches]
 

@@ -1,0 +1,379 @@
+// FlashAttention forward, second design: two query tiles per CTA in
+// ping-pong, O accumulated in TMEM by the tensor cores, P handed to the PV
+// MMA through TMEM, lazy rescaling.
+//
+// One CTA = 256 queries (two 128-row tiles t = 0, 1) of one (batch, head);
+// both tiles share the K/V stream.
+//
+//   warp 0     TMA producer: Q0, Q1 once, then K_j / V_j into a 3-stage (head_dim
+//              64) or 2-stage (128) ring
+//   warp 1     owns TMEM (512 columns); one thread issues, per key block j,
+//              PV_t(j) = P_t(j) V_j (A = P from TMEM, accumulated into O_t)
+//              followed by S_t(j+1) = Q_t K_{j+1}^T, alternating t, so the
+//              tensor core works on one tile while the other tile's softmax
+//              warps run
+//   warps 2-5  softmax of tile 0, warps 6-9 softmax of tile 1: thread owns
+//              one query row (TMEM lane); reads the 128 scores of its row in
+//              one go, takes the row max, and keeps a running reference max
+//              that is raised only when a score exceeds it by more than
+//              2^8 (then the O row in TMEM and the row sum are rescaled;
+//              otherwise P = exp2(s - ref) <= 256 is exact enough in bf16 and
+//              fp32). P is written back into the S columns as packed bf16
+//              (tcgen05.st) and consumed there by the PV MMA.
+//
+// TMEM columns: S_t at [128 t, 128 t + 128) (P_t aliases its first 64),
+// O_t at [256 + HD t, 256 + HD (t + 1)).
+// MMAs issued by one thread complete in issue order, so S_t(j+1) may reuse
+// the columns PV_t(j) reads, and the completion of S_t(j+1) (s_full) implies
+// PV_t(j) has finished accumulating into O_t (which the softmax warps may
+// then rescale). Causal masking touches only the diagonal block; keys >= S
+// are masked; rows >= S are not stored. Every mbarrier wait is bounded.
+//
+// Reference parity: same math as the reference's CPU FlashAttention-2
+// forward (scirs2-neural/src/layers/flash_attention_v2.rs:220,369-482,
+// scirs2-neural/src/attention/flash_v2.rs:96-300); LSE is natural-log.
+#include "host_common.h"
+
+namespace scirs {
+namespace fa2t {
+
+using bf16 = __nv_bfloat16;
+constexpr int BM = 128, BN = 128;
+constexpr int kThreads = 320;
+constexpr float kRescaleLog2 = 8.f;  // raise the reference max only past 2^8
+
+struct Params {
+  bf16* out;
+  float* lse;
+  long o_rs;
+  int B, H, S;
+  float scale_log2;
+  DevStatus* st;
+};
+
+template <int HD>
+struct Cfg {
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int KV_BYTES = BN * HD * 2;
+  // K/V ring depth: 3 stages for head_dim 64 (which also keeps the CTA at
+  // one per SM, matching its 512-column TMEM allocation), 2 for 128
+  static constexpr int NST = (HD == 64) ? 3 : 2;
+  static constexpr int OFF_Q = 0;                         // 2 tiles
+  static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;       // NST stages
+  static constexpr int OFF_V = OFF_K + NST * KV_BYTES;    // NST stages
+  static constexpr int OFF_BAR = OFF_V + NST * KV_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr uint32_t IDESC_S = umma_idesc_bf16(BM, BN, 0, 0);
+  static constexpr uint32_t IDESC_O = umma_idesc_bf16(BM, HD, 0, 1);
+};
+
+template <int HD, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  constexpr int NST = C::NST;
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;              // [NST] stages
+  uint64_t* v_full = k_full + NST;          // [NST]
+  uint64_t* kv_empty = v_full + NST;        // [NST]
+  uint64_t* s_full = kv_empty + NST;        // [2] tiles
+  uint64_t* p_full = s_full + 2;            // [2] tiles (4 warps each)
+  uint64_t* o_final = p_full + 2;           // [2] tiles
+  uint64_t* drain = o_final + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.S, H = p.H;
+  const int qp = gridDim.x - 1 - blockIdx.x;  // longest causal work first
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int q0 = qp * 2 * BM;
+  const int row_base = b * S;
+  const int nkv_all = (S + BN - 1) / BN;
+  // key blocks each tile needs (tile t covers queries [q0 + 128 t, +128))
+  const int nkv0 = (q0 >= S) ? 0 : (CAUSAL ? min(nkv_all, q0 / BM + 1) : nkv_all);
+  const int nkv1 = (q0 + BM >= S) ? 0 : (CAUSAL ? min(nkv_all, q0 / BM + 2) : nkv_all);
+  const int nkv = max(nkv0, nkv1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_final[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      const int col = h * HD;
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(smem + C::OFF_Q + t * C::Q_BYTES + c * (BM * 128), &tmQ, q_full, col + c * 64,
+                      row_base + q0 + t * BM);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % NST;
+        if (!mbar_wait(&kv_empty[s], ((j / NST) & 1) ^ 1, p.st, 50, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + c * (BN * 128), &tmK, &k_full[s], col + c * 64,
+                      row_base + j * BN);
+        mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + c * (BN * 128), &tmV, &v_full[s], col + c * 64,
+                      row_base + j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, p.st, 51, abort_flag);
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      auto issue_s = [&](int t, int j) -> bool {
+        const int s = j % NST;
+        if (!mbar_wait(&k_full[s], (j / NST) & 1, p.st, 52, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + C::OFF_K + s * C::KV_BYTES);
+        const uint32_t qa = q_addr + t * C::Q_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(tmem + t * BN, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(k_addr + offk, 16, 1024),
+                        C::IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[t]);
+        return true;
+      };
+      tc_fence_after();
+      if (nkv0 > 0) ok = issue_s(0, 0);
+      if (ok && nkv1 > 0) ok = issue_s(1, 0);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j % NST;
+        bool v_ready = false;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int nt = t ? nkv1 : nkv0;
+          if (!ok || j >= nt) continue;
+          if (!mbar_wait(&p_full[t], j & 1, p.st, 53, abort_flag)) { ok = false; break; }
+          if (!v_ready) {
+            if (!mbar_wait(&v_full[s], (j / NST) & 1, p.st, 54, abort_flag)) { ok = false; break; }
+            v_ready = true;
+          }
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + C::OFF_V + s * C::KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            // A = P_t from TMEM (16 keys = 8 packed columns per step);
+            // B = V [keys][HD] MN-major: k-step = 16 key rows = 2048 bytes
+            const uint64_t bdesc = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+            tc_mma_f16_ts(tmem + 2 * BN + t * HD, tmem + t * BN + kk * 8, bdesc, C::IDESC_O,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (j + 1 < nt) {
+            ok = issue_s(t, j + 1);
+          } else {
+            tc_commit(&o_final[t]);
+          }
+        }
+        if (ok) tc_commit(&kv_empty[s]);
+      }
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int t = (warp - 2) >> 2;   // tile of this warpgroup
+    const int q = warp & 3;          // TMEM lane quarter
+    const int r = q * 32 + lane;     // query row within the tile
+    const int qrow = q0 + t * BM + r;
+    const uint32_t lane_off = uint32_t(q * 32) << 16;
+    const uint32_t s_base = tmem + lane_off + t * BN;
+    const uint32_t o_base = tmem + lane_off + 2 * BN + t * HD;
+    const int my_nkv = t ? nkv1 : nkv0;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < my_nkv && ok; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, p.st, 55, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float sv[BN];
+      {
+        uint32_t* u = reinterpret_cast<uint32_t*>(sv);
+#pragma unroll
+        for (int c = 0; c < BN; c += 32) tmem_ld_32x32b_x32(s_base + c, u + c);
+        tc_wait_ld();
+      }
+      const int kv0 = j * BN;
+      const bool mask = (kv0 + BN > S) || (CAUSAL && kv0 + BN > q0 + t * BM);
+      if (mask) {
+#pragma unroll
+        for (int e = 0; e < BN; ++e) {
+          const int key = kv0 + e;
+          if (key >= S || (CAUSAL && key > qrow)) sv[e] = -INFINITY;
+        }
+      }
+      float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int e = 4; e < BN; e += 4) {
+        m4[0] = fmaxf(m4[0], sv[e]);
+        m4[1] = fmaxf(m4[1], sv[e + 1]);
+        m4[2] = fmaxf(m4[2], sv[e + 2]);
+        m4[3] = fmaxf(m4[3], sv[e + 3]);
+      }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
+      // raise the reference max (and rescale O and l) only when needed
+      const bool raise = mx > m_ref + kRescaleLog2;
+      float alpha = 1.f;
+      if (raise) {
+        alpha = (m_ref == -INFINITY) ? 0.f : ex2_fast(m_ref - mx);
+        m_ref = mx;
+        l *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, raise)) {
+        // O_t holds PV_t(0..j-1), complete (implied by s_full above)
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_base + c, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st_32x32b_x16(o_base + c, ov);
+          tmem_st_32x32b_x16(o_base + c + 16, ov + 16);
+        }
+        tc_wait_st();
+      }
+      const float ref = (m_ref == -INFINITY) ? 0.f : m_ref;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        // 32 scores -> 16 packed bf16 pairs -> TMEM columns [c/2, c/2 + 16)
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = ex2_fast(fmaf(sv[c + e], p.scale_log2, -ref));
+          const float p1 = ex2_fast(fmaf(sv[c + e + 1], p.scale_log2, -ref));
+          rs0 += p0;
+          rs1 += p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16(s_base + (c >> 1), pk);
+      }
+      l += rs0 + rs1;
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && my_nkv > 0 && mbar_wait(&o_final[t], 0, p.st, 56, abort_flag)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = p.out + (long)(row_base + qrow) * p.o_rs + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(o_base + c, ov);
+        tc_wait_ld();
+        if (qrow < S) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 o;
+            const float* f = reinterpret_cast<const float*>(ov) + g * 8;
+            o.x = pack_bf16x2(f[0] * inv, f[1] * inv);
+            o.y = pack_bf16x2(f[2] * inv, f[3] * inv);
+            o.z = pack_bf16x2(f[4] * inv, f[5] * inv);
+            o.w = pack_bf16x2(f[6] * inv, f[7] * inv);
+            *reinterpret_cast<uint4*>(orow + c + g * 8) = o;
+          }
+        }
+      }
+      if (qrow < S) p.lse[((long)b * H + h) * S + qrow] = (m_ref + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fa2t
+
+// q/k/v/out: [B, S, H, HD] token-major views with contiguous heads; lse [B,H,S].
+void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       bool causal, double scale) {
+  const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
+  for (auto* t : {&q, &k, &v, &out}) {
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == S &&
+                    t->size(2) == H && t->size(3) == HD,
+                "q/k/v/out must be bf16 [B, S, H, HD]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == S * t->stride(1),
+                "q/k/v/out must be token-major with contiguous heads");
+  }
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * H * S && lse.is_contiguous(), "lse fp32 [B,H,S]");
+  c10::cuda::CUDAGuard guard(q.get_device());
+  auto mk = [&](const torch::Tensor& t) {
+    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * S),
+                        (uint64_t)t.stride(1) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  CUtensorMap tq = mk(q), tk = mk(k), tv = mk(v);
+  fa2t::Params p{};
+  p.out = reinterpret_cast<fa2t::bf16*>(out.data_ptr());
+  p.lse = lse.data_ptr<float>();
+  p.o_rs = out.stride(1);
+  p.B = (int)B;
+  p.H = (int)H;
+  p.S = (int)S;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.st = status_ptr(q.get_device());
+  dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
+  auto st = cur_stream();
+#define FA2T(HD_, C_)                                                          \
+  {                                                                            \
+    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_>;                               \
+    set_max_smem((const void*)kern, fa2t::Cfg<HD_>::SMEM);                     \
+    kern<<<grid, fa2t::kThreads, fa2t::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);   \
+  }
+  if (HD == 64) {
+    if (causal) FA2T(64, true) else FA2T(64, false)
+  } else {
+    if (causal) FA2T(128, true) else FA2T(128, false)
+  }
+#undef FA2T
+  SCIRS_CHECK_LAUNCH();
+}
+
+}  // namespace scirs

@@ -33,6 +33,28 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
                     torch::Tensor delta, bool causal, double scale, int64_t impl);
 void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale);
+void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
+             c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
+             bool accumulate, int64_t splits, int64_t rank, int64_t world, std::vector<int64_t> a_peers,
+             std::vector<int64_t> b_peers, std::vector<int64_t> rs_dst, c10::optional<torch::Tensor> flags,
+             c10::optional<torch::Tensor> epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
+             double timeout_s);
+void tp_signal(std::vector<int64_t> sig_flags, torch::Tensor epoch, int64_t idx);
+void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       bool causal, double scale);
+void tp_step_begin(torch::Tensor epoch);
+void tp_reduce(torch::Tensor recv, torch::Tensor out, c10::optional<torch::Tensor> bias,
+               c10::optional<torch::Tensor> resid, int64_t rank, c10::optional<torch::Tensor> flags,
+               torch::Tensor epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
+               double timeout_s);
+void rope_apply(torch::Tensor qkv, torch::Tensor cos_t, torch::Tensor sin_t, int64_t S, int64_t H, int64_t hd,
+                bool inverse);
+void tp_xent_stats(torch::Tensor logits, torch::Tensor targets, int64_t nvalid, int64_t v0, int64_t rank,
+                   std::vector<int64_t> stats_dst, std::vector<int64_t> sig_flags, torch::Tensor epoch,
+                   int64_t sig_idx);
+void tp_xent_finish(torch::Tensor logits, torch::Tensor targets, torch::Tensor stats, c10::optional<torch::Tensor> loss,
+                    int64_t nvalid, int64_t v0, int64_t rank, double scale, torch::Tensor flags, torch::Tensor epoch,
+                    int64_t wait_idx, double timeout_s);
 }  // namespace scirs
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -52,6 +74,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("grads"), py::arg("params16"), py::arg("n_decay"), py::arg("decay_mask"), py::arg("hp"),
         py::arg("part"), py::arg("norm_out"), py::arg("parts_ready") = 0);
   m.def("grad_sumsq", &scirs::grad_sumsq);
+  m.def("gemm_tp", &scirs::gemm_tp, "tensor-parallel tcgen05 GEMM (fused all-gather / reduce-scatter)",
+        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"),
+        py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("out2") = py::none(),
+        py::arg("accumulate") = false, py::arg("splits") = 0, py::arg("rank") = 0, py::arg("world") = 1,
+        py::arg("a_peers") = std::vector<int64_t>{}, py::arg("b_peers") = std::vector<int64_t>{},
+        py::arg("rs_dst") = std::vector<int64_t>{}, py::arg("flags") = py::none(), py::arg("epoch") = py::none(),
+        py::arg("wait_idx") = 0, py::arg("sig_flags") = std::vector<int64_t>{}, py::arg("sig_idx") = 0,
+        py::arg("timeout_s") = 10.0);
+  m.def("tp_signal", &scirs::tp_signal);
+  m.def("flash_attn_fwd_pp", &scirs::flash_attn_fwd_pp);
+  m.def("tp_step_begin", &scirs::tp_step_begin);
+  m.def("tp_reduce", &scirs::tp_reduce);
+  m.def("rope_apply", &scirs::rope_apply);
+  m.def("tp_xent_stats", &scirs::tp_xent_stats);
+  m.def("tp_xent_finish", &scirs::tp_xent_finish);
   m.def("patchify", &scirs::patchify);
   m.def("vit_embed_fwd", &scirs::vit_embed_fwd);
   m.def("vit_embed_bwd", &scirs::vit_embed_bwd);

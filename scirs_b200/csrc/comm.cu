@@ -612,6 +612,96 @@ void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t
   SCIRS_CHECK_LAUNCH();
 }
 
+// ---------------------------------------------------------------------------
+// Symmetric heap: one device allocation per rank of the same size, mapped
+// into every peer (CUDA IPC). Tensors placed at the same offset on every rank
+// can then be read by peers (TMA loads without multicast, plain loads) or
+// written by them (the reduce-scatter epilogues, flags).
+// ---------------------------------------------------------------------------
+namespace {
+struct SymHeap {
+  int rank = 0, world = 1, device = 0;
+  long bytes = 0;
+  char* local = nullptr;
+  char* base[comm::kMaxRanks] = {nullptr};
+  std::vector<char*> opened;
+};
+std::unordered_map<int64_t, SymHeap> g_syms;
+int64_t g_next_sym = 1;
+}  // namespace
+
+std::tuple<int64_t, py::bytes> sym_create(int64_t device, int64_t rank, int64_t world, int64_t bytes) {
+  TORCH_CHECK(world >= 1 && world <= comm::kMaxRanks && rank >= 0 && rank < world, "bad rank/world");
+  TORCH_CHECK(bytes > 0 && bytes % 256 == 0, "bytes must be a positive multiple of 256");
+  c10::cuda::CUDAGuard guard((int)device);
+  SymHeap h;
+  h.rank = (int)rank;
+  h.world = (int)world;
+  h.device = (int)device;
+  h.bytes = bytes;
+  SCIRS_CHECK_CUDA(cudaMalloc(&h.local, bytes));
+  SCIRS_CHECK_CUDA(cudaMemset(h.local, 0, bytes));
+  SCIRS_CHECK_CUDA(cudaDeviceSynchronize());
+  h.base[h.rank] = h.local;
+  cudaIpcMemHandle_t ih;
+  SCIRS_CHECK_CUDA(cudaIpcGetMemHandle(&ih, h.local));
+  std::lock_guard<std::mutex> lk(g_mu);
+  const int64_t id = g_next_sym++;
+  g_syms[id] = h;
+  return {id, py::bytes(reinterpret_cast<const char*>(&ih), sizeof(ih))};
+}
+
+void sym_open(int64_t id, std::vector<py::bytes> handles) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_syms.find(id);
+  TORCH_CHECK(it != g_syms.end(), "unknown symmetric heap");
+  SymHeap& h = it->second;
+  TORCH_CHECK((int)handles.size() == h.world, "need one handle per rank");
+  c10::cuda::CUDAGuard guard(h.device);
+  for (int r = 0; r < h.world; ++r) {
+    if (r == h.rank) continue;
+    std::string str = handles[r];
+    TORCH_CHECK(str.size() == sizeof(cudaIpcMemHandle_t), "bad handle size");
+    cudaIpcMemHandle_t ih;
+    memcpy(&ih, str.data(), sizeof(ih));
+    void* p = nullptr;
+    SCIRS_CHECK_CUDA(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess));
+    h.base[r] = reinterpret_cast<char*>(p);
+    h.opened.push_back(reinterpret_cast<char*>(p));
+  }
+}
+
+// The local allocation as a uint8 tensor (views of it are placed by offset).
+torch::Tensor sym_tensor(int64_t id) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_syms.find(id);
+  TORCH_CHECK(it != g_syms.end(), "unknown symmetric heap");
+  SymHeap& h = it->second;
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, h.device);
+  return torch::from_blob(h.local, {h.bytes}, [](void*) {}, opts);
+}
+
+std::vector<int64_t> sym_ptrs(int64_t id) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_syms.find(id);
+  TORCH_CHECK(it != g_syms.end(), "unknown symmetric heap");
+  std::vector<int64_t> v;
+  for (int r = 0; r < it->second.world; ++r) v.push_back(reinterpret_cast<int64_t>(it->second.base[r]));
+  return v;
+}
+
+void sym_destroy(int64_t id) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_syms.find(id);
+  if (it == g_syms.end()) return;
+  SymHeap& h = it->second;
+  c10::cuda::CUDAGuard guard(h.device);
+  cudaDeviceSynchronize();
+  for (char* p : h.opened) cudaIpcCloseMemHandle(p);
+  cudaFree(h.local);
+  g_syms.erase(it);
+}
+
 // Runs a bounded wait on a flag that is never set; returns the status word
 // the kernel left behind. Used by the failure-detection tests.
 std::vector<int64_t> comm_timeout_probe(int64_t device, double timeout_s) {

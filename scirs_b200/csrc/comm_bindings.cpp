@@ -11,6 +11,11 @@ void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, do
                          double timeout_s);
 void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t blocks, double timeout_s);
 std::vector<int64_t> comm_timeout_probe(int64_t device, double timeout_s);
+std::tuple<int64_t, py::bytes> sym_create(int64_t device, int64_t rank, int64_t world, int64_t bytes);
+void sym_open(int64_t id, std::vector<py::bytes> handles);
+torch::Tensor sym_tensor(int64_t id);
+std::vector<int64_t> sym_ptrs(int64_t id);
+void sym_destroy(int64_t id);
 }  // namespace scirs
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -23,5 +28,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_scatter", &scirs::comm_reduce_scatter);
   m.def("allgather", &scirs::comm_allgather);
   m.def("timeout_probe", &scirs::comm_timeout_probe);
+  m.def("sym_create", &scirs::sym_create);
+  m.def("sym_open", &scirs::sym_open);
+  m.def("sym_tensor", &scirs::sym_tensor);
+  m.def("sym_ptrs", &scirs::sym_ptrs);
+  m.def("sym_destroy", &scirs::sym_destroy);
   m.def("status_read_and_clear", &scirs::status_read_and_clear);
 }

@@ -696,7 +696,8 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   const int64_t Kb = b_mn ? b.size(0) * (bp ? world : 1) : b.size(1);
   const int64_t N = b_mn ? b.size(1) : b.size(0);
   TORCH_CHECK(K == Kb, "gemm K mismatch: ", K, " vs ", Kb);
-  TORCH_CHECK(N % 8 == 0 && K % BK == 0 && M % BM == 0, "tensor-parallel gemm needs M % 128, K % 64, N % 8 == 0");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "tensor-parallel gemm needs K and N multiples of 8");
+  TORCH_CHECK(!((ap && !a_mn) || rs) || M % (BM * world) == 0, "row-split operands need M % (128*world) == 0");
   if (ap) TORCH_CHECK(a_mn ? (a.size(0) % BK == 0) : (a.size(0) % BM == 0), "segment not tile aligned");
   if (bp) TORCH_CHECK(b.size(0) % BK == 0, "B segment not tile aligned");
   const int dev = a.get_device();
@@ -706,8 +707,8 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
-  args.num_kb = (int)(K / BK);
-  args.m_blocks = (int)(M / BM);
+  args.num_kb = (int)((K + BK - 1) / BK);
+  args.m_blocks = (int)((M + BM - 1) / BM);
   args.st = status_ptr(dev);
   args.group_m = 16;
   args.rank = (int)rank;
@@ -750,8 +751,11 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
   } else {
     TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "out must be [M, N]");
-    if (epi == EPI_F32) CHECK_DTYPE(out, at::kFloat);
-    else CHECK_DTYPE(out, at::kBFloat16);
+    if (epi == EPI_F32) {
+      CHECK_DTYPE(out, at::kFloat);
+    } else {
+      CHECK_DTYPE(out, at::kBFloat16);
+    }
     args.C = out.data_ptr();
     args.ldc = out.stride(0);
     if (epi == EPI_F32)

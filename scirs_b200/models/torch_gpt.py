@@ -21,8 +21,9 @@ from .gpt import GPTConfig
 class TorchBlock(nn.Module):
     """Pre-LN transformer block (GPT-2 parameter names)."""
 
-    def __init__(self, D: int, H: int, Fd: int, eps: float, causal: bool = True):
+    def __init__(self, D: int, H: int, Fd: int, eps: float, causal: bool = True, rope=None):
         super().__init__()
+        self.rope = rope  # (cos, sin) tables [S, hd/2] or None
         self.ln_1 = nn.LayerNorm(D, eps=eps)
         self.attn = nn.Module()
         self.attn.c_attn = nn.Linear(D, 3 * D)
@@ -39,6 +40,8 @@ class TorchBlock(nn.Module):
         h = self.ln_1(x)
         qkv = self.attn.c_attn(h).view(B, S, 3, self.H, D // self.H)
         q, k, v = qkv.unbind(2)
+        if self.rope is not None:
+            q, k = _rotate(q, *self.rope), _rotate(k, *self.rope)
         a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                            is_causal=self.causal)
         x = x + self.attn.c_proj(a.transpose(1, 2).reshape(B, S, D))
@@ -109,3 +112,57 @@ def _from_torch_name(n: str) -> str:
     if n.startswith("h."):
         return "h" + n[2:]
     return n
+
+
+def _rotate(x, cos, sin):
+    """Half-rotation rotary embedding of x [B, S, H, hd] with tables [S, hd/2]."""
+    S, half = x.shape[1], x.shape[-1] // 2
+    c = cos[:S].view(1, S, 1, half).to(x.dtype)
+    s = sin[:S].view(1, S, 1, half).to(x.dtype)
+    x1, x2 = x[..., :half], x[..., half:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+class TorchDecoder(nn.Module):
+    """Plain-PyTorch rotary-position decoder with an untied LM head: oracle for
+    the tensor-parallel engine (same full-size parameter names) and the
+    cuBLAS + NCCL baseline of the 1.3B configuration."""
+
+    def __init__(self, cfg, seq: int | None = None):
+        super().__init__()
+        from .tp_gpt import rope_tables
+
+        self.cfg = cfg
+        S = seq or cfg.max_position_embeddings
+        cos, sin = rope_tables(S, cfg.head_dim, cfg.rope_theta, "cpu")
+        self.register_buffer("cos", cos, persistent=False)
+        self.register_buffer("sin", sin, persistent=False)
+        self.wte = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+        self.h = nn.ModuleList([TorchBlock(cfg.hidden_size, cfg.num_attention_heads, cfg.intermediate_size,
+                                           cfg.layer_norm_eps, True) for _ in range(cfg.num_hidden_layers)])
+        self.ln_f = nn.LayerNorm(cfg.hidden_size, eps=cfg.layer_norm_eps)
+        self.lm_head = nn.Linear(cfg.hidden_size, cfg.vocab_size, bias=False)
+        with torch.no_grad():
+            for n, p in self.named_parameters():
+                if p.dim() == 2:
+                    p.normal_(0.0, cfg.initializer_range)
+
+    def forward(self, tokens, targets=None):
+        x = self.wte(tokens)
+        for blk in self.h:
+            blk.rope = (self.cos, self.sin)
+            x = blk(x)
+        logits = self.lm_head(self.ln_f(x))
+        if targets is None:
+            return logits
+        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
+
+    @torch.no_grad()
+    def load_full(self, named):
+        """Load (name, tensor) pairs named like TPDecoder.full_init."""
+        own = dict(self.named_parameters())
+        for k, v in named:
+            own["wte.weight" if k == "wte" else _to_torch_name(k)].copy_(v)
+
+    def full_grads(self) -> dict:
+        return {("wte" if n == "wte.weight" else _from_torch_name(n)): p.grad for n, p in self.named_parameters()}

@@ -1,0 +1,165 @@
+"""Tensor parallelism (Megatron-style, sequence-parallel) on fused
+communication + GEMM kernels.
+
+Activations between the column- and row-parallel layers are split over the
+ranks by tokens (rank r holds rows [r*Mr, (r+1)*Mr) of the M = world*Mr
+tokens). The four communication points of a block become:
+
+  all-gather -> GEMM  (QKV, FC1 forward; proj/FC2 data gradients):
+      the producer writes its rows into the symmetric heap and signals; the
+      GEMM's TMA producer reads every rank's rows straight from the peers'
+      heaps (plain TMA loads, no multicast), starting with its own rows, and
+      waits (bounded) on a peer's flag only before its first tile from that
+      peer -- the transfer overlaps the MMAs tile by tile.
+  GEMM -> reduce-scatter  (proj, FC2 forward; QKV/FC1 data gradients):
+      the epilogue pushes each output row's bf16 partial sums into the
+      owner's receive slot over NVLink as soon as the tile is done; the last
+      CTA signals; the owner sums the world slots (+ bias + residual) in one
+      pass.
+  weight gradients of both kinds read the token-split operand's K blocks
+      from the peers in the same way.
+
+Mode "nccl" runs the same schedule with torch.distributed all_gather /
+reduce_scatter and separate GEMMs: the unfused baseline.
+
+Reference parity: scirs2-neural/src/training/tensor_parallel.rs:85-385
+(ColumnParallelLinear / RowParallelLinear / vocabulary-partitioned layers as
+single-process slices).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import _ext
+from ..ops import kernels as K
+from .symmetric import SymmetricHeap
+
+
+class TPContext:
+    def __init__(self, heap_bytes: int, mode: str = "fused", timeout_s: float = 10.0, group=None):
+        assert mode in ("fused", "nccl")
+        self.mode = mode
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.timeout_s = float(timeout_s)
+        self.heap = SymmetricHeap(heap_bytes, group=group) if mode == "fused" else None
+        if self.heap is not None:
+            self.flags = self.heap.alloc((8,), torch.int32, align=256)
+            self.sig = [a + 4 * self.rank for a in self.heap.peer_addrs(self.flags)]
+        else:
+            self.flags, self.sig = None, []
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.idx = 0
+        self._recv = None
+        self._recv_i = 0
+        self.launches = 0
+
+    # ------------------------------------------------------------- buffers
+    def alloc(self, shape, dtype=torch.bfloat16) -> torch.Tensor:
+        """A buffer peers can read (heap in fused mode, plain otherwise)."""
+        if self.heap is not None:
+            return self.heap.alloc(shape, dtype)
+        return torch.empty(*shape, dtype=dtype, device=self.device)
+
+    def recv_buffers(self, rows: int, D: int):
+        """Two alternating receive buffers [world, rows, D] for GEMM->RS. A
+        rank reuses a buffer only two reductions later, after every peer has
+        consumed the one in between, so two suffice."""
+        if self._recv is None:
+            if self.heap is not None:
+                self._recv = [self.heap.alloc((self.world, rows, D)) for _ in range(2)]
+            else:
+                self._recv = [torch.empty(self.world, rows, D, dtype=torch.bfloat16, device=self.device)
+                              for _ in range(2)]
+        assert self._recv[0].shape[1] == rows and self._recv[0].shape[2] == D, "one receive shape per context"
+        r = self._recv[self._recv_i]
+        self._recv_i ^= 1
+        return r
+
+    # ------------------------------------------------------------- signals
+    def begin_step(self):
+        _ext.kernels().tp_step_begin(self.epoch)
+        self.idx = 0
+        self._recv_i = 0
+
+    def _next(self) -> int:
+        self.idx += 1
+        return self.idx
+
+    def publish(self) -> int:
+        """Signal that everything this rank wrote so far (on this stream) is
+        visible to the peers. Returns the signal id consumers wait on."""
+        if self.mode != "fused":
+            return 0
+        i = self._next()
+        _ext.kernels().tp_signal(self.sig, self.epoch, i)
+        self.launches += 1
+        return i
+
+    # ------------------------------------------------------------- GEMMs
+    def ag_gemm(self, a_local, ready: int, b, out, *, b_mn=False, epi=K.EPI_BF16, bias=None, aux=None, out2=None,
+                gathered=None):
+        """out[M, N] = gather_rows(a_local over ranks) @ op(b) (A K-major).
+        `ready` is the signal id after which every rank's a_local is valid.
+        In nccl mode `gathered` ([M, K]) receives the all-gathered A."""
+        if self.mode == "fused":
+            _ext.kernels().gemm_tp(a_local, b, out, 0, int(b_mn), int(epi), bias, aux, out2, False, 0, self.rank,
+                                   self.world, self.heap.peer_addrs(a_local), [], [], self.flags, self.epoch,
+                                   ready, [], 0, self.timeout_s)
+        else:
+            dist.all_gather_into_tensor(gathered, a_local, group=self.group)
+            K.gemm(gathered, b, out, b_mn=b_mn, epi=epi, bias=bias, aux=aux, out2=out2)
+        self.launches += 1
+        return out
+
+    def gemm_rs(self, a, b, rows: int, *, b_mn=False, partial=None):
+        """Partial products a @ op(b) of all M rows, reduce-scattered by rows:
+        returns (recv buffer, signal id) for :meth:`reduce`. In nccl mode
+        `partial` ([M, N] bf16) is the local product buffer."""
+        N = b.shape[1] if b_mn else b.shape[0]
+        recv = self.recv_buffers(rows, N)
+        if self.mode == "fused":
+            i = self._next()
+            _ext.kernels().gemm_tp(a, b, recv, 0, int(b_mn), K.EPI_BF16, None, None, None, False, 0, self.rank,
+                                   self.world, [], [], self.heap.peer_addrs(recv[self.rank]), None, self.epoch, 0,
+                                   self.sig, i, self.timeout_s)
+            self.launches += 1
+            return recv, i
+        K.gemm(a, b, partial, b_mn=b_mn)
+        dist.reduce_scatter_tensor(recv[0], partial, group=self.group)
+        return recv, 0
+
+    def reduce(self, recv, sig: int, out, bias=None, resid=None):
+        """out = resid + bias + sum of the receive slots."""
+        if self.mode == "fused":
+            _ext.kernels().tp_reduce(recv, out, bias, resid, self.rank, self.flags, self.epoch, sig, [], 0,
+                                     self.timeout_s)
+        else:
+            _ext.kernels().tp_reduce(recv[:1], out, bias, resid, 0, None, self.epoch, 0, [], 0, self.timeout_s)
+        self.launches += 1
+        return out
+
+    def wgrad(self, a, b, out, *, a_peer: bool, b_peer: bool, a_full=None, b_full=None):
+        """out[M', N] += A^T B over all tokens (both operands MN-major, token
+        dimension = K). The operand flagged *_peer is token-split over the
+        ranks (its rows on rank r are tokens [r*Mr, (r+1)*Mr)); its data was
+        published earlier in the step and already waited for by an AG-GEMM,
+        so no wait is needed here."""
+        if self.mode == "fused":
+            _ext.kernels().gemm_tp(a, b, out, 1, 1, K.EPI_F32, None, None, None, True, 0, self.rank, self.world,
+                                   self.heap.peer_addrs(a) if a_peer else [],
+                                   self.heap.peer_addrs(b) if b_peer else [], [], None, None, 0, [], 0,
+                                   self.timeout_s)
+        else:
+            K.gemm(a_full if a_peer else a, b_full if b_peer else b, out, a_mn=True, b_mn=True, epi=K.EPI_F32,
+                   accumulate=True)
+        self.launches += 1
+        return out
+
+    def close(self):
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None

@@ -47,6 +47,8 @@ ext_modules = [
                 "attention.cu",
                 "attention_sm100.cu",
                 "vision.cu",
+                "tp.cu",
+                "attention_fwd_sm100.cu",
             ]
         ),
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},

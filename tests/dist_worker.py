@@ -147,10 +147,52 @@ def case_zero_vit():
     return res
 
 
+def case_tp_decoder():
+    """Tensor-parallel decoder (fused AG->GEMM / GEMM->RS, and the NCCL
+    baseline schedule) == the same model on one GPU (TP=1)."""
+    from scirs_b200.models.tp_gpt import DecoderConfig, TPDecoder
+    from scirs_b200.parallel.tensor_parallel import TPContext
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = DecoderConfig.tiny(vocab=1024, seq=256)
+    B, S = 4, 256
+    g = torch.Generator().manual_seed(21)
+    toks = [torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g) for _ in range(4)]
+    hp = dict(lr=1e-3, weight_decay=0.0, max_grad_norm=1.0)
+
+    def run(ctx, graph_from=2):
+        m = TPDecoder(cfg, ctx, batch=B, seq=S, seed=3)
+        m.configure_adamw(**hp)
+        out = []
+        for i, t in enumerate(toks):
+            if i == graph_from:
+                m.enable_cuda_graph()
+            t = t.to(dev)
+            out.append(float(m.train_step(t[:, :-1].contiguous(), t[:, 1:].contiguous())))
+        torch.cuda.synchronize()
+        m.close()
+        return out
+
+    res = {}
+    for mode in ("fused", "nccl"):
+        ctx = TPContext(TPDecoder.heap_bytes(cfg, B, S, world), mode=mode, timeout_s=10.0)
+        res[mode] = {"losses": run(ctx)}
+        ctx.close()
+    sub = dist.new_group([0])
+    if rank == 0:
+        ctx = TPContext(TPDecoder.heap_bytes(cfg, B, S, 1), mode="fused", group=sub)
+        res["single"] = {"losses": run(ctx, graph_from=99)}
+        ctx.close()
+    _ext.check_status()
+    return res
+
+
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
-    res = {"collectives": case_collectives, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit}[case]()
+    res = {"collectives": case_collectives, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
+           "tp_decoder": case_tp_decoder}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))
     dist.barrier()

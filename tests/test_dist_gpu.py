@@ -57,3 +57,11 @@ def test_zero_vit_2gpu(tmp_path):
     for mode in ("fused", "nccl"):
         for a, b in zip(res[mode]["losses"], ref):
             assert abs(a - b) < 3e-2, (mode, res[mode]["losses"], ref)
+
+
+def test_tensor_parallel_decoder_2gpu(tmp_path):
+    res = _run("tp_decoder", tmp_path, port=29614)
+    ref = res["single"]["losses"]
+    for mode in ("fused", "nccl"):
+        for a, b in zip(res[mode]["losses"], ref):
+            assert abs(a - b) < 3e-2, (mode, res[mode]["losses"], ref)
