@@ -17,7 +17,7 @@ rows, AdamW over a 32M-element flat buffer. Each op's working set is
 larger than the 126 MB L2.
 
 Without a profiler it prints one line per op with the CUDA-event time of the
-last round, the achieved TFLOP/s or GB/s, and the fraction of the measured
+last round (averaged over --iters back-to-back launches), the achieved TFLOP/s or GB/s, and the fraction of the measured
 peaks (MEASURED_PEAKS.json at the repository root, if present).
 """
 from __future__ import annotations
@@ -60,6 +60,7 @@ def build(dev):
     t["qkv"] = r(M, 3 * D)
     t["att"] = torch.empty(M, D, device=dev, dtype=bf)
     t["lse"] = torch.empty(B, H, S, device=dev, dtype=f32)
+    t["lse128"] = torch.empty(B, H // 2, S, device=dev, dtype=f32)
     t["datt"] = r(M, D)
     t["dqkv"] = torch.empty(M, 3 * D, device=dev, dtype=bf)
     t["dq_acc"] = torch.empty(M * D, device=dev, dtype=f32)
@@ -112,6 +113,21 @@ def op_attn_fwd(t):
     K.flash_attn_fwd(q, k, v, t["att"].view(B, S, H, HD), t["lse"], causal=True)
 
 
+def op_attn_fwd_pp(t):
+    q, k, v = _attn_views(t)
+    K.flash_attn_fwd_impl("pingpong", q, k, v, t["att"].view(B, S, H, HD), t["lse"], causal=True)
+
+
+def op_attn_fwd_hd128(t):
+    q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
+    K.flash_attn_fwd_impl("tcgen05", q, k, v, t["att"].view(B, S, H // 2, 2 * HD), t["lse128"], causal=True)
+
+
+def op_attn_fwd_pp_hd128(t):
+    q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
+    K.flash_attn_fwd_impl("pingpong", q, k, v, t["att"].view(B, S, H // 2, 2 * HD), t["lse128"], causal=True)
+
+
 def op_attn_bwd(t):
     q, k, v = _attn_views(t)
     dq, dk, dv = t["dqkv"].view(B, S, 3, H, HD).unbind(2)
@@ -143,6 +159,9 @@ OPS = {
     "gemm_wgrad": (op_gemm_wgrad, 2 * M * D * F, (M * D + M * F) * 2 + 2 * D * F * 4),
     "gemm_dgelu": (op_gemm_dgelu, 2 * M * D * F, (M * D + F * D + 2 * M * F) * 2),
     "attn_fwd": (op_attn_fwd, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
+    "attn_fwd_pp": (op_attn_fwd_pp, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
+    "attn_fwd_hd128": (op_attn_fwd_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
+    "attn_fwd_pp_hd128": (op_attn_fwd_pp_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_bwd": (op_attn_bwd, 10 * B * H * S * S * HD // 2, (8 * M * D) * 2),
     "ln_fwd": (op_ln_fwd, 0, 2 * M * D * 2),
     "ln_bwd": (op_ln_bwd, 0, 4 * M * D * 2),
@@ -154,6 +173,7 @@ OPS = {
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--rounds", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=1, help="back-to-back launches timed per op per round")
     ap.add_argument("--ops", default=",".join(OPS))
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
@@ -168,10 +188,11 @@ def main():
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             e0.record()
-            OPS[n][0](t)
+            for _ in range(args.iters):
+                OPS[n][0](t)
             e1.record()
             torch.cuda.synchronize()
-            ms[n] = e0.elapsed_time(e1)
+            ms[n] = e0.elapsed_time(e1) / args.iters
     _ext.check_status(0)
     for n in names:
         _, fl, by = OPS[n]

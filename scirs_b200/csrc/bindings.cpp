@@ -40,6 +40,11 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
              c10::optional<torch::Tensor> epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
              double timeout_s);
 void tp_signal(std::vector<int64_t> sig_flags, torch::Tensor epoch, int64_t idx);
+void paged_kv_append(torch::Tensor k_new, torch::Tensor v_new, torch::Tensor k_pool, torch::Tensor v_pool,
+                     torch::Tensor block_tables, torch::Tensor seq, torch::Tensor pos);
+void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor block_tables,
+                            torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
+                            int64_t tokens_per_split, double scale);
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale);
 void tp_step_begin(torch::Tensor epoch);
@@ -83,6 +88,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("wait_idx") = 0, py::arg("sig_flags") = std::vector<int64_t>{}, py::arg("sig_idx") = 0,
         py::arg("timeout_s") = 10.0);
   m.def("tp_signal", &scirs::tp_signal);
+  m.def("paged_kv_append", &scirs::paged_kv_append);
+  m.def("paged_attention_decode", &scirs::paged_attention_decode);
   m.def("flash_attn_fwd_pp", &scirs::flash_attn_fwd_pp);
   m.def("tp_step_begin", &scirs::tp_step_begin);
   m.def("tp_reduce", &scirs::tp_reduce);

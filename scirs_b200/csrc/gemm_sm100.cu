@@ -714,11 +714,14 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   args.rank = (int)rank;
   args.world = (int)world;
   args.timeout_ns = (long long)(timeout_s * 1e9);
+  if (epoch.has_value() && epoch->defined()) {
+    TORCH_CHECK(epoch->element_size() == 4 && epoch->is_cuda(), "epoch: 32-bit device scalar");
+    args.epoch_ptr = reinterpret_cast<const unsigned*>(epoch->data_ptr());
+  }
   if (flags.has_value() && flags->defined()) {
     TORCH_CHECK(flags->numel() >= world && flags->element_size() == 4, "flags: 32-bit [world]");
-    TORCH_CHECK(epoch.has_value() && epoch->defined() && epoch->element_size() == 4, "epoch: 32-bit device scalar");
+    TORCH_CHECK(args.epoch_ptr != nullptr, "waiting on flags needs the epoch counter");
     args.wait_flags = reinterpret_cast<const unsigned*>(flags->data_ptr());
-    args.epoch_ptr = reinterpret_cast<const unsigned*>(epoch->data_ptr());
     args.wait_idx = (unsigned)wait_idx;
   }
   if (!sig_flags.empty()) {

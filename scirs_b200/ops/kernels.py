@@ -279,6 +279,16 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
     return out
 
 
+def flash_attn_fwd_impl(impl, q, k, v, out, lse, causal=True, scale=None):
+    """flash_attn_fwd with an explicit implementation ("pingpong", "tcgen05", "mma")."""
+    global ATTN_FWD_IMPL
+    old, ATTN_FWD_IMPL = ATTN_FWD_IMPL, impl
+    try:
+        return flash_attn_fwd(q, k, v, out, lse, causal, scale)
+    finally:
+        ATTN_FWD_IMPL = old
+
+
 def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=True, scale=None):
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
