@@ -51,6 +51,17 @@ def comm():
     return _COMM
 
 
+def data():
+    """The `_data` module (native host batch prefetcher)."""
+    mod = _load("_data")
+    if mod is None:
+        raise RuntimeError(
+            "scirs_b200._data is not built; run `python setup.py build_ext --inplace` "
+            f"(import error: {_ERR.get('_data')})"
+        )
+    return mod
+
+
 def available() -> bool:
     try:
         kernels()

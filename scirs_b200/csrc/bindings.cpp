@@ -47,7 +47,7 @@ void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                             int64_t tokens_per_split, double scale);
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale);
-void tp_step_begin(torch::Tensor epoch);
+void tp_step_begin(torch::Tensor epoch, c10::optional<torch::Tensor> vals);
 void tp_reduce(torch::Tensor recv, torch::Tensor out, c10::optional<torch::Tensor> bias,
                c10::optional<torch::Tensor> resid, int64_t rank, c10::optional<torch::Tensor> flags,
                torch::Tensor epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
@@ -91,7 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_kv_append", &scirs::paged_kv_append);
   m.def("paged_attention_decode", &scirs::paged_attention_decode);
   m.def("flash_attn_fwd_pp", &scirs::flash_attn_fwd_pp);
-  m.def("tp_step_begin", &scirs::tp_step_begin);
+  m.def("tp_step_begin", &scirs::tp_step_begin, py::arg("epoch"), py::arg("vals") = py::none());
   m.def("tp_reduce", &scirs::tp_reduce);
   m.def("rope_apply", &scirs::rope_apply);
   m.def("tp_xent_stats", &scirs::tp_xent_stats);

@@ -702,6 +702,21 @@ void sym_destroy(int64_t id) {
   g_syms.erase(it);
 }
 
+// Copy `nbytes` from local device memory to each destination (peer
+// addresses from a symmetric heap; entries equal to `src` are skipped) with
+// the copy engines, in order on the current stream. A later copy on the same
+// stream (e.g. of a flag word) lands only after these completed, so it can
+// announce the data to the peer without using any SM.
+void peer_copy(std::vector<int64_t> dsts, int64_t src, int64_t nbytes) {
+  TORCH_CHECK(nbytes >= 0, "negative size");
+  cudaStream_t st = cur_stream();
+  for (int64_t d : dsts) {
+    if (d == src || nbytes == 0) continue;
+    SCIRS_CHECK_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(d), reinterpret_cast<const void*>(src), (size_t)nbytes,
+                                     cudaMemcpyDeviceToDevice, st));
+  }
+}
+
 // Runs a bounded wait on a flag that is never set; returns the status word
 // the kernel left behind. Used by the failure-detection tests.
 std::vector<int64_t> comm_timeout_probe(int64_t device, double timeout_s) {

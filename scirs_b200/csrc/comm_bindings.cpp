@@ -16,6 +16,7 @@ void sym_open(int64_t id, std::vector<py::bytes> handles);
 torch::Tensor sym_tensor(int64_t id);
 std::vector<int64_t> sym_ptrs(int64_t id);
 void sym_destroy(int64_t id);
+void peer_copy(std::vector<int64_t> dsts, int64_t src, int64_t nbytes);
 }  // namespace scirs
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -33,5 +34,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sym_tensor", &scirs::sym_tensor);
   m.def("sym_ptrs", &scirs::sym_ptrs);
   m.def("sym_destroy", &scirs::sym_destroy);
+  m.def("peer_copy", &scirs::peer_copy);
   m.def("status_read_and_clear", &scirs::status_read_and_clear);
 }

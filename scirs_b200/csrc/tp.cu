@@ -83,8 +83,14 @@ __global__ void signal_kernel(FlagPtrs sig, int world, const unsigned* epoch, un
   }
 }
 
-__global__ void step_begin_kernel(unsigned* epoch) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) *epoch = *epoch + 1u;
+// Advance the step epoch and (optionally) lay out this step's flag values
+// vals[i] = epoch * 4096 + i, the words the copy engines write into peers'
+// flag arrays to announce data they pushed.
+__global__ void step_begin_kernel(unsigned* epoch, unsigned* vals, int n) {
+  const unsigned e = *epoch + 1u;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) vals[i] = e * kSigStride + (unsigned)i;
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch = e;
 }
 
 // out[row] = resid[row] + bias + sum_r recv[r][row]   (fixed rank order)
@@ -253,9 +259,17 @@ void tp_signal(std::vector<int64_t> sig_flags, torch::Tensor epoch, int64_t idx)
   SCIRS_CHECK_LAUNCH();
 }
 
-void tp_step_begin(torch::Tensor epoch) {
+void tp_step_begin(torch::Tensor epoch, c10::optional<torch::Tensor> vals) {
   c10::cuda::CUDAGuard guard(epoch.get_device());
-  tp::step_begin_kernel<<<1, 32, 0, cur_stream()>>>(reinterpret_cast<unsigned*>(epoch.data_ptr()));
+  unsigned* vp = nullptr;
+  int n = 0;
+  if (vals.has_value() && vals->defined()) {
+    TORCH_CHECK(vals->element_size() == 4 && vals->is_contiguous() && vals->numel() <= (long)tp::kSigStride,
+                "vals: contiguous 32-bit, at most 4096 entries");
+    vp = reinterpret_cast<unsigned*>(vals->data_ptr());
+    n = (int)vals->numel();
+  }
+  tp::step_begin_kernel<<<1, 256, 0, cur_stream()>>>(reinterpret_cast<unsigned*>(epoch.data_ptr()), vp, n);
   SCIRS_CHECK_LAUNCH();
 }
 

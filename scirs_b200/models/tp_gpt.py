@@ -16,7 +16,7 @@ The residual stream is split by tokens: rank r holds tokens
 [r*M/w, (r+1)*M/w) of the M = batch*seq tokens of the step, so LayerNorms,
 residual adds and the embedding touch only local rows. Every block:
 
-  x_l --LN1--> ln1 (heap) ==AG-GEMM==> qkv [M, 3D/w] -> RoPE -> attention over
+  x_l --LN1--> ln1 (own rows of a gathered heap buffer) ==AG-GEMM==> qkv [M, 3D/w] -> RoPE -> attention over
   this rank's heads -> att [M, D/w] ==GEMM-RS==> + c_proj.bias + x_l = xm
   --LN2--> ln2 (heap) ==AG-GEMM(+bias, GELU)==> g [M, F/w] ==GEMM-RS==>
   + mlp.c_proj.bias + xm = x_{l+1}
@@ -25,8 +25,8 @@ then LN_f -> AG-GEMM with this rank's vocabulary slice -> vocabulary-
 parallel softmax cross-entropy (row statistics exchanged through the heap).
 The backward mirrors it (data gradients of row-parallel layers are AG-GEMMs
 of the token-split residual gradient, those of column-parallel layers are
-GEMM-RS; weight gradients read the token-split operand's K blocks from the
-peers). The input embedding is replicated rather than vocabulary-split: it
+GEMM-RS; weight gradients read the gathered full-size operands locally).
+The input embedding is replicated rather than vocabulary-split: it
 costs 131 MB per GPU at this size and saves a reduce-scatter of [M, D] per
 step.
 
@@ -206,8 +206,9 @@ class TPDecoder(FusedTrainerMixin):
         """Symmetric-heap bytes the model allocates from its TPContext."""
         M = batch * seq
         Mr, D, L = M // world, cfg.hidden_size, cfg.num_hidden_layers
-        act = (4 * L + 1) * Mr * D * 2 + world * M * 16 + 2 * world * Mr * D * 2
-        return act + 1024 * (4 * L + 16)
+        gathered = (2 * L + 1 + 4) * M * D * 2  # ln1 / ln2 per layer, ln_f, 2 x (dY, dYm)
+        act = gathered + world * M * 16 + 2 * world * Mr * D * 2
+        return act + 1024 * (2 * L + 16)
 
     # ------------------------------------------------------------ buffers
     def _alloc(self):
@@ -216,12 +217,16 @@ class TPDecoder(FusedTrainerMixin):
         Dl, Fl, Vl, Hl, S, B = self.Dl, self.Fl, self.Vl, self.Hl, self.S, self.B
         bf, f32, dev = torch.bfloat16, torch.float32, self.device
         e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
-        # peer-readable (symmetric heap in fused mode)
-        self.ln1 = [ctx.alloc((Mr, D)) for _ in range(L)]
-        self.ln2 = [ctx.alloc((Mr, D)) for _ in range(L)]
-        self.lnf = ctx.alloc((Mr, D))
-        self.dY = [ctx.alloc((Mr, D)) for _ in range(L)]  # d loss / d x_{l+1}
-        self.dYm = [ctx.alloc((Mr, D)) for _ in range(L)]  # d loss / d xm_l
+        # full-size gathered buffers (symmetric heap in fused mode); this rank
+        # writes its own rows, the gather fills in the peers' rows
+        self.gln1 = [ctx.alloc((M, D)) for _ in range(L)]
+        self.gln2 = [ctx.alloc((M, D)) for _ in range(L)]
+        self.glnf = ctx.alloc((M, D))
+        self.gdY = [ctx.alloc((M, D)) for _ in range(2)]   # d loss / d x_{l+1}, slot l % 2
+        self.gdYm = [ctx.alloc((M, D)) for _ in range(2)]  # d loss / d xm_l, slot l % 2
+        self.ln1 = [ctx.segment(t) for t in self.gln1]
+        self.ln2 = [ctx.segment(t) for t in self.gln2]
+        self.lnf = ctx.segment(self.glnf)
         self.stats = ctx.alloc((self.world, M, 4), torch.float32)
         ctx.recv_buffers(Mr, D)
         # local
@@ -246,17 +251,11 @@ class TPDecoder(FusedTrainerMixin):
         self.delta = e(B * Hl * S, dt=f32)
         self.ln_part = K.ln_partials(Mr, D, dev)
         if ctx.mode == "nccl":
-            # the unfused baseline keeps the gathered operands and full partials
-            self.g_ln1 = [e(M, D) for _ in range(L)]
-            self.g_ln2 = [e(M, D) for _ in range(L)]
-            self.g_lnf = e(M, D)
-            self.g_dY = e(M, D)
-            self.g_dYm = e(M, D)
+            # the unfused baseline's full partial products before reduce-scatter
             self.partial = e(M, D)
             self.stats_local = e(M, 4, dt=f32)
         else:
-            self.g_ln1 = self.g_ln2 = [None] * L
-            self.g_lnf = self.g_dY = self.g_dYm = self.partial = None
+            self.partial = None
 
     # ------------------------------------------------------------ forward
     def _forward(self, tok_local):
@@ -269,9 +268,9 @@ class TPDecoder(FusedTrainerMixin):
             p = f"h{l}."
             K.layernorm_fwd(self.x[l], fp.w(p + "ln_1.weight"), fp.w(p + "ln_1.bias"), self.ln1[l], self.mu[0][l],
                             self.rs[0][l], eps)
-            s = ctx.publish()
-            ctx.ag_gemm(self.ln1[l], s, fp.w(p + "attn.c_attn.weight"), self.qkv[l],
-                        bias=fp.w(p + "attn.c_attn.bias"), gathered=self.g_ln1[l])
+            s = ctx.gather(self.gln1[l])
+            ctx.ag_gemm(self.gln1[l], s, fp.w(p + "attn.c_attn.weight"), self.qkv[l],
+                        bias=fp.w(p + "attn.c_attn.bias"))
             kx.rope_apply(self.qkv[l], self.cos, self.sin, S, Hl, hd, False)
             q, k, v = self.qkv[l].view(B, S, 3, Hl, hd).unbind(2)
             K.flash_attn_fwd(q, k, v, self.att[l].view(B, S, Hl, hd), self.lse[l], causal=True)
@@ -279,14 +278,14 @@ class TPDecoder(FusedTrainerMixin):
             ctx.reduce(recv, s, self.xm[l], bias=fp.w(p + "attn.c_proj.bias"), resid=self.x[l])
             K.layernorm_fwd(self.xm[l], fp.w(p + "ln_2.weight"), fp.w(p + "ln_2.bias"), self.ln2[l], self.mu[1][l],
                             self.rs[1][l], eps)
-            s = ctx.publish()
-            ctx.ag_gemm(self.ln2[l], s, fp.w(p + "mlp.c_fc.weight"), self.g[l], epi=K.EPI_BIAS_GELU,
-                        bias=fp.w(p + "mlp.c_fc.bias"), out2=self.h[l], gathered=self.g_ln2[l])
+            s = ctx.gather(self.gln2[l])
+            ctx.ag_gemm(self.gln2[l], s, fp.w(p + "mlp.c_fc.weight"), self.g[l], epi=K.EPI_BIAS_GELU,
+                        bias=fp.w(p + "mlp.c_fc.bias"), out2=self.h[l])
             recv, s = ctx.gemm_rs(self.g[l], fp.w(p + "mlp.c_proj.weight"), Mr, partial=self.partial)
             ctx.reduce(recv, s, self.x[l + 1], bias=fp.w(p + "mlp.c_proj.bias"), resid=self.xm[l])
         K.layernorm_fwd(self.x[L], fp.w("ln_f.weight"), fp.w("ln_f.bias"), self.lnf, self.muf, self.rsf, eps)
-        s = ctx.publish()
-        ctx.ag_gemm(self.lnf, s, fp.w("lm_head.weight"), self.logits, gathered=self.g_lnf)
+        s = ctx.gather(self.glnf)
+        ctx.ag_gemm(self.glnf, s, fp.w("lm_head.weight"), self.logits)
 
     def _xent(self, tgt_full):
         ctx, kx = self.ctx, _ext.kernels()
@@ -309,33 +308,33 @@ class TPDecoder(FusedTrainerMixin):
         L, S, B, Hl, hd, Mr = cfg.num_hidden_layers, self.S, self.B, self.Hl, cfg.head_dim, self.Mr
         dlog = self.logits  # d loss / d logits after the cross-entropy
         recv, s = ctx.gemm_rs(dlog, fp.w("lm_head.weight"), Mr, b_mn=True, partial=self.partial)
-        ctx.wgrad(dlog, self.lnf, fp.g("lm_head.weight"), a_peer=False, b_peer=True, b_full=self.g_lnf)
+        ctx.wgrad(dlog, self.glnf, fp.g("lm_head.weight"))
         ctx.reduce(recv, s, self.dln)
-        K.layernorm_bwd(self.dln, self.x[L], fp.w("ln_f.weight"), self.muf, self.rsf, self.dY[L - 1],
+        dY = lambda l: ctx.segment(self.gdY[l % 2])  # noqa: E731
+        dYm = lambda l: ctx.segment(self.gdYm[l % 2])  # noqa: E731
+        K.layernorm_bwd(self.dln, self.x[L], fp.w("ln_f.weight"), self.muf, self.rsf, dY(L - 1),
                         fp.g("ln_f.weight"), fp.g("ln_f.bias"), self.ln_part,
                         dsum=fp.g(f"h{L - 1}.mlp.c_proj.bias"))
         for l in reversed(range(L)):
             p = f"h{l}."
             # fc2 (row-parallel): dh = gather(dY) @ W2 * gelu'(h); dW2 = gather(dY)^T g
-            s = ctx.publish()
-            ctx.ag_gemm(self.dY[l], s, fp.w(p + "mlp.c_proj.weight"), self.dh, b_mn=True, epi=K.EPI_DGELU,
-                        aux=self.h[l], gathered=self.g_dY)
-            ctx.wgrad(self.dY[l], self.g[l], fp.g(p + "mlp.c_proj.weight"), a_peer=True, b_peer=False,
-                      a_full=self.g_dY)
+            gdy = self.gdY[l % 2]
+            s = ctx.gather(gdy)
+            ctx.ag_gemm(gdy, s, fp.w(p + "mlp.c_proj.weight"), self.dh, b_mn=True, epi=K.EPI_DGELU, aux=self.h[l])
+            ctx.wgrad(gdy, self.g[l], fp.g(p + "mlp.c_proj.weight"))
             K.bias_grad(self.dh, fp.g(p + "mlp.c_fc.bias"))
             # fc1 (column-parallel): d ln2 = RS(dh @ W1); dW1 = dh^T gather(ln2)
             recv, s = ctx.gemm_rs(self.dh, fp.w(p + "mlp.c_fc.weight"), Mr, b_mn=True, partial=self.partial)
-            ctx.wgrad(self.dh, self.ln2[l], fp.g(p + "mlp.c_fc.weight"), a_peer=False, b_peer=True,
-                      b_full=self.g_ln2[l])
+            ctx.wgrad(self.dh, self.gln2[l], fp.g(p + "mlp.c_fc.weight"))
             ctx.reduce(recv, s, self.dln)
-            K.layernorm_bwd(self.dln, self.xm[l], fp.w(p + "ln_2.weight"), self.mu[1][l], self.rs[1][l], self.dYm[l],
-                            fp.g(p + "ln_2.weight"), fp.g(p + "ln_2.bias"), self.ln_part, dresid=self.dY[l],
+            K.layernorm_bwd(self.dln, self.xm[l], fp.w(p + "ln_2.weight"), self.mu[1][l], self.rs[1][l], dYm(l),
+                            fp.g(p + "ln_2.weight"), fp.g(p + "ln_2.bias"), self.ln_part, dresid=dY(l),
                             dsum=fp.g(p + "attn.c_proj.bias"))
             # proj (row-parallel)
-            s = ctx.publish()
-            ctx.ag_gemm(self.dYm[l], s, fp.w(p + "attn.c_proj.weight"), self.datt, b_mn=True, gathered=self.g_dYm)
-            ctx.wgrad(self.dYm[l], self.att[l], fp.g(p + "attn.c_proj.weight"), a_peer=True, b_peer=False,
-                      a_full=self.g_dYm)
+            gdym = self.gdYm[l % 2]
+            s = ctx.gather(gdym)
+            ctx.ag_gemm(gdym, s, fp.w(p + "attn.c_proj.weight"), self.datt, b_mn=True)
+            ctx.wgrad(gdym, self.att[l], fp.g(p + "attn.c_proj.weight"))
             # attention over this rank's heads, then the inverse rotation of dq, dk
             q, k, v = self.qkv[l].view(B, S, 3, Hl, hd).unbind(2)
             dq, dk, dv = self.dqkv.view(B, S, 3, Hl, hd).unbind(2)
@@ -344,15 +343,15 @@ class TPDecoder(FusedTrainerMixin):
             _ext.kernels().rope_apply(self.dqkv, self.cos, self.sin, S, Hl, hd, True)
             # qkv (column-parallel)
             recv, s = ctx.gemm_rs(self.dqkv, fp.w(p + "attn.c_attn.weight"), Mr, b_mn=True, partial=self.partial)
-            ctx.wgrad(self.dqkv, self.ln1[l], fp.g(p + "attn.c_attn.weight"), a_peer=False, b_peer=True,
-                      b_full=self.g_ln1[l])
+            ctx.wgrad(self.dqkv, self.gln1[l], fp.g(p + "attn.c_attn.weight"))
             K.bias_grad(self.dqkv, fp.g(p + "attn.c_attn.bias"))
             ctx.reduce(recv, s, self.dln)
-            dst = self.dY[l - 1] if l > 0 else self.dx0
+            dst = dY(l - 1) if l > 0 else self.dx0
             K.layernorm_bwd(self.dln, self.x[l], fp.w(p + "ln_1.weight"), self.mu[0][l], self.rs[0][l], dst,
-                            fp.g(p + "ln_1.weight"), fp.g(p + "ln_1.bias"), self.ln_part, dresid=self.dYm[l],
+                            fp.g(p + "ln_1.weight"), fp.g(p + "ln_1.bias"), self.ln_part, dresid=dYm(l),
                             dsum=fp.g(f"h{l - 1}.mlp.c_proj.bias") if l > 0 else None)
         K.embedding_bwd(tok_local, self.dx0, fp.g("wte"), None, S)
+        ctx.finish()
 
     # ------------------------------------------------------------ API
     def forward_backward(self, tokens, targets):
@@ -371,6 +370,7 @@ class TPDecoder(FusedTrainerMixin):
         tok = tokens.reshape(-1)
         self._forward(tok[self.rank * self.Mr : (self.rank + 1) * self.Mr])
         self._xent(targets.reshape(-1))
+        self.ctx.finish()
         return self.losses.mean()
 
     def configure_adamw(self, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_grad_norm=1.0):

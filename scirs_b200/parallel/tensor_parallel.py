@@ -5,19 +5,22 @@ Activations between the column- and row-parallel layers are split over the
 ranks by tokens (rank r holds rows [r*Mr, (r+1)*Mr) of the M = world*Mr
 tokens). The four communication points of a block become:
 
-  all-gather -> GEMM  (QKV, FC1 forward; proj/FC2 data gradients):
-      the producer writes its rows into the symmetric heap and signals; the
-      GEMM's TMA producer reads every rank's rows straight from the peers'
-      heaps (plain TMA loads, no multicast), starting with its own rows, and
-      waits (bounded) on a peer's flag only before its first tile from that
-      peer -- the transfer overlaps the MMAs tile by tile.
+  all-gather -> GEMM  (QKV, FC1 forward; proj/FC2 data gradients): every
+      rank keeps a full-size gathered buffer in its symmetric heap. The
+      producer writes its rows into its own buffer, then the copy engines
+      push those rows into every peer's buffer at the same offset and, on
+      the same copy stream, write the step's flag value into each peer's
+      flag word (no SM involved, so a peer whose SMs are all busy in a GEMM
+      still receives data and flags). The GEMM reads only local memory: its
+      TMA producer starts with this rank's own rows and waits (bounded) on a
+      peer's flag only before its first tile of that peer's rows, so the
+      transfer overlaps the MMAs, and every row crosses NVLink exactly once.
   GEMM -> reduce-scatter  (proj, FC2 forward; QKV/FC1 data gradients):
       the epilogue pushes each output row's bf16 partial sums into the
       owner's receive slot over NVLink as soon as the tile is done; the last
       CTA signals; the owner sums the world slots (+ bias + residual) in one
       pass.
-  weight gradients of both kinds read the token-split operand's K blocks
-      from the peers in the same way.
+  weight gradients read the gathered buffers locally.
 
 Mode "nccl" runs the same schedule with torch.distributed all_gather /
 reduce_scatter and separate GEMMs: the unfused baseline.
@@ -47,11 +50,20 @@ class TPContext:
         self.timeout_s = float(timeout_s)
         self.heap = SymmetricHeap(heap_bytes, group=group) if mode == "fused" else None
         if self.heap is not None:
-            self.flags = self.heap.alloc((8,), torch.int32, align=256)
+            # Two flag arrays (one word per source rank): row 0 is written by
+            # the copy engines (gathers, in copy-stream order), row 1 by
+            # kernels (reduce-scatter / statistics, in main-stream order), so
+            # each word only ever increases.
+            fl = self.heap.alloc((2, 8), torch.int32, align=256)
+            self.flags_ce, self.flags = fl[0], fl[1]
+            self.sig_ce = [a + 4 * self.rank for a in self.heap.peer_addrs(self.flags_ce)]
             self.sig = [a + 4 * self.rank for a in self.heap.peer_addrs(self.flags)]
         else:
-            self.flags, self.sig = None, []
+            self.flags = self.flags_ce = None
+            self.sig, self.sig_ce = [], []
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.vals = torch.zeros(4096, dtype=torch.int32, device=self.device)  # this step's flag values
+        self.copy_stream = torch.cuda.Stream(self.device) if mode == "fused" else None
         self.idx = 0
         self._recv = None
         self._recv_i = 0
@@ -81,9 +93,40 @@ class TPContext:
 
     # ------------------------------------------------------------- signals
     def begin_step(self):
-        _ext.kernels().tp_step_begin(self.epoch)
+        _ext.kernels().tp_step_begin(self.epoch, self.vals)
         self.idx = 0
         self._recv_i = 0
+
+    def finish(self):
+        """Join the copy stream (before anything outside the step reads or
+        reuses buffers the copies touch)."""
+        if self.copy_stream is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.copy_stream)
+
+    def segment(self, full: torch.Tensor) -> torch.Tensor:
+        """This rank's rows of a gathered [M, ...] buffer."""
+        n = full.shape[0] // self.world
+        return full[self.rank * n : (self.rank + 1) * n]
+
+    def gather(self, full: torch.Tensor) -> int:
+        """All-gather the rows of `full` (this rank's segment is written):
+        fused -> copy-engine pushes + flag words, returns the signal id the
+        consumer waits on; nccl -> in-place all_gather, returns 0."""
+        seg = self.segment(full)
+        if self.mode != "fused":
+            if self.world > 1:
+                dist.all_gather_into_tensor(full, seg, group=self.group)
+            return 0
+        i = self._next()
+        if self.world > 1:
+            main = torch.cuda.current_stream(self.device)
+            self.copy_stream.wait_stream(main)
+            with torch.cuda.stream(self.copy_stream):
+                comm = _ext.comm()
+                comm.peer_copy(self.heap.peer_addrs(seg), seg.data_ptr(), seg.numel() * seg.element_size())
+                comm.peer_copy(self.sig_ce, self.vals.data_ptr() + 4 * i, 4)
+        self.launches += 1
+        return i
 
     def _next(self) -> int:
         self.idx += 1
@@ -100,18 +143,18 @@ class TPContext:
         return i
 
     # ------------------------------------------------------------- GEMMs
-    def ag_gemm(self, a_local, ready: int, b, out, *, b_mn=False, epi=K.EPI_BF16, bias=None, aux=None, out2=None,
-                gathered=None):
-        """out[M, N] = gather_rows(a_local over ranks) @ op(b) (A K-major).
-        `ready` is the signal id after which every rank's a_local is valid.
-        In nccl mode `gathered` ([M, K]) receives the all-gathered A."""
-        if self.mode == "fused":
-            _ext.kernels().gemm_tp(a_local, b, out, 0, int(b_mn), int(epi), bias, aux, out2, False, 0, self.rank,
-                                   self.world, self.heap.peer_addrs(a_local), [], [], self.flags, self.epoch,
-                                   ready, [], 0, self.timeout_s)
+    def ag_gemm(self, full, ready: int, b, out, *, b_mn=False, epi=K.EPI_BF16, bias=None, aux=None, out2=None):
+        """out[M, N] = full[M, K] @ op(b), where `full` is a gathered buffer
+        whose peer segments arrive after signal `ready` (see :meth:`gather`)."""
+        if self.mode == "fused" and self.world > 1:
+            seg = self.segment(full)
+            step = seg.numel() * seg.element_size()
+            addrs = [full.data_ptr() + r * step for r in range(self.world)]
+            _ext.kernels().gemm_tp(seg, b, out, 0, int(b_mn), int(epi), bias, aux, out2, False, 0, self.rank,
+                                   self.world, addrs, [], [], self.flags_ce, self.epoch, ready, [], 0,
+                                   self.timeout_s)
         else:
-            dist.all_gather_into_tensor(gathered, a_local, group=self.group)
-            K.gemm(gathered, b, out, b_mn=b_mn, epi=epi, bias=bias, aux=aux, out2=out2)
+            K.gemm(full, b, out, b_mn=b_mn, epi=epi, bias=bias, aux=aux, out2=out2)
         self.launches += 1
         return out
 
@@ -142,20 +185,10 @@ class TPContext:
         self.launches += 1
         return out
 
-    def wgrad(self, a, b, out, *, a_peer: bool, b_peer: bool, a_full=None, b_full=None):
-        """out[M', N] += A^T B over all tokens (both operands MN-major, token
-        dimension = K). The operand flagged *_peer is token-split over the
-        ranks (its rows on rank r are tokens [r*Mr, (r+1)*Mr)); its data was
-        published earlier in the step and already waited for by an AG-GEMM,
-        so no wait is needed here."""
-        if self.mode == "fused":
-            _ext.kernels().gemm_tp(a, b, out, 1, 1, K.EPI_F32, None, None, None, True, 0, self.rank, self.world,
-                                   self.heap.peer_addrs(a) if a_peer else [],
-                                   self.heap.peer_addrs(b) if b_peer else [], [], None, None, 0, [], 0,
-                                   self.timeout_s)
-        else:
-            K.gemm(a_full if a_peer else a, b_full if b_peer else b, out, a_mn=True, b_mn=True, epi=K.EPI_F32,
-                   accumulate=True)
+    def wgrad(self, a, b, out):
+        """out[M', N] += a^T b over all tokens (both [tokens, .]; gathered
+        operands are local full-size buffers)."""
+        K.gemm(a, b, out, a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
         self.launches += 1
         return out
 

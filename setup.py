@@ -8,7 +8,7 @@ import glob
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("scirs_b200", "csrc")
@@ -53,6 +53,11 @@ ext_modules = [
             ]
         ),
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+    ),
+    CppExtension(
+        name="scirs_b200._data",
+        sources=_sources(["dataloader.cpp"]),
+        extra_compile_args={"cxx": CXX_FLAGS},
     ),
     CUDAExtension(
         name="scirs_b200._comm",

