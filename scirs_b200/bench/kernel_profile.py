@@ -135,6 +135,13 @@ def op_attn_bwd(t):
                      t["dq_acc"], t["delta"], causal=True)
 
 
+def op_attn_bwd_hd128(t):
+    q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
+    dq, dk, dv = t["dqkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
+    K.flash_attn_bwd(t["datt"].view(B, S, H // 2, 2 * HD), q, k, v, t["att"].view(B, S, H // 2, 2 * HD),
+                     t["lse128"], dq, dk, dv, t["dq_acc"], t["delta"], causal=True)
+
+
 def op_ln_fwd(t):
     K.layernorm_fwd(t["x"], t["ln_w"], t["ln_b"], t["ln_y"], t["mu"], t["rs"], 1e-5)
 
@@ -163,6 +170,7 @@ OPS = {
     "attn_fwd_hd128": (op_attn_fwd_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_fwd_pp_hd128": (op_attn_fwd_pp_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_bwd": (op_attn_bwd, 10 * B * H * S * S * HD // 2, (8 * M * D) * 2),
+    "attn_bwd_hd128": (op_attn_bwd_hd128, 10 * B * H * S * S * HD // 2, (8 * M * D) * 2),
     "ln_fwd": (op_ln_fwd, 0, 2 * M * D * 2),
     "ln_bwd": (op_ln_bwd, 0, 4 * M * D * 2),
     "xent": (op_xent, 0, 2 * (M // 4) * 50304 * 2),

@@ -564,6 +564,10 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
                        double scale);
 
 // impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernel (head_dim 64).
+void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
+                         torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
+                         double scale);
+
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
                     torch::Tensor delta, bool causal, double scale, int64_t impl) {
@@ -615,6 +619,8 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
   }
   if (impl == 1 && HD == 64) {
     flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale);
+  } else if (impl == 1 && HD == 128) {
+    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale);
   } else {
   dim3 grid((unsigned)((S + 63) / 64), (unsigned)(B * H));
 #define FA_BWD(HD_, CAUSAL_)                                                                             \

@@ -64,6 +64,7 @@ class TPContext:
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.vals = torch.zeros(4096, dtype=torch.int32, device=self.device)  # this step's flag values
         self.copy_stream = torch.cuda.Stream(self.device) if mode == "fused" else None
+        self._copied = False
         self.idx = 0
         self._recv = None
         self._recv_i = 0
@@ -100,8 +101,9 @@ class TPContext:
     def finish(self):
         """Join the copy stream (before anything outside the step reads or
         reuses buffers the copies touch)."""
-        if self.copy_stream is not None:
+        if self.copy_stream is not None and self._copied:
             torch.cuda.current_stream(self.device).wait_stream(self.copy_stream)
+            self._copied = False
 
     def segment(self, full: torch.Tensor) -> torch.Tensor:
         """This rank's rows of a gathered [M, ...] buffer."""
@@ -121,6 +123,7 @@ class TPContext:
         if self.world > 1:
             main = torch.cuda.current_stream(self.device)
             self.copy_stream.wait_stream(main)
+            self._copied = True
             with torch.cuda.stream(self.copy_stream):
                 comm = _ext.comm()
                 comm.peer_copy(self.heap.peer_addrs(seg), seg.data_ptr(), seg.numel() * seg.element_size())

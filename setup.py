@@ -49,6 +49,7 @@ ext_modules = [
                 "vision.cu",
                 "tp.cu",
                 "attention_fwd_sm100.cu",
+                "attention_bwd_sm100.cu",
                 "paged_attention.cu",
             ]
         ),
