@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
                     help="gpt1.3b: fused collective GEMMs, or NCCL all-gather/reduce-scatter + separate GEMMs")
     ap.add_argument("--images", type=int, default=256, help="global batch of the ViT workload")
+    ap.add_argument("--kernel-summary", action="store_true",
+                    help="after the timed runs, profile one extra step on rank 0 (torch.profiler, CUDA "
+                    "activity) and print the top kernels by device time to stderr; not part of any number")
     a = ap.parse_args()
     if a.global_batch is None:
         a.global_batch = 32 if a.model == "gpt1.3b" else GLOBAL_BATCH
@@ -513,6 +516,20 @@ def main():
             "d2h_bytes_per_step": 4,
             "api": W["api"],
         }
+    if args.kernel_summary:
+        from torch.profiler import ProfilerActivity, profile
+
+        sdist.barrier()
+        a, b = dev_batches[0]
+        if rank == 0:
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                step(a, b)
+                torch.cuda.synchronize()
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30), file=sys.stderr, flush=True)
+        else:
+            step(a, b)
+            torch.cuda.synchronize()
+        sdist.barrier()
     W["cleanup"]()
 
     peaks = {}
