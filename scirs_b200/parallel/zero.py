@@ -167,15 +167,26 @@ class ZeroSharding:
         dist.all_reduce(part[:n], group=self.group)
 
     @torch.no_grad()
-    def consolidated_master(self) -> torch.Tensor:
-        """All-gather the fp32 master shards into the full flat layout."""
-        full = torch.empty(self.fp.total, dtype=torch.float32, device=self.master.device)
+    def consolidate(self, shard: torch.Tensor) -> torch.Tensor:
+        """All-gather an fp32 shard-layout buffer into the full flat layout."""
+        full = torch.zeros(self.fp.total, dtype=torch.float32, device=shard.device)
         for (s, e), (ss, se) in zip(self.bounds, self.shard_bounds):
             if self.cuda:
-                dist.all_gather_into_tensor(full[s:e], self.master[ss:se].contiguous(), group=self.group)
+                dist.all_gather_into_tensor(full[s:e], shard[ss:se].contiguous(), group=self.group)
             else:
-                self._ag_host(self.master[ss:se], full[s:e])
+                self._ag_host(shard[ss:se], full[s:e])
         return full
+
+    @torch.no_grad()
+    def take_shard(self, full: torch.Tensor, shard: torch.Tensor):
+        """Copy this rank's part of a full flat buffer into a shard buffer."""
+        N, r = self.world, self.rank
+        for (s, e), (ss, se) in zip(self.bounds, self.shard_bounds):
+            ln = (e - s) // N
+            shard[ss:se].copy_(full[s + r * ln : s + (r + 1) * ln])
+
+    def consolidated_master(self) -> torch.Tensor:
+        return self.consolidate(self.master)
 
     @torch.no_grad()
     def sync_full_master(self):
@@ -216,6 +227,43 @@ class ZeroAdamW:
         z.norm_allreduce(o.part, n)
         K.optim_step(o.mode, z.master, o.state1, o.state2, z.grad, z.p16, z.master.numel(), o.hp, part=o.part,
                      norm_out=o.grad_norm, decay_mask=z.view.decay_mask, parts_ready=n)
+
+
+def zero_state_dict(model) -> dict:
+    """World-size independent optimizer + parameter state of a ZeRO model:
+    per-parameter fp32 tensors (master weights and both Adam moments) keyed
+    by parameter name, plus the step counter. Collective: every rank calls
+    it; every rank gets the full dict."""
+    z, o = model.param_sync, model.optimizer.inner
+    fp = z.fp
+    out = {"step": int(o.t), "params": {}, "exp_avg": {}, "exp_avg_sq": {}}
+    for key, shard in (("params", z.master), ("exp_avg", o.state1), ("exp_avg_sq", o.state2)):
+        full = z.consolidate(shard)
+        for name in fp.order:
+            out[key][name] = fp.view(full, name).detach().clone().cpu()
+    return out
+
+
+@torch.no_grad()
+def load_zero_state_dict(model, sd: dict):
+    """Inverse of :func:`zero_state_dict` for any world size: lays the named
+    tensors out in this run's flat layout (bucket padding depends on the
+    world size) and keeps this rank's shards; also refreshes the full master
+    and bf16 buffers."""
+    z, o = model.param_sync, model.optimizer.inner
+    fp = z.fp
+    for key, shard in (("params", z.master), ("exp_avg", o.state1), ("exp_avg_sq", o.state2)):
+        full = torch.zeros(fp.total, dtype=torch.float32, device=shard.device)
+        for name in fp.order:
+            fp.view(full, name).copy_(sd[key][name].reshape(fp.slots[name].shape))
+        z.take_shard(full, shard)
+        if key == "params":
+            fp.master.copy_(full)
+            fp.sync_bf16()
+    z.p16.copy_(z.master)
+    o.t = int(sd["step"])
+    o.hp[9] = float(o.t)
+    o._uploaded = None
 
 
 def zero_data_parallel(model, mode: str = "fused", comm=None, lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
