@@ -4,9 +4,14 @@
         -m scirs_b200.bench.allreduce [--min 1024] [--max 1073741824] [--iters 20]
 
 Payload sizes are bf16 bytes on the wire (fp32 gradients in, fp32 out; the
-kernel scales by 1/N and casts to bf16 when publishing). NCCL runs
+push kernel scales by 1/N and casts to bf16 when publishing). NCCL runs
 all_reduce(AVG) on a bf16 tensor of the same element count, i.e. the same
-bytes. Every number is device time from CUDA events, max over ranks.
+bytes. Where the GPUs support NVLink multicast, the NVLS kernel runs in
+place on a bf16 buffer of the same size (reduction inside the NVSwitch,
+fp32 accumulation); its roofline moves (N+1)/N payloads per GPU per
+direction (every byte to the switch once, the reduced 1/N back, the
+multicast store's 1/N out and every byte back in). Every number is device
+time from CUDA events, max over ranks.
 Bus bandwidth = 2 (N-1)/N * bytes / time; roofline = the time to move
 2 (N-1)/N * bytes per rank over NVLink at the measured 770 GB/s per
 direction. Rank 0 prints one JSON line per size.
@@ -49,6 +54,8 @@ def main():
     rank, world, local = sdist.init(timeout_s=120)
     dev = torch.device("cuda", local)
     comm = NVLinkComm(area_bytes=max(args.max, 1 << 20) + (1 << 20), timeout_s=10.0)
+    nvls = comm.nvls_supported()
+    nbuf = comm.nvls_buffer(max(args.max // 2, 1 << 20), torch.bfloat16) if nvls else None
     size = args.min
     while size <= args.max:
         n = max(8 * world, (size // 2) // (8 * world) * (8 * world))
@@ -57,6 +64,11 @@ def main():
         xb = x.to(torch.bfloat16)
         t_ours = _time(lambda: comm.allreduce(x, y, 1.0 / world), args.iters)
         t_nccl = _time(lambda: dist.all_reduce(xb, op=dist.ReduceOp.AVG), args.iters)
+        t_nvls = None
+        if nvls:
+            v = nbuf[:n]
+            v.copy_(xb)
+            t_nvls = _time(lambda: comm.allreduce_nvls_(v, 1.0 / world), args.iters)
         nbytes = 2 * n
         bus = lambda t: 2 * (world - 1) / world * nbytes / (t * 1e-3) / 1e9  # noqa: E731
         roof_ms = 2 * (world - 1) / world * nbytes / (LINK_GBS * 1e9) * 1e3
@@ -65,6 +77,10 @@ def main():
                 "bytes": nbytes, "n_gpus": world, "ours_ms": round(t_ours, 4), "nccl_ms": round(t_nccl, 4),
                 "ours_busbw_GBs": round(bus(t_ours), 1), "nccl_busbw_GBs": round(bus(t_nccl), 1),
                 "speedup_vs_nccl": round(t_nccl / t_ours, 3), "roofline_frac": round(roof_ms / t_ours, 3),
+                **({} if t_nvls is None else {
+                    "nvls_ms": round(t_nvls, 4), "nvls_busbw_GBs": round(bus(t_nvls), 1),
+                    "nvls_speedup_vs_nccl": round(t_nccl / t_nvls, 3),
+                    "nvls_roofline_frac": round((world + 1) / world * nbytes / (LINK_GBS * 1e9) * 1e3 / t_nvls, 3)}),
             }), flush=True)
         size *= 4
     _ext.check_status(local)

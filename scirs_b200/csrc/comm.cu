@@ -74,6 +74,7 @@ struct Args {
   unsigned* ctl;     // local [call counter, finished-block counter]
   DevStatus* st;
   long long timeout_ns;
+  unsigned long long mc;  // NVLS: multicast address of the payload
 };
 
 __device__ __forceinline__ unsigned* flag_ptr(char* base, long area_bytes, int barrier, int block, int src) {
@@ -407,6 +408,97 @@ __global__ void __launch_bounds__(kCommThreads, 4) allgather_kernel(const Args a
   call_end(a, c);
 }
 
+// ---------------------------------------------------------------------------
+// NVLS all-reduce (in place on a buffer bound to an NVLink multicast object):
+// the payload lives at the same offset of every rank's symmetric buffer and
+// `a.mc` addresses it through the multicast mapping. Rank r owns 1/world of
+// the 16-byte vectors; for each it issues one multimem.ld_reduce (the
+// NVSwitch reads the vector from every GPU and returns the sum, fp32
+// accumulation for bf16 payloads) and one multimem.st (the switch writes the
+// scaled sum into every GPU's copy). Each GPU therefore sends and receives
+// about one payload over NVLink, half of a ring or two-shot all-reduce.
+//   entry barrier (block b of every rank): everything written before the
+//     kernel on each rank is complete;
+//   exit barrier: every rank's stores of sub-slice b landed; since each
+//     block b waits for block b of all ranks, a rank leaving the kernel
+//     implies all stores of all ranks landed (same grid on every rank).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+template <bool BF16>
+__device__ __forceinline__ uint4 mc_ld_reduce(unsigned long long p) {
+  uint4 q;
+  if (BF16)
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                 : "l"(p)
+                 : "memory");
+  else
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                 : "l"(p)
+                 : "memory");
+  return q;
+}
+template <bool BF16>
+__device__ __forceinline__ void mc_store(unsigned long long p, const uint4& q) {
+  if (BF16)
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(q.x), "r"(q.y),
+                 "r"(q.z), "r"(q.w)
+                 : "memory");
+  else
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(q.x), "r"(q.y),
+                 "r"(q.z), "r"(q.w)
+                 : "memory");
+}
+template <bool BF16>
+__device__ __forceinline__ uint4 scale_vec(uint4 q, float s) {
+  if (BF16) {
+    float f[8];
+    unpack8(q, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] *= s;
+    return pack8(f);
+  }
+  q.x = __float_as_uint(__uint_as_float(q.x) * s);
+  q.y = __float_as_uint(__uint_as_float(q.y) * s);
+  q.z = __float_as_uint(__uint_as_float(q.z) * s);
+  q.w = __float_as_uint(__uint_as_float(q.w) * s);
+  return q;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kCommThreads, 4) nvls_allreduce_kernel(const Args a) {
+  __shared__ volatile int sfail;
+  if (threadIdx.x == 0) sfail = 0;
+  const CallCtx c = call_begin(a);
+  const long nvec = a.n * (BF16 ? 2 : 4) / 16;
+  const long cv = (nvec + a.world - 1) / a.world;
+  long s0, s1;
+  sub_slice(cv, s0, s1);
+  const long e0 = min(nvec, (long)a.rank * cv + s0), e1 = min(nvec, (long)a.rank * cv + s1);
+  if (block_barrier(a, 0, c.epoch, &sfail)) {
+    fence_proxy_alias();
+    const long bd = blockDim.x;
+    const bool do_scale = a.scale != 1.0f;
+    for (long v = e0 + threadIdx.x; v < e1; v += bd * kU) {
+      uint4 q[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * bd < e1) q[u] = mc_ld_reduce<BF16>(a.mc + (unsigned long long)(v + u * bd) * 16ull);
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * bd < e1) {
+          const uint4 r = do_scale ? scale_vec<BF16>(q[u], a.scale) : q[u];
+          mc_store<BF16>(a.mc + (unsigned long long)(v + u * bd) * 16ull, r);
+        }
+    }
+    fence_proxy_alias();
+    block_barrier(a, 1, c.epoch, &sfail);
+  }
+  call_end(a, c);
+}
+
 // Fault-injection helper for tests: waits on a flag nothing ever sets, with
 // the same bounded wait as the collectives, so the timeout path and the
 // status word can be exercised on a single GPU without any hang.
@@ -567,6 +659,34 @@ void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double 
     const int nb = pick_blocks((nvec + cs.world - 1) / cs.world, cs.world, blocks);
     comm::allreduce_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   }
+  SCIRS_CHECK_LAUNCH();
+}
+
+// In place: buf = scale * sum over ranks, through the NVLink multicast
+// mapping `mc_addr` of `buf` (fp32 or bf16; both 16-byte aligned, a whole
+// number of 16-byte vectors). buf must be at the same offset of every rank's
+// multicast-bound symmetric buffer, with the same size on every rank.
+void comm_allreduce_nvls(int64_t id, torch::Tensor buf, int64_t mc_addr, double scale, int64_t blocks,
+                         double timeout_s) {
+  CommState& cs = get_cs(id);
+  CHECK_CONTIG(buf);
+  const bool bf16 = buf.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf16 || buf.scalar_type() == at::kFloat, "NVLS all-reduce: fp32 or bf16 payload");
+  const long n = buf.numel();
+  TORCH_CHECK((n * buf.element_size()) % 16 == 0, "NVLS all-reduce: payload must be a multiple of 16 bytes");
+  TORCH_CHECK(mc_addr != 0 && mc_addr % 16 == 0 && reinterpret_cast<uintptr_t>(buf.data_ptr()) % 16 == 0,
+              "NVLS all-reduce: 16-byte aligned buffer and multicast address required");
+  if (n == 0) return;
+  comm::Args a = make_args(cs, n, timeout_s);
+  a.scale = (float)scale;
+  a.mc = (unsigned long long)mc_addr;
+  c10::cuda::CUDAGuard guard(cs.device);
+  const long nvec = n * buf.element_size() / 16;
+  const int nb = pick_blocks((nvec + cs.world - 1) / cs.world, cs.world, blocks);
+  if (bf16)
+    comm::nvls_allreduce_kernel<true><<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
+  else
+    comm::nvls_allreduce_kernel<false><<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   SCIRS_CHECK_LAUNCH();
 }
 

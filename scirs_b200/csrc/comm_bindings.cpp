@@ -7,6 +7,8 @@ void comm_open_peers(int64_t id, std::vector<py::bytes> handles);
 void comm_destroy(int64_t id);
 void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double scale, int64_t blocks,
                     double timeout_s, int64_t algo);
+void comm_allreduce_nvls(int64_t id, torch::Tensor buf, int64_t mc_addr, double scale, int64_t blocks,
+                         double timeout_s);
 void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, double scale, int64_t blocks,
                          double timeout_s);
 void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t blocks, double timeout_s);
@@ -26,6 +28,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("destroy", &scirs::comm_destroy);
   m.def("allreduce", &scirs::comm_allreduce, py::arg("id"), py::arg("in32"), py::arg("out32"), py::arg("scale"),
         py::arg("blocks"), py::arg("timeout_s"), py::arg("algo") = 0);
+  m.def("allreduce_nvls", &scirs::comm_allreduce_nvls);
   m.def("reduce_scatter", &scirs::comm_reduce_scatter);
   m.def("allgather", &scirs::comm_allgather);
   m.def("timeout_probe", &scirs::comm_timeout_probe);

@@ -34,6 +34,7 @@ class NVLinkComm:
         dist.all_gather_object(handles, bytes(handle), group=group)
         self.mod.open_peers(self.id, handles)
         dist.barrier(group=group)
+        self._nvls = []
 
     @property
     def max_elems(self) -> int:
@@ -50,6 +51,46 @@ class NVLinkComm:
         self.mod.allreduce(self.id, src, dst, float(scale), int(blocks), self.timeout_s, int(algo))
         return dst
 
+    # ------------------------------------------------------------- NVLS
+    def nvls_supported(self) -> bool:
+        """True when this GPU can bind memory to an NVLink multicast object
+        (NVSwitch with multicast enabled)."""
+        try:
+            from torch._C._distributed_c10d import _SymmetricMemory
+
+            return bool(_SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, self.device))
+        except Exception:
+            return False
+
+    def nvls_buffer(self, numel: int, dtype=torch.float32) -> torch.Tensor:
+        """A tensor in symmetric memory bound to an NVLink multicast object
+        (same size and dtype on every rank; collective). In-place NVLS
+        all-reduces run on it and on any 16-byte aligned slice of it."""
+        import torch.distributed._symmetric_memory as symm
+
+        t = symm.empty(int(numel), dtype=dtype, device=torch.device("cuda", self.device))
+        h = symm.rendezvous(t, self.group if self.group is not None else dist.group.WORLD)
+        mc = int(h.multicast_ptr)
+        if mc == 0:
+            raise RuntimeError("symmetric memory has no NVLink multicast mapping on this system")
+        base = int(h.buffer_ptrs[self.rank])
+        self._nvls.append((t.data_ptr(), t.numel() * t.element_size(), mc + (t.data_ptr() - base), h, t))
+        return t
+
+    def _mc_addr(self, t: torch.Tensor) -> int:
+        p = t.data_ptr()
+        for start, size, mc, _h, _t in self._nvls:
+            if start <= p and p + t.numel() * t.element_size() <= start + size:
+                return mc + (p - start)
+        raise ValueError("tensor is not inside an NVLS buffer of this communicator")
+
+    def allreduce_nvls_(self, t: torch.Tensor, scale: float = 1.0, blocks: int = 0) -> torch.Tensor:
+        """In place: t <- scale * sum over ranks, reduced inside the NVSwitch
+        (fp32, or bf16 with fp32 accumulation). `t` must lie in a buffer from
+        :meth:`nvls_buffer`, at the same offset on every rank."""
+        self.mod.allreduce_nvls(self.id, t, self._mc_addr(t), float(scale), int(blocks), self.timeout_s)
+        return t
+
     def reduce_scatter(self, src: torch.Tensor, dst: torch.Tensor, scale: float = 1.0, blocks: int = 0):
         """dst (this rank's shard, fp32) = scale * sum over ranks of src's shard."""
         self.mod.reduce_scatter(self.id, src, dst, float(scale), int(blocks), self.timeout_s)
@@ -63,6 +104,7 @@ class NVLinkComm:
     def close(self):
         if self.id is not None:
             torch.cuda.synchronize()
+            self._nvls = []
             self.mod.destroy(self.id)
             self.id = None
 

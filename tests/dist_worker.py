@@ -62,6 +62,38 @@ def case_collectives():
     return res
 
 
+def case_nvls():
+    from scirs_b200.parallel.nvlink import NVLinkComm
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    comm = NVLinkComm(area_bytes=16 << 20, timeout_s=10.0)
+    if not comm.nvls_supported():
+        return {"skipped": "no NVLink multicast support"}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = {}
+    for dtype in (torch.float32, torch.bfloat16):
+        buf = comm.nvls_buffer(1 << 22, dtype)
+        for off, n in [(0, 8 * world), (64, 4096 + 8), (1024, 1 << 20), (0, 1 << 22)]:
+            view = buf[off:off + n]
+            for rep in range(3):  # repeated calls exercise the epoch protocol
+                g = torch.Generator().manual_seed(1000 * rep + rank)
+                x = torch.randn(n, generator=g).to(dev).to(dtype)
+                view.copy_(x)
+                ref = x.float()
+                dist.all_reduce(ref)
+                ref /= world
+                comm.allreduce_nvls_(view, 1.0 / world)
+            torch.cuda.synchronize()
+            got = view.float()
+            err = float((got - ref).abs().max() / ref.abs().max())
+            o0 = got.clone()
+            dist.broadcast(o0, 0)
+            res[f"nvls_{str(dtype)[6:]}_{off}_{n}"] = {"max_err": err, "identical": bool(torch.equal(o0, got))}
+    _ext.check_status()
+    comm.close()
+    return res
+
+
 def case_dp_gpt():
     """DP training with the fused all-reduce == single-process training on the
     concatenated global batch (same weights, same data)."""
@@ -191,7 +223,7 @@ def case_tp_decoder():
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
-    res = {"collectives": case_collectives, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
+    res = {"collectives": case_collectives, "nvls": case_nvls, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
            "tp_decoder": case_tp_decoder}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))

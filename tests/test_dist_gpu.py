@@ -42,6 +42,16 @@ def test_nvlink_collectives_2gpu(tmp_path):
             assert v["equal"], k
 
 
+def test_nvls_allreduce_2gpu(tmp_path):
+    res = _run("nvls", tmp_path, port=29615)
+    if "skipped" in res:
+        pytest.skip(res["skipped"])
+    for k, v in res.items():
+        assert v["identical"], k
+        tol = 1e-5 if "float32" in k else 2e-2
+        assert v["max_err"] < tol, (k, v)
+
+
 def test_data_parallel_gpt_2gpu(tmp_path):
     res = _run("dp_gpt", tmp_path, port=29612)
     ref = res["single"]["losses"]
