@@ -45,7 +45,9 @@ def parse():
     ap.add_argument("--global-batch", type=int, default=None,
                     help="sequences per step (default 64 for gpt2, 32 for gpt1.3b)")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default 1024 gpt2, 2048 gpt1.3b)")
-    ap.add_argument("--dp-mode", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--dp-mode", default="fused", choices=["fused", "push", "nvls", "nccl"],
+                    help="data-parallel gradient all-reduce: fused = NVLS in-switch reduction where the GPUs "
+                    "support NVLink multicast, else the push all-reduce; nccl = the baseline")
     ap.add_argument("--layers", type=int, default=None, help="layers (default: the model's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="run the step eagerly instead of as a CUDA graph")
@@ -174,6 +176,8 @@ def build_gpt(args, rank, world, local, dev):
         model.configure_adamw(lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
         if world > 1:
             data_parallel(model, mode=args.dp_mode)
+        dp_desc = {"nvls": "NVLS in-switch all-reduce (fp32, in place)", "push": "push all-reduce (bf16 wire)",
+                   "nccl": "nccl"}.get(getattr(model.grad_sync, "mode", None))
         if not args.no_graph:
             model.enable_cuda_graph()
 
@@ -182,7 +186,7 @@ def build_gpt(args, rank, world, local, dev):
 
         def launches():
             n = K.STATS.launches
-            if model.grad_sync is not None and args.dp_mode == "fused":
+            if model.grad_sync is not None and model.grad_sync.mode != "nccl":
                 n += model.grad_sync.launches
             return n
 
@@ -232,7 +236,7 @@ def build_gpt(args, rank, world, local, dev):
             "global_batch": args.global_batch,
             "seq_len": S,
             "parallelism": f"dp{world}",
-            "dp_allreduce": (args.dp_mode if args.impl == "ours" else "nccl (DDP, bf16 compress hook)")
+            "dp_allreduce": (dp_desc if args.impl == "ours" else "nccl (DDP, bf16 compress hook)")
             if world > 1
             else None,
             "optimizer": "AdamW (fp32 master, wd 0.1, clip 1.0)",
@@ -275,7 +279,7 @@ def build_vit(args, rank, world, local, dev):
 
         model = ViTModel(cfg, device=dev, seed=0, bucket_align=64 * world)
         if world > 1:
-            zero_data_parallel(model, mode=args.dp_mode, **hp)
+            zero_data_parallel(model, mode="nccl" if args.dp_mode == "nccl" else "fused", **hp)
         else:
             model.configure_adamw(**hp)
         if not args.no_graph:
@@ -286,7 +290,7 @@ def build_vit(args, rank, world, local, dev):
 
         def launches():
             n = K.STATS.launches
-            if model.grad_sync is not None and args.dp_mode == "fused":
+            if model.grad_sync is not None and model.grad_sync.mode != "nccl":
                 n += model.grad_sync.launches
             return n
 

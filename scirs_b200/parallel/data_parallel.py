@@ -11,9 +11,15 @@ backward kernels. :meth:`GradSync.finish` joins the streams before the
 optimizer step.
 
 Modes:
-  "fused": the in-kernel NVLink all-reduce (scale by 1/world and the
+  "nvls" : the gradient buffer itself lives in symmetric memory bound to an
+           NVLink multicast object; each bucket is all-reduced IN PLACE by
+           the NVLS kernel (fp32 multimem.ld_reduce inside the NVSwitch +
+           multimem.st of the 1/world-scaled sum): no staging copy, no cast,
+           about one payload per GPU per direction over NVLink.
+  "push" : the in-kernel NVLink push all-reduce (scale by 1/world and the
            fp32->bf16 cast fused into the publish phase, bf16 on the wire,
            fp32 accumulation, identical result on every rank).
+  "fused": "nvls" where the GPUs support NVLink multicast, else "push".
   "nccl" : torch.distributed.all_reduce (fp32, AVG) on the same stream
            schedule; the baseline.
 
@@ -35,7 +41,7 @@ class GradSync:
         self.mode = mode
         self.world = dist.get_world_size()
         self.comm = comm
-        if mode == "fused":
+        if mode == "push":
             assert comm is not None
             biggest = max(e - s for s, e in bounds)
             assert biggest <= comm.max_elems, f"bucket of {biggest} elements exceeds the symmetric buffer"
@@ -50,7 +56,9 @@ class GradSync:
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(ev)
             sl = self.grad[s:e]
-            if self.mode == "fused":
+            if self.mode == "nvls":
+                self.comm.allreduce_nvls_(sl, 1.0 / self.world)
+            elif self.mode == "push":
                 self.comm.allreduce_(sl, 1.0 / self.world)
             else:
                 dist.all_reduce(sl, op=dist.ReduceOp.AVG)
@@ -72,8 +80,16 @@ def data_parallel(model, mode: str = "fused", comm=None, area_bytes: int | None 
     fp = model.fp
     dist.broadcast(fp.master, src=0)
     fp.sync_bf16()
-    if mode == "fused" and comm is None:
+    if mode in ("fused", "push", "nvls") and comm is None:
         biggest = max(e - s for s, e in model.bucket_bounds)
         comm = NVLinkComm(area_bytes=area_bytes or (biggest * 2 + (1 << 20)))
+    if mode == "fused":
+        mode = "nvls" if comm.nvls_supported() else "push"
+    if mode == "nvls":
+        # move the flat gradient buffer into multicast-bound symmetric memory
+        # (kernels take their gradient views from fp.grad at every call)
+        g = comm.nvls_buffer(fp.total, torch.float32)
+        g.copy_(fp.grad)
+        fp.grad = g
     model.grad_sync = GradSync(fp.grad, model.bucket_bounds, mode=mode, comm=comm)
     return model
