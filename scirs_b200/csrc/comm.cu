@@ -216,7 +216,8 @@ __device__ __forceinline__ void push_scaled_shards(const Args& a, const CallCtx&
       if (t < tot && (long)k * sv + s < nvec) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
-        areaA(a, k, c)[(long)a.rank * sv + s] = pack8(f[u]);
+        if (SCIRS_KCHECK_IDX((long)a.rank * sv + s, a.area_bytes / 16, a.st, 120))
+          areaA(a, k, c)[(long)a.rank * sv + s] = pack8(f[u]);
       }
     }
   }
@@ -267,7 +268,8 @@ __global__ void __launch_bounds__(kCommThreads, 4) allreduce_kernel(const Args a
         if (s + u * bd < mine_end) {
           const uint4 q = pack8(acc[u]);
           for (int j = 0; j < a.world; ++j)
-            areaB(a, (a.rank + 1 + j) % a.world, c)[(long)a.rank * sv + s + u * bd] = q;
+            if (SCIRS_KCHECK_IDX((long)a.rank * sv + s + u * bd, a.area_bytes / 16, a.st, 121))
+              areaB(a, (a.rank + 1 + j) % a.world, c)[(long)a.rank * sv + s + u * bd] = q;
         }
       }
     }
@@ -319,7 +321,9 @@ __global__ void __launch_bounds__(kCommThreads, 4) allreduce_oneshot_kernel(cons
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[u][e] *= a.scale;
         const uint4 q = pack8(f[u]);
-        for (int j = 0; j < a.world; ++j) areaA(a, (a.rank + 1 + j) % a.world, c)[(long)a.rank * nvec + base + u * bd] = q;
+        for (int j = 0; j < a.world; ++j)
+          if (SCIRS_KCHECK_IDX((long)a.rank * nvec + base + u * bd, a.area_bytes / 16, a.st, 122))
+            areaA(a, (a.rank + 1 + j) % a.world, c)[(long)a.rank * nvec + base + u * bd] = q;
       }
     }
   }

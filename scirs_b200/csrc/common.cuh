@@ -42,6 +42,22 @@ __device__ __forceinline__ void report_status(DevStatus* st, unsigned code, unsi
   }
 }
 
+// Bounds checks. Indices that come from user data (token ids, page tables)
+// are always checked: an out-of-range value is recorded as kStBounds in the
+// status word and the access is skipped (the host raises on the next
+// check_status). Checks of internal index arithmetic compile in only with
+// -DSCIRS_KCHECK (setup.py: SCIRS_KCHECK=1), for debug builds.
+__device__ __forceinline__ bool input_in_range(long v, long n, DevStatus* st, unsigned where) {
+  if (v >= 0 && v < n) return true;
+  report_status(st, kStBounds, where, (unsigned)v);
+  return false;
+}
+#ifdef SCIRS_KCHECK
+#define SCIRS_KCHECK_IDX(v, n, st, where) ::scirs::input_in_range((long)(v), (long)(n), (st), (where))
+#else
+#define SCIRS_KCHECK_IDX(v, n, st, where) true
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -431,11 +431,13 @@ __global__ void __launch_bounds__(THREADS) xent_fwd_kernel(const bf16* __restric
 // Embedding: out[m] = wte[tok[m]] + wpe[m % S]  (wpe may be null)
 // ===========================================================================
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ wte,
-                                 const bf16* __restrict__ wpe, bf16* __restrict__ out, int M, int S, int D) {
+                                 const bf16* __restrict__ wpe, bf16* __restrict__ out, int M, int S, int D, long V,
+                                 DevStatus* st) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const long t = tok[row];
+  if (!input_in_range(t, V, st, 80)) return;  // token id outside the vocabulary
   const uint4* a = reinterpret_cast<const uint4*>(wte + t * D);
   const uint4* p = wpe ? reinterpret_cast<const uint4*>(wpe + (long)(row % S) * D) : nullptr;
   uint4* o = reinterpret_cast<uint4*>(out + (long)row * D);
@@ -454,11 +456,13 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const bf16* __
 
 // dwte[tok[m]] += dout[m]; dwpe[m % S] += dout[m]  (fp32 atomics)
 __global__ void embed_bwd_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ dout,
-                                 float* __restrict__ dwte, float* __restrict__ dwpe, int M, int S, int D) {
+                                 float* __restrict__ dwte, float* __restrict__ dwpe, int M, int S, int D, long V,
+                                 DevStatus* st) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const long t = tok[row];
+  if (!input_in_range(t, V, st, 81)) return;
   const uint4* g = reinterpret_cast<const uint4*>(dout + (long)row * D);
   float* a = dwte + t * D;
   float* p = dwpe ? dwpe + (long)(row % S) * D : nullptr;
@@ -629,7 +633,8 @@ void embedding_fwd(torch::Tensor tok, torch::Tensor wte, c10::optional<torch::Te
   c10::cuda::CUDAGuard g(tok.get_device());
   const bf16* pp = (wpe.has_value() && wpe->defined()) ? (const bf16*)wpe->data_ptr() : nullptr;
   embed_fwd_kernel<<<(M + 7) / 8, 256, 0, cur_stream()>>>(tok.data_ptr<int64_t>(), (const bf16*)wte.data_ptr(), pp,
-                                                          (bf16*)out.data_ptr(), M, (int)S, D);
+                                                          (bf16*)out.data_ptr(), M, (int)S, D, (long)wte.size(0),
+                                                          status_ptr(tok.get_device()));
   SCIRS_CHECK_LAUNCH();
 }
 
@@ -641,7 +646,8 @@ void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor dwte, c1
   c10::cuda::CUDAGuard g(tok.get_device());
   float* pp = (dwpe.has_value() && dwpe->defined()) ? dwpe->data_ptr<float>() : nullptr;
   embed_bwd_kernel<<<(M + 7) / 8, 256, 0, cur_stream()>>>(tok.data_ptr<int64_t>(), (const bf16*)dout.data_ptr(),
-                                                          dwte.data_ptr<float>(), pp, M, (int)S, D);
+                                                          dwte.data_ptr<float>(), pp, M, (int)S, D,
+                                                          (long)dwte.size(0), status_ptr(tok.get_device()));
   SCIRS_CHECK_LAUNCH();
 }
 

@@ -32,12 +32,15 @@ constexpr int kMaxHD = 128;
 __global__ void append_kernel(const __nv_bfloat16* __restrict__ k_new, const __nv_bfloat16* __restrict__ v_new,
                               __nv_bfloat16* __restrict__ k_pool, __nv_bfloat16* __restrict__ v_pool,
                               const int* __restrict__ block_tables, const int* __restrict__ seq,
-                              const int* __restrict__ pos, int n, int max_pages, int bs, int row_vecs) {
+                              const int* __restrict__ pos, int n, int max_pages, int bs, int row_vecs,
+                              int num_seqs, int num_pages, DevStatus* st) {
   const long total = (long)n * row_vecs;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int tok = (int)(i / row_vecs), c = (int)(i % row_vecs);
     const int s = seq[tok], p = pos[tok];
+    if (!input_in_range(s, num_seqs, st, 90) || !input_in_range(p / bs, max_pages, st, 91) || p < 0) continue;
     const int page = block_tables[(long)s * max_pages + p / bs];
+    if (!input_in_range(page, num_pages, st, 92)) continue;
     const long dst = ((long)page * bs + p % bs) * row_vecs + c;
     reinterpret_cast<uint4*>(k_pool)[dst] = reinterpret_cast<const uint4*>(k_new)[i];
     reinterpret_cast<uint4*>(v_pool)[dst] = reinterpret_cast<const uint4*>(v_new)[i];
@@ -51,7 +54,8 @@ __global__ void __launch_bounds__(kT) decode_kernel(const __nv_bfloat16* __restr
                                                     const int* __restrict__ block_tables,
                                                     const int* __restrict__ seq_lens, float* __restrict__ part_o,
                                                     float* __restrict__ part_ml, int H, int Hkv, int bs,
-                                                    int max_pages, int tokens_per_split, float scale_log2) {
+                                                    int max_pages, int tokens_per_split, float scale_log2,
+                                                    int num_pages, DevStatus* st) {
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = H / Hkv;
   const int tid = threadIdx.x;
@@ -74,7 +78,8 @@ __global__ void __launch_bounds__(kT) decode_kernel(const __nv_bfloat16* __restr
 #pragma unroll
   for (int e = 0; e < ODIM; ++e) acc[e] = 0.f;
   __syncthreads();
-  const int len = seq_lens[b];
+  const int len = min(seq_lens[b], max_pages * bs);  // tokens past the page table are not addressable
+  if (tid == 0 && seq_lens[b] > max_pages * bs) report_status(st, kStBounds, 93, (unsigned)seq_lens[b]);
   const int t_begin = split * tokens_per_split;
   const int t_end = min(len, t_begin + tokens_per_split);
   const long row = (long)Hkv * HD;  // elements per token slot
@@ -85,8 +90,9 @@ __global__ void __launch_bounds__(kT) decode_kernel(const __nv_bfloat16* __restr
     float sc[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; ++g) sc[g] = -INFINITY;
-    if (t < t_end) {
-      const int page = bt[t / bs];
+    const int kpage = (t < t_end) ? bt[t / bs] : 0;
+    if (t < t_end && input_in_range(kpage, num_pages, st, 94)) {
+      const int page = kpage;
       const __nv_bfloat16* kr = k_pool + ((long)page * bs + t % bs) * row + (long)hk * HD;
 #pragma unroll
       for (int g = 0; g < kMaxG; ++g) sc[g] = 0.f;
@@ -146,6 +152,7 @@ __global__ void __launch_bounds__(kT) decode_kernel(const __nv_bfloat16* __restr
       for (int i = 0; i < n; ++i) {
         const int tt = c0 + i;
         const int page = bt[tt / bs];
+        if (page < 0 || page >= num_pages) continue;  // reported in the score pass; its score is -inf
         const __nv_bfloat16* vr = v_pool + ((long)page * bs + tt % bs) * row + (long)hk * HD + od;
         const float pv = ps[og][i];
         if (ODIM == 8) {
@@ -226,7 +233,7 @@ void paged_kv_append(torch::Tensor k_new, torch::Tensor v_new, torch::Tensor k_p
       reinterpret_cast<const __nv_bfloat16*>(k_new.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(v_new.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(k_pool.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_pool.data_ptr()),
       block_tables.data_ptr<int>(), seq.data_ptr<int>(), pos.data_ptr<int>(), n, (int)block_tables.size(1), bs,
-      (int)(row / 8));
+      (int)(row / 8), (int)block_tables.size(0), (int)k_pool.size(0), status_ptr(k_pool.get_device()));
   SCIRS_CHECK_LAUNCH();
 }
 
@@ -262,13 +269,13 @@ void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_pool.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(v_pool.data_ptr()), block_tables.data_ptr<int>(),
         seq_lens.data_ptr<int>(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), H, Hkv, bs,
-        (int)block_tables.size(1), (int)tokens_per_split, sl2);
+        (int)block_tables.size(1), (int)tokens_per_split, sl2, (int)k_pool.size(0), status_ptr(q.get_device()));
   else
     paged::decode_kernel<128><<<grid, paged::kT, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_pool.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(v_pool.data_ptr()), block_tables.data_ptr<int>(),
         seq_lens.data_ptr<int>(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), H, Hkv, bs,
-        (int)block_tables.size(1), (int)tokens_per_split, sl2);
+        (int)block_tables.size(1), (int)tokens_per_split, sl2, (int)k_pool.size(0), status_ptr(q.get_device()));
   SCIRS_CHECK_LAUNCH();
   paged::combine_kernel<<<B * H, 64, 0, st>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
                                               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), splits, HD);

@@ -25,6 +25,8 @@ NVCC_FLAGS = ARCH + [
     "-U__CUDA_NO_HALF_CONVERSIONS__",
     "-U__CUDA_NO_BFLOAT162_OPERATORS__",
 ]
+if os.environ.get("SCIRS_KCHECK") == "1":  # debug build: internal index checks -> status word
+    NVCC_FLAGS.append("-DSCIRS_KCHECK")
 if os.environ.get("SCIRS_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 CXX_FLAGS = ["-O3", "-std=c++17"]

@@ -36,3 +36,18 @@ def test_peer_wait_timeout_reports_status_and_context_survives():
     assert float(x.sum()) == float(1 << 20)
     torch.cuda.synchronize()
     _ext.check_status(0)
+
+
+def test_out_of_range_token_is_reported_not_faulted():
+    dev = torch.device("cuda", 0)
+    _ext.check_status(0)
+    V, D, S = 100, 64, 4
+    wte = torch.randn(V, D, device=dev).bfloat16()
+    tok = torch.tensor([[1, 2, V + 5, 3]], device=dev)  # one id past the vocabulary
+    out = torch.zeros(4, D, device=dev, dtype=torch.bfloat16)
+    _ext.kernels().embedding_fwd(tok.reshape(-1), wte, None, out, S)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="bounds check failed"):
+        _ext.check_status(0)
+    torch.testing.assert_close(out[0].float(), wte[1].float())
+    assert float(out[2].float().abs().sum()) == 0.0  # the bad row was skipped
