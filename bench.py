@@ -279,9 +279,13 @@ def build_vit(args, rank, world, local, dev):
 
         model = ViTModel(cfg, device=dev, seed=0, bucket_align=64 * world)
         if world > 1:
-            zero_data_parallel(model, mode="nccl" if args.dp_mode == "nccl" else "fused", **hp)
+            zero_data_parallel(model, mode={"nccl": "nccl", "push": "push", "nvls": "nvls"}.get(args.dp_mode, "fused"),
+                               **hp)
         else:
             model.configure_adamw(**hp)
+        zero_desc = {"nvls": "NVLS reduce-scatter (multimem.ld_reduce) + all-gather (multimem.st)",
+                     "push": "push reduce-scatter / all-gather", "nccl": "nccl"}.get(
+            getattr(model.param_sync, "mode", None))
         if not args.no_graph:
             model.enable_cuda_graph()
 
@@ -345,7 +349,7 @@ def build_vit(args, rank, world, local, dev):
             "seq_len": T,
             "tokens_per_image": T,
             "parallelism": f"zero-dp{world}" if world > 1 else "dp1",
-            "zero_collectives": (args.dp_mode if args.impl == "ours" else "nccl (DDP + ZeroRedundancyOptimizer)")
+            "zero_collectives": (zero_desc if args.impl == "ours" else "nccl (DDP + ZeroRedundancyOptimizer)")
             if world > 1
             else None,
             "optimizer": "AdamW (fp32 master, wd 0.05, clip 1.0)",

@@ -503,6 +503,68 @@ __global__ void __launch_bounds__(kCommThreads, 4) nvls_allreduce_kernel(const A
   call_end(a, c);
 }
 
+// NVLS reduce-scatter: `a.mc` addresses the full payload (n elements, fp32)
+// through the multicast mapping; rank r reduces its shard [r*n/W, (r+1)*n/W)
+// inside the switch and stores scale * sum into its local fp32 shard
+// (a.out32). Exit barrier: no rank may overwrite its payload (e.g. the next
+// backward pass) while a peer still reduces from it.
+__global__ void __launch_bounds__(kCommThreads, 4) nvls_reduce_scatter_kernel(const Args a) {
+  __shared__ volatile int sfail;
+  if (threadIdx.x == 0) sfail = 0;
+  const CallCtx c = call_begin(a);
+  const long sv = a.n / a.world / 4;  // 16-byte vectors per shard
+  long s0, s1;
+  sub_slice(sv, s0, s1);
+  if (block_barrier(a, 0, c.epoch, &sfail)) {
+    fence_proxy_alias();
+    const long bd = blockDim.x, off = (long)a.rank * sv;
+    uint4* out = reinterpret_cast<uint4*>(a.out32);
+    for (long v = s0 + threadIdx.x; v < s1; v += bd * kU) {
+      uint4 q[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * bd < s1) q[u] = mc_ld_reduce<false>(a.mc + (unsigned long long)(off + v + u * bd) * 16ull);
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * bd < s1) out[v + u * bd] = scale_vec<false>(q[u], a.scale);
+    }
+    fence_proxy_alias();
+    block_barrier(a, 1, c.epoch, &sfail);
+  }
+  call_end(a, c);
+}
+
+// NVLS all-gather: rank r stores its bf16 shard (a.in16, n/W elements) with
+// multimem.st into every rank's full buffer at [r*n/W, (r+1)*n/W) (`a.mc`
+// addresses the full buffer). Entry barrier: every rank has finished the
+// work queued before this call (nobody still reads the old contents); exit
+// barrier: every rank's shard has landed everywhere.
+__global__ void __launch_bounds__(kCommThreads, 4) nvls_allgather_kernel(const Args a) {
+  __shared__ volatile int sfail;
+  if (threadIdx.x == 0) sfail = 0;
+  const CallCtx c = call_begin(a);
+  const long sv = a.n / a.world / 8;  // 16-byte vectors per shard
+  long s0, s1;
+  sub_slice(sv, s0, s1);
+  if (block_barrier(a, 0, c.epoch, &sfail)) {
+    fence_proxy_alias();
+    const long bd = blockDim.x, off = (long)a.rank * sv;
+    const uint4* in = reinterpret_cast<const uint4*>(a.in16);
+    for (long v = s0 + threadIdx.x; v < s1; v += bd * kU) {
+      uint4 q[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * bd < s1) q[u] = __ldcg(in + v + u * bd);
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * bd < s1) mc_store<true>(a.mc + (unsigned long long)(off + v + u * bd) * 16ull, q[u]);
+    }
+    fence_proxy_alias();
+    block_barrier(a, 1, c.epoch, &sfail);
+  }
+  call_end(a, c);
+}
+
 // Fault-injection helper for tests: waits on a flag nothing ever sets, with
 // the same bounded wait as the collectives, so the timeout path and the
 // status word can be exercised on a single GPU without any hang.
@@ -691,6 +753,54 @@ void comm_allreduce_nvls(int64_t id, torch::Tensor buf, int64_t mc_addr, double 
     comm::nvls_allreduce_kernel<true><<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   else
     comm::nvls_allreduce_kernel<false><<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
+  SCIRS_CHECK_LAUNCH();
+}
+
+// NVLS reduce-scatter: shard (fp32, n/world) = scale * sum over ranks of
+// this rank's shard of the full fp32 payload `full` (in a multicast-bound
+// symmetric buffer; mc_addr = its multicast address).
+void comm_reduce_scatter_nvls(int64_t id, torch::Tensor full, int64_t mc_addr, torch::Tensor shard, double scale,
+                              int64_t blocks, double timeout_s) {
+  CommState& cs = get_cs(id);
+  CHECK_DTYPE(full, at::kFloat);
+  CHECK_DTYPE(shard, at::kFloat);
+  CHECK_CONTIG(full);
+  CHECK_CONTIG(shard);
+  const long n = full.numel();
+  TORCH_CHECK(n % (4L * cs.world) == 0 && shard.numel() == n / cs.world, "shard must be n/world, n a multiple of 4*world");
+  TORCH_CHECK(mc_addr != 0 && mc_addr % 16 == 0 && reinterpret_cast<uintptr_t>(shard.data_ptr()) % 16 == 0,
+              "16-byte aligned shard and multicast address required");
+  if (n == 0) return;
+  comm::Args a = make_args(cs, n, timeout_s);
+  a.out32 = shard.data_ptr<float>();
+  a.scale = (float)scale;
+  a.mc = (unsigned long long)mc_addr;
+  c10::cuda::CUDAGuard guard(cs.device);
+  const int nb = pick_blocks(n / 4 / cs.world, cs.world, blocks);
+  comm::nvls_reduce_scatter_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
+  SCIRS_CHECK_LAUNCH();
+}
+
+// NVLS all-gather: full (bf16, n, multicast-bound; mc_addr) = concat over
+// ranks of shard (bf16, n/world).
+void comm_allgather_nvls(int64_t id, torch::Tensor shard, torch::Tensor full, int64_t mc_addr, int64_t blocks,
+                         double timeout_s) {
+  CommState& cs = get_cs(id);
+  CHECK_DTYPE(full, at::kBFloat16);
+  CHECK_DTYPE(shard, at::kBFloat16);
+  CHECK_CONTIG(full);
+  CHECK_CONTIG(shard);
+  const long n = full.numel();
+  TORCH_CHECK(n % (8L * cs.world) == 0 && shard.numel() == n / cs.world, "shard must be n/world, n a multiple of 8*world");
+  TORCH_CHECK(mc_addr != 0 && mc_addr % 16 == 0 && reinterpret_cast<uintptr_t>(shard.data_ptr()) % 16 == 0,
+              "16-byte aligned shard and multicast address required");
+  if (n == 0) return;
+  comm::Args a = make_args(cs, n, timeout_s);
+  a.in16 = reinterpret_cast<const __nv_bfloat16*>(shard.data_ptr());
+  a.mc = (unsigned long long)mc_addr;
+  c10::cuda::CUDAGuard guard(cs.device);
+  const int nb = pick_blocks(n / 8 / cs.world, cs.world, blocks);
+  comm::nvls_allgather_kernel<<<nb, comm::kCommThreads, 0, cur_stream()>>>(a);
   SCIRS_CHECK_LAUNCH();
 }
 

@@ -9,6 +9,10 @@ void comm_allreduce(int64_t id, torch::Tensor in32, torch::Tensor out32, double 
                     double timeout_s, int64_t algo);
 void comm_allreduce_nvls(int64_t id, torch::Tensor buf, int64_t mc_addr, double scale, int64_t blocks,
                          double timeout_s);
+void comm_reduce_scatter_nvls(int64_t id, torch::Tensor full, int64_t mc_addr, torch::Tensor shard, double scale,
+                              int64_t blocks, double timeout_s);
+void comm_allgather_nvls(int64_t id, torch::Tensor shard, torch::Tensor full, int64_t mc_addr, int64_t blocks,
+                         double timeout_s);
 void comm_reduce_scatter(int64_t id, torch::Tensor in32, torch::Tensor out32, double scale, int64_t blocks,
                          double timeout_s);
 void comm_allgather(int64_t id, torch::Tensor in16, torch::Tensor out16, int64_t blocks, double timeout_s);
@@ -30,6 +34,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("blocks"), py::arg("timeout_s"), py::arg("algo") = 0);
   m.def("allreduce_nvls", &scirs::comm_allreduce_nvls);
   m.def("reduce_scatter", &scirs::comm_reduce_scatter);
+  m.def("reduce_scatter_nvls", &scirs::comm_reduce_scatter_nvls);
+  m.def("allgather_nvls", &scirs::comm_allgather_nvls);
   m.def("allgather", &scirs::comm_allgather);
   m.def("timeout_probe", &scirs::comm_timeout_probe);
   m.def("sym_create", &scirs::sym_create);

