@@ -76,6 +76,54 @@ def test_gemm_large_m_persistent():
     assert rel_err(out, a.float() @ b.float().t()) < 1e-2
 
 
+# Shapes large enough for the 2-SM (cta_group::2) tiles: >= 74 tiles of 256 x 256.
+@pytest.mark.parametrize("M,N,K_", [(4096, 3072, 768), (4224, 3000, 512), (2304, 8192, 256)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_pair_layouts(M, N, K_, a_mn, b_mn):
+    a = rnd(K_, M, seed=11) if a_mn else rnd(M, K_, seed=11)
+    b = rnd(K_, N, scale=0.1, seed=12) if b_mn else rnd(N, K_, scale=0.1, seed=12)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, b, out, a_mn=a_mn, b_mn=b_mn)
+    ref = (a.t() if a_mn else a).float() @ (b if b_mn else b.t()).float()
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-2
+    single = torch.empty_like(out)
+    K.gemm(a, b, single, a_mn=a_mn, b_mn=b_mn, bn=128)  # the single-CTA kernel
+    assert rel_err(out, single) < 5e-3
+
+
+def test_gemm_pair_epilogues():
+    M, N, K_ = 4096, 3072, 768
+    a, w = rnd(M, K_, seed=13), rnd(N, K_, scale=0.05, seed=14)
+    bias, aux = rnd(N, seed=15), rnd(M, N, seed=16)
+    acc = a.float() @ w.float().t()
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, w, out, bias=bias)
+    assert rel_err(out, acc + bias.float()) < 1e-2
+    K.gemm(a, w, out, epi=K.EPI_RESID, bias=bias, aux=aux)
+    assert rel_err(out, acc + bias.float() + aux.float()) < 1e-2
+    pre = torch.empty_like(out)
+    K.gemm(a, w, out, epi=K.EPI_BIAS_GELU, bias=bias, out2=pre)
+    h = acc + bias.float()
+    assert rel_err(pre, h) < 1e-2 and rel_err(out, K.gelu_tanh(h)) < 1e-2
+    bg = torch.zeros(N, device=DEV)
+    K.gemm(a, w, out, epi=K.EPI_DGELU, aux=aux, bias_grad=bg)
+    want = acc * K.gelu_tanh_grad(aux.float())
+    assert rel_err(out, want) < 1e-2
+    assert rel_err(bg, out.float().sum(0)) < 1e-2
+    # fp32 weight gradient over a long token dimension (split-K with TMA reduce-add)
+    dy, x = rnd(16384, 768, seed=17), rnd(16384, 3072, seed=18)
+    g = torch.zeros(768, 3072, device=DEV)
+    K.gemm(dy, x, g, a_mn=True, b_mn=True, epi=K.EPI_F32)
+    assert rel_err(g, dy.float().t() @ x.float()) < 5e-3
+    K.gemm(dy, x, g, a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
+    assert rel_err(g, 2 * (dy.float().t() @ x.float())) < 5e-3
+    torch.cuda.synchronize()
+    from scirs_b200 import _ext
+
+    _ext.check_status()
+
+
 # ---------------------------------------------------------------------------- LayerNorm
 @pytest.mark.parametrize("D", [256, 768, 1024, 2048, 96])
 def test_layernorm(D):
