@@ -68,7 +68,30 @@ struct Cfg {
   static constexpr uint32_t IDESC_O = umma_idesc_bf16(BM, HD, 0, 1);
 };
 
-template <int HD, bool CAUSAL>
+// 2^x on the FMA pipe (for x <= 0, softmax arguments): x = n + f with n the
+// nearest integer (added into the low mantissa bits of 1.5 * 2^23) and f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients come from a
+// Remez fit of the relative error on [-0.5, 0.5] (max 7.5e-5, far below the
+// bf16 rounding of P); 2^n is applied by adding n to the exponent field.
+// Arguments below -125 return 0, as ex2 of a masked (-inf) score does.
+__device__ __forceinline__ float exp2_poly3(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float j = xc + 12582912.f;
+  const float f = xc - (j - 12582912.f);
+  float q = fmaf(5.517166906e-02f, f, 2.426111222e-01f);
+  q = fmaf(q, f, 6.932609855e-01f);
+  q = fmaf(q, f, 9.999280735e-01f);
+  const float r = __int_as_float(__float_as_int(q) + (__float_as_int(j) << 23));
+  return x < -125.f ? 0.f : r;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+template <int HD, bool CAUSAL, bool POLY = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -242,13 +265,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (key >= S || (CAUSAL && key > qrow)) sv[e] = -INFINITY;
         }
       }
+      // row max: four independent chains of 3-input max instructions
       float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int e = 4; e < BN; e += 4) {
-        m4[0] = fmaxf(m4[0], sv[e]);
-        m4[1] = fmaxf(m4[1], sv[e + 1]);
-        m4[2] = fmaxf(m4[2], sv[e + 2]);
-        m4[3] = fmaxf(m4[3], sv[e + 3]);
+      for (int e = 4; e < BN; e += 8) {
+        m4[0] = fmax3(m4[0], sv[e], sv[e + 4]);
+        m4[1] = fmax3(m4[1], sv[e + 1], sv[e + 5]);
+        m4[2] = fmax3(m4[2], sv[e + 2], sv[e + 6]);
+        m4[3] = fmax3(m4[3], sv[e + 3], sv[e + 7]);
       }
       const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
       // raise the reference max (and rescale O and l) only when needed
@@ -274,22 +298,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_st();
       }
       const float ref = (m_ref == -INFINITY) ? 0.f : m_ref;
-      float rs0 = 0.f, rs1 = 0.f;
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BN; c += 32) {
-        // 32 scores -> 16 packed bf16 pairs -> TMEM columns [c/2, c/2 + 16)
+        // 32 scores -> 16 packed bf16 pairs -> TMEM columns [c/2, c/2 + 16);
+        // with POLY every second exponential runs on the FMA pipe, halving
+        // the MUFU work
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const float p0 = ex2_fast(fmaf(sv[c + e], p.scale_log2, -ref));
-          const float p1 = ex2_fast(fmaf(sv[c + e + 1], p.scale_log2, -ref));
-          rs0 += p0;
-          rs1 += p1;
+          const float x1 = fmaf(sv[c + e + 1], p.scale_log2, -ref);
+          const float p1 = POLY ? exp2_poly3(x1) : ex2_fast(x1);
+          rs[(e >> 1) & 3] += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
         tmem_st_32x32b_x16(s_base + (c >> 1), pk);
       }
-      l += rs0 + rs1;
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -333,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // q/k/v/out: [B, S, H, HD] token-major views with contiguous heads; lse [B,H,S].
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                       bool causal, double scale) {
+                       bool causal, double scale, bool poly) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
   for (auto* t : {&q, &k, &v, &out}) {
@@ -361,16 +387,24 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   p.st = status_ptr(q.get_device());
   dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
   auto st = cur_stream();
-#define FA2T(HD_, C_)                                                          \
+#define FA2T(HD_, C_, P_)                                                      \
   {                                                                            \
-    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_>;                               \
+    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_>;                           \
     set_max_smem((const void*)kern, fa2t::Cfg<HD_>::SMEM);                     \
     kern<<<grid, fa2t::kThreads, fa2t::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);   \
   }
-  if (HD == 64) {
-    if (causal) FA2T(64, true) else FA2T(64, false)
+  if (poly) {
+    if (HD == 64) {
+      if (causal) FA2T(64, true, true) else FA2T(64, false, true)
+    } else {
+      if (causal) FA2T(128, true, true) else FA2T(128, false, true)
+    }
   } else {
-    if (causal) FA2T(128, true) else FA2T(128, false)
+    if (HD == 64) {
+      if (causal) FA2T(64, true, false) else FA2T(64, false, false)
+    } else {
+      if (causal) FA2T(128, true, false) else FA2T(128, false, false)
+    }
   }
 #undef FA2T
   SCIRS_CHECK_LAUNCH();

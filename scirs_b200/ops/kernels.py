@@ -265,8 +265,9 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
     """q/k/v/out: [B, S, H, D] token-major views (heads contiguous)."""
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        if ATTN_FWD_IMPL == "pingpong":
-            _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(causal), float(scale))
+        if ATTN_FWD_IMPL in ("pingpong", "pingpong_poly"):
+            _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(causal), float(scale),
+                                             ATTN_FWD_IMPL == "pingpong_poly")
         elif ATTN_FWD_IMPL == "tcgen05":
             _ext.kernels().flash_attn_fwd_tc(q, k, v, out, lse, bool(causal), float(scale))
         else:
