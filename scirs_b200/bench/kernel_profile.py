@@ -99,6 +99,16 @@ def op_gemm_fc1(t):
     K.gemm(t["x"], t["w_fc"], t["gout"], epi=K.EPI_BIAS_GELU, bias=t["b_fc"], out2=t["h"])
 
 
+def op_gemm_fc1_plain(t):
+    # same shape as fc1, no epilogue math (isolates the epilogue's cost)
+    K.gemm(t["x"], t["w_fc"], t["gout"])
+
+
+def op_gemm_fc2(t):
+    # FC2 forward: [M, 3072] x [768, 3072]^T + bias + residual (K = 3072)
+    K.gemm(t["gout"], t["w_fc"].view(D, F), t["att"], epi=K.EPI_RESID, bias=t["ln_b"], aux=t["dres"])
+
+
 def op_gemm_wgrad(t):
     K.gemm(t["dres"], t["gout"], t["wgrad"], a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
 
@@ -173,6 +183,8 @@ def op_adamw(t):
 # name -> (fn, FLOPs, algorithmic bytes)
 OPS = {
     "gemm_fc1": (op_gemm_fc1, 2 * M * D * F, (M * D + F * D + 2 * M * F) * 2),
+    "gemm_fc1_plain": (op_gemm_fc1_plain, 2 * M * D * F, (M * D + F * D + M * F) * 2),
+    "gemm_fc2": (op_gemm_fc2, 2 * M * D * F, (M * F + F * D + 2 * M * D) * 2),
     "gemm_wgrad": (op_gemm_wgrad, 2 * M * D * F, (M * D + M * F) * 2 + 2 * D * F * 4),
     "gemm_dgelu": (op_gemm_dgelu, 2 * M * D * F, (M * D + F * D + 2 * M * F) * 2),
     "attn_fwd": (op_attn_fwd, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),

@@ -17,6 +17,17 @@
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
+// Pair mode (PAIR = true, BN = 256): two CTAs of a cluster compute one
+// 256 x 256 tile with tcgen05.mma.cta_group::2. Each CTA loads its own 128
+// rows of A and its own 128 of the 256 columns of B (so each SM moves 32 KB
+// per 64-deep k-block instead of 48 KB: the single-CTA kernel is bound by
+// L2->SM bandwidth), both CTAs' TMA loads complete on the leader CTA's
+// full barrier (cp.async.bulk.tensor .cta_group::2, no multicast), the leader
+// alone issues the MMAs, and its commits arrive on both CTAs' empty / tfull
+// barriers (tcgen05.commit .multicast::cluster). Each CTA's TMEM holds its
+// 128 rows x 256 columns; the epilogue is unchanged, and both CTAs'
+// epilogue warps release the accumulator on the leader's tempty barrier.
+//
 // Reference parity: replaces the SIMT / WMMA GEMMs of the reference
 // (scirs2-core/src/gpu/kernels/gemm_f32.cu:4, scirs2-core/src/gpu/tensor_cores.rs:636,
 // scirs2-linalg/kernels/matmul_f32.cu:159) and the Dense layer's forward and
@@ -83,12 +94,12 @@ struct PeerMaps {
   CUtensorMap b[kMaxPeers];
 };
 
-template <int BN>
+template <int BN, bool PAIR = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // pair: this CTA's half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = PAIR ? 6 : ((BN == 256) ? 4 : 6);
   static constexpr int TMEM_COLS = 2 * BN;
   // Epilogue staging: per epilogue warp two 2 KB slots (32 rows x 64 bytes,
   // 64-byte swizzle) that feed TMA stores / reduce-adds.
@@ -134,6 +145,66 @@ __device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// ---- cluster-pair helpers (PAIR mode) ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `p` (a local shared variable) in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's smem whose completion is counted on the leader's
+// barrier (`bar_cluster`, a shared::cluster address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                   uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// commit the leader's MMAs to the barrier at the same offset in both CTAs
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                   "r"(smem_u32(bar)),
+               "h"((uint16_t)3)
+               : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 // Wait (bounded) until peer r's flag reaches this kernel's expected value;
 // afterwards the peer's data may be read, also by TMA (async proxy).
 __device__ __forceinline__ bool wait_peer(const Args& a, int r, volatile int* abort_flag) {
@@ -172,16 +243,24 @@ __device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap* local,
   return peers + r;
 }
 
-template <int BN, int A_MN, int B_MN, int EPI, bool PEER>
+template <int BN, int A_MN, int B_MN, int EPI, bool PEER, bool PAIR = false>
 __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorMap* pB, const CUtensorMap* pC,
                                           const CUtensorMap* pC2, const PeerMaps* pm, const Args& args) {
-  using C = Cfg<BN>;
+  static_assert(!PAIR || (BN == 256 && !PEER), "pair mode: BN 256, local operands");
+  using C = Cfg<BN, PAIR>;
   const CUtensorMap& tmA = *pA;
   const CUtensorMap& tmB = *pB;
   const CUtensorMap& tmC = *pC;
   const CUtensorMap& tmC2 = *pC2;
   constexpr int STAGES = C::STAGES;
-  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+  constexpr uint32_t IDESC = umma_idesc_bf16(PAIR ? 2 * BM : BM, BN, A_MN, B_MN);
+  // pair mode: CTA rank in the pair, the units are walked per cluster
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = crank == 0;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int row_sub = PAIR ? (int)crank * BM : 0;  // this CTA's rows within the unit's 256
+  constexpr int MT = PAIR ? 2 * BM : BM;            // rows per unit
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -204,7 +283,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(drain, 1);
     for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_bar[w], 1);
@@ -216,11 +295,19 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
     if (EPI == EPI_BIAS_GELU || EPI == EPI_RESID || EPI == EPI_DGELU) prefetch_tmap(&tmC2);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync_all();  // both CTAs' barriers exist before any remote arrive / TMA completion
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -230,7 +317,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
       int it = 0;
       bool ok = true;
       uint32_t ready = 0;  // peers whose data is known to be ready
-      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
+      const uint32_t full_leader0 = PAIR ? mapa_shared(&full[0], 0) : 0u;
+      for (int u = unit0; u < args.num_units && ok; u += ustep) {
         int m_blk, n_blk, split;
         decode_unit(args, u, m_blk, n_blk, split);
         const int kb0 = split * args.kb_per_split;
@@ -246,6 +334,26 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
           uint8_t* sB = sA + C::A_BYTES;
           const int kbp = args.kb_rot ? (kb + args.kb_rot) % args.num_kb : kb;
           // split coordinates (rewritten to the owner's local coordinate for peer operands)
+          if (PAIR) {
+            // this CTA's 128 rows of A and 128 columns of B; completion on the leader's barrier
+            const uint32_t fb = full_leader0 + s * 8;
+            const int arow = m_blk * MT + row_sub;
+            const int bcol = n_blk * BN + (int)crank * (BN / 2);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+            if (A_MN) {
+              tma_load_2d_pair(sA, &tmA, fb, arow, kbp * BK);
+              tma_load_2d_pair(sA + 8192, &tmA, fb, arow + 64, kbp * BK);
+            } else {
+              tma_load_2d_pair(sA, &tmA, fb, kbp * BK, arow);
+            }
+            if (B_MN) {
+              tma_load_2d_pair(sB, &tmB, fb, bcol, kbp * BK);
+              tma_load_2d_pair(sB + 8192, &tmB, fb, bcol + 64, kbp * BK);
+            } else {
+              tma_load_2d_pair(sB, &tmB, fb, kbp * BK, bcol);
+            }
+            continue;
+          }
           int ca = A_MN ? kbp * BK : m_blk * BM;
           int cb = kbp * BK;
           const CUtensorMap* mA =
@@ -270,8 +378,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
       }
       if (!ok) {
         *abort_flag = 1;
-        // Let copies already in flight land before the CTA exits.
-        for (int j = 1; j <= STAGES && it - j >= 0; ++j) {
+        // Let copies already in flight land before the CTA exits (pair mode:
+        // they complete on the leader's barriers; the final cluster barrier
+        // keeps both CTAs alive until then).
+        for (int j = 1; j <= STAGES && it - j >= 0 && (!PAIR || leader); ++j) {
           const int i2 = it - j;
           mbar_wait(&full[i2 % STAGES], (i2 / STAGES) & 1, nullptr, 0, nullptr);
         }
@@ -279,10 +389,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || leader)) {
       int it = 0, local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x, ++local) {
+      for (int u = unit0; u < args.num_units && ok; u += ustep, ++local) {
         int m_blk, n_blk, split;
         decode_unit(args, u, m_blk, n_blk, split);
         const int kb0 = split * args.kb_per_split;
@@ -311,16 +421,28 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
                                         : umma_desc_sw128(a_base + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_base + kk * 2048, 8192, 1024)
                                         : umma_desc_sw128(b_base + kk * 32, 16, 1024);
-            tc_mma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if (PAIR)
+              tc_mma_f16_ss_pair(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else
+              tc_mma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&empty[s]);
+          if (PAIR)
+            tc_commit_pair(&empty[s]);
+          else
+            tc_commit(&empty[s]);
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if (PAIR)
+          tc_commit_pair(&tfull[acc]);
+        else
+          tc_commit(&tfull[acc]);
       }
       // Drain: make sure every MMA this thread issued has completed before
       // TMEM is released at the end of the kernel.
-      tc_commit(drain);
+      if (PAIR)
+        tc_commit_pair_local(drain);
+      else
+        tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 0, nullptr);
     }
   } else {
@@ -338,12 +460,20 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
     uint64_t* my_aux_bar = &aux_bar[warp - 2];
     uint32_t aux_phase = 0;
     int local = 0;
-    for (int u = blockIdx.x; u < args.num_units; u += gridDim.x, ++local) {
+    // the accumulator is released on the leader's tempty barrier (pair mode)
+    const uint32_t tempty_leader0 = PAIR ? mapa_shared(&tempty[0], 0) : 0u;
+    auto release_acc = [&](int acc) {
+      if (PAIR)
+        mbar_arrive_cluster(tempty_leader0 + acc * 8);
+      else
+        mbar_arrive(&tempty[acc]);
+    };
+    for (int u = unit0; u < args.num_units; u += ustep, ++local) {
       int m_blk, n_blk, split;
       decode_unit(args, u, m_blk, n_blk, split);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      const int row0 = m_blk * BM + q * 32;
+      const int row0 = m_blk * MT + row_sub + q * 32;
       const int row = row0 + lane;
       const bool row_ok = row < args.M;
       // number of 32-column chunks of this warp's half that lie inside N
@@ -358,7 +488,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
       if (nch == 0) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (lane == 0) release_acc(acc);
       }
 #pragma unroll 1
       for (int ci = 0; ci < nch; ++ci) {
@@ -372,7 +502,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
           // so the MMA warp can start the next tile while we finish the math
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if (lane == 0) release_acc(acc);
         }
         float v[32];
 #pragma unroll
@@ -514,10 +644,16 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync_all();  // no CTA leaves while its pair still signals its barriers / reads its smem
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if (PEER && args.sig_flags[0] != nullptr && threadIdx.x == 0) {
     // last CTA to finish tells every peer that this rank's output is complete
@@ -536,6 +672,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const Args args) {
   gemm_body<BN, A_MN, B_MN, EPI, false>(&tmA, &tmB, &tmC, &tmC2, nullptr, args);
+}
+
+// Pair variant: clusters of two CTAs share each 256 x 256 tile (cta_group::2).
+template <int A_MN, int B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
+                     const Args args) {
+  gemm_body<256, A_MN, B_MN, EPI, false, true>(&tmA, &tmB, &tmC, &tmC2, nullptr, args);
 }
 
 // Tensor-parallel variant: operands may be split over the ranks' symmetric
@@ -624,6 +769,73 @@ static void launch_bn(int a_mn, int b_mn, int epi, const Maps& m, const Args& ar
   else if (!a_mn && b_mn) launch_epi<BN, 0, 1>(epi, m, args, grid, s);
   else if (a_mn && !b_mn) launch_epi<BN, 1, 0>(epi, m, args, grid, s);
   else launch_epi<BN, 1, 1>(epi, m, args, grid, s);
+}
+
+// Clusters of two that can be resident at once (SMs of a GPC pair up; an odd
+// SM count leaves one out). A persistent grid larger than this would run its
+// last clusters after the others finished.
+static int pair_slots(int dev) {
+  static int slots[64] = {0};
+  if (slots[dev] == 0) {
+    auto kern = gemm_pair_kernel<0, 0, EPI_BF16>;
+    set_max_smem(reinterpret_cast<const void*>(kern), Cfg<256, true>::SMEM);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms(dev), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg<256, true>::SMEM;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms(dev) / 2;
+    }
+    slots[dev] = std::min(n, num_sms(dev) / 2);
+  }
+  return slots[dev];
+}
+
+template <int A_MN, int B_MN, int EPI>
+static void launch_pair_t(const Maps& m, const Args& args, int grid, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  set_max_smem(reinterpret_cast<const void*>(kern), Cfg<256, true>::SMEM);
+  kern<<<grid, kThreads, Cfg<256, true>::SMEM, stream>>>(m.a, m.b, m.c, m.c2, args);
+  SCIRS_CHECK_LAUNCH();
+}
+
+template <int A_MN, int B_MN>
+static void launch_pair_epi(int epi, const Maps& m, const Args& args, int grid, cudaStream_t s) {
+  switch (epi) {
+    case EPI_BF16: launch_pair_t<A_MN, B_MN, EPI_BF16>(m, args, grid, s); break;
+    case EPI_BIAS_GELU: launch_pair_t<A_MN, B_MN, EPI_BIAS_GELU>(m, args, grid, s); break;
+    case EPI_RESID: launch_pair_t<A_MN, B_MN, EPI_RESID>(m, args, grid, s); break;
+    case EPI_DGELU: launch_pair_t<A_MN, B_MN, EPI_DGELU>(m, args, grid, s); break;
+    case EPI_F32: launch_pair_t<A_MN, B_MN, EPI_F32>(m, args, grid, s); break;
+    default: TORCH_CHECK(false, "bad epilogue ", epi);
+  }
+}
+
+static void launch_pair(int a_mn, int b_mn, int epi, const Maps& m, const Args& args, int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) launch_pair_epi<0, 0>(epi, m, args, grid, s);
+  else if (!a_mn && b_mn) launch_pair_epi<0, 1>(epi, m, args, grid, s);
+  else if (a_mn && !b_mn) launch_pair_epi<1, 0>(epi, m, args, grid, s);
+  else launch_pair_epi<1, 1>(epi, m, args, grid, s);
+}
+
+// 2-CTA (cta_group::2) tiles for large GEMMs: SCIRS_GEMM_PAIR=0 disables,
+// =1 enables (default), read once per process.
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SCIRS_GEMM_PAIR");
+    v = (e == nullptr) ? 1 : atoi(e);
+  }
+  return v != 0;
 }
 
 template <int A_MN, int B_MN, int EPI>
@@ -921,6 +1133,12 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     if (N <= 128 || (!can_split && cost(128) < cost(256))) BN = 128;
   }
   if (bn_force == 128 || bn_force == 256) BN = (int)bn_force;
+  // Pair mode (two SMs per 256 x 256 tile) when the tiles are wide and there
+  // are enough of them to fill the GPU with pairs.
+  const bool pair = pair_enabled() && BN == 256 && bn_force != 128 && M >= 2 * BM &&
+                    (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256) >= sms / 2;
+  if (pair) args.m_blocks = (int)((M + 2 * BM - 1) / (2 * BM));
+  const int usms = pair ? pair_slots(dev) : sms;  // scheduling slots: resident SM pairs in pair mode
   args.n_blocks = (int)((N + BN - 1) / BN);
   const long tiles = (long)args.m_blocks * args.n_blocks;
 
@@ -928,15 +1146,15 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   if (can_split) {
     if (splits > 0) {
       sp = (int)splits;
-    } else if (tiles < 2L * sms) {
+    } else if (tiles < 2L * usms) {
       // choose the split that fills whole waves best (mild penalty per split)
       const int max_sp = std::max(1, std::min(16, args.num_kb / 4));
       double best = -1e9;
       for (int s = 1; s <= max_sp; ++s) {
         const double units = (double)tiles * s;
-        const double waves = std::ceil(units / sms);
-        const double eff = units / (waves * sms);
-        const double score = eff - 0.01 * s - (units < sms ? 0.5 : 0.0);
+        const double waves = std::ceil(units / usms);
+        const double eff = units / (waves * usms);
+        const double score = eff - 0.01 * s - (units < usms ? 0.5 : 0.0);
         if (score > best) {
           best = score;
           sp = s;
@@ -951,7 +1169,7 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   args.atomic_out = (epi == EPI_F32 && (accumulate || sp > 1)) ? 1 : 0;
   if (epi == EPI_F32 && sp > 1 && !accumulate) out.zero_();
   args.num_units = (int)(tiles * sp);
-  const int grid = (int)std::min<long>(args.num_units, sms);
+  const int grid = pair ? 2 * (int)std::min<long>(args.num_units, usms) : (int)std::min<long>(args.num_units, sms);
 
   // Operand maps (SWIZZLE_128B, 64-element inner boxes) and output maps
   // (32x32 bf16 or 32x16 fp32 boxes, SWIZZLE_64B, matching the staging slots).
@@ -960,7 +1178,7 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   maps.a = a_mn ? get_tmap(a.data_ptr(), (uint64_t)M, (uint64_t)K, lda_b, 64, 64)
                 : get_tmap(a.data_ptr(), (uint64_t)K, (uint64_t)M, lda_b, 64, BM);
   maps.b = b_mn ? get_tmap(b.data_ptr(), (uint64_t)N, (uint64_t)K, ldb_b, 64, 64)
-                : get_tmap(b.data_ptr(), (uint64_t)K, (uint64_t)N, ldb_b, 64, (uint32_t)BN);
+                : get_tmap(b.data_ptr(), (uint64_t)K, (uint64_t)N, ldb_b, 64, (uint32_t)(pair ? BN / 2 : BN));
   if (epi == EPI_F32) {
     maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)out.stride(0) * 4, 16, 32,
                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -979,7 +1197,8 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   }
 
   cudaStream_t s = cur_stream();
-  if (BN == 256) launch_bn<256>((int)a_mn, (int)b_mn, (int)epi, maps, args, grid, s);
+  if (pair) launch_pair((int)a_mn, (int)b_mn, (int)epi, maps, args, grid, s);
+  else if (BN == 256) launch_bn<256>((int)a_mn, (int)b_mn, (int)epi, maps, args, grid, s);
   else launch_bn<128>((int)a_mn, (int)b_mn, (int)epi, maps, args, grid, s);
 }
 
