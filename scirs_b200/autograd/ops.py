@@ -25,6 +25,7 @@ OPS = {
     "constant": lambda value: value if isinstance(value, torch.Tensor) else torch.as_tensor(value, dtype=torch.float32),
     "zeros": lambda shape: torch.zeros(shape),
     "ones": lambda shape: torch.ones(shape),
+    "identity": lambda x: x,
     "add": torch.add,
     "sub": torch.sub,
     "mul": torch.mul,

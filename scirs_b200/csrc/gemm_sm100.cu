@@ -490,13 +490,25 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
         __syncwarp();
         if (lane == 0) release_acc(acc);
       }
-#pragma unroll 1
-      for (int ci = 0; ci < nch; ++ci) {
+      // TMEM reads are software-pipelined: chunk ci+1 is loaded while chunk
+      // ci is processed (two register buffers; the dGELU epilogue, which
+      // needs its registers for the column-sum butterfly, loads one at a time)
+      constexpr bool PREFETCH = (EPI != EPI_DGELU);
+      uint32_t rb0[32], rb1[32];
+      if (PREFETCH && nch > 0) tmem_ld_32x32b_x32(trow + c_begin, rb0);
+#pragma unroll
+      for (int ci = 0; ci < BN / 64; ++ci) {
+        if (ci >= nch) break;
         const int c = c_begin + ci * 32;
         const int col0 = n_blk * BN + c;
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(trow + c, r);
-        tc_wait_ld();
+        uint32_t* r = (ci & 1) ? rb1 : rb0;
+        if (PREFETCH) {
+          tc_wait_ld_regs(r);
+          if (ci + 1 < nch) tmem_ld_32x32b_x32(trow + c + 32, (ci & 1) ? rb0 : rb1);
+        } else {
+          tmem_ld_32x32b_x32(trow + c, r);
+          tc_wait_ld_regs(r);
+        }
         if (ci == nch - 1) {
           // last TMEM read of this tile by this warp: release the accumulator
           // so the MMA warp can start the next tile while we finish the math
