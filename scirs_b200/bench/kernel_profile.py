@@ -138,6 +138,30 @@ def op_attn_fwd_pp_poly_hd128(t):
     K.flash_attn_fwd_impl("pingpong_poly", q, k, v, t["att"].view(B, S, H // 2, 2 * HD), t["lse128"], causal=True)
 
 
+def attn_fwd_pp_trace(t, hd=64):
+    """Per-phase clock64 cycles of the ping-pong forward's softmax threads
+    (one per tile per CTA), averaged over CTAs and per key block."""
+    from .. import _ext
+
+    if hd == 64:
+        q, k, v = _attn_views(t)
+        att, lse = t["att"].view(B, S, H, HD), t["lse"]
+    else:
+        q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
+        att, lse = t["att"].view(B, S, H // 2, 2 * HD), t["lse128"]
+    nh = q.shape[2]
+    grid = ((S + 255) // 256) * B * nh
+    tr = torch.zeros(grid * 2 * 5, dtype=torch.int64, device=q.device)
+    _ext.kernels().flash_attn_fwd_pp(q, k, v, att, lse, True, float(q.shape[-1]) ** -0.5, False, tr)
+    torch.cuda.synchronize()
+    ph = tr.view(grid, 2, 5).double()
+    nq = (S + 255) // 256
+    avg_blocks = sum(2 * qp + 1 + tt for qp in range(nq) for tt in (0, 1)) / (2 * nq)  # causal key blocks per tile
+    per_tile = ph.sum(0).sum(0) / (grid * 2)
+    names = ["wait_S", "tmem_load", "max_rescale", "exp_store_P", "signal"]
+    return {n: round(float(x) / avg_blocks, 1) for n, x in zip(names, per_tile)}
+
+
 def op_attn_fwd_hd128(t):
     q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
     K.flash_attn_fwd_impl("tcgen05", q, k, v, t["att"].view(B, S, H // 2, 2 * HD), t["lse128"], causal=True)
@@ -207,6 +231,8 @@ def main():
     ap.add_argument("--rounds", type=int, default=3)
     ap.add_argument("--iters", type=int, default=1, help="back-to-back launches timed per op per round")
     ap.add_argument("--ops", default=",".join(OPS))
+    ap.add_argument("--trace-attn", action="store_true",
+                    help="print the ping-pong forward's per-phase cycles per key block (head_dim 64 and 128)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     t = build(dev)
@@ -215,6 +241,11 @@ def main():
     tf_peak = peaks.get("bf16_tflops", 1590.0)
     bw_peak = peaks.get("hbm_gbs", 6650.0)
     ms = {}
+    if args.trace_attn:
+        for hd in (64, 128):
+            attn_fwd_pp_trace(t, hd)  # warm-up
+            print(json.dumps({"trace": f"attn_fwd_pp_hd{hd}", "cycles_per_key_block": attn_fwd_pp_trace(t, hd)}),
+                  flush=True)
     for _ in range(args.rounds):
         for n in names:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -49,6 +49,10 @@ struct Params {
   int B, H, S;
   float scale_log2;
   DevStatus* st;
+  // optional phase timing (clock64 cycles summed over the loop) of one
+  // softmax thread per tile: [CTA][tile][wait S, TMEM load, max/rescale,
+  // exp + P store, signal]; nullptr = off
+  unsigned long long* trace;
 };
 
 template <int HD>
@@ -246,9 +250,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_nkv = t ? nkv1 : nkv0;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
+    const bool tr = p.trace != nullptr && q == 0 && lane == 0;
+    unsigned long long ph[5] = {0, 0, 0, 0, 0};
+    long long tk = tr ? clock64() : 0;
+    auto lap = [&](int k) {
+      if (tr) {
+        const long long now = clock64();
+        ph[k] += (unsigned long long)(now - tk);
+        tk = now;
+      }
+    };
     for (int j = 0; j < my_nkv && ok; ++j) {
       if (!mbar_wait(&s_full[t], j & 1, p.st, 55, abort_flag)) { ok = false; break; }
       tc_fence_after();
+      lap(0);
       float sv[BN];
       {
         uint32_t* u = reinterpret_cast<uint32_t*>(sv);
@@ -256,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BN; c += 32) tmem_ld_32x32b_x32(s_base + c, u + c);
         tc_wait_ld();
       }
+      lap(1);
       const int kv0 = j * BN;
       const bool mask = (kv0 + BN > S) || (CAUSAL && kv0 + BN > q0 + t * BM);
       if (mask) {
@@ -297,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_wait_st();
       }
+      lap(2);
       const float ref = (m_ref == -INFINITY) ? 0.f : m_ref;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -317,9 +334,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tc_wait_st();
+      lap(3);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
+      lap(4);
+    }
+    if (tr) {
+      unsigned long long* dst = p.trace + ((long)(blockIdx.y * gridDim.x + blockIdx.x) * 2 + t) * 5;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) dst[k] = ph[k];
     }
     if (ok && my_nkv > 0 && mbar_wait(&o_final[t], 0, p.st, 56, abort_flag)) {
       tc_fence_after();
@@ -359,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // q/k/v/out: [B, S, H, HD] token-major views with contiguous heads; lse [B,H,S].
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                       bool causal, double scale, bool poly) {
+                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
   for (auto* t : {&q, &k, &v, &out}) {
@@ -386,6 +410,12 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
   dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                    trace->numel() >= (long)grid.x * grid.y * 2 * 5,
+                "trace: int64 [grid, 2, 5]");
+    p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
+  }
   auto st = cur_stream();
 #define FA2T(HD_, C_, P_)                                                      \
   {                                                                            \
