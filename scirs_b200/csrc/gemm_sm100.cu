@@ -985,6 +985,8 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     }
     args.C = out.data_ptr();
     args.ldc = out.stride(0);
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(args.C) & 15) == 0 && args.ldc % 8 == 0,
+                "out must be 16-byte aligned with rows a multiple of 8 elements");
     if (epi == EPI_F32)
       maps.c = get_tmap(out.data_ptr(), (uint64_t)N, (uint64_t)M, (uint64_t)out.stride(0) * 4, 16, 32,
                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -1001,6 +1003,7 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     TORCH_CHECK(out2.has_value() && out2->defined() && out2->size(0) == M && out2->size(1) == N, "gelu needs out2");
     args.C2 = out2->data_ptr();
     args.ldc2 = out2->stride(0);
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(args.C2) & 15) == 0 && args.ldc2 % 8 == 0, "out2 must be 16-byte aligned");
     maps.c2 = get_tmap(args.C2, (uint64_t)N, (uint64_t)M, (uint64_t)args.ldc2 * 2, 32, 32,
                        CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_64B);
   }
@@ -1129,6 +1132,7 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
                 "out2 must be [M,N]");
     args.C2 = out2->data_ptr();
     args.ldc2 = out2->stride(0);
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(args.C2) & 15) == 0, "out2 must be 16-byte aligned");
   }
 
   // Tile width: BN=256 unless BN=128 gives fewer waves for this shape.

@@ -26,7 +26,7 @@ OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
 # (warp-level mma.sync kernel). Both are sm_100a kernels of this library.
 # Attention forward: "tcgen05" (one 128-query tile per CTA, O in registers),
 # "pingpong" (two tiles per CTA, O in TMEM, P through TMEM) or "mma".
-ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "tcgen05")
+ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "pingpong")
 # Attention backward: "tcgen05" (head_dim 64; other head dims use mma) or "mma".
 ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05")
 

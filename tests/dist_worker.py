@@ -114,6 +114,32 @@ def case_nvls():
     return res
 
 
+def case_ring_attn():
+    from scirs_b200.ops import kernels as K
+    from scirs_b200.parallel.context_parallel import ring_attention
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, Sc, H, D = 2, 256, 4, 64
+    g = torch.Generator().manual_seed(5)
+    q, k, v, do = (torch.randn(B, world * Sc, H, D, generator=g).to(dev, torch.bfloat16) for _ in range(4))
+    sl = slice(rank * Sc, (rank + 1) * Sc)
+    res = {}
+    for causal in (True, False):
+        ql, kl, vl = (t[:, sl].contiguous().requires_grad_(True) for t in (q, k, v))
+        o, lse = ring_attention(ql, kl, vl, causal=causal)
+        o.backward(do[:, sl].contiguous())
+        qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+        o_ref, lse_ref = K.attention_reference(qf, kf, vf, causal, D ** -0.5)
+        o_ref.backward(do.float())
+        rel = lambda a, b: float((a.float() - b).norm() / (b.norm() + 1e-12))  # noqa: E731
+        res[f"ring_causal{int(causal)}"] = {
+            "o": rel(o, o_ref[:, sl].detach()), "lse": float((lse - lse_ref[:, :, sl]).abs().max()),
+            "dq": rel(ql.grad, qf.grad[:, sl]), "dk": rel(kl.grad, kf.grad[:, sl]), "dv": rel(vl.grad, vf.grad[:, sl])}
+    _ext.check_status()
+    return res
+
+
 def case_dp_gpt():
     """DP training with the fused all-reduce == single-process training on the
     concatenated global batch (same weights, same data)."""
@@ -243,7 +269,7 @@ def case_tp_decoder():
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
-    res = {"collectives": case_collectives, "nvls": case_nvls, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
+    res = {"collectives": case_collectives, "nvls": case_nvls, "ring_attn": case_ring_attn, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
            "tp_decoder": case_tp_decoder}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))

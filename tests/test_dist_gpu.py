@@ -52,6 +52,14 @@ def test_nvls_allreduce_2gpu(tmp_path):
         assert v["max_err"] < tol, (k, v)
 
 
+def test_ring_attention_2gpu(tmp_path):
+    res = _run("ring_attn", tmp_path, port=29616)
+    for k, v in res.items():
+        for name in ("o", "dq", "dk", "dv"):
+            assert v[name] < 2e-2, (k, name, v)
+        assert v["lse"] < 2e-2, (k, v)
+
+
 def test_data_parallel_gpt_2gpu(tmp_path):
     res = _run("dp_gpt", tmp_path, port=29612)
     ref = res["single"]["losses"]
