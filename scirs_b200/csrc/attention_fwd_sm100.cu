@@ -95,7 +95,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-template <int HD, bool CAUSAL, bool POLY = false>
+template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -250,11 +250,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_nkv = t ? nkv1 : nkv0;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    const bool tr = p.trace != nullptr && q == 0 && lane == 0;
+    const bool tr = TRACE && q == 0 && lane == 0;
     unsigned long long ph[5] = {0, 0, 0, 0, 0};
-    long long tk = tr ? clock64() : 0;
+    long long tk = (TRACE && tr) ? clock64() : 0;
     auto lap = [&](int k) {
-      if (tr) {
+      if (TRACE && tr) {
         const long long now = clock64();
         ph[k] += (unsigned long long)(now - tk);
         tk = now;
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[t]);
       lap(4);
     }
-    if (tr) {
+    if (TRACE && tr) {
       unsigned long long* dst = p.trace + ((long)(blockIdx.y * gridDim.x + blockIdx.x) * 2 + t) * 5;
 #pragma unroll
       for (int k = 0; k < 5; ++k) dst[k] = ph[k];
@@ -417,25 +417,28 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
   }
   auto st = cur_stream();
-#define FA2T(HD_, C_, P_)                                                      \
+#define FA2T(HD_, C_, P_, R_)                                                  \
   {                                                                            \
-    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_>;                           \
+    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_>;                       \
     set_max_smem((const void*)kern, fa2t::Cfg<HD_>::SMEM);                     \
     kern<<<grid, fa2t::kThreads, fa2t::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);   \
   }
-  if (poly) {
-    if (HD == 64) {
-      if (causal) FA2T(64, true, true) else FA2T(64, false, true)
-    } else {
-      if (causal) FA2T(128, true, true) else FA2T(128, false, true)
-    }
-  } else {
-    if (HD == 64) {
-      if (causal) FA2T(64, true, false) else FA2T(64, false, false)
-    } else {
-      if (causal) FA2T(128, true, false) else FA2T(128, false, false)
-    }
+#define FA2T_HD(P_, R_)                                                        \
+  if (HD == 64) {                                                              \
+    if (causal) FA2T(64, true, P_, R_) else FA2T(64, false, P_, R_)            \
+  } else {                                                                     \
+    if (causal) FA2T(128, true, P_, R_) else FA2T(128, false, P_, R_)          \
   }
+  const bool traced = p.trace != nullptr;
+  TORCH_CHECK(!(traced && poly), "the trace is available for the plain variant");
+  if (traced) {
+    FA2T_HD(false, true)
+  } else if (poly) {
+    FA2T_HD(true, false)
+  } else {
+    FA2T_HD(false, false)
+  }
+#undef FA2T_HD
 #undef FA2T
   SCIRS_CHECK_LAUNCH();
 }

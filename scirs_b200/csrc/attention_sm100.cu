@@ -398,12 +398,15 @@ void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
 //                dV  += P^T dO_i       (TMEM [256,320), accumulated over i)
 //                dK  += dS^T Q_i       (TMEM [320,384), accumulated over i)
 //                dQ_i = dS K           (TMEM [384,448); A = dS^T read MN-major)
-//   warps 2-5  dS warps: thread = key row. P = exp2(S*scale*log2e - LSE*log2e)
-//              (masked to 0), dS = P (dP - delta); both stored as 128B-swizzled
-//              K-major bf16 tiles [key][q].
-//   warps 6-9  dQ warps: TMEM dQ_i -> 128B-swizzled fp32 smem slots -> TMA
-//              reduce-add into the fp32 dQ accumulator [B*S, H*HD]; at the
-//              end they write dK * scale and dV (bf16).
+//   warps 2-9  dS: thread = key row, warps 2-5 take queries [0, 64) of the
+//              block and warps 6-9 queries [64, 128) (two warps per scheduler
+//              share the exponentials). P = exp2(S*scale*log2e - LSE*log2e)
+//              (masked to 0), dS = P (dP - delta); both stored as
+//              128B-swizzled K-major bf16 tiles [key][q].
+//   warps 6-9  also move dQ_i: TMEM -> 128B-swizzled fp32 smem slots -> TMA
+//              reduce-add into the fp32 dQ accumulator [B*S, H*HD] (while the
+//              tensor core starts the next block); at the end they write
+//              dK * scale and dV (bf16).
 // dQ is scaled by the softmax scale in the follow-up conversion kernel.
 // ===========================================================================
 namespace fabw {
@@ -483,8 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qdo_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
+    mbar_init(s_free, 8);
+    mbar_init(p_full, 8);
     mbar_init(pt_free, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
@@ -578,8 +581,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 0, nullptr);
     }
-  } else if (warp < 6) {
-    // ------------------------------------------------------------ dS warps
+  } else {
+    // ------------------------------------------------------------ dS (+ dQ) warps
+    // All eight warps compute P / dS for each query block: warps 2-5 the
+    // first 64 queries of every key row, warps 6-9 the other 64 (two warps
+    // per scheduler share the MUFU / issue work). Warps 6-9 then also copy
+    // the block's dQ out of TMEM while the tensor core starts the next block.
+    const bool dq_role = warp >= 6;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;   // key row in the tile
     const int key = k0 + r;
@@ -590,23 +598,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* pt_row = smem + OFF_PT + r * 128;
     uint8_t* ds_row = smem + OFF_DST + r * 128;
     const float LOG2E = 1.4426950408889634f;
+    const int c_begin = dq_role ? BQ / 2 : 0;
+    uint8_t* slot0 = smem + OFF_DQS + (dq_role ? (warp - 6) : 0) * 8192;
+    uint8_t* slot1 = slot0 + 4096;
+    bool ok = true;
     for (int i = i0, n = 0; i < nq; ++i, ++n) {
       const int q0 = i * BQ;
       float* sL = sLD + (n & 1) * 256;
-      {
+      if (!dq_role) {
         const int q = q0 + t128;
         sL[t128] = q < S ? lse_g[q] * LOG2E : 0.f;
         sL[128 + t128] = q < S ? del_g[q] : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ld_bar[n & 1]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ld_bar[n & 1]);
-      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) break;
-      if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) break;
-      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) break;
+      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const bool need_mask = (q0 + BQ > S) || (k0 + BK > S) || (CAUSAL && i == i0);
 #pragma unroll 1
-      for (int c = 0; c < BQ; c += 32) {
+      for (int c = c_begin; c < c_begin + BQ / 2; c += 32) {
         uint32_t sv[32], dv[32];
         tmem_ld_32x32b_x32(lane_base + T_S + c, sv);
         tmem_ld_32x32b_x32(lane_base + T_DP + c, dv);
@@ -643,15 +655,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(s_free);
         mbar_arrive(p_full);
       }
-    }
-  } else {
-    // ------------------------------------------------------------ dQ warps
-    const int q4 = warp & 3;                 // TMEM lane quarter (query rows of dQ)
-    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
-    uint8_t* slot0 = smem + OFF_DQS + (warp - 6) * 8192;
-    uint8_t* slot1 = slot0 + 4096;
-    bool ok = true;
-    for (int i = i0, n = 0; i < nq; ++i, ++n) {
+      if (!dq_role) continue;
+      // ---- dQ_i: TMEM -> fp32 smem slots -> TMA reduce-add into dq_acc
       if (!mbar_wait(dq_full, n & 1, p.st, 58, abort_flag)) { ok = false; break; }
       tc_fence_after();
       uint32_t a0[32], a1[32];
@@ -682,33 +687,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_commit();
       }
     }
-    if (lane == 0) tma_store_wait0();
-    __syncwarp();
-    // dK, dV (TMEM lane = key row)
-    if (ok && mbar_wait(dkv_full, 0, p.st, 59, abort_flag)) {
-      tc_fence_after();
-      const int r = q4 * 32 + lane;
-      const int key = k0 + r;
-      uint32_t kv[32];
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        bf16* dst = which ? (p.dv + (long)(row_base + key) * p.dv_rs + col)
-                          : (p.dk + (long)(row_base + key) * p.dk_rs + col);
-        const float sc = which ? 1.f : p.scale;
-#pragma unroll
-        for (int c = 0; c < HD; c += 32) {
-          tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
-          tc_wait_ld();
-          if (key < S) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
-              uint4 o;
-              o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
-              o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
-              o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
-              o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
-              *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+    if (dq_role) {
+      if (lane == 0) tma_store_wait0();
+      __syncwarp();
+      // dK, dV (TMEM lane = key row)
+      if (ok && mbar_wait(dkv_full, 0, p.st, 59, abort_flag)) {
+        tc_fence_after();
+        const int r = q4 * 32 + lane;
+        const int key = k0 + r;
+        uint32_t kv[32];
+  #pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          bf16* dst = which ? (p.dv + (long)(row_base + key) * p.dv_rs + col)
+                            : (p.dk + (long)(row_base + key) * p.dk_rs + col);
+          const float sc = which ? 1.f : p.scale;
+  #pragma unroll
+          for (int c = 0; c < HD; c += 32) {
+            tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
+            tc_wait_ld();
+            if (key < S) {
+  #pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
+                uint4 o;
+                o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
+                o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
+                o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
+                o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
+                *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+              }
             }
           }
         }
