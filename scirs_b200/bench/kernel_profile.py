@@ -133,6 +133,16 @@ def op_attn_fwd_pp_poly(t):
     K.flash_attn_fwd_impl("pingpong_poly", q, k, v, t["att"].view(B, S, H, HD), t["lse"], causal=True)
 
 
+def op_attn_fwd_pp_x2(t):
+    q, k, v = _attn_views(t)
+    K.flash_attn_fwd_impl("pingpong_x2", q, k, v, t["att"].view(B, S, H, HD), t["lse"], causal=True)
+
+
+def op_attn_fwd_pp_x2_hd128(t):
+    q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
+    K.flash_attn_fwd_impl("pingpong_x2", q, k, v, t["att"].view(B, S, H // 2, 2 * HD), t["lse128"], causal=True)
+
+
 def op_attn_fwd_pp_poly_hd128(t):
     q, k, v = t["qkv"].view(B, S, 3, H // 2, 2 * HD).unbind(2)
     K.flash_attn_fwd_impl("pingpong_poly", q, k, v, t["att"].view(B, S, H // 2, 2 * HD), t["lse128"], causal=True)
@@ -213,6 +223,8 @@ OPS = {
     "gemm_dgelu": (op_gemm_dgelu, 2 * M * D * F, (M * D + F * D + 2 * M * F) * 2),
     "attn_fwd": (op_attn_fwd, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_fwd_pp": (op_attn_fwd_pp, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
+    "attn_fwd_pp_x2": (op_attn_fwd_pp_x2, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
+    "attn_fwd_pp_x2_hd128": (op_attn_fwd_pp_x2_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_fwd_pp_poly": (op_attn_fwd_pp_poly, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_fwd_pp_poly_hd128": (op_attn_fwd_pp_poly_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),
     "attn_fwd_hd128": (op_attn_fwd_hd128, 4 * B * H * S * S * HD // 2, (4 * M * D) * 2),

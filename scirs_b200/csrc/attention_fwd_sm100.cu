@@ -89,13 +89,34 @@ __device__ __forceinline__ float exp2_poly3(float x) {
   return x < -125.f ? 0.f : r;
 }
 
+// Packed fp32 pairs (Blackwell f32x2 instructions): one FFMA2 / FADD2 does
+// the work of two scalar instructions.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
 }
 
-template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false>
+template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false, bool X2 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -316,23 +337,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       lap(2);
       const float ref = (m_ref == -INFINITY) ? 0.f : m_ref;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      uint64_t rs2[2] = {0ull, 0ull};  // X2: packed row-sum accumulators
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nref2 = f2_pack(-ref, -ref);
 #pragma unroll
       for (int c = 0; c < BN; c += 32) {
         // 32 scores -> 16 packed bf16 pairs -> TMEM columns [c/2, c/2 + 16);
         // with POLY every second exponential runs on the FMA pipe, halving
-        // the MUFU work
+        // the MUFU work; with X2 the scale / subtract and the row sums run
+        // as packed pair instructions
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_fast(fmaf(sv[c + e], p.scale_log2, -ref));
-          const float x1 = fmaf(sv[c + e + 1], p.scale_log2, -ref);
-          const float p1 = POLY ? exp2_poly3(x1) : ex2_fast(x1);
-          rs[(e >> 1) & 3] += p0 + p1;
+          float p0, p1;
+          if (X2) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(sv[c + e], sv[c + e + 1]), sc2, nref2), x0, x1);
+            p0 = ex2_fast(x0);
+            p1 = ex2_fast(x1);
+            rs2[(e >> 1) & 1] = f2_add(rs2[(e >> 1) & 1], f2_pack(p0, p1));
+          } else {
+            p0 = ex2_fast(fmaf(sv[c + e], p.scale_log2, -ref));
+            const float x1 = fmaf(sv[c + e + 1], p.scale_log2, -ref);
+            p1 = POLY ? exp2_poly3(x1) : ex2_fast(x1);
+            rs[(e >> 1) & 3] += p0 + p1;
+          }
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
         tmem_st_32x32b_x16(s_base + (c >> 1), pk);
       }
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      if (X2) {
+        f2_unpack(f2_add(rs2[0], rs2[1]), rs[0], rs[1]);
+        l += rs[0] + rs[1];
+      } else {
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      }
       tc_wait_st();
       lap(3);
       tc_fence_before();
@@ -383,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // q/k/v/out: [B, S, H, HD] token-major views with contiguous heads; lse [B,H,S].
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace) {
+                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
   for (auto* t : {&q, &k, &v, &out}) {
@@ -417,26 +455,33 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
   }
   auto st = cur_stream();
-#define FA2T(HD_, C_, P_, R_)                                                  \
+#define FA2T(HD_, C_, P_, R_, X_)                                              \
   {                                                                            \
-    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_>;                       \
+    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_, X_>;                   \
     set_max_smem((const void*)kern, fa2t::Cfg<HD_>::SMEM);                     \
     kern<<<grid, fa2t::kThreads, fa2t::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);   \
   }
-#define FA2T_HD(P_, R_)                                                        \
+#define FA2T_HD(P_, R_, X_)                                                    \
   if (HD == 64) {                                                              \
-    if (causal) FA2T(64, true, P_, R_) else FA2T(64, false, P_, R_)            \
+    if (causal) FA2T(64, true, P_, R_, X_) else FA2T(64, false, P_, R_, X_)    \
   } else {                                                                     \
-    if (causal) FA2T(128, true, P_, R_) else FA2T(128, false, P_, R_)          \
+    if (causal) FA2T(128, true, P_, R_, X_) else FA2T(128, false, P_, R_, X_)  \
   }
   const bool traced = p.trace != nullptr;
   TORCH_CHECK(!(traced && poly), "the trace is available for the plain variant");
+  TORCH_CHECK(!(x2 && poly), "poly and x2 variants are exclusive");
   if (traced) {
-    FA2T_HD(false, true)
+    if (x2) {
+      FA2T_HD(false, true, true)
+    } else {
+      FA2T_HD(false, true, false)
+    }
   } else if (poly) {
-    FA2T_HD(true, false)
+    FA2T_HD(true, false, false)
+  } else if (x2) {
+    FA2T_HD(false, false, true)
   } else {
-    FA2T_HD(false, false)
+    FA2T_HD(false, false, false)
   }
 #undef FA2T_HD
 #undef FA2T

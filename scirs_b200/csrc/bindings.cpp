@@ -46,7 +46,7 @@ void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                             torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
                             int64_t tokens_per_split, double scale);
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace);
+                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2);
 void tp_step_begin(torch::Tensor epoch, c10::optional<torch::Tensor> vals);
 void tp_reduce(torch::Tensor recv, torch::Tensor out, c10::optional<torch::Tensor> bias,
                c10::optional<torch::Tensor> resid, int64_t rank, c10::optional<torch::Tensor> flags,
@@ -92,7 +92,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_decode", &scirs::paged_attention_decode);
   m.def("flash_attn_fwd_pp", &scirs::flash_attn_fwd_pp, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("lse"), py::arg("causal"), py::arg("scale"), py::arg("poly") = false,
-        py::arg("trace") = py::none());
+        py::arg("trace") = py::none(), py::arg("x2") = false);
   m.def("tp_step_begin", &scirs::tp_step_begin, py::arg("epoch"), py::arg("vals") = py::none());
   m.def("tp_reduce", &scirs::tp_reduce);
   m.def("rope_apply", &scirs::rope_apply);

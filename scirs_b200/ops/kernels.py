@@ -26,7 +26,7 @@ OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
 # (warp-level mma.sync kernel). Both are sm_100a kernels of this library.
 # Attention forward: "tcgen05" (one 128-query tile per CTA, O in registers),
 # "pingpong" (two tiles per CTA, O in TMEM, P through TMEM) or "mma".
-ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "pingpong")
+ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "pingpong_x2")
 # Attention backward: "tcgen05" (head_dim 64; other head dims use mma) or "mma".
 ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05")
 
@@ -265,9 +265,9 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
     """q/k/v/out: [B, S, H, D] token-major views (heads contiguous)."""
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        if ATTN_FWD_IMPL in ("pingpong", "pingpong_poly"):
+        if ATTN_FWD_IMPL in ("pingpong", "pingpong_poly", "pingpong_x2"):
             _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(causal), float(scale),
-                                             ATTN_FWD_IMPL == "pingpong_poly")
+                                             ATTN_FWD_IMPL == "pingpong_poly", None, ATTN_FWD_IMPL == "pingpong_x2")
         elif ATTN_FWD_IMPL == "tcgen05":
             _ext.kernels().flash_attn_fwd_tc(q, k, v, out, lse, bool(causal), float(scale))
         else:
