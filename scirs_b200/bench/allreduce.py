@@ -1,7 +1,7 @@
 """Fused gradient all-reduce sweep: in-kernel NVLink all-reduce vs NCCL.
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
-        -m scirs_b200.bench.allreduce [--min 1024] [--max 1073741824] [--iters 20]
+        -m scirs_b200.bench.allreduce [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20]
 
 Payload sizes are bf16 bytes on the wire (fp32 gradients in, fp32 out; the
 push kernel scales by 1/N and casts to bf16 when publishing). NCCL runs
@@ -47,17 +47,17 @@ def _time(fn, iters, warmup=5):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--min", type=int, default=1024)
-    ap.add_argument("--max", type=int, default=1 << 30)
+    ap.add_argument("--min-bytes", type=int, default=1024)
+    ap.add_argument("--max-bytes", type=int, default=1 << 30)
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     rank, world, local = sdist.init(timeout_s=120)
     dev = torch.device("cuda", local)
-    comm = NVLinkComm(area_bytes=max(args.max, 1 << 20) + (1 << 20), timeout_s=10.0)
+    comm = NVLinkComm(area_bytes=max(args.max_bytes, 1 << 20) + (1 << 20), timeout_s=10.0)
     nvls = comm.nvls_supported()
-    nbuf = comm.nvls_buffer(max(args.max // 2, 1 << 20), torch.bfloat16) if nvls else None
-    size = args.min
-    while size <= args.max:
+    nbuf = comm.nvls_buffer(max(args.max_bytes // 2, 1 << 20), torch.bfloat16) if nvls else None
+    size = args.min_bytes
+    while size <= args.max_bytes:
         n = max(8 * world, (size // 2) // (8 * world) * (8 * world))
         x = torch.randn(n, device=dev)
         y = torch.empty_like(x)
