@@ -1151,8 +1151,11 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   if (bn_force == 128 || bn_force == 256) BN = (int)bn_force;
   // Pair mode (two SMs per 256 x 256 tile) when the tiles are wide and there
   // are enough of them to fill the GPU with pairs.
-  const bool pair = pair_enabled() && BN == 256 && bn_force != 128 && M >= 2 * BM &&
-                    (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256) >= sms / 2;
+  // (fp32 weight gradients count their split-K work units: a long K splits
+  // into enough units even when the output has few tiles)
+  const long pair_tiles = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+  const long pair_units = can_split ? pair_tiles * std::max(1, std::min(16, args.num_kb / 4)) : pair_tiles;
+  const bool pair = pair_enabled() && BN == 256 && bn_force != 128 && M >= 2 * BM && pair_units >= sms / 2;
   if (pair) args.m_blocks = (int)((M + 2 * BM - 1) / (2 * BM));
   const int usms = pair ? pair_slots(dev) : sms;  // scheduling slots: resident SM pairs in pair mode
   args.n_blocks = (int)((N + BN - 1) / BN);
