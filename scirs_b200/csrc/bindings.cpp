@@ -40,6 +40,15 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
              c10::optional<torch::Tensor> epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
              double timeout_s);
 void tp_signal(std::vector<int64_t> sig_flags, torch::Tensor epoch, int64_t idx);
+void ep_dispatch(torch::Tensor src, torch::Tensor idx, c10::optional<torch::Tensor> scale, std::vector<int64_t> dst,
+                 int64_t L, int64_t C, int64_t sl, int64_t sr, int64_t rank, std::vector<int64_t> sig_flags,
+                 torch::Tensor epoch, int64_t sig_idx);
+void ep_combine(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor slot, c10::optional<torch::Tensor> wt,
+                torch::Tensor out, int64_t L, int64_t C, int64_t rank, c10::optional<torch::Tensor> flags,
+                torch::Tensor epoch, int64_t wait_idx, double timeout_s);
+void ep_grad_w(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor slot, torch::Tensor dout,
+               torch::Tensor gw, int64_t L, int64_t C, int64_t rank);
+void tp_wait(torch::Tensor flags, torch::Tensor epoch, int64_t idx, int64_t rank, int64_t world, double timeout_s);
 void paged_kv_append(torch::Tensor k_new, torch::Tensor v_new, torch::Tensor k_pool, torch::Tensor v_pool,
                      torch::Tensor block_tables, torch::Tensor seq, torch::Tensor pos);
 void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor block_tables,
@@ -88,6 +97,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("wait_idx") = 0, py::arg("sig_flags") = std::vector<int64_t>{}, py::arg("sig_idx") = 0,
         py::arg("timeout_s") = 10.0);
   m.def("tp_signal", &scirs::tp_signal);
+  m.def("tp_wait", &scirs::tp_wait);
+  m.def("ep_dispatch", &scirs::ep_dispatch, "expert-parallel dispatch: gather rows and store them into peers");
+  m.def("ep_combine", &scirs::ep_combine, "expert-parallel combine: read expert outputs from peers, weighted sum");
+  m.def("ep_grad_w", &scirs::ep_grad_w, "routing-weight gradient against peers' expert outputs");
   m.def("paged_kv_append", &scirs::paged_kv_append);
   m.def("paged_attention_decode", &scirs::paged_attention_decode);
   m.def("flash_attn_fwd_pp", &scirs::flash_attn_fwd_pp, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),

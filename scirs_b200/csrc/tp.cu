@@ -1,6 +1,6 @@
 // Tensor-parallel helper kernels: cross-rank signals, the reduction half of
-// GEMM -> reduce-scatter, rotary position embedding, and the vocabulary-
-// parallel softmax cross-entropy.
+// GEMM -> reduce-scatter, rotary position embedding, the vocabulary-parallel
+// softmax cross-entropy, and the expert-parallel dispatch / combine.
 //
 // Synchronisation model: every rank owns a small array of 32-bit flag words
 // (one per source rank) inside its symmetric buffer. A producer sets its word
@@ -229,6 +229,165 @@ __global__ void __launch_bounds__(256) xent_finish_kernel(__nv_bfloat16* __restr
   }
 }
 
+// ---------------------------------------------------------------------------
+// Expert parallelism: top-k mixture of experts with a per-expert capacity of C
+// slots, L experts per rank, W ranks (expert e lives on rank e / L). A rank's
+// assignments are numbered destination-major, send row q = (w * L + l) * C + c
+// for expert e = w * L + l and slot c; every rank keeps, for each local expert,
+// a receive buffer [L, W, C, D] (source-rank-major inside each expert).
+//
+// ep_dispatch_kernel: the permutation and the all-to-all in one pass. A warp
+//   takes one send row, reads row idx[q] of `src` (zeros for an empty slot),
+//   optionally scales it by scale[q], and stores it directly into rank w's
+//   buffer, row l * sl + rank * sr + c, over NVLink. The last block to finish
+//   signals every peer.
+// ep_combine_kernel: the return all-to-all and the weighted sum in one pass.
+//   After the owners' signals, a warp takes one token and reads its k expert
+//   outputs straight from the owners' buffers (row ((e % L) * W + rank) * C +
+//   slot), accumulating sum_j w_j * y_j in fp32.
+// ep_grad_w_kernel: the routing-weight gradient <dout[t], y_j>, y_j read from
+//   the owner's buffer.
+//
+// Reference parity: scirs2-neural/src/layers/moe.rs:120-440 (top-k gating,
+// capacity, weighted combination; single device there).
+
+struct PeerBase {
+  char* p[kMaxPeers];
+};
+
+constexpr int kEpMaxK = 8;
+
+__device__ __forceinline__ void scale_bf16x8(uint4& q, float s) {
+  uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) w[e] = pack_bf16x2(bf16_lo(w[e]) * s, bf16_hi(w[e]) * s);
+  q = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* __restrict__ src, long nsrc,
+                                                          const int* __restrict__ idx,
+                                                          const float* __restrict__ scale, PeerBase dst, int L,
+                                                          int C, long sl, long sr, int D, int rank, int world,
+                                                          DevStatus* st, FlagPtrs sig, const unsigned* epoch,
+                                                          unsigned sig_idx, unsigned* done) {
+  const int lane = threadIdx.x & 31;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  const long rows = (long)world * L * C;
+  const long per_rank = (long)L * C;
+  const int dv = D / 8;
+  for (long q = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; q < rows; q += nwarps) {
+    const int w = (int)(q / per_rank);
+    const long rem = q - w * per_rank;
+    const int l = (int)(rem / C);
+    const int c = (int)(rem - (long)l * C);
+    const int t = idx[q];
+    const bool have = t >= 0 && input_in_range(t, nsrc, st, 80);
+    const float s = (have && scale != nullptr) ? scale[q] : 1.f;
+    const uint4* sp = reinterpret_cast<const uint4*>(src + (have ? (long)t * D : 0L));
+    uint4* dp = reinterpret_cast<uint4*>(dst.p[w] + ((long)l * sl + (long)rank * sr + c) * D * (long)sizeof(__nv_bfloat16));
+    for (int v = lane; v < dv; v += 32) {
+      uint4 x = make_uint4(0u, 0u, 0u, 0u);
+      if (have) {
+        x = sp[v];
+        if (scale != nullptr) scale_bf16x8(x, s);
+      }
+      dp[v] = x;
+    }
+  }
+  last_block_signal(sig, world, epoch, sig_idx, done);
+}
+
+// Pointers to the (at most kEpMaxK) kept expert outputs of token t; returns
+// how many.
+__device__ __forceinline__ int ep_rows(const PeerBase& srcp, const int* expert, const int* slot, const float* wt,
+                                       long t, int k, int L, int C, int D, int rank, int world, DevStatus* st,
+                                       const uint4** rows, float* wj) {
+  int n = 0;
+  for (int j = 0; j < k; ++j) {
+    const int e = expert[t * k + j];
+    const int s = slot[t * k + j];
+    if (s < 0) continue;
+    if (!input_in_range(e, (long)L * world, st, 82) || !input_in_range(s, C, st, 83)) continue;
+    const int w = e / L;
+    const int l = e - w * L;
+    rows[n] = reinterpret_cast<const uint4*>(srcp.p[w] +
+                                             ((((long)l * world + rank) * C + s) * D) * (long)sizeof(__nv_bfloat16));
+    wj[n] = wt != nullptr ? wt[t * k + j] : 1.f;
+    ++n;
+  }
+  return n;
+}
+
+__global__ void __launch_bounds__(256) ep_combine_kernel(PeerBase srcp, const int* __restrict__ expert,
+                                                         const int* __restrict__ slot, const float* __restrict__ wt,
+                                                         int k, long T, int L, int C, int D, int rank, int world,
+                                                         const unsigned* flags, const unsigned* epoch,
+                                                         unsigned wait_idx, long long timeout_ns, DevStatus* st,
+                                                         __nv_bfloat16* __restrict__ out) {
+  if (flags != nullptr && !block_wait(flags, epoch, wait_idx, rank, world, timeout_ns, st, 81)) return;
+  const int lane = threadIdx.x & 31;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  const int dv = D / 8;
+  for (long t = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += nwarps) {
+    const uint4* rows[kEpMaxK];
+    float wj[kEpMaxK];
+    const int n = ep_rows(srcp, expert, slot, wt, t, k, L, C, D, rank, world, st, rows, wj);
+    uint4* op = reinterpret_cast<uint4*>(out + t * D);
+    for (int v = lane; v < dv; v += 32) {
+      float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < n; ++j) {
+        const uint4 q = __ldcg(rows[j] + v);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) f[2 * e] += wj[j] * bf16_lo(w[e]), f[2 * e + 1] += wj[j] * bf16_hi(w[e]);
+      }
+      op[v] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                         pack_bf16x2(f[6], f[7]));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) ep_grad_w_kernel(PeerBase srcp, const int* __restrict__ expert,
+                                                        const int* __restrict__ slot,
+                                                        const __nv_bfloat16* __restrict__ dout,
+                                                        float* __restrict__ gw, int k, long T, int L, int C, int D,
+                                                        int rank, int world, DevStatus* st) {
+  const int lane = threadIdx.x & 31;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  const int dv = D / 8;
+  for (long a = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; a < T * k; a += nwarps) {
+    const long t = a / k;
+    const int e = expert[a];
+    const int s = slot[a];
+    float acc = 0.f;
+    if (s >= 0 && input_in_range(e, (long)L * world, st, 85) && input_in_range(s, C, st, 86)) {
+      const int w = e / L;
+      const int l = e - w * L;
+      const uint4* yr = reinterpret_cast<const uint4*>(
+          srcp.p[w] + ((((long)l * world + rank) * C + s) * D) * (long)sizeof(__nv_bfloat16));
+      const uint4* dr = reinterpret_cast<const uint4*>(dout + t * D);
+      for (int v = lane; v < dv; v += 32) {
+        const uint4 qy = __ldcg(yr + v);
+        const uint4 qd = dr[v];
+        const uint32_t a4[4] = {qy.x, qy.y, qy.z, qy.w};
+        const uint32_t b4[4] = {qd.x, qd.y, qd.z, qd.w};
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) acc += bf16_lo(a4[e2]) * bf16_lo(b4[e2]) + bf16_hi(a4[e2]) * bf16_hi(b4[e2]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) gw[a] = acc;
+  }
+}
+
+// A bounded wait on every peer's signal `idx`, for consumers that are not
+// kernels of this file (library GEMMs on the received rows).
+__global__ void wait_kernel(const unsigned* flags, const unsigned* epoch, unsigned idx, int rank, int world,
+                            long long timeout_ns, DevStatus* st) {
+  block_wait(flags, epoch, idx, rank, world, timeout_ns, st, 84);
+}
+
 static FlagPtrs to_ptrs(const std::vector<int64_t>& v) {
   FlagPtrs f;
   memset(&f, 0, sizeof(f));
@@ -362,6 +521,119 @@ void tp_xent_finish(torch::Tensor logits, torch::Tensor targets, torch::Tensor s
       (float)scale, reinterpret_cast<const unsigned*>(flags.data_ptr()),
       reinterpret_cast<const unsigned*>(epoch.data_ptr()), (unsigned)wait_idx, (long long)(timeout_s * 1e9),
       status_ptr(dev));
+  SCIRS_CHECK_LAUNCH();
+}
+
+static tp::PeerBase to_base(const std::vector<int64_t>& v) {
+  tp::PeerBase b;
+  memset(&b, 0, sizeof(b));
+  TORCH_CHECK(!v.empty() && v.size() <= (size_t)tp::kMaxPeers, "1..8 ranks");
+  for (size_t i = 0; i < v.size(); ++i) {
+    TORCH_CHECK(v[i] % 16 == 0, "peer buffers must be 16-byte aligned");
+    b.p[i] = reinterpret_cast<char*>(v[i]);
+  }
+  return b;
+}
+
+static int warp_grid(long warps, int dev) {
+  return (int)std::max<long>(1, std::min<long>((warps + 7) / 8, 8L * num_sms(dev)));
+}
+
+// Expert-parallel dispatch (see ep_dispatch_kernel): `dst[w]` is rank w's
+// receive buffer, `idx` [W * L * C] int32 the source row of every send row
+// (-1: empty slot), `scale` an optional fp32 factor per send row.
+void ep_dispatch(torch::Tensor src, torch::Tensor idx, c10::optional<torch::Tensor> scale, std::vector<int64_t> dst,
+                 int64_t L, int64_t C, int64_t sl, int64_t sr, int64_t rank, std::vector<int64_t> sig_flags,
+                 torch::Tensor epoch, int64_t sig_idx) {
+  CHECK_DTYPE(src, at::kBFloat16);
+  CHECK_CONTIG(src);
+  CHECK_DTYPE(idx, at::kInt);
+  CHECK_CONTIG(idx);
+  TORCH_CHECK(src.dim() == 2 && src.size(1) % 8 == 0, "src [rows, D], D a multiple of 8");
+  const int world = (int)dst.size();
+  TORCH_CHECK(idx.numel() == world * L * C, "idx must have world * L * C entries");
+  TORCH_CHECK(sig_flags.empty() || (int)sig_flags.size() == world, "one signal word per rank");
+  const float* sp = nullptr;
+  if (scale.has_value() && scale->defined()) {
+    CHECK_DTYPE((*scale), at::kFloat);
+    CHECK_CONTIG((*scale));
+    TORCH_CHECK(scale->numel() == idx.numel(), "scale must match idx");
+    sp = scale->data_ptr<float>();
+  }
+  const int dev = src.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  tp::ep_dispatch_kernel<<<warp_grid(idx.numel(), dev), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.size(0), idx.data_ptr<int>(), sp, to_base(dst),
+      (int)L, (int)C, sl, sr, (int)src.size(1), (int)rank, world, status_ptr(dev), tp::to_ptrs(sig_flags),
+      reinterpret_cast<const unsigned*>(epoch.data_ptr()), (unsigned)sig_idx, tp::done_ctr(dev));
+  SCIRS_CHECK_LAUNCH();
+}
+
+// Expert-parallel combine (see ep_combine_kernel): `srcs[w]` is rank w's
+// output buffer [L, W, C, D]; waits for signal `wait_idx` when `flags` given.
+void ep_combine(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor slot, c10::optional<torch::Tensor> wt,
+                torch::Tensor out, int64_t L, int64_t C, int64_t rank, c10::optional<torch::Tensor> flags,
+                torch::Tensor epoch, int64_t wait_idx, double timeout_s) {
+  CHECK_DTYPE(expert, at::kInt);
+  CHECK_DTYPE(slot, at::kInt);
+  CHECK_CONTIG(expert);
+  CHECK_CONTIG(slot);
+  CHECK_DTYPE(out, at::kBFloat16);
+  CHECK_CONTIG(out);
+  TORCH_CHECK(expert.dim() == 2 && expert.sizes() == slot.sizes() && expert.size(1) <= tp::kEpMaxK,
+              "expert / slot [T, k], k <= 8");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == expert.size(0) && out.size(1) % 8 == 0, "out [T, D]");
+  const float* wp = nullptr;
+  if (wt.has_value() && wt->defined()) {
+    CHECK_DTYPE((*wt), at::kFloat);
+    CHECK_CONTIG((*wt));
+    TORCH_CHECK(wt->sizes() == expert.sizes(), "wt [T, k]");
+    wp = wt->data_ptr<float>();
+  }
+  const int world = (int)srcs.size();
+  const int dev = out.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  const unsigned* fp = (flags.has_value() && flags->defined()) ? reinterpret_cast<const unsigned*>(flags->data_ptr())
+                                                               : nullptr;
+  tp::ep_combine_kernel<<<warp_grid(out.size(0), dev), 256, 0, cur_stream()>>>(
+      to_base(srcs), expert.data_ptr<int>(), slot.data_ptr<int>(), wp, (int)expert.size(1), out.size(0), (int)L,
+      (int)C, (int)out.size(1), (int)rank, world, fp, reinterpret_cast<const unsigned*>(epoch.data_ptr()),
+      (unsigned)wait_idx, (long long)(timeout_s * 1e9), status_ptr(dev),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  SCIRS_CHECK_LAUNCH();
+}
+
+// gw[t, j] = <dout[t], expert output j of token t> (0 for dropped assignments).
+void ep_grad_w(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor slot, torch::Tensor dout,
+               torch::Tensor gw, int64_t L, int64_t C, int64_t rank) {
+  CHECK_DTYPE(expert, at::kInt);
+  CHECK_DTYPE(slot, at::kInt);
+  CHECK_CONTIG(expert);
+  CHECK_CONTIG(slot);
+  CHECK_DTYPE(dout, at::kBFloat16);
+  CHECK_CONTIG(dout);
+  CHECK_DTYPE(gw, at::kFloat);
+  CHECK_CONTIG(gw);
+  TORCH_CHECK(expert.dim() == 2 && expert.sizes() == slot.sizes() && gw.sizes() == expert.sizes(),
+              "expert / slot / gw [T, k]");
+  TORCH_CHECK(dout.dim() == 2 && dout.size(0) == expert.size(0) && dout.size(1) % 8 == 0, "dout [T, D]");
+  const int dev = dout.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  tp::ep_grad_w_kernel<<<warp_grid(expert.numel(), dev), 256, 0, cur_stream()>>>(
+      to_base(srcs), expert.data_ptr<int>(), slot.data_ptr<int>(),
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), gw.data_ptr<float>(), (int)expert.size(1),
+      expert.size(0), (int)L, (int)C, (int)dout.size(1), (int)rank, (int)srcs.size(), status_ptr(dev));
+  SCIRS_CHECK_LAUNCH();
+}
+
+void tp_wait(torch::Tensor flags, torch::Tensor epoch, int64_t idx, int64_t rank, int64_t world, double timeout_s) {
+  TORCH_CHECK(world >= 1 && world <= tp::kMaxPeers && flags.numel() >= world && flags.element_size() == 4,
+              "flags: one 32-bit word per rank");
+  const int dev = flags.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  tp::wait_kernel<<<1, 32, 0, cur_stream()>>>(reinterpret_cast<const unsigned*>(flags.data_ptr()),
+                                              reinterpret_cast<const unsigned*>(epoch.data_ptr()), (unsigned)idx,
+                                              (int)rank, (int)world, (long long)(timeout_s * 1e9), status_ptr(dev));
   SCIRS_CHECK_LAUNCH();
 }
 

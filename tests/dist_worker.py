@@ -266,11 +266,42 @@ def case_tp_decoder():
     return res
 
 
+def case_ep_moe():
+    """Expert parallel MoE on the peer-memory dispatch / combine kernels
+    against the NCCL all-to-all path (fp32), three steps (buffer reuse)."""
+    from scirs_b200.nn.moe import ExpertParallelMoE, MoEConfig
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = MoEConfig(num_experts=2 * world, expert_dim=256, top_k=2, capacity_factor=1.0)
+    peer = ExpertParallelMoE(128, cfg, seed=3, transport="peer", timeout_s=10.0).to(dev)
+    ref = ExpertParallelMoE(128, cfg, seed=3, transport="nccl").to(dev)
+    res = {}
+    for it in range(3):
+        g = torch.Generator().manual_seed(100 * it + rank)
+        x = torch.randn(384, 128, generator=g).to(dev)
+        xp, xr = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
+        for m in (peer, ref):
+            m.zero_grad(set_to_none=True)
+        yp, yr = peer(xp), ref(xr)
+        yp.square().sum().backward()
+        yr.square().sum().backward()
+        rel = lambda a, b: float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))  # noqa: E731
+        res[f"it{it}"] = {"y": rel(yp, yr), "dx": rel(xp.grad, xr.grad),
+                          "gate": rel(peer.gate.weight.grad, ref.gate.weight.grad),
+                          "w1": rel(peer.experts.w1.grad, ref.experts.w1.grad),
+                          "w2": rel(peer.experts.w2.grad, ref.experts.w2.grad)}
+    torch.cuda.synchronize()
+    _ext.check_status()
+    peer.close()
+    return res
+
+
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
     res = {"collectives": case_collectives, "nvls": case_nvls, "ring_attn": case_ring_attn, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
-           "tp_decoder": case_tp_decoder}[case]()
+           "tp_decoder": case_tp_decoder, "ep_moe": case_ep_moe}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))
     dist.barrier()

@@ -83,3 +83,10 @@ def test_tensor_parallel_decoder_2gpu(tmp_path):
     for mode in ("fused", "nccl"):
         for a, b in zip(res[mode]["losses"], ref):
             assert abs(a - b) < 3e-2, (mode, res[mode]["losses"], ref)
+
+
+def test_expert_parallel_peer_kernels_2gpu(tmp_path):
+    res = _run("ep_moe", tmp_path, port=29617)
+    for it, v in res.items():
+        for name, err in v.items():
+            assert err < 3e-2, (it, name, v)
