@@ -387,6 +387,20 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   return r;
 }
 
+// gelu_tanh of two packed fp32 values: the polynomial and the final
+// 0.5 x (1 + t) in f32x2 instructions, the two tanh evaluations scalar.
+__device__ __forceinline__ uint64_t gelu_tanh2(uint64_t x) {
+  const uint64_t k0 = f2_pack(0.7978845608028654f, 0.7978845608028654f);
+  const uint64_t k1 = f2_pack(0.044715f, 0.044715f);
+  const uint64_t one = f2_pack(1.f, 1.f), half = f2_pack(0.5f, 0.5f);
+  const uint64_t a = f2_fma(f2_mul(x, x), k1, one);  // 1 + k1 x^2
+  float u0, u1;
+  f2_unpack(f2_mul(f2_mul(x, a), k0), u0, u1);      // k0 (x + k1 x^3)
+  const uint64_t t = f2_pack(tanh_fast(u0), tanh_fast(u1));
+  const uint64_t hx = f2_mul(x, half);
+  return f2_fma(hx, t, hx);
+}
+
 // d/dx of gelu_tanh.
 __device__ __forceinline__ float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;

@@ -69,6 +69,7 @@ struct Args {
   long ldaux;
   float* bias_grad;  // EPI_DGELU: += column sums of the output (fp32 [N])
   int atomic_out;
+  int gelu_x2;  // EPI_BIAS_GELU: GELU in packed f32x2 instructions
   DevStatus* st;
   int m_rot;   // rotation of the m-block order (tensor parallel: start with local rows)
   int kb_rot;  // rotation of the k-block order (tensor parallel: start with local K rows)
@@ -607,7 +608,13 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
                                    pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7])));
             }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+            if (args.gelu_x2) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) f2_unpack(gelu_tanh2(f2_pack(v[j], v[j + 1])), v[j], v[j + 1]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+            }
           }
 #pragma unroll
           for (int uu = 0; uu < 4; ++uu) {
@@ -839,6 +846,17 @@ static void launch_pair(int a_mn, int b_mn, int epi, const Maps& m, const Args& 
   else launch_pair_epi<1, 1>(epi, m, args, grid, s);
 }
 
+// Packed f32x2 GELU in the bias + GELU epilogue: SCIRS_GEMM_GELU_X2=0
+// selects the scalar form, read once per process.
+static bool gelu_x2_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SCIRS_GEMM_GELU_X2");
+    v = (e == nullptr) ? 1 : atoi(e);
+  }
+  return v != 0;
+}
+
 // 2-CTA (cta_group::2) tiles for large GEMMs: SCIRS_GEMM_PAIR=0 disables,
 // =1 enables (default), read once per process.
 static bool pair_enabled() {
@@ -1045,6 +1063,7 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   sp = (args.num_kb + args.kb_per_split - 1) / args.kb_per_split;
   args.splits = sp;
   args.atomic_out = (epi == EPI_F32 && (accumulate || sp > 1)) ? 1 : 0;
+  args.gelu_x2 = gelu_x2_enabled() ? 1 : 0;
   if (epi == EPI_F32 && sp > 1 && !accumulate) out.zero_();
   args.num_units = (int)(tiles * sp);
   const int grid = (int)std::min<long>(args.num_units, sms);
@@ -1186,6 +1205,7 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
   sp = (args.num_kb + args.kb_per_split - 1) / args.kb_per_split;  // every split non-empty
   args.splits = sp;
   args.atomic_out = (epi == EPI_F32 && (accumulate || sp > 1)) ? 1 : 0;
+  args.gelu_x2 = gelu_x2_enabled() ? 1 : 0;
   if (epi == EPI_F32 && sp > 1 && !accumulate) out.zero_();
   args.num_units = (int)(tiles * sp);
   const int grid = pair ? 2 * (int)std::min<long>(args.num_units, usms) : (int)std::min<long>(args.num_units, sms);
