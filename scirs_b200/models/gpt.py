@@ -38,7 +38,7 @@ import torch
 
 from ..ops import kernels as K
 from ..utils.flat import FlatParams
-from .transformer import BlockActs, FusedTrainerMixin, add_block_params, block_backward, block_forward
+from .transformer import BLOCK_PARAMS, BlockActs, FusedTrainerMixin, add_block_params, block_backward, block_forward
 
 
 @dataclass
@@ -103,6 +103,38 @@ class GPTConfig:
         return 3.0 * (mm + attn)
 
 
+def gpt_param_shapes(cfg: GPTConfig):
+    """(name, shape) of every parameter in the canonical order: wte (padded
+    vocabulary), wpe, the blocks, ln_f."""
+    D, F = cfg.hidden_size, cfg.intermediate_size
+    out = [("wte", (cfg.vocab_padded, D)), ("wpe", (cfg.max_position_embeddings, D))]
+    for l in range(cfg.num_hidden_layers):
+        out += [(f"h{l}." + n, shape(D, F)) for n, shape, _ in BLOCK_PARAMS]
+    return out + [("ln_f.weight", (D,)), ("ln_f.bias", (D,))]
+
+
+def gpt_init_values(cfg: GPTConfig, seed: int):
+    """Initial values (CPU fp32), drawn in the canonical order from one
+    generator, so a model split over pipeline stages starts from exactly the
+    weights of the unsplit model: N(0, 0.02), residual projections scaled by
+    1/sqrt(2 L), LayerNorm weights 1, biases 0, padded vocabulary rows 0."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    std = cfg.initializer_range
+    for name, shape in gpt_param_shapes(cfg):
+        if name.endswith("ln_1.weight") or name.endswith("ln_2.weight") or name == "ln_f.weight":
+            t = torch.ones(shape)
+        elif name.endswith("bias"):
+            t = torch.zeros(shape)
+        else:
+            sd = std
+            if name.endswith("c_proj.weight"):  # GPT-2 residual scaling
+                sd = std / math.sqrt(2 * cfg.num_hidden_layers)
+            t = torch.randn(shape, generator=g) * sd
+            if name == "wte":
+                t[cfg.vocab_size :] = 0.0  # padded rows never receive gradient
+        yield name, t
+
+
 class _Acts(BlockActs):
     """Preallocated activations for one micro-batch shape."""
 
@@ -158,22 +190,8 @@ class GPTModel(FusedTrainerMixin):
 
     # ------------------------------------------------------------------ init
     def _init_weights(self, seed: int):
-        cfg, fp = self.cfg, self.fp
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        std = cfg.initializer_range
-        for name in fp.order:
-            s = fp.slots[name]
-            if name.endswith("ln_1.weight") or name.endswith("ln_2.weight") or name == "ln_f.weight":
-                t = torch.ones(s.shape)
-            elif name.endswith("bias"):
-                t = torch.zeros(s.shape)
-            else:
-                sd = std
-                if name.endswith("c_proj.weight"):  # GPT-2 residual scaling
-                    sd = std / math.sqrt(2 * cfg.num_hidden_layers)
-                t = torch.randn(s.shape, generator=g) * sd
-                if name == "wte":
-                    t[cfg.vocab_size :] = 0.0  # padded rows never receive gradient
+        fp = self.fp
+        for name, t in gpt_init_values(self.cfg, seed):
             fp.m(name).copy_(t)
         fp.sync_bf16()
 

@@ -297,11 +297,48 @@ def case_ep_moe():
     return res
 
 
+def case_pp_gpt():
+    """Pipeline-parallel GPT (1F1B and GPipe, 4 micro-batches) == single-
+    process training on the whole batch; the tied embedding copies on the
+    first and last stage stay identical."""
+    from scirs_b200.models.gpt import GPTConfig, GPTModel
+    from scirs_b200.models.gpt_pipeline import GPTPipelineStage
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = GPTConfig.tiny(vocab=1024, seq=128)
+    cfg.num_hidden_layers = 2 * world
+    g = torch.Generator().manual_seed(11)
+    tok = torch.randint(0, cfg.vocab_size, (8, 129), generator=g)
+    x, y = tok[:, :-1].contiguous().to(dev), tok[:, 1:].contiguous().to(dev)
+    res = {}
+    for sched in ("1f1b", "gpipe"):
+        st = GPTPipelineStage(cfg, stage=rank, num_stages=world, num_micro=4, device=dev, seed=5, schedule=sched)
+        st.configure_adamw(lr=1e-3, weight_decay=0.1, max_grad_norm=0.5)
+        losses = []
+        for _ in range(3):
+            l = st.train_step(x if st.first else None, y if st.last else None)
+            v = torch.tensor([float(l) if l is not None else 0.0], device=dev)
+            dist.all_reduce(v)
+            losses.append(float(v))
+        torch.cuda.synchronize()
+        wsum = float(st.fp.m("wte").double().abs().sum()) if (st.first or st.last) else 0.0
+        sums = [None] * world
+        dist.all_gather_object(sums, wsum)
+        res[sched] = {"losses": losses, "tied_diff": abs(sums[0] - sums[-1])}
+    if rank == 0:
+        m = GPTModel(cfg, device=dev, seed=5)
+        m.configure_adamw(lr=1e-3, weight_decay=0.1, max_grad_norm=0.5)
+        res["single"] = {"losses": [float(m.train_step(x, y)) for _ in range(3)]}
+    _ext.check_status()
+    return res
+
+
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
     res = {"collectives": case_collectives, "nvls": case_nvls, "ring_attn": case_ring_attn, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
-           "tp_decoder": case_tp_decoder, "ep_moe": case_ep_moe}[case]()
+           "tp_decoder": case_tp_decoder, "ep_moe": case_ep_moe, "pp_gpt": case_pp_gpt}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))
     dist.barrier()

@@ -90,3 +90,12 @@ def test_expert_parallel_peer_kernels_2gpu(tmp_path):
     for it, v in res.items():
         for name, err in v.items():
             assert err < 3e-2, (it, name, v)
+
+
+def test_pipeline_parallel_gpt_2gpu(tmp_path):
+    res = _run("pp_gpt", tmp_path, port=29618)
+    ref = res["single"]["losses"]
+    for sched in ("1f1b", "gpipe"):
+        assert res[sched]["tied_diff"] == 0.0, (sched, res[sched])
+        for a, b in zip(res[sched]["losses"], ref):
+            assert abs(a - b) < 2e-2, (sched, res[sched]["losses"], ref)
