@@ -410,6 +410,22 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
   return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * fmaf(3.f * k1, x2, 1.f);
 }
 
+// gelu_tanh_grad of two packed fp32 values (f32x2 instructions except the
+// two tanh evaluations):
+// 0.5 (1 + t) + 0.5 x k0 (1 + 3 k1 x^2) (1 - t^2), t = tanh(k0 (x + k1 x^3)).
+__device__ __forceinline__ uint64_t gelu_tanh_grad2(uint64_t x) {
+  const uint64_t k0 = f2_pack(0.7978845608028654f, 0.7978845608028654f);
+  const uint64_t k1 = f2_pack(0.044715f, 0.044715f), k13 = f2_pack(3.f * 0.044715f, 3.f * 0.044715f);
+  const uint64_t one = f2_pack(1.f, 1.f), half = f2_pack(0.5f, 0.5f);
+  const uint64_t xx = f2_mul(x, x);
+  float u0, u1;
+  f2_unpack(f2_mul(f2_mul(x, f2_fma(xx, k1, one)), k0), u0, u1);
+  const float t0 = tanh_fast(u0), t1 = tanh_fast(u1);
+  const uint64_t t = f2_pack(t0, t1), nt = f2_pack(-t0, -t1);
+  const uint64_t c = f2_mul(f2_mul(x, half), f2_mul(k0, f2_fma(xx, k13, one)));  // 0.5 x k0 (1 + 3 k1 x^2)
+  return f2_fma(c, f2_fma(nt, t, one), f2_fma(half, t, half));
+}
+
 #endif  // __CUDACC__
 
 }  // namespace scirs

@@ -69,7 +69,7 @@ struct Args {
   long ldaux;
   float* bias_grad;  // EPI_DGELU: += column sums of the output (fp32 [N])
   int atomic_out;
-  int gelu_x2;  // EPI_BIAS_GELU: GELU in packed f32x2 instructions
+  int gelu_x2;  // EPI_BIAS_GELU / EPI_DGELU: GELU and its derivative in packed f32x2 instructions
   DevStatus* st;
   int m_rot;   // rotation of the m-block order (tensor parallel: start with local rows)
   int kb_rot;  // rotation of the k-block order (tensor parallel: start with local K rows)
@@ -558,6 +558,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
               if (EPI == EPI_RESID) {
                 v[g * 8 + 2 * e] += x0;
                 v[g * 8 + 2 * e + 1] += x1;
+              } else if (args.gelu_x2) {
+                const uint64_t d = f2_mul(f2_pack(v[g * 8 + 2 * e], v[g * 8 + 2 * e + 1]),
+                                          gelu_tanh_grad2(f2_pack(x0, x1)));
+                f2_unpack(d, v[g * 8 + 2 * e], v[g * 8 + 2 * e + 1]);
               } else {
                 v[g * 8 + 2 * e] *= gelu_tanh_grad(x0);
                 v[g * 8 + 2 * e + 1] *= gelu_tanh_grad(x1);
@@ -566,21 +570,33 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
           }
         }
         if (PEER && args.rs_seg > 0) {
-          // GEMM -> reduce-scatter: push this row's 32 partial sums (bf16)
-          // straight into the owner's receive slot over NVLink
-          if (row_ok) {
-            const int owner = row / args.rs_seg;
-            uint4* dst = reinterpret_cast<uint4*>(args.rs_dst[owner] + (long)(row - owner * args.rs_seg) * args.rs_ld +
-                                                  col0);
+          // GEMM -> reduce-scatter: push the chunk's bf16 partial sums
+          // straight into the owners' receive slots over NVLink. The chunk
+          // (32 rows x 64 bytes, one row per lane) is transposed through this
+          // warp's staging slot so that each store instruction writes eight
+          // whole 64-byte row segments (four lanes per row) instead of 32
+          // scattered 16-byte pieces.
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              if (col0 + g * 8 < args.N) {
-                const int j = g * 8;
-                dst[g] = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                                    pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
-              }
+          for (int uu = 0; uu < 4; ++uu) {
+            const int j = uu * 8;
+            slot_st16(slot0, lane, uu,
+                      make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                 pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7])));
+          }
+          __syncwarp();
+          const int u = lane & 3;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int r = k * 8 + (lane >> 2);
+            const int grow = row0 + r;
+            const uint4 val = *reinterpret_cast<const uint4*>(slot0 + r * 64 + ((u ^ ((r >> 1) & 3)) << 4));
+            if (grow < args.M && col0 + u * 8 < args.N) {
+              const int owner = grow / args.rs_seg;
+              *reinterpret_cast<uint4*>(args.rs_dst[owner] + (long)(grow - owner * args.rs_seg) * args.rs_ld + col0 +
+                                        u * 8) = val;
             }
           }
+          __syncwarp();  // the slot is rewritten by the next chunk
           continue;
         }
         // slots are free once the previous chunk's stores have read them
@@ -846,8 +862,8 @@ static void launch_pair(int a_mn, int b_mn, int epi, const Maps& m, const Args& 
   else launch_pair_epi<1, 1>(epi, m, args, grid, s);
 }
 
-// Packed f32x2 GELU in the bias + GELU epilogue: SCIRS_GEMM_GELU_X2=0
-// selects the scalar form, read once per process.
+// Packed f32x2 GELU / GELU' in the bias + GELU and dGELU epilogues:
+// SCIRS_GEMM_GELU_X2=0 selects the scalar forms, read once per process.
 static bool gelu_x2_enabled() {
   static int v = -1;
   if (v < 0) {

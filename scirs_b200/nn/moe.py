@@ -349,7 +349,7 @@ class ExpertParallelMoE(nn.Module):
                                "top_k <= 8 and d_model a multiple of 8")
         return ok
 
-    def _buffers(self, C: int, device) -> _PeerBuffers:
+    def _peer_buffers(self, C: int, device) -> _PeerBuffers:
         b = self._bufs
         if b is None or b.C != C:
             if b is not None:
@@ -359,7 +359,7 @@ class ExpertParallelMoE(nn.Module):
 
     def _forward_peer(self, x, x2, r: Routing) -> torch.Tensor:
         T, E = x2.shape[0], self.config.num_experts
-        bufs = self._buffers(r.capacity, x2.device)
+        bufs = self._peer_buffers(r.capacity, x2.device)
         q, tok, _ = _send_rows(r, E, T)
         idx = torch.full((E * r.capacity,), -1, dtype=torch.int32, device=x2.device)
         idx[q] = tok.int()
