@@ -253,7 +253,9 @@ class _PeerDispatch(torch.autograd.Function):
         bufs.push(x.contiguous(), idx, None, "recv")
         ctx.bufs, ctx.T = bufs, x.shape[0]
         ctx.save_for_backward(expert, slot)
-        return bufs.bufs["recv"].view(bufs.L, bufs.world * bufs.C, bufs.d)
+        # a copy: the heap buffers are views of one allocation that later
+        # transfers overwrite in place, so autograd must not save the view
+        return bufs.bufs["recv"].view(bufs.L, bufs.world * bufs.C, bufs.d).clone()
 
     @staticmethod
     def backward(ctx, g):

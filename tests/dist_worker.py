@@ -291,9 +291,17 @@ def case_ep_moe():
                           "gate": rel(peer.gate.weight.grad, ref.gate.weight.grad),
                           "w1": rel(peer.experts.w1.grad, ref.experts.w1.grad),
                           "w2": rel(peer.experts.w2.grad, ref.experts.w2.grad)}
+    # bf16 parameters: the expert GEMMs read the received rows without a cast
+    pb = ExpertParallelMoE(128, cfg, seed=3, transport="peer", timeout_s=10.0).to(dev, torch.bfloat16)
+    xb = torch.randn(384, 128, generator=torch.Generator().manual_seed(rank)).to(dev, torch.bfloat16)
+    for _ in range(2):
+        xb.grad = None
+        pb(xb.requires_grad_(True)).float().square().sum().backward()
+    res["bf16_finite"] = {"dx": 0.0 if bool(torch.isfinite(xb.grad).all()) else 1.0}
     torch.cuda.synchronize()
     _ext.check_status()
     peer.close()
+    pb.close()
     return res
 
 
