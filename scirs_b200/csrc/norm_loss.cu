@@ -11,6 +11,10 @@
 //                 softmax, here one online pass + one gradient pass)
 //   Embedding     scirs2-neural/src/layers/embedding.rs:256-330
 #include "host_common.h"
+#include "scirs_noalloc.h"
+
+#include <climits>
+#include <cstdint>
 
 namespace scirs {
 
@@ -671,37 +675,24 @@ void bias_grad(torch::Tensor dy, torch::Tensor out) {
 
 
 // ===========================================================================
-// No-allocation entry point (C ABI). This entry point has no counterpart in
-// the reference; it exists for callers of this library that cannot allocate
-// device memory: code that drives the kernels from C or another language
-// through a fixed device-memory budget with no allocator of its own, and code
-// that must not call cudaMalloc at the point of the call (cudaMalloc may
-// synchronise the device and is not allowed while a stream is being captured
-// into a CUDA graph).
+// No-allocation entry point (C ABI, declared in scirs_noalloc.h, which also
+// states the contract: size limit, first-call set-up, the shared array and
+// its race). It has no counterpart in the reference. It serves callers that
+// cannot allocate device memory at the point of the call: C or
+// other-language hosts working inside a fixed device-memory budget with no
+// allocator of their own, and code that must not call cudaMalloc where it
+// runs (cudaMalloc can synchronise the device).
 //
 // scirs_layernorm_bwd_noalloc() computes the same LayerNorm backward as
-// layernorm_bwd() (same kernels), but its per-block partial column sums live
-// in the file-scope array below instead of a caller-provided scratch tensor.
-//   * Limit: kNoAllocScratchFloats fp32 values (4 MiB) per device. A call needs
-//     nblocks * 3 * D of them; nblocks is reduced to fit, and a row width D
-//     whose single block would not fit (D > kNoAllocMaxD) is rejected with a
-//     clear error. Every GPU that loads this library holds the array until
-//     the process exits.
-//   * The first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current); make that first call
-//     before any stream capture. Later calls do no set-up.
-//   * All calls share the array. Each call writes every partial it later
-//     reads, so nothing needs clearing between calls, but calls whose
-//     executions overlap on the GPU (different streams without ordering, or
-//     different host threads) race on it; serialise them.
-//   * dw, db and (if given) dsum are accumulated into, exactly like
-//     layernorm_bwd(). No cudaMalloc, cudaFree or allocating library routine
-//     is called.
-// Returns 0 on success, a negative code on invalid arguments (message via
-// scirs_noalloc_last_error()), or a positive cudaError_t.
+// layernorm_bwd() with the same kernels; its per-block partial column sums
+// live in the file-scope array below instead of a caller-provided scratch
+// tensor. A call needs nblocks * 3 * D floats; nblocks is reduced to fit the
+// array and a row width whose single block would not fit is rejected. Each
+// call writes every partial it later reads, so nothing needs clearing.
 // ===========================================================================
-constexpr long kNoAllocScratchFloats = 1L << 20;
-constexpr int kNoAllocMaxD = (int)(kNoAllocScratchFloats / 3);
+constexpr long kNoAllocScratchFloats = SCIRS_NOALLOC_SCRATCH_FLOATS;
+constexpr int kNoAllocMaxD = SCIRS_NOALLOC_LN_MAX_D;
+static_assert(kNoAllocMaxD == (int)(kNoAllocScratchFloats / 3), "header and implementation disagree");
 static __device__ __align__(256) float g_noalloc_ln_scratch[kNoAllocScratchFloats];
 
 namespace {
@@ -709,7 +700,8 @@ float* g_noalloc_ptr[64] = {nullptr};
 std::mutex g_noalloc_mu;
 thread_local std::string g_noalloc_err;
 
-// Device address of the scratch array for `device` (looked up once).
+// Device address of the scratch array for `device` (looked up once, with
+// `device` current on the calling thread).
 cudaError_t noalloc_scratch(int device, float** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[device] == nullptr) {
@@ -721,6 +713,8 @@ cudaError_t noalloc_scratch(int device, float** out) {
   *out = g_noalloc_ptr[device];
   return cudaSuccess;
 }
+
+inline bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) const char* scirs_noalloc_last_error() {
@@ -731,26 +725,48 @@ extern "C" __attribute__((visibility("default"))) int scirs_layernorm_bwd_noallo
     const void* dy, const void* x, const void* w, const float* mean, const float* rstd, const void* dresid,
     void* dx, float* dw, float* db, float* dsum, long long rows, int D, void* stream) {
   g_noalloc_err.clear();
-  if (rows <= 0 || D <= 0 || D % 8 != 0) {
-    g_noalloc_err = "rows must be > 0 and D a positive multiple of 8";
-    return -1;
+  if (rows <= 0 || rows > (long long)INT_MAX || D <= 0 || D % 8 != 0) {
+    g_noalloc_err = "rows must be in 1..INT_MAX and D a positive multiple of 8 (rows = " + std::to_string(rows) +
+                    ", D = " + std::to_string(D) + ")";
+    return SCIRS_NOALLOC_EARG;
   }
   if (D > kNoAllocMaxD) {
     g_noalloc_err = "D = " + std::to_string(D) + " exceeds the no-allocation scratch limit (D <= " +
                     std::to_string(kNoAllocMaxD) + ")";
-    return -2;
+    return SCIRS_NOALLOC_ETOOBIG;
   }
   if (dy == nullptr || x == nullptr || w == nullptr || mean == nullptr || rstd == nullptr || dx == nullptr ||
       dw == nullptr || db == nullptr) {
     g_noalloc_err = "null pointer argument";
-    return -3;
+    return SCIRS_NOALLOC_ENULL;
   }
+  const void* bf_ptrs[] = {dy, x, w, dresid, dx};
+  const void* f_ptrs[] = {mean, rstd, dw, db, dsum};
+  bool vec_ok = true;  // every bf16 operand 16-byte aligned: the vectorised kernels apply
+  for (const void* p : bf_ptrs) {
+    if (p == nullptr) continue;
+    if (!aligned_to(p, 2)) {
+      g_noalloc_err = "a bf16 pointer is not 2-byte aligned";
+      return SCIRS_NOALLOC_EALIGN;
+    }
+    vec_ok = vec_ok && aligned_to(p, 16);
+  }
+  for (const void* p : f_ptrs) {
+    if (p != nullptr && !aligned_to(p, 4)) {
+      g_noalloc_err = "an fp32 pointer is not 4-byte aligned";
+      return SCIRS_NOALLOC_EALIGN;
+    }
+  }
+  // An error left pending by earlier work is returned as is (and stays
+  // pending) rather than being reported later as this call's failure.
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return (int)e;
   int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
+  e = cudaGetDevice(&device);
   if (e != cudaSuccess) return (int)e;
   if (device < 0 || device >= 64) {
     g_noalloc_err = "device index out of range";
-    return -4;
+    return SCIRS_NOALLOC_EDEVICE;
   }
   float* part = nullptr;
   e = noalloc_scratch(device, &part);
@@ -773,7 +789,7 @@ extern "C" __attribute__((visibility("default"))) int scirs_layernorm_bwd_noallo
     if (e != cudaSuccess) return (int)e;                                                           \
     ln_bwd_kernel<NV, RW><<<inb, 256, smem_b, s>>>(dyp, xp, wp, mean, rstd, dr, dxp, part, M);     \
   }
-  switch (D) {
+  switch (vec_ok ? D : -1) {
     case 256: NOALLOC_LNB(1, 1); break;
     case 512: NOALLOC_LNB(2, 1); break;
     case 768: NOALLOC_LNB(3, 1); break;
