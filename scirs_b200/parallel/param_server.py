@@ -1,384 +1,526 @@
-"""Parameter server, gossip averaging and vector clocks.
+"""Parameter server with a staleness-bounded clock table, rank-sharded
+server over a process group, push-sum gossip averaging and vector clocks.
 
-`ParameterServer` keeps named parameter tensors (any device) and applies the
-workers' pushed values under a consistency model
-(scirs2-core/src/distributed/param_server/server.rs:27-300, types.rs:5-140):
-  BSP  updates are buffered; `barrier_sync` (all live workers pushed) sets
-       every key to the aggregate (mean / sum / weighted mean by worker id)
-       of its buffered values and bumps the global version
-  ASP  a push replaces the value immediately
-  SSP  a push whose version is within `max_staleness` of the slowest live
-       worker is applied immediately; a staler one waits in the buffer for
-       the next barrier
-`FaultTolerantPS` adds heartbeats, dead-worker handling (a dead worker no
-longer blocks the BSP barrier) and periodic checkpoints
-(fault_tolerance.rs:136-250); `VectorClock` orders events causally
-(fault_tolerance.rs:257-340).
+Design
+------
+One rule covers every consistency model: each worker carries a logical clock
+(the number of iterations it has finished) and the server admits an update
+made at clock ``c`` once ``c <= floor + bound``, where ``floor`` is the
+smallest clock of the live workers and ``bound`` the configured staleness:
 
-`PSGroup` runs the BSP protocol across processes: rank `server` owns the
-store; each step every rank's pushed tensor is gathered to the server
-(torch.distributed gather; NCCL on GPUs), aggregated there, and the new
-value is broadcast back (pull).
+  * ``bound = 0``   synchronous rounds: updates of clock ``c`` wait until
+                     every live worker has finished ``c`` (``floor > c``) and
+                     are then combined into one new value per key
+  * ``bound = k``   bounded staleness: an update is applied when it is made
+                     unless its worker runs more than ``k`` clocks ahead of
+                     the slowest live worker; held updates are released as
+                     the floor advances
+  * ``bound = None`` asynchronous: every update is applied when it arrives
 
-Gossip: `GossipAllReduce` is the push-sum protocol (gossip.rs:59-330): in a
-round every node keeps (1 - f) of its (value, weight) and sends f to a peer
-(ring: r + 1; random; exponential: r + 2^j); estimates are value / weight
-and converge to the average. `gossip_allreduce` runs the ring variant across
-processes with point-to-point send/recv.
+Updates are kept in a table keyed by clock, so releasing work after a clock
+advance is a scan of the admissible clocks only. Liveness is a lease table
+(each worker renews a lease; an expired lease removes the worker from the
+floor and from synchronous rounds, so a dead worker never blocks the
+others). Snapshots of the parameters and the clock table are taken every
+``snapshot_every`` versions into a bounded ring and can be restored.
+
+``ShardedParameterServer`` runs the synchronous mode across processes: every
+key has an owner rank (stable hash of the key), pushes are reduced to the
+owner (``torch.distributed.reduce``), the owner applies the combined update
+and broadcasts the new value. Keys are visited in sorted order so every rank
+issues the same collectives.
+
+Gossip (``PushSum``) is written as a product of column-stochastic mixing
+matrices: in round ``t`` node ``i`` keeps a fraction ``1 - f`` of its
+(value, weight) pair and sends ``f`` to ``peer_t(i)``. The estimate
+value / weight of every node converges to the average. ``push_sum_allreduce``
+runs the shift topologies (ring, exponential) across ranks with
+point-to-point send/recv.
+
+The reference has the same features as in-process structures
+(scirs2-core/src/distributed/param_server/server.rs:45-260 BSP/ASP/SSP
+server, fault_tolerance.rs:34-320 heartbeats, checkpoints and vector clocks,
+gossip.rs:59-271 push-sum); this module shares their purpose, not their
+structure.
 """
 from __future__ import annotations
 
-import copy
 import enum
-import random
-import threading
+import math
+import time
+import zlib
+from collections import defaultdict, deque
 from dataclasses import dataclass, field
+from typing import Callable
 
 import torch
 import torch.distributed as dist
 
-
-class ConsistencyModel(enum.Enum):
-    BSP = "bsp"
-    ASP = "asp"
-    SSP = "ssp"
+# --------------------------------------------------------------------- combine
 
 
-@dataclass
-class AggregationMethod:
-    kind: str = "mean"  # "mean" | "sum" | "weighted_mean"
-    weights: list[float] | None = None
-
-    @staticmethod
-    def mean():
-        return AggregationMethod("mean")
-
-    @staticmethod
-    def sum():
-        return AggregationMethod("sum")
-
-    @staticmethod
-    def weighted_mean(weights):
-        return AggregationMethod("weighted_mean", list(weights))
+def combine_mean(values: list[torch.Tensor], workers: list[int]) -> torch.Tensor:
+    return torch.stack(values).mean(0)
 
 
-@dataclass
-class ParamServerConfig:
-    num_workers: int = 4
-    consistency: ConsistencyModel = ConsistencyModel.BSP
-    max_staleness: int = 0
-    aggregation: AggregationMethod = field(default_factory=AggregationMethod)
-    checkpoint_interval: int = 100
-    replication_factor: int = 1
+def combine_sum(values: list[torch.Tensor], workers: list[int]) -> torch.Tensor:
+    return torch.stack(values).sum(0)
 
 
-@dataclass
-class ParameterUpdate:
-    key: str
-    values: torch.Tensor
-    worker_id: int
-    version: int
+def combine_weighted(weights: dict[int, float] | list[float]) -> Callable:
+    """Weighted mean by worker id (missing ids weigh 1)."""
+    table = dict(enumerate(weights)) if isinstance(weights, (list, tuple)) else dict(weights)
 
-
-@dataclass
-class WorkerState:
-    worker_id: int
-    version: int = 0
-    is_alive: bool = True
-    last_heartbeat: int = 0
-
-
-@dataclass
-class ServerCheckpoint:
-    parameters: dict
-    version: int
-    worker_states: list
-
-
-def aggregate_updates(updates: list[ParameterUpdate], method: AggregationMethod) -> torch.Tensor | None:
-    if not updates:
-        return None
-    vals = torch.stack([u.values for u in updates])
-    if method.kind == "sum":
-        return vals.sum(0)
-    if method.kind == "weighted_mean":
-        w = torch.tensor([(method.weights or [])[u.worker_id] if u.worker_id < len(method.weights or []) else 1.0
-                          for u in updates], dtype=vals.dtype, device=vals.device)
+    def fn(values, workers):
+        w = torch.tensor([float(table.get(k, 1.0)) for k in workers], dtype=values[0].dtype)
+        s = sum(v * wi for v, wi in zip(values, w.to(values[0].device)))
         tot = float(w.sum())
-        s = (vals * w.view(-1, *([1] * (vals.dim() - 1)))).sum(0)
-        return s if abs(tot) < 1e-300 else s / tot
-    return vals.mean(0)
+        return s if tot == 0.0 else s / tot
+
+    return fn
+
+
+_COMBINE = {"mean": combine_mean, "sum": combine_sum}
+
+
+class Consistency(enum.Enum):
+    """Named staleness bounds (the reference's BSP / SSP / ASP)."""
+
+    SYNC = "sync"
+    BOUNDED = "bounded"
+    ASYNC = "async"
+
+
+@dataclass
+class PSConfig:
+    num_workers: int = 4
+    staleness: int | None = 0  # 0 synchronous, k bounded, None asynchronous
+    combine: str | Callable = "mean"
+    apply: str = "replace"  # "replace": key <- combined push; "sgd": key <- key - lr * combined push
+    lr: float = 1.0
+    lease_s: float = 30.0
+    snapshot_every: int = 0  # 0: no automatic snapshots
+    snapshot_keep: int = 4
+
+    @property
+    def mode(self) -> Consistency:
+        if self.staleness is None:
+            return Consistency.ASYNC
+        return Consistency.SYNC if self.staleness == 0 else Consistency.BOUNDED
+
+
+# ----------------------------------------------------------------- liveness
+
+
+class LeaseTable:
+    """Worker leases: a worker is live while now < its expiry time."""
+
+    def __init__(self, lease_s: float):
+        self.lease_s = float(lease_s)
+        self.expiry: dict[int, float] = {}
+        self.revoked: set[int] = set()
+
+    def renew(self, worker: int, now: float | None = None):
+        if worker in self.revoked:
+            raise RuntimeError(f"worker {worker} was declared failed and cannot renew its lease")
+        self.expiry[worker] = (time.monotonic() if now is None else now) + self.lease_s
+
+    def revoke(self, worker: int):
+        self.revoked.add(worker)
+        self.expiry.pop(worker, None)
+
+    def live(self, now: float | None = None) -> set[int]:
+        t = time.monotonic() if now is None else now
+        return {w for w, e in self.expiry.items() if e > t}
+
+    def lapsed(self, now: float | None = None) -> list[int]:
+        t = time.monotonic() if now is None else now
+        return sorted(w for w, e in self.expiry.items() if e <= t)
+
+
+# -------------------------------------------------------------------- server
+
+
+@dataclass
+class _Pending:
+    worker: int
+    value: torch.Tensor
+
+
+@dataclass
+class Snapshot:
+    version: int
+    params: dict[str, torch.Tensor]
+    clocks: dict[int, int]
+    failed: set[int] = field(default_factory=set)
 
 
 class ParameterServer:
-    def __init__(self, config: ParamServerConfig | None = None):
-        self.config = config or ParamServerConfig()
-        self.parameters: dict[str, tuple[torch.Tensor, int]] = {}
-        self.workers: list[WorkerState] = []
-        self.global_version = 0
-        self.update_buffer: dict[str, list[ParameterUpdate]] = {}
-        self.bsp_pushed: list[bool] = []
-        self._lock = threading.RLock()
+    """Staleness-bounded parameter server (see the module docstring).
 
-    def register_worker(self) -> int:
-        with self._lock:
-            wid = len(self.workers)
-            self.workers.append(WorkerState(wid))
-            self.bsp_pushed.append(False)
-            return wid
+    Typical synchronous use::
 
-    def init_parameter(self, key: str, values: torch.Tensor):
-        with self._lock:
-            self.parameters[key] = (values.detach().clone(), 0)
+        ps = ParameterServer(PSConfig(num_workers=3))
+        ids = [ps.join() for _ in range(3)]
+        ps.create("w", torch.zeros(4))
+        for w in ids:
+            ps.push(w, "w", value)      # at the worker's current clock
+            ps.advance(w)               # worker w finished this clock
+        value, version = ps.pull("w")
+    """
 
-    def _check_worker(self, wid: int):
-        if wid >= len(self.workers):
-            raise ValueError(f"unknown worker id {wid}")
+    def __init__(self, config: PSConfig | None = None):
+        self.config = config or PSConfig()
+        c = self.config.combine
+        self._combine = _COMBINE[c] if isinstance(c, str) else c
+        self.params: dict[str, torch.Tensor] = {}
+        self.key_version: dict[str, int] = {}
+        self.clock: dict[int, int] = {}  # worker -> finished iterations
+        self.leases = LeaseTable(self.config.lease_s)
+        self.table: dict[int, dict[str, list[_Pending]]] = defaultdict(lambda: defaultdict(list))
+        self.version = 0  # bumped once per applied combine / async apply
+        self.snapshots: deque[Snapshot] = deque(maxlen=max(1, self.config.snapshot_keep))
+        self._sync_done = -1  # last clock whose synchronous round was committed
 
-    def push(self, update: ParameterUpdate):
-        with self._lock:
-            self._check_worker(update.worker_id)
-            w = self.workers[update.worker_id]
-            if not w.is_alive:
-                raise RuntimeError(f"worker {update.worker_id} is not alive")
-            w.version = update.version
-            c = self.config.consistency
-            if c == ConsistencyModel.BSP:
-                self.update_buffer.setdefault(update.key, []).append(update)
-                self.bsp_pushed[update.worker_id] = True
-            elif c == ConsistencyModel.ASP:
-                self._apply(update)
-            else:
-                slowest = min((x.version for x in self.workers if x.is_alive), default=0)
-                if update.version - slowest <= self.config.max_staleness:
-                    self._apply(update)
+    # ------------------------------------------------------------ membership
+    def join(self, now: float | None = None) -> int:
+        if len(self.clock) >= self.config.num_workers:
+            raise RuntimeError(f"all {self.config.num_workers} worker slots are taken")
+        w = len(self.clock)
+        self.clock[w] = 0
+        self.leases.renew(w, now)
+        return w
+
+    def heartbeat(self, worker: int, now: float | None = None):
+        self._known(worker)
+        self.leases.renew(worker, now)
+
+    def fail(self, worker: int):
+        """Declare a worker failed: it leaves the floor and synchronous rounds
+        at once (its pending updates of uncommitted clocks still count)."""
+        self._known(worker)
+        if worker in self.leases.revoked:
+            raise RuntimeError(f"worker {worker} is already marked failed")
+        self.leases.revoke(worker)
+        self._release()
+
+    def reap(self, now: float | None = None) -> list[int]:
+        """Fail every worker whose lease has lapsed; returns their ids."""
+        gone = self.leases.lapsed(now)
+        for w in gone:
+            self.leases.revoke(w)
+        if gone:
+            self._release(now)
+        return gone
+
+    def live_workers(self, now: float | None = None) -> list[int]:
+        return sorted(self.leases.live(now))
+
+    def _known(self, worker: int):
+        if worker not in self.clock:
+            raise KeyError(f"worker {worker} never joined")
+
+    # ------------------------------------------------------------------ data
+    def create(self, key: str, value: torch.Tensor):
+        self.params[key] = value.detach().clone()
+        self.key_version[key] = 0
+
+    def pull(self, key: str) -> tuple[torch.Tensor, int]:
+        return self.params[key].clone(), self.key_version[key]
+
+    def floor(self, now: float | None = None) -> int | None:
+        live = self.leases.live(now)
+        return min((self.clock[w] for w in live), default=None)
+
+    def admissible(self, clock: int, now: float | None = None) -> bool:
+        b = self.config.staleness
+        if b is None:
+            return True
+        f = self.floor(now)
+        if f is None:
+            return True
+        return clock < f if b == 0 else clock <= f + b
+
+    def push(self, worker: int, key: str, value: torch.Tensor, clock: int | None = None,
+             now: float | None = None) -> bool:
+        """Record worker's update of `key` made at `clock` (default: the
+        worker's current clock). Returns True if it was applied now."""
+        self._known(worker)
+        if worker in self.leases.revoked:
+            raise RuntimeError(f"worker {worker} was declared failed")
+        if key not in self.params:
+            raise KeyError(f"unknown key {key!r}")
+        c = self.clock[worker] if clock is None else int(clock)
+        self.leases.renew(worker, now)
+        entry = _Pending(worker, value.detach().clone())
+        if self.config.staleness != 0 and self.admissible(c, now):
+            self._apply(key, [entry])
+            return True
+        self.table[c][key].append(entry)
+        return False
+
+    def advance(self, worker: int, now: float | None = None):
+        """Worker finished its current clock; commit what became admissible."""
+        self._known(worker)
+        self.clock[worker] += 1
+        self.leases.renew(worker, now)
+        self._release(now)
+
+    def _apply(self, key: str, entries: list[_Pending]):
+        upd = self._combine([e.value for e in entries], [e.worker for e in entries])
+        if self.config.apply == "sgd":
+            self.params[key] = self.params[key] - self.config.lr * upd.to(self.params[key].dtype)
+        else:
+            self.params[key] = upd.to(self.params[key].dtype)
+        self.key_version[key] += 1
+        self.version += 1
+        n = self.config.snapshot_every
+        if n and self.version % n == 0:
+            self.snapshots.append(self.snapshot())
+
+    def _release(self, now: float | None = None):
+        for c in sorted(self.table):
+            if not self.admissible(c, now):
+                break
+            for key in sorted(self.table[c]):
+                ents = self.table[c][key]
+                if self.config.staleness == 0:
+                    self._apply(key, ents)  # one combined value per key per round
                 else:
-                    self.update_buffer.setdefault(update.key, []).append(update)
+                    for e in ents:
+                        self._apply(key, [e])
+            del self.table[c]
+            self._sync_done = max(self._sync_done, c)
 
-    def _apply(self, u: ParameterUpdate):
-        self.parameters[u.key] = (u.values.detach().clone(), u.version)
+    def waiting_on(self, clock: int, now: float | None = None) -> list[int]:
+        """Live workers that have not finished `clock` yet."""
+        return sorted(w for w in self.leases.live(now) if self.clock[w] <= clock)
 
-    def pull(self, key: str, worker_id: int) -> tuple[torch.Tensor, int]:
-        with self._lock:
-            self._check_worker(worker_id)
-            if key not in self.parameters:
-                raise KeyError(f"unknown key {key}")
-            v, ver = self.parameters[key]
-            return v.clone(), ver
+    def pending(self) -> int:
+        return sum(len(v) for d in self.table.values() for v in d.values())
 
-    def ready(self) -> bool:
-        return all(self.bsp_pushed[w.worker_id] for w in self.workers if w.is_alive)
-
-    def barrier_sync(self):
-        with self._lock:
-            for w in self.workers:
-                if w.is_alive and not self.bsp_pushed[w.worker_id]:
-                    raise RuntimeError(f"BSP barrier: worker {w.worker_id} has not pushed yet")
-            for key, ups in self.update_buffer.items():
-                agg = aggregate_updates(ups, self.config.aggregation)
-                if agg is not None:
-                    self.parameters[key] = (agg, self.global_version + 1)
-            self.update_buffer.clear()
-            self.bsp_pushed = [False] * len(self.workers)
-            self.global_version += 1
-
-    def checkpoint(self) -> ServerCheckpoint:
-        with self._lock:
-            return ServerCheckpoint({k: (v.clone(), ver) for k, (v, ver) in self.parameters.items()},
-                                    self.global_version, copy.deepcopy(self.workers))
+    # ------------------------------------------------------------- snapshots
+    def snapshot(self) -> Snapshot:
+        return Snapshot(self.version, {k: v.clone() for k, v in self.params.items()}, dict(self.clock),
+                        set(self.leases.revoked))
 
     @classmethod
-    def restore(cls, cp: ServerCheckpoint, config: ParamServerConfig) -> "ParameterServer":
+    def from_snapshot(cls, snap: Snapshot, config: PSConfig, now: float | None = None) -> "ParameterServer":
         ps = cls(config)
-        ps.parameters = {k: (v.clone(), ver) for k, (v, ver) in cp.parameters.items()}
-        ps.workers = copy.deepcopy(cp.worker_states)
-        ps.global_version = cp.version
-        ps.bsp_pushed = [False] * len(ps.workers)
+        for k, v in snap.params.items():
+            ps.create(k, v)
+        ps.version = snap.version
+        ps.clock = dict(snap.clocks)
+        for w in ps.clock:
+            if w in snap.failed:
+                ps.leases.revoke(w)
+            else:
+                ps.leases.renew(w, now)
         return ps
 
-    def num_workers(self) -> int:
-        return len(self.workers)
+
+# ---------------------------------------------------------- across processes
 
 
-class FaultTolerantPS:
-    def __init__(self, config: ParamServerConfig | None = None, server: ParameterServer | None = None):
-        self.server = server or ParameterServer(config)
-        self.last_checkpoint: ServerCheckpoint | None = None
-        self.last_checkpoint_step = 0
-
-    def heartbeat(self, worker_id: int, timestamp: int):
-        self.server._check_worker(worker_id)
-        w = self.server.workers[worker_id]
-        w.last_heartbeat = timestamp
-        w.is_alive = True
-
-    def check_workers(self, current_time: int, timeout: int) -> list[int]:
-        return [w.worker_id for w in self.server.workers
-                if w.is_alive and current_time - w.last_heartbeat > timeout]
-
-    def handle_worker_failure(self, worker_id: int):
-        self.server._check_worker(worker_id)
-        w = self.server.workers[worker_id]
-        if not w.is_alive:
-            raise RuntimeError(f"worker {worker_id} is already marked as dead")
-        w.is_alive = False
-
-    def checkpoint_if_needed(self, step: int) -> ServerCheckpoint | None:
-        iv = self.server.config.checkpoint_interval
-        if iv and step > 0 and step % iv == 0 and step > self.last_checkpoint_step:
-            self.last_checkpoint = self.server.checkpoint()
-            self.last_checkpoint_step = step
-            return self.last_checkpoint
-        return None
-
-    @classmethod
-    def recover_from_checkpoint(cls, cp: ServerCheckpoint, config: ParamServerConfig) -> "FaultTolerantPS":
-        ft = cls(server=ParameterServer.restore(cp, config))
-        ft.last_checkpoint = cp
-        return ft
+def owner_of(key: str, world: int) -> int:
+    return zlib.crc32(key.encode()) % world
 
 
-class VectorClock:
-    def __init__(self, num_workers: int):
-        self.clocks = [0] * num_workers
+class ShardedParameterServer:
+    """Synchronous parameter server whose keys are spread over the ranks of a
+    process group. Every rank is a worker and hosts the keys it owns.
 
-    def increment(self, worker_id: int):
-        if worker_id >= len(self.clocks):
-            raise ValueError("worker id out of range")
-        self.clocks[worker_id] += 1
+    ``step(updates)`` with one tensor per key (same keys on every rank):
+    each key's updates are summed onto its owner, the owner combines them
+    (mean over ranks) and applies them (replace or SGD), then broadcasts the
+    new value, which ``step`` returns for every key.
+    """
 
-    def merge(self, other: "VectorClock"):
-        if len(other.clocks) != len(self.clocks):
-            raise ValueError("vector clock size mismatch")
-        self.clocks = [max(a, b) for a, b in zip(self.clocks, other.clocks)]
+    def __init__(self, apply: str = "replace", lr: float = 1.0, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.apply = apply
+        self.lr = lr
+        self.values: dict[str, torch.Tensor] = {}
+        self.version = 0
 
-    def happens_before(self, other: "VectorClock") -> bool:
-        return all(a <= b for a, b in zip(self.clocks, other.clocks)) and self.clocks != other.clocks
+    def create(self, key: str, value: torch.Tensor):
+        """Collective: all ranks register the same keys (owner's value wins)."""
+        t = value.detach().clone()
+        dist.broadcast(t, src=self._global(owner_of(key, self.world)), group=self.group)
+        self.values[key] = t
 
-    def is_concurrent(self, other: "VectorClock") -> bool:
-        return not self.happens_before(other) and not other.happens_before(self) and self.clocks != other.clocks
+    def _global(self, r: int) -> int:
+        return dist.get_global_rank(self.group, r) if self.group is not None else r
 
+    def owned(self) -> list[str]:
+        return sorted(k for k in self.values if owner_of(k, self.world) == self.rank)
 
-# ----------------------------------------------------------------- across processes
-class PSGroup:
-    """BSP parameter server across the ranks of a process group."""
-
-    def __init__(self, config: ParamServerConfig | None = None, server: int = 0, group=None):
-        self.group, self.server_rank = group, server
-        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
-        cfg = config or ParamServerConfig(num_workers=self.world)
-        self.ps = ParameterServer(cfg) if self.rank == server else None
-        if self.ps is not None:
-            for _ in range(self.world):
-                self.ps.register_worker()
-
-    def init_parameter(self, key: str, values: torch.Tensor):
-        if self.ps is not None:
-            self.ps.init_parameter(key, values)
-
-    def step(self, key: str, values: torch.Tensor, version: int) -> torch.Tensor:
-        """Push this rank's values, run the barrier on the server, pull the
-        aggregate (returned on every rank)."""
-        gathered = [torch.empty_like(values) for _ in range(self.world)] if self.ps is not None else None
-        dist.gather(values.contiguous(), gathered, dst=self.server_rank, group=self.group)
-        out = torch.empty_like(values)
-        if self.ps is not None:
-            for wid, v in enumerate(gathered):
-                self.ps.push(ParameterUpdate(key, v, wid, version))
-            self.ps.barrier_sync()
-            out.copy_(self.ps.pull(key, self.rank)[0])
-        dist.broadcast(out, src=self.server_rank, group=self.group)
+    def step(self, updates: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+        out = {}
+        for key in sorted(updates):
+            own = owner_of(key, self.world)
+            buf = updates[key].detach().to(self.values[key].dtype).clone()
+            dist.reduce(buf, dst=self._global(own), op=dist.ReduceOp.SUM, group=self.group)
+            if self.rank == own:
+                buf /= self.world
+                self.values[key] = self.values[key] - self.lr * buf if self.apply == "sgd" else buf
+            v = self.values[key]
+            dist.broadcast(v, src=self._global(own), group=self.group)
+            out[key] = v
+        self.version += 1
         return out
 
 
-class GossipAllReduce:
-    def __init__(self, topology: str = "ring", num_rounds: int = 10, push_fraction: float = 0.5, num_nodes: int = 0,
-                 seed: int = 0):
-        assert topology in ("ring", "random", "exponential")
-        self.topology, self.num_rounds, self.push_fraction = topology, num_rounds, push_fraction
-        self.num_nodes = num_nodes
-        self.rng = random.Random(seed)
-        self.values: list[torch.Tensor] = []
-        self.weights: list[float] = []
-        self.rounds_completed = 0
-
-    def init_values(self, node_values):
-        if len(node_values) != self.num_nodes:
-            raise ValueError("one value per node")
-        self.values = [torch.as_tensor(v, dtype=torch.float64).clone() for v in node_values]
-        self.weights = [1.0] * self.num_nodes
-
-    def select_peer(self, sender: int) -> int:
-        n = self.num_nodes
-        if n <= 1:
-            return 0
-        if self.topology == "ring":
-            return (sender + 1) % n
-        if self.topology == "random":
-            while True:
-                p = self.rng.randrange(n)
-                if p != sender:
-                    return p
-        j = self.rng.randrange(max(1, (n - 1).bit_length()))
-        return (sender + (1 << j)) % n
-
-    def run_round(self):
-        f = self.push_fraction
-        msgs = []
-        for s in range(self.num_nodes):
-            r = self.select_peer(s)
-            msgs.append((r, self.values[s] * f, self.weights[s] * f))
-            self.values[s] = self.values[s] * (1 - f)
-            self.weights[s] *= 1 - f
-        for r, v, w in msgs:
-            self.values[r] = self.values[r] + v
-            self.weights[r] += w
-        self.rounds_completed += 1
-
-    def get_estimate(self, node: int) -> torch.Tensor:
-        w = self.weights[node]
-        return self.values[node].clone() if abs(w) < 1e-300 else self.values[node] / w
-
-    def is_converged(self, tol: float) -> bool:
-        if self.num_nodes <= 1:
-            return True
-        est = torch.stack([self.get_estimate(i) for i in range(self.num_nodes)])
-        return bool(((est - est.mean(0)).abs() <= tol).all())
-
-    def run_to_convergence(self, tolerance: float) -> int:
-        for i in range(self.num_rounds):
-            self.run_round()
-            if self.is_converged(tolerance):
-                return i + 1
-        return self.num_rounds
+# --------------------------------------------------------------------- gossip
 
 
-def gossip_allreduce_simulate(node_values, config: GossipAllReduce) -> list[torch.Tensor]:
-    config.num_nodes = len(node_values)
-    config.init_values(node_values)
-    for _ in range(config.num_rounds):
-        config.run_round()
-    return [config.get_estimate(i) for i in range(config.num_nodes)]
+def peer_ring(i: int, t: int, n: int) -> int:
+    return (i + 1) % n
 
 
-def gossip_allreduce(t: torch.Tensor, rounds: int = 10, push_fraction: float = 0.5, group=None) -> torch.Tensor:
-    """Ring push-sum across ranks: returns this rank's estimate of the mean
-    of `t` over ranks after `rounds` rounds (exact for push_fraction 0.5 and
-    rounds -> inf; every rank's (value, weight) mass is conserved)."""
-    rank, world = dist.get_rank(group), dist.get_world_size(group)
+def peer_exponential(i: int, t: int, n: int) -> int:
+    hops = max(1, math.ceil(math.log2(n)))
+    return (i + (1 << (t % hops))) % n
+
+
+def make_peer_random(seed: int) -> Callable[[int, int, int], int]:
+    """A different non-self peer per (node, round), reproducible from seed."""
+
+    def fn(i, t, n):
+        g = torch.Generator().manual_seed(seed * 1_000_003 + t * 7919 + i)
+        return (i + 1 + int(torch.randint(0, n - 1, (1,), generator=g))) % n
+
+    return fn
+
+
+TOPOLOGIES = {"ring": peer_ring, "exponential": peer_exponential}
+
+
+class PushSum:
+    """Push-sum averaging of n node vectors as repeated mixing-matrix
+    products: X <- P_t X, w <- P_t w with P_t[i, i] = 1 - f and
+    P_t[peer_t(i), i] += f (columns sum to 1, so the total mass is kept)."""
+
+    def __init__(self, values: list[torch.Tensor] | torch.Tensor, topology: str | Callable = "ring",
+                 fraction: float = 0.5, seed: int = 0):
+        x = torch.stack([torch.as_tensor(v, dtype=torch.float64).reshape(-1) for v in values]) \
+            if not torch.is_tensor(values) else values.to(torch.float64).reshape(values.shape[0], -1)
+        self.n = x.shape[0]
+        self.shape = torch.as_tensor(values[0]).shape
+        self.x = x.clone()
+        self.w = torch.ones(self.n, dtype=torch.float64)
+        if callable(topology):
+            self.peer = topology
+        elif topology == "random":
+            self.peer = make_peer_random(seed)
+        else:
+            self.peer = TOPOLOGIES[topology]
+        self.f = float(fraction)
+        self.t = 0
+        self.target = self.x.mean(0)
+
+    def mixing_matrix(self, t: int) -> torch.Tensor:
+        P = torch.eye(self.n, dtype=torch.float64) * (1.0 - self.f)
+        for i in range(self.n):
+            P[self.peer(i, t, self.n), i] += self.f
+        return P
+
+    def round(self):
+        P = self.mixing_matrix(self.t)
+        self.x = P @ self.x
+        self.w = P @ self.w
+        self.t += 1
+
+    def estimates(self) -> torch.Tensor:
+        return self.x / self.w[:, None]
+
+    def estimate(self, i: int) -> torch.Tensor:
+        return self.estimates()[i].reshape(self.shape)
+
+    def spread(self) -> float:
+        """Largest deviation of any estimate from the true average."""
+        return float((self.estimates() - self.target).abs().max())
+
+    def run(self, tol: float, max_rounds: int = 10_000) -> int:
+        while self.spread() > tol and self.t < max_rounds:
+            self.round()
+        return self.t
+
+
+def push_sum_allreduce(t: torch.Tensor, rounds: int = 30, topology: str = "ring", fraction: float = 0.5,
+                       group=None) -> torch.Tensor:
+    """Approximate average of `t` over the ranks by push-sum gossip with
+    point-to-point messages. Shift topologies only: in round k every rank
+    sends to (r + s_k) and receives from (r - s_k), so each exchange pairs
+    one send with one receive."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
     if world == 1:
         return t.clone()
-    val = torch.cat([t.reshape(-1).double(), torch.ones(1, dtype=torch.float64, device=t.device)])
-    dst, src = (rank + 1) % world, (rank - 1) % world
-    gdst = dist.get_global_rank(group, dst) if group is not None else dst
-    gsrc = dist.get_global_rank(group, src) if group is not None else src
-    for _ in range(rounds):
-        send = val * push_fraction
-        val = val * (1 - push_fraction)
-        recv = torch.empty_like(val)
-        reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, send, gdst, group),
-                                       dist.P2POp(dist.irecv, recv, gsrc, group)])
+    peer = TOPOLOGIES[topology]
+    gr = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+    x = torch.cat([t.detach().reshape(-1).to(torch.float64), torch.ones(1, dtype=torch.float64)])
+    if t.is_cuda:
+        x = x.to(t.device)
+    for k in range(rounds):
+        dst = peer(rank, k, world)
+        shift = (dst - rank) % world
+        src = (rank - shift) % world
+        out = x * fraction
+        inc = torch.empty_like(x)
+        reqs = [dist.isend(out, gr(dst), group=group), dist.irecv(inc, gr(src), group=group)]
         for r in reqs:
             r.wait()
-        val = val + recv
-    return (val[:-1] / val[-1]).to(t.dtype).view_as(t)
+        x = x * (1.0 - fraction) + inc
+    return (x[:-1] / x[-1]).to(t.dtype).reshape(t.shape)
+
+
+# --------------------------------------------------------------- vector clock
+
+
+class Order(enum.Enum):
+    BEFORE = "before"
+    AFTER = "after"
+    EQUAL = "equal"
+    CONCURRENT = "concurrent"
+
+
+class VectorClock:
+    """Vector clock over a fixed set of processes."""
+
+    def __init__(self, n: int, counts=None):
+        self.c = list(counts) if counts is not None else [0] * n
+
+    def tick(self, i: int) -> "VectorClock":
+        self.c[i] += 1
+        return self
+
+    def observe(self, other: "VectorClock") -> "VectorClock":
+        """Merge a received clock (element-wise max)."""
+        self.c = [max(a, b) for a, b in zip(self.c, other.c)]
+        return self
+
+    def compare(self, other: "VectorClock") -> Order:
+        le = all(a <= b for a, b in zip(self.c, other.c))
+        ge = all(a >= b for a, b in zip(self.c, other.c))
+        if le and ge:
+            return Order.EQUAL
+        if le:
+            return Order.BEFORE
+        if ge:
+            return Order.AFTER
+        return Order.CONCURRENT
+
+    def happens_before(self, other: "VectorClock") -> bool:
+        return self.compare(other) is Order.BEFORE
+
+    def concurrent(self, other: "VectorClock") -> bool:
+        return self.compare(other) is Order.CONCURRENT
+
+    def copy(self) -> "VectorClock":
+        return VectorClock(len(self.c), self.c)
+
+    def __repr__(self):
+        return f"VectorClock({self.c})"
