@@ -45,9 +45,13 @@ def parse():
     ap.add_argument("--global-batch", type=int, default=None,
                     help="sequences per step (default 64 for gpt2, 32 for gpt1.3b)")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default 1024 gpt2, 2048 gpt1.3b)")
-    ap.add_argument("--dp-mode", default="fused", choices=["fused", "push", "nvls", "nccl"],
-                    help="data-parallel gradient all-reduce: fused = NVLS in-switch reduction where the GPUs "
-                    "support NVLink multicast, else the push all-reduce; nccl = the baseline")
+    ap.add_argument("--dp-mode", default="fused", choices=["fused", "zero-nccl", "push", "nvls", "nccl"],
+                    help="gpt2 data parallel: fused = sharded optimizer (ZeRO-1) with in-switch NVLS "
+                    "reduce-scatter / all-gather (push collectives without NVLink multicast), early LM-head "
+                    "reduction and embedding rows routed to their owners; zero-nccl = the same schedule on NCCL; "
+                    "nvls / push / nccl = replicated optimizer with a bucketed all-reduce")
+    ap.add_argument("--no-torch-arm", action="store_true",
+                    help="skip the same-process PyTorch (DDP + cuBLAS + NCCL) comparison arm")
     ap.add_argument("--layers", type=int, default=None, help="layers (default: the model's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="run the step eagerly instead of as a CUDA graph")
@@ -171,13 +175,25 @@ def build_gpt(args, rank, world, local, dev):
         from scirs_b200.models.gpt import GPTModel
         from scirs_b200.ops import kernels as K
         from scirs_b200.parallel.data_parallel import data_parallel
+        from scirs_b200.parallel.zero import zero_data_parallel
 
-        model = GPTModel(cfg, device=dev, seed=0)
-        model.configure_adamw(lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
-        if world > 1:
-            data_parallel(model, mode=args.dp_mode)
-        dp_desc = {"nvls": "NVLS in-switch all-reduce (fp32, in place)", "push": "push all-reduce (bf16 wire)",
-                   "nccl": "nccl"}.get(getattr(model.grad_sync, "mode", None))
+        hp = dict(lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
+        model = GPTModel(cfg, device=dev, seed=0, bucket_align=64 * world)
+        sharded = world > 1 and args.dp_mode in ("fused", "zero-nccl")
+        if sharded:
+            zero_data_parallel(model, mode="nccl" if args.dp_mode == "zero-nccl" else "fused", **hp)
+            zs = model.grad_sync
+            dp_desc = {"nvls": "ZeRO-1: NVLS reduce-scatter (multimem.ld_reduce, fp32) + all-gather (multimem.st, "
+                       "bf16)", "push": "ZeRO-1: push reduce-scatter / all-gather (bf16 wire)",
+                       "nccl": "ZeRO-1 on NCCL reduce-scatter / all-gather"}[zs.mode]
+            if zs.early_vocab:
+                dp_desc += "; LM-head wte gradient reduced at the start of backward, lookup rows routed to owners"
+        else:
+            model.configure_adamw(**hp)
+            if world > 1:
+                data_parallel(model, mode=args.dp_mode)
+            dp_desc = {"nvls": "NVLS in-switch all-reduce (fp32, in place)", "push": "push all-reduce (bf16 wire)",
+                       "nccl": "nccl"}.get(getattr(model.grad_sync, "mode", None))
         if not args.no_graph:
             model.enable_cuda_graph()
 
@@ -443,25 +459,15 @@ def build_tp(args, rank, world, local, dev):
     }
 
 
-def main():
-    args = parse()
-    if args.impl == "reference":
-        reference_unavailable()
-        return 0
-
+def time_arm(args, W, rank, dev, sample_clocks: bool):
+    """Warm up, then time exactly args.steps steps on the device (CUDA events
+    on the launching stream, barrier + synchronize on both sides, max over
+    ranks), then the end-to-end pass through the public API. Returns a dict."""
     import torch
 
-    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     from scirs_b200.parallel import dist as sdist
 
-    rank, world, local = sdist.init(timeout_s=300)
     N = args.gpus
-    if N != world:
-        raise SystemExit(f"--gpus {N} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    dev = torch.device("cuda", local)
-    torch.manual_seed(0)
-    builders = {"gpt2": build_gpt, "vit": build_vit, "gpt1.3b": build_tp}
-    W = builders[args.model](args, rank, world, local, dev)
     step, launches, batches = W["step"], W["launches"], W["batches"]
     dev_batches = [(a.to(dev), b.to(dev)) for a, b in batches]
 
@@ -473,7 +479,7 @@ def main():
 
     # ---- device-timed region
     clocks = ClockSampler()
-    if rank == 0:
+    if rank == 0 and sample_clocks:
         clocks.start()
         time.sleep(0.3)
     l0 = launches()
@@ -489,7 +495,7 @@ def main():
     sdist.barrier()
     ms_local = e0.elapsed_time(e1)
     n_launch = launches() - l0
-    clk = clocks.stop(N) if rank == 0 else None
+    clk = clocks.stop(N) if (rank == 0 and sample_clocks) else None
     ms = sdist.max_over_ranks(ms_local)
     ms_step = ms / args.steps
     tokens_per_step = W["tokens_per_step"]
@@ -524,21 +530,83 @@ def main():
             "d2h_bytes_per_step": 4,
             "api": W["api"],
         }
+    return {"value": value, "ms_step": ms_step, "clocks": clk, "e2e": e2e, "launches": n_launch,
+            "final_loss": final_loss}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable()
+        return 0
+
+    import gc
+
+    import torch
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from scirs_b200.parallel import dist as sdist
+
+    rank, world, local = sdist.init(timeout_s=300)
+    N = args.gpus
+    if N != world:
+        raise SystemExit(f"--gpus {N} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    builders = {"gpt2": build_gpt, "vit": build_vit, "gpt1.3b": build_tp}
+    W = builders[args.model](args, rank, world, local, dev)
+    R = time_arm(args, W, rank, dev, sample_clocks=True)
+
     if args.kernel_summary:
         from torch.profiler import ProfilerActivity, profile
 
         sdist.barrier()
-        a, b = dev_batches[0]
+        a, b = W["batches"][0]
+        a, b = a.to(dev), b.to(dev)
         if rank == 0:
             with profile(activities=[ProfilerActivity.CUDA]) as prof:
-                step(a, b)
+                W["step"](a, b)
                 torch.cuda.synchronize()
             print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30), file=sys.stderr, flush=True)
         else:
-            step(a, b)
+            W["step"](a, b)
             torch.cuda.synchronize()
         sdist.barrier()
     W["cleanup"]()
+    if args.impl == "ours":
+        from scirs_b200 import _ext
+
+        _ext.check_status(local)
+
+    # ---- same-process comparison arm: the PyTorch + cuBLAS + NCCL build of
+    # the same model and config (DDP / ZeroRedundancyOptimizer), same N,
+    # steps and warm-up, timed the same way
+    torch_arm = None
+    if args.impl == "ours" and not args.no_torch_arm:
+        cfg_ours, flops_ours = W["config"], W["flops_per_token"]
+        tokens_ours, data_ours = W["tokens_per_step"], W["data"]
+        W = None
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        targs = argparse.Namespace(**vars(args))
+        targs.impl = "torch"
+        WT = builders[args.model](targs, rank, world, local, dev)
+        RT = time_arm(targs, WT, rank, dev, sample_clocks=True)
+        torch_arm = {
+            "value": round(RT["value"], 1),
+            "ms_per_step": round(RT["ms_step"], 3),
+            "ratio": round(R["value"] / RT["value"], 4),
+            "e2e": RT["e2e"]["value"] if RT["e2e"] else None,
+            "e2e_ratio": round(R["e2e"]["value"] / RT["e2e"]["value"], 4) if (R["e2e"] and RT["e2e"]) else None,
+            "api": WT["api"],
+            "parallelism": WT["config"].get("dp_allreduce") or WT["config"].get("zero_collectives")
+            or WT["config"].get("parallelism"),
+            "clocks": RT["clocks"],
+            "final_loss": round(RT["final_loss"], 4),
+        }
+        WT["cleanup"]()
+        W = {"config": cfg_ours, "flops_per_token": flops_ours, "tokens_per_step": tokens_ours, "data": data_ours}
 
     peaks = {}
     try:
@@ -547,6 +615,7 @@ def main():
         pass
     flops_tok = W["flops_per_token"]
     peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
+    value = R["value"]
     mfu = value * flops_tok / (peak_tf * 1e12 * N)
 
     if rank == 0:
@@ -564,25 +633,23 @@ def main():
             "n_gpus": N,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 3),
+            "ms_per_step": round(R["ms_step"], 3),
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": W["data"],
             "config": cfg_out,
-            "clocks": clk,
-            "e2e": e2e,
-            "gpu_launches": n_launch if args.impl == "ours" else 0,
-            "final_loss": round(final_loss, 4),
+            "clocks": R["clocks"],
+            "e2e": R["e2e"],
+            "gpu_launches": R["launches"] if args.impl == "ours" else 0,
+            "final_loss": round(R["final_loss"], 4),
         }
+        if torch_arm is not None:
+            out["torch_arm"] = torch_arm
         if args.impl != "ours":
             out["impl"] = args.impl
         print(json.dumps(out), flush=True)
-    if args.impl == "ours":
-        from scirs_b200 import _ext
-
-        _ext.check_status(local)
     sdist.shutdown()
     return 0
 

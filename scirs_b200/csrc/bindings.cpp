@@ -15,7 +15,7 @@ void xent_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor los
 void xent_fwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss, int64_t V, int64_t ignore_index);
 void embedding_fwd(torch::Tensor tok, torch::Tensor wte, c10::optional<torch::Tensor> wpe, torch::Tensor out,
                    int64_t S);
-void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor dwte, c10::optional<torch::Tensor> dwpe,
+void embedding_bwd(torch::Tensor tok, torch::Tensor dout, c10::optional<torch::Tensor> dwte, c10::optional<torch::Tensor> dwpe,
                    int64_t S);
 void bias_grad(torch::Tensor dy, torch::Tensor out);
 void optim_step(int64_t mode, torch::Tensor params, torch::Tensor state1, torch::Tensor state2, torch::Tensor grads,
@@ -49,6 +49,11 @@ void ep_combine(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor s
 void ep_grad_w(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor slot, torch::Tensor dout,
                torch::Tensor gw, int64_t L, int64_t C, int64_t rank);
 void tp_wait(torch::Tensor flags, torch::Tensor epoch, int64_t idx, int64_t rank, int64_t world, double timeout_s);
+void vocab_route(torch::Tensor tok, torch::Tensor dout, int64_t R, int64_t V, std::vector<int64_t> rows,
+                 std::vector<int64_t> ids, int64_t rank, std::vector<int64_t> sig_flags, torch::Tensor epoch,
+                 int64_t sig_idx);
+void vocab_accum(torch::Tensor rows, torch::Tensor ids, torch::Tensor shard, double scale, int64_t rank,
+                 torch::Tensor flags, torch::Tensor epoch, int64_t wait_idx, double timeout_s);
 void paged_kv_append(torch::Tensor k_new, torch::Tensor v_new, torch::Tensor k_pool, torch::Tensor v_pool,
                      torch::Tensor block_tables, torch::Tensor seq, torch::Tensor pos);
 void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor block_tables,
@@ -98,6 +103,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("timeout_s") = 10.0);
   m.def("tp_signal", &scirs::tp_signal);
   m.def("tp_wait", &scirs::tp_wait);
+  m.def("vocab_route", &scirs::vocab_route, "send embedding-gradient rows to the rank owning each vocabulary row");
+  m.def("vocab_accum", &scirs::vocab_accum, "add the routed embedding-gradient rows into this rank's shard");
   m.def("ep_dispatch", &scirs::ep_dispatch, "expert-parallel dispatch: gather rows and store them into peers");
   m.def("ep_combine", &scirs::ep_combine, "expert-parallel combine: read expert outputs from peers, weighted sum");
   m.def("ep_grad_w", &scirs::ep_grad_w, "routing-weight gradient against peers' expert outputs");

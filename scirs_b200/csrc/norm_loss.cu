@@ -458,23 +458,29 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const bf16* __
   }
 }
 
-// dwte[tok[m]] += dout[m]; dwpe[m % S] += dout[m]  (fp32 atomics)
+// dwte[tok[m]] += dout[m]; dwpe[m % S] += dout[m]  (fp32 atomics; either
+// table may be null)
 __global__ void embed_bwd_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ dout,
                                  float* __restrict__ dwte, float* __restrict__ dwpe, int M, int S, int D, long V,
                                  DevStatus* st) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  const long t = tok[row];
-  if (!input_in_range(t, V, st, 81)) return;
-  const uint4* g = reinterpret_cast<const uint4*>(dout + (long)row * D);
-  float* a = dwte + t * D;
+  float* a = nullptr;
+  if (dwte != nullptr) {
+    const long t = tok[row];
+    if (input_in_range(t, V, st, 81)) a = dwte + t * D;
+  }
   float* p = dwpe ? dwpe + (long)(row % S) * D : nullptr;
+  if (a == nullptr && p == nullptr) return;
+  const uint4* g = reinterpret_cast<const uint4*>(dout + (long)row * D);
   for (int i = lane; i < D / 8; i += 32) {
     float f[8];
     unpack8(g[i], f);
-    atomicAdd(reinterpret_cast<float4*>(a + 8 * i), make_float4(f[0], f[1], f[2], f[3]));
-    atomicAdd(reinterpret_cast<float4*>(a + 8 * i + 4), make_float4(f[4], f[5], f[6], f[7]));
+    if (a) {
+      atomicAdd(reinterpret_cast<float4*>(a + 8 * i), make_float4(f[0], f[1], f[2], f[3]));
+      atomicAdd(reinterpret_cast<float4*>(a + 8 * i + 4), make_float4(f[4], f[5], f[6], f[7]));
+    }
     if (p) {
       atomicAdd(reinterpret_cast<float4*>(p + 8 * i), make_float4(f[0], f[1], f[2], f[3]));
       atomicAdd(reinterpret_cast<float4*>(p + 8 * i + 4), make_float4(f[4], f[5], f[6], f[7]));
@@ -642,16 +648,37 @@ void embedding_fwd(torch::Tensor tok, torch::Tensor wte, c10::optional<torch::Te
   SCIRS_CHECK_LAUNCH();
 }
 
-void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor dwte, c10::optional<torch::Tensor> dwpe,
-                   int64_t S) {
-  const int D = (int)dwte.size(1);
+void embedding_bwd(torch::Tensor tok, torch::Tensor dout, c10::optional<torch::Tensor> dwte,
+                   c10::optional<torch::Tensor> dwpe, int64_t S) {
+  const bool has_wte = dwte.has_value() && dwte->defined();
+  const bool has_wpe = dwpe.has_value() && dwpe->defined();
+  TORCH_CHECK(has_wte || has_wpe, "embedding_bwd needs dwte or dwpe");
+  CHECK_DTYPE(tok, at::kLong);
+  CHECK_CONTIG(tok);
+  CHECK_DTYPE(dout, at::kBFloat16);
+  CHECK_CONTIG(dout);
+  const int D = (int)dout.size(-1);
   const int M = (int)tok.numel();
-  CHECK_DTYPE(dwte, at::kFloat);
+  TORCH_CHECK(D % 8 == 0 && dout.numel() == (long)M * D, "dout [M, D] with D % 8 == 0");
+  float* wp = nullptr;
+  long V = 0;
+  if (has_wte) {
+    CHECK_DTYPE((*dwte), at::kFloat);
+    CHECK_CONTIG((*dwte));
+    TORCH_CHECK(dwte->size(1) == D, "dwte [V, D]");
+    wp = dwte->data_ptr<float>();
+    V = (long)dwte->size(0);
+  }
+  float* pp = nullptr;
+  if (has_wpe) {
+    CHECK_DTYPE((*dwpe), at::kFloat);
+    CHECK_CONTIG((*dwpe));
+    TORCH_CHECK(dwpe->size(-1) == D && dwpe->size(0) >= S, "dwpe [>= S, D]");
+    pp = dwpe->data_ptr<float>();
+  }
   c10::cuda::CUDAGuard g(tok.get_device());
-  float* pp = (dwpe.has_value() && dwpe->defined()) ? dwpe->data_ptr<float>() : nullptr;
-  embed_bwd_kernel<<<(M + 7) / 8, 256, 0, cur_stream()>>>(tok.data_ptr<int64_t>(), (const bf16*)dout.data_ptr(),
-                                                          dwte.data_ptr<float>(), pp, M, (int)S, D,
-                                                          (long)dwte.size(0), status_ptr(tok.get_device()));
+  embed_bwd_kernel<<<(M + 7) / 8, 256, 0, cur_stream()>>>(tok.data_ptr<int64_t>(), (const bf16*)dout.data_ptr(), wp,
+                                                          pp, M, (int)S, D, V, status_ptr(tok.get_device()));
   SCIRS_CHECK_LAUNCH();
 }
 

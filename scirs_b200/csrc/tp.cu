@@ -381,6 +381,72 @@ __global__ void __launch_bounds__(256) ep_grad_w_kernel(PeerBase srcp, const int
   }
 }
 
+// ---------------------------------------------------------------------------
+// Vocabulary-gradient routing for sharded data parallelism. The fp32
+// gradient of a [V, D] embedding table is sharded by rows over the W ranks
+// (rank o owns rows [o * R, (o + 1) * R)). The lookup part of the gradient
+// (row tok[m] += dout[m] for this rank's M tokens) is sent to the owners
+// instead of being reduced densely:
+//
+// vocab_route_kernel: a warp per token row m. Lane w < W writes the id word
+//   ids_w[rank * M + m] = tok[m] - o * R on the owner o (-1 on every other
+//   rank) and the warp stores the bf16 row into rows_o[rank * M + m] over
+//   NVLink. The last block signals every peer.
+// vocab_accum_kernel: on the owner, after every source's signal, a warp per
+//   received row adds scale * row into its shard row with fp32 vector
+//   atomics (local memory only).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) vocab_route_kernel(const int64_t* __restrict__ tok,
+                                                          const __nv_bfloat16* __restrict__ dout, long M, int D,
+                                                          long R, long V, PeerBase rows, PeerBase ids, int rank,
+                                                          int world, DevStatus* st, FlagPtrs sig,
+                                                          const unsigned* epoch, unsigned sig_idx, unsigned* done) {
+  const int lane = threadIdx.x & 31;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  const int dv = D / 8;
+  for (long m = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < M; m += nwarps) {
+    const long t = tok[m];
+    const bool valid = input_in_range(t, V, st, 87);
+    const int o = valid ? (int)(t / R) : -1;
+    if (lane < world) {
+      int* ip = reinterpret_cast<int*>(ids.p[lane]) + (long)rank * M + m;
+      *ip = (lane == o) ? (int)(t - (long)o * R) : -1;
+    }
+    if (!valid) continue;
+    const uint4* sp = reinterpret_cast<const uint4*>(dout + m * D);
+    uint4* dp = reinterpret_cast<uint4*>(rows.p[o] + ((long)rank * M + m) * D * (long)sizeof(__nv_bfloat16));
+    for (int v = lane; v < dv; v += 32) dp[v] = sp[v];
+  }
+  last_block_signal(sig, world, epoch, sig_idx, done);
+}
+
+__global__ void __launch_bounds__(256) vocab_accum_kernel(const __nv_bfloat16* __restrict__ rows,
+                                                          const int* __restrict__ ids, float* __restrict__ shard,
+                                                          float scale, long M, int D, long R, int rank, int world,
+                                                          const unsigned* flags, const unsigned* epoch,
+                                                          unsigned wait_idx, long long timeout_ns, DevStatus* st) {
+  if (!block_wait(flags, epoch, wait_idx, rank, world, timeout_ns, st, 88)) return;
+  const int lane = threadIdx.x & 31;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  const int dv = D / 8;
+  const long total = (long)world * M;
+  for (long q = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; q < total; q += nwarps) {
+    const int id = __ldcg(ids + q);
+    if (id < 0) continue;
+    if (!input_in_range(id, R, st, 89)) continue;
+    const uint4* rp = reinterpret_cast<const uint4*>(rows + q * D);
+    float* gp = shard + (long)id * D;
+    for (int v = lane; v < dv; v += 32) {
+      const uint4 x = __ldcg(rp + v);
+      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+      atomicAdd(reinterpret_cast<float4*>(gp + 8 * v),
+                make_float4(scale * bf16_lo(w[0]), scale * bf16_hi(w[0]), scale * bf16_lo(w[1]), scale * bf16_hi(w[1])));
+      atomicAdd(reinterpret_cast<float4*>(gp + 8 * v + 4),
+                make_float4(scale * bf16_lo(w[2]), scale * bf16_hi(w[2]), scale * bf16_lo(w[3]), scale * bf16_hi(w[3])));
+    }
+  }
+}
+
 // A bounded wait on every peer's signal `idx`, for consumers that are not
 // kernels of this file (library GEMMs on the received rows).
 __global__ void wait_kernel(const unsigned* flags, const unsigned* epoch, unsigned idx, int rank, int world,
@@ -623,6 +689,53 @@ void ep_grad_w(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor sl
       to_base(srcs), expert.data_ptr<int>(), slot.data_ptr<int>(),
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), gw.data_ptr<float>(), (int)expert.size(1),
       expert.size(0), (int)L, (int)C, (int)dout.size(1), (int)rank, (int)srcs.size(), status_ptr(dev));
+  SCIRS_CHECK_LAUNCH();
+}
+
+// Vocabulary-gradient routing (see vocab_route_kernel): rows[w] / ids[w] are
+// rank w's receive buffers [W, M, D] bf16 and [W, M] int32.
+void vocab_route(torch::Tensor tok, torch::Tensor dout, int64_t R, int64_t V, std::vector<int64_t> rows,
+                 std::vector<int64_t> ids, int64_t rank, std::vector<int64_t> sig_flags, torch::Tensor epoch,
+                 int64_t sig_idx) {
+  CHECK_DTYPE(tok, at::kLong);
+  CHECK_CONTIG(tok);
+  CHECK_DTYPE(dout, at::kBFloat16);
+  CHECK_CONTIG(dout);
+  TORCH_CHECK(dout.dim() == 2 && dout.size(0) == tok.numel() && dout.size(1) % 8 == 0, "dout [M, D], D % 8 == 0");
+  const int world = (int)rows.size();
+  TORCH_CHECK(world >= 1 && world <= tp::kMaxPeers && (int)ids.size() == world && (int)sig_flags.size() == world,
+              "one receive buffer, id buffer and signal word per rank");
+  TORCH_CHECK(R > 0 && R * world >= V, "rows per rank must cover the vocabulary");
+  const int dev = tok.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  tp::vocab_route_kernel<<<warp_grid(tok.numel(), dev), 256, 0, cur_stream()>>>(
+      tok.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), tok.numel(),
+      (int)dout.size(1), R, V, to_base(rows), to_base(ids), (int)rank, world, status_ptr(dev), tp::to_ptrs(sig_flags),
+      reinterpret_cast<const unsigned*>(epoch.data_ptr()), (unsigned)sig_idx, tp::done_ctr(dev));
+  SCIRS_CHECK_LAUNCH();
+}
+
+// shard [R, D] fp32 += scale * (received rows routed to this rank).
+void vocab_accum(torch::Tensor rows, torch::Tensor ids, torch::Tensor shard, double scale, int64_t rank,
+                 torch::Tensor flags, torch::Tensor epoch, int64_t wait_idx, double timeout_s) {
+  CHECK_DTYPE(rows, at::kBFloat16);
+  CHECK_CONTIG(rows);
+  CHECK_DTYPE(ids, at::kInt);
+  CHECK_CONTIG(ids);
+  CHECK_DTYPE(shard, at::kFloat);
+  CHECK_CONTIG(shard);
+  TORCH_CHECK(rows.dim() == 3 && ids.dim() == 2 && rows.size(0) == ids.size(0) && rows.size(1) == ids.size(1),
+              "rows [W, M, D], ids [W, M]");
+  TORCH_CHECK(shard.dim() == 2 && shard.size(1) == rows.size(2) && rows.size(2) % 8 == 0, "shard [R, D]");
+  const int world = (int)rows.size(0);
+  TORCH_CHECK(world <= tp::kMaxPeers && flags.numel() >= world && flags.element_size() == 4, "flags per rank");
+  const int dev = rows.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  tp::vocab_accum_kernel<<<warp_grid(ids.numel(), dev), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()), ids.data_ptr<int>(), shard.data_ptr<float>(),
+      (float)scale, rows.size(1), (int)rows.size(2), shard.size(0), (int)rank, world,
+      reinterpret_cast<const unsigned*>(flags.data_ptr()), reinterpret_cast<const unsigned*>(epoch.data_ptr()),
+      (unsigned)wait_idx, (long long)(timeout_s * 1e9), status_ptr(dev));
   SCIRS_CHECK_LAUNCH();
 }
 

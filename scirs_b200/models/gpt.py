@@ -166,12 +166,18 @@ class GPTModel(FusedTrainerMixin):
         self.device = torch.device(device)
         D, F, Vp = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_padded
         fp = FlatParams()
-        # Layout: [wte, wpe] [block 0] ... [block L-1, ln_f]; each block is a
-        # contiguous gradient bucket (ln_f rides with the last block).
+        # Layout: [wte] [wpe] [block 0] ... [block L-1, ln_f]; each is a
+        # contiguous gradient bucket (ln_f rides with the last block), padded
+        # so buckets split evenly into per-rank shards (ZeRO). wte is a bucket
+        # of its own: its LM-head gradient is final at the start of the
+        # backward pass and can be reduced while the blocks run.
         fp.add("wte", (Vp, D), decay=True)
-        fp.add("wpe", (cfg.max_position_embeddings, D), decay=True)
-        fp.pad_to(bucket_align)  # buckets split evenly into per-rank shards (ZeRO)
+        fp.pad_to(bucket_align)
         self.bucket_bounds = [(0, fp.mark())]
+        s = fp.mark()
+        fp.add("wpe", (cfg.max_position_embeddings, D), decay=True)
+        fp.pad_to(bucket_align)
+        self.bucket_bounds.append((s, fp.mark()))
         for l in range(cfg.num_hidden_layers):
             s = fp.mark()
             add_block_params(fp, f"h{l}.", D, F)
@@ -180,6 +186,8 @@ class GPTModel(FusedTrainerMixin):
                 fp.add("ln_f.bias", (D,), False)
             fp.pad_to(bucket_align)
             self.bucket_bounds.append((s, fp.mark()))
+        # bucket 0 is a [vocab_padded, D] table (rows may be owned by ranks)
+        self.vocab_grad_spec = {"rows": Vp, "dim": D, "valid": cfg.vocab_size}
         fp.allocate(self.device)
         self.fp = fp
         self._init_weights(seed)
@@ -224,10 +232,11 @@ class GPTModel(FusedTrainerMixin):
         n = 0
         self._params_begin()
         self._wait_params(0)
+        self._wait_params(1)
         K.embedding_fwd(tokens, fp.w("wte"), fp.w("wpe")[:S], A.x[0], S)
         n += 1
         for l in range(cfg.num_hidden_layers):
-            self._wait_params(l + 1)
+            self._wait_params(l + 2)
             n += block_forward(fp, f"h{l}.", A, l, H, hd, eps, causal=True)
         L = cfg.num_hidden_layers
         K.layernorm_fwd(A.x[L], fp.w("ln_f.weight"), fp.w("ln_f.bias"), A.lnf, A.muf, A.rsf, eps)
@@ -242,9 +251,15 @@ class GPTModel(FusedTrainerMixin):
         S, H, hd, L = A.S, cfg.num_attention_heads, cfg.head_dim, cfg.num_hidden_layers
         n = 0
         dlog = A.logits  # now holds dloss/dlogits
+        gs = self.grad_sync
+        early = gs is not None and getattr(gs, "early_vocab", False)
         # LM head (tied to wte): dx_f = dlogits @ wte ; dwte += dlogits^T @ lnf
         K.gemm(dlog, fp.w("wte"), A.dln, b_mn=True)
         K.gemm(dlog, A.lnf, fp.g("wte"), a_mn=True, b_mn=True, epi=K.EPI_F32, accumulate=True)
+        if early:
+            # the LM-head part of the wte gradient is final: reduce it now,
+            # overlapped with the whole backward pass
+            gs.bucket_ready(0)
         # colsum(d x[L]) is the bias gradient of the last block's fc2
         K.layernorm_bwd(A.dln, A.x[L], fp.w("ln_f.weight"), A.muf, A.rsf, A.dres, fp.g("ln_f.weight"),
                         fp.g("ln_f.bias"), A.ln_part, dsum=fp.g(f"h{L - 1}.mlp.c_proj.bias"))
@@ -254,12 +269,20 @@ class GPTModel(FusedTrainerMixin):
             # was produced by the LayerNorm backward that wrote it
             n += block_backward(fp, f"h{l}.", A, l, H, hd, causal=True,
                                 prev_fc2_bias=f"h{l - 1}.mlp.c_proj.bias" if l > 0 else None)
-            if self.grad_sync is not None:
-                self.grad_sync.bucket_ready(l + 1)
-        K.embedding_bwd(tokens, A.dres, fp.g("wte"), fp.g("wpe")[:S], S)
+            if gs is not None:
+                gs.bucket_ready(l + 2)
+        if early:
+            # lookup part of the wte gradient: rows go to their shard owners
+            gs.route_vocab(tokens, A.dres)
+            K.embedding_bwd(tokens, A.dres, None, fp.g("wpe")[:S], S)
+            gs.vocab_ready()
+        else:
+            K.embedding_bwd(tokens, A.dres, fp.g("wte"), fp.g("wpe")[:S], S)
+            if gs is not None:
+                gs.bucket_ready(0)
         n += 1
-        if self.grad_sync is not None:
-            self.grad_sync.bucket_ready(0)
+        if gs is not None:
+            gs.bucket_ready(1)
         return n
 
     # ----------------------------------------------------------------- API

@@ -226,9 +226,10 @@ def embedding_bwd(tok, dout, dwte, dwpe, S):
         _ext.kernels().embedding_bwd(tok, dout, dwte, dwpe, int(S))
         _count(1)
         return
-    D = dwte.shape[1]
+    D = dout.shape[-1]
     g = dout.float().reshape(-1, D)
-    dwte.index_add_(0, tok.reshape(-1), g)
+    if dwte is not None:
+        dwte.index_add_(0, tok.reshape(-1), g)
     if dwpe is not None:
         pos = torch.arange(tok.numel(), device=tok.device) % S
         dwpe.index_add_(0, pos, g)

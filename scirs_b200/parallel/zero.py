@@ -16,6 +16,14 @@ shard buffers, so the optimizer over them is still ONE fused launch:
              the forward on the communication stream; block i waits only for
              its own bucket (prefetch overlapped with compute)
 
+Tied vocabulary tables (the GPT engine's wte, used by the input embedding and
+the LM head) get an early reduce-scatter: the engine hands over the wte
+bucket right after the LM-head weight-gradient GEMM, so its reduce-scatter
+overlaps the whole backward pass, and the input-embedding part of the
+gradient (only the rows of this step's tokens) is sent to the rank that owns
+each row (`VocabGradRoute`: one peer-store kernel on the sender, one local
+accumulation kernel on the owner) instead of waiting for a dense reduction.
+
 The fp32 master weights and both Adam moments exist only as shards (1/world
 of the model each); the bf16 parameters and the fp32 gradient accumulator
 stay full size (the kernels read full weights; the gradient is produced
@@ -62,6 +70,84 @@ class ShardView:
         return self.master.numel()
 
 
+class VocabGradRoute:
+    """Sends the embedding-lookup part of a row-sharded vocabulary gradient to
+    the rows' owners over NVLink.
+
+    The fp32 gradient of a [V_padded, D] table is owned by rows: rank o holds
+    rows [o * R, (o + 1) * R), R = V_padded / world, as its shard of the
+    table's gradient bucket. `route(tok, dout)` (compute stream) stores each
+    of this rank's token rows dout[m] (bf16) and its row id into the owner's
+    receive buffers and signals every peer; `accumulate(shard, scale)`
+    (any stream ordered after it) waits (bounded) for every peer's signal and
+    adds scale * the received rows into the owner's shard. Receive buffers
+    live in a symmetric heap: [world, M, D] bf16 rows and [world, M] int32
+    ids (-1 where a source row belongs to another owner). A buffer is rewritten
+    one step later only after a collective that every owner joins after its
+    accumulation (the optimizer's norm all-reduce), so no read-done signal is
+    needed.
+    """
+
+    SIG = 1
+
+    def __init__(self, rows_per_rank: int, dim: int, vocab: int, timeout_s: float = 5.0, group=None):
+        self.R, self.D, self.V = int(rows_per_rank), int(dim), int(vocab)
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout_s = float(timeout_s)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.M = 0
+        self.heap = None
+        self.launches = 0
+
+    def _ensure(self, M: int):
+        """(Re)allocate the receive buffers for M tokens per rank. Collective:
+        every rank reaches it with the same M (same step shapes)."""
+        if M == self.M:
+            return
+        from .symmetric import SymmetricHeap
+
+        W, D = self.world, self.D
+        if self.heap is not None:
+            self.heap.close()
+        self.heap = SymmetricHeap(W * M * D * 2 + W * M * 4 + 8192, group=self.group)
+        self.rows = self.heap.alloc((W, M, D), torch.bfloat16)
+        self.ids = self.heap.alloc((W, M), torch.int32)
+        self.flags = self.heap.alloc((W,), torch.int32)
+        self.flags.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.rows_at = self.heap.peer_addrs(self.rows)
+        self.ids_at = self.heap.peer_addrs(self.ids)
+        self.sig = [a + 4 * self.rank for a in self.heap.peer_addrs(self.flags)]
+        self.M = M
+
+    def route(self, tok: torch.Tensor, dout: torch.Tensor):
+        from .. import _ext
+
+        self._ensure(tok.numel())
+        k = _ext.kernels()
+        k.tp_step_begin(self.epoch, None)
+        k.vocab_route(tok, dout, self.R, self.V, self.rows_at, self.ids_at, self.rank, self.sig, self.epoch,
+                      self.SIG)
+        self.launches += 2
+
+    def accumulate(self, shard: torch.Tensor, scale: float):
+        from .. import _ext
+
+        _ext.kernels().vocab_accum(self.rows, self.ids, shard, float(scale), self.rank, self.flags, self.epoch,
+                                   self.SIG, self.timeout_s)
+        self.launches += 1
+
+    def close(self):
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None
+            self.M = 0
+
+
 class ZeroSharding:
     """Owns the shard buffers and the two collectives of a ZeRO step.
 
@@ -106,6 +192,7 @@ class ZeroSharding:
             self.ag_events = [torch.cuda.Event() for _ in self.bounds]
         self.launches = 0
         self._gathered = False
+        self.vocab_route: VocabGradRoute | None = None  # set by zero_data_parallel for tied vocab tables
 
     # Host-only ranks (gloo, CPU tensors) run the same schedule synchronously
     # with collectives that gloo provides; used to test the sharding logic.
@@ -143,6 +230,30 @@ class ZeroSharding:
     def finish(self):
         if self.cuda:
             torch.cuda.current_stream().wait_stream(self.stream)
+
+    @property
+    def early_vocab(self) -> bool:
+        """True when the engine may hand over the vocabulary bucket (0) right
+        after the LM-head weight gradient and route the lookup part of the
+        gradient with :meth:`route_vocab` / :meth:`vocab_ready`."""
+        return self.vocab_route is not None
+
+    def route_vocab(self, tok: torch.Tensor, dout: torch.Tensor):
+        """Compute stream: send this rank's lookup-gradient rows to their owners."""
+        self.vocab_route.route(tok, dout)
+        self.launches += 2
+        self._route_ev = torch.cuda.Event()
+        self._route_ev.record(torch.cuda.current_stream())
+
+    def vocab_ready(self):
+        """Communication stream, after bucket 0's reduce-scatter: add the rows
+        routed to this rank (scaled by 1/world) into its shard of bucket 0."""
+        ss, se = self.shard_bounds[0]
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_event(self._route_ev)
+            vr = self.vocab_route
+            self.vocab_route.accumulate(self.grad[ss:se].view(vr.R, vr.D), 1.0 / self.world)
+            self.launches += 1
 
     # ------------------------------------------------------------ parameters
     def begin_forward(self):
@@ -308,6 +419,13 @@ def zero_data_parallel(model, mode: str = "fused", comm=None, lr=1e-3, betas=(0.
     elif mode == "nvls":
         raise RuntimeError("NVLS requested but this GPU has no NVLink multicast support")
     z = ZeroSharding(model, mode=mode, comm=comm)
+    spec = getattr(model, "vocab_grad_spec", None)
+    if spec is not None and mode in ("nvls", "push") and fp.master.is_cuda:
+        rows, dim, valid = spec["rows"], spec["dim"], spec["valid"]
+        s0, e0 = model.bucket_bounds[0]
+        N = z.world
+        if rows % N == 0 and e0 - s0 == rows * dim and N <= 8:
+            z.vocab_route = VocabGradRoute(rows // N, dim, valid)
     model.grad_sync = z
     model.param_sync = z
     model.optimizer = ZeroAdamW(z, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,

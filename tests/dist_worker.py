@@ -182,6 +182,60 @@ def case_dp_gpt():
     return res
 
 
+def case_zero_gpt():
+    """GPT with the sharded optimizer (ZeRO-1): fused (NVLS or push
+    collectives, early LM-head wte reduce-scatter, lookup-gradient rows routed
+    to their owners by the peer kernels) and the NCCL schedule == single-
+    process training on the concatenated batch; the gathered bf16 weights are
+    identical on every rank."""
+    from scirs_b200.models.gpt import GPTConfig, GPTModel
+    from scirs_b200.parallel.zero import zero_data_parallel
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = GPTConfig.tiny(vocab=1000, seq=128)
+    g = torch.Generator().manual_seed(7)
+    lb = 4
+    tok = torch.randint(0, cfg.vocab_size, (lb * world, 129), generator=g)
+    x, y = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
+    hp = dict(lr=1e-3, weight_decay=0.1, max_grad_norm=1.0)
+    res = {}
+    for mode in ("fused", "nccl"):
+        m = GPTModel(cfg, device=dev, seed=3, bucket_align=64 * world)
+        zero_data_parallel(m, mode=mode, **hp)
+        m.enable_cuda_graph()
+        losses = []
+        for _ in range(4):  # eager, capture + replay, replays
+            l = m.train_step(x[rank * lb : (rank + 1) * lb].to(dev), y[rank * lb : (rank + 1) * lb].to(dev))
+            lt = l.detach().clone()
+            dist.all_reduce(lt)
+            losses.append(float(lt) / world)
+        torch.cuda.synchronize()
+        m.param_sync.begin_forward()  # gather the last update
+        m.param_sync.finish()
+        torch.cuda.synchronize()
+        w = m.fp.p16.float()
+        w0 = w.clone()
+        dist.broadcast(w0, 0)
+        res[mode] = {"losses": losses, "replica_max_diff": float((w - w0).abs().max()),
+                     "early_vocab": bool(m.param_sync.early_vocab), "collectives": m.param_sync.mode}
+        m.release_cuda_graph()
+        if m.param_sync.vocab_route is not None:
+            m.param_sync.vocab_route.close()
+        if m.param_sync.comm is not None:
+            m.param_sync.comm.close()
+    if rank == 0:
+        from scirs_b200.optim.fused import FusedFlatOptimizer
+
+        m = GPTModel(cfg, device=dev, seed=3)
+        m.optimizer = FusedFlatOptimizer(m.fp, "adamw", lr=1e-3, betas=(0.9, 0.999), weight_decay=0.1,
+                                         max_grad_norm=1.0)
+        ref = [float(m.train_step(x.to(dev), y.to(dev))) for _ in range(4)]
+        res["single"] = {"losses": ref}
+    _ext.check_status()
+    return res
+
+
 def case_zero_vit():
     """ZeRO (sharded AdamW, reduce-scatter of gradients, all-gather of bf16
     parameters) with the fused collectives and with NCCL == single-process
@@ -234,6 +288,8 @@ def case_tp_decoder():
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg = DecoderConfig.tiny(vocab=1024, seq=256)
+    if world > 2:  # heads split over the ranks: 8 heads of 64
+        cfg.hidden_size, cfg.num_attention_heads, cfg.intermediate_size = 512, 8, 2048
     B, S = 4, 256
     g = torch.Generator().manual_seed(21)
     toks = [torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g) for _ in range(4)]
@@ -345,7 +401,7 @@ def case_pp_gpt():
 def main():
     case, out = sys.argv[1], sys.argv[2]
     sdist.init(timeout_s=60)
-    res = {"collectives": case_collectives, "nvls": case_nvls, "ring_attn": case_ring_attn, "dp_gpt": case_dp_gpt, "zero_vit": case_zero_vit,
+    res = {"collectives": case_collectives, "nvls": case_nvls, "ring_attn": case_ring_attn, "dp_gpt": case_dp_gpt, "zero_gpt": case_zero_gpt, "zero_vit": case_zero_vit,
            "tp_decoder": case_tp_decoder, "ep_moe": case_ep_moe, "pp_gpt": case_pp_gpt}[case]()
     if dist.get_rank() == 0:
         json.dump(res, open(out, "w"))

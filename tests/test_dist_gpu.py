@@ -1,8 +1,9 @@
 """Multi-GPU tests: in-kernel NVLink collectives and data-parallel training.
 
 Each test launches tests/dist_worker.py with torchrun as child processes
-(NVLS disabled, short process-group timeout, hard `timeout` around it) and
-checks rank 0's JSON verdict. Skipped when fewer than 2 GPUs are visible.
+(NCCL's NVLS disabled, short process-group timeout, hard `timeout` around it)
+and checks rank 0's JSON verdict. Every case runs at 2, 4 and 8 ranks; a
+size is skipped when fewer GPUs are visible.
 """
 import json
 import os
@@ -17,7 +18,11 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
+NPROC = [2, 4, 8]
+
+
 def _run(case, tmp_path, nproc=2, port=29611):
+    port += 40 * {2: 0, 4: 1, 8: 2}.get(nproc, 3)
     if torch.cuda.device_count() < nproc:
         pytest.skip(f"needs {nproc} GPUs")
     out = tmp_path / f"{case}.json"
@@ -30,8 +35,9 @@ def _run(case, tmp_path, nproc=2, port=29611):
     return json.load(open(out))
 
 
-def test_nvlink_collectives_2gpu(tmp_path):
-    res = _run("collectives", tmp_path, port=29611)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_nvlink_collectives(tmp_path, nproc):
+    res = _run("collectives", tmp_path, nproc=nproc, port=29611)
     for k, v in res.items():
         if k.startswith("allreduce"):
             assert v["identical"], k
@@ -42,8 +48,9 @@ def test_nvlink_collectives_2gpu(tmp_path):
             assert v["equal"], k
 
 
-def test_nvls_allreduce_2gpu(tmp_path):
-    res = _run("nvls", tmp_path, port=29615)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_nvls_allreduce(tmp_path, nproc):
+    res = _run("nvls", tmp_path, nproc=nproc, port=29615)
     if "skipped" in res:
         pytest.skip(res["skipped"])
     for k, v in res.items():
@@ -52,16 +59,18 @@ def test_nvls_allreduce_2gpu(tmp_path):
         assert v["max_err"] < tol, (k, v)
 
 
-def test_ring_attention_2gpu(tmp_path):
-    res = _run("ring_attn", tmp_path, port=29616)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_ring_attention(tmp_path, nproc):
+    res = _run("ring_attn", tmp_path, nproc=nproc, port=29616)
     for k, v in res.items():
         for name in ("o", "dq", "dk", "dv"):
             assert v[name] < 2e-2, (k, name, v)
         assert v["lse"] < 2e-2, (k, v)
 
 
-def test_data_parallel_gpt_2gpu(tmp_path):
-    res = _run("dp_gpt", tmp_path, port=29612)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_data_parallel_gpt(tmp_path, nproc):
+    res = _run("dp_gpt", tmp_path, nproc=nproc, port=29612)
     ref = res["single"]["losses"]
     for mode in ("fused", "nccl"):
         assert res[mode]["replica_max_diff"] == 0.0, mode
@@ -69,33 +78,48 @@ def test_data_parallel_gpt_2gpu(tmp_path):
             assert abs(a - b) < 2e-2, (mode, res[mode]["losses"], ref)
 
 
-def test_zero_vit_2gpu(tmp_path):
-    res = _run("zero_vit", tmp_path, port=29613)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_zero_vit(tmp_path, nproc):
+    res = _run("zero_vit", tmp_path, nproc=nproc, port=29613)
     ref = res["single"]["losses"]
     for mode in ("fused", "nccl"):
         for a, b in zip(res[mode]["losses"], ref):
             assert abs(a - b) < 3e-2, (mode, res[mode]["losses"], ref)
 
 
-def test_tensor_parallel_decoder_2gpu(tmp_path):
-    res = _run("tp_decoder", tmp_path, port=29614)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_tensor_parallel_decoder(tmp_path, nproc):
+    res = _run("tp_decoder", tmp_path, nproc=nproc, port=29614)
     ref = res["single"]["losses"]
     for mode in ("fused", "nccl"):
         for a, b in zip(res[mode]["losses"], ref):
             assert abs(a - b) < 3e-2, (mode, res[mode]["losses"], ref)
 
 
-def test_expert_parallel_peer_kernels_2gpu(tmp_path):
-    res = _run("ep_moe", tmp_path, port=29617)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_expert_parallel_peer_kernels(tmp_path, nproc):
+    res = _run("ep_moe", tmp_path, nproc=nproc, port=29617)
     for it, v in res.items():
         for name, err in v.items():
             assert err < 3e-2, (it, name, v)
 
 
-def test_pipeline_parallel_gpt_2gpu(tmp_path):
-    res = _run("pp_gpt", tmp_path, port=29618)
+@pytest.mark.parametrize("nproc", NPROC)
+def test_pipeline_parallel_gpt(tmp_path, nproc):
+    res = _run("pp_gpt", tmp_path, nproc=nproc, port=29618)
     ref = res["single"]["losses"]
     for sched in ("1f1b", "gpipe"):
         assert res[sched]["tied_diff"] == 0.0, (sched, res[sched])
         for a, b in zip(res[sched]["losses"], ref):
             assert abs(a - b) < 2e-2, (sched, res[sched]["losses"], ref)
+
+
+@pytest.mark.parametrize("nproc", NPROC)
+def test_zero_gpt(tmp_path, nproc):
+    res = _run("zero_gpt", tmp_path, nproc=nproc, port=29619)
+    ref = res["single"]["losses"]
+    assert res["fused"]["early_vocab"], res["fused"]
+    for mode in ("fused", "nccl"):
+        assert res[mode]["replica_max_diff"] == 0.0, mode
+        for a, b in zip(res[mode]["losses"], ref):
+            assert abs(a - b) < 2e-2, (mode, res[mode]["losses"], ref)
