@@ -224,7 +224,7 @@ class Evaluator:
                 args = [ev(i) for i in node.inputs]
                 v = OPS[op](*args, **node.attrs)
             for h in node.hooks:
-                h(v.detach())
+                h(tuple(t.detach() for t in v) if isinstance(v, tuple) else v.detach())
             memo[node.id] = v
             return v
 

@@ -12,6 +12,7 @@ import torch
 import torch.nn.functional as F
 
 from ..ops import functional as FN
+from . import linalg as _LA
 from .graph import Tensor, grad  # noqa: F401
 
 
@@ -85,12 +86,12 @@ OPS = {
     "scale_gradient": lambda x, scale: _ScaleGrad.apply(x, scale),
     "checkpoint": lambda x, fn: torch.utils.checkpoint.checkpoint(fn, x, use_reentrant=False),
     "custom": lambda *xs, fn: fn(*xs),
-    "matrix_inverse": torch.linalg.inv,
-    "determinant": torch.linalg.det,
+    "matrix_inverse": lambda a: _LA.inverse(a),
+    "determinant": lambda a: _LA.det(a),
     "trace": torch.trace,
     "norm": lambda x, ord_: torch.linalg.norm(x, ord_),
     "svd_values": torch.linalg.svdvals,
-    "cholesky": torch.linalg.cholesky,
+    "cholesky": lambda a: _LA.cholesky(a),
     "solve": torch.linalg.solve,
     "eigh_values": lambda x: torch.linalg.eigvalsh(x),
 }
@@ -297,3 +298,157 @@ def checkpoint(x, fn):
 def custom_op(fn, *inputs):
     """Node evaluating an arbitrary differentiable torch function of the inputs."""
     return _n("custom", *inputs, fn=fn)
+
+
+# ---------------------------------------------------------------------------
+# Extended op table. Names follow the reference's tensor_ops
+# (scirs2-autograd/src/tensor_ops/mod.rs:447-530 and the submodules
+# math_ops, reduction_ops, array_ops, activation_ops, linalg, loss_ops).
+# Every entry evaluates with differentiable torch ops (or the hand-written
+# decompositions of scirs_b200.autograd.linalg), so `grad` works through it.
+# ---------------------------------------------------------------------------
+def _rms_norm(x, g, eps):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * g
+
+
+def _focal(logits, t, gamma, alpha):
+    p = torch.sigmoid(logits)
+    ce = F.binary_cross_entropy_with_logits(logits, t, reduction="none")
+    pt = p * t + (1 - p) * (1 - t)
+    a = alpha * t + (1 - alpha) * (1 - t)
+    return a * (1 - pt) ** gamma * ce
+
+
+_UNARY_EXTRA = {
+    "tan": torch.tan, "asin": torch.asin, "acos": torch.acos, "atan": torch.atan, "sinh": torch.sinh,
+    "cosh": torch.cosh, "asinh": torch.asinh, "acosh": torch.acosh, "atanh": torch.atanh, "exp2": torch.exp2,
+    "expm1": torch.expm1, "log2": torch.log2, "log10": torch.log10, "log1p": torch.log1p, "rsqrt": torch.rsqrt,
+    "reciprocal": torch.reciprocal, "inv": torch.reciprocal, "sign": torch.sign, "floor": torch.floor,
+    "ceil": torch.ceil, "round": torch.round, "trunc": torch.trunc, "frac": torch.frac, "erf": torch.erf,
+    "erfc": torch.erfc, "erfinv": torch.erfinv, "lgamma": torch.lgamma, "digamma": torch.digamma,
+    "sinc": torch.sinc, "logit": torch.logit, "hard_sigmoid": F.hardsigmoid, "hard_tanh": F.hardtanh,
+    "hard_swish": F.hardswish, "mish": F.mish, "selu": F.selu, "softsign": F.softsign,
+    "log_sigmoid": F.logsigmoid, "relu6": F.relu6, "silu": F.silu, "gelu_exact": F.gelu,
+    "tanhshrink": F.tanhshrink, "neg_log": lambda x: -torch.log(x), "cube": lambda x: x * x * x,
+    "ones_like": torch.ones_like, "zeros_like": torch.zeros_like, "isfinite": lambda x: torch.isfinite(x).float(),
+    "isnan": lambda x: torch.isnan(x).float(), "logical_not": lambda x: (~x.bool()).float(),
+    "flatten": lambda x: x.reshape(x.shape[0], -1), "size": lambda x: torch.tensor(float(x.numel())),
+    "shape": lambda x: torch.tensor(list(x.shape)), "rank": lambda x: torch.tensor(x.dim()),
+    "diag": torch.diag, "diag_part": lambda x: torch.diagonal(x, dim1=-2, dim2=-1),
+    "diag_embed": torch.diag_embed, "tril": torch.tril, "triu": torch.triu,
+    "global_avg_pool2d": lambda x: x.mean((2, 3)), "frobenius_norm": lambda x: torch.linalg.norm(x, "fro"),
+    "nuclear_norm": lambda x: _LA.svd(x)[1].sum(), "spectral_norm": lambda x: _LA.svd(x)[1].max(),
+    "logabsdet": lambda a: _LA.logabsdet(a), "matrix_exp": torch.linalg.matrix_exp,
+    "pinv": lambda a: _LA.pinv(a), "qr": lambda a: _LA.qr(a), "svd": lambda a: _LA.svd(a),
+    "eigh": lambda a: _LA.eigh(a), "eig": torch.linalg.eig, "eigvals": torch.linalg.eigvals,
+    "l2_normalize": lambda x: F.normalize(x, dim=-1), "var_all": torch.var, "std_all": torch.std,
+}
+
+_BINARY_EXTRA = {
+    "atan2": torch.atan2, "hypot": torch.hypot, "fmod": torch.fmod, "remainder": torch.remainder,
+    "pow_tensor": torch.pow, "squared_difference": lambda a, b: (a - b) ** 2, "logaddexp": torch.logaddexp,
+    "xlogy": torch.xlogy, "copysign": torch.copysign, "floor_div": torch.floor_divide,
+    "greater": lambda a, b: (a > b).float(), "greater_equal": lambda a, b: (a >= b).float(),
+    "less": lambda a, b: (a < b).float(), "less_equal": lambda a, b: (a <= b).float(),
+    "equal": lambda a, b: (a == b).float(), "not_equal": lambda a, b: (a != b).float(),
+    "logical_and": lambda a, b: (a.bool() & b.bool()).float(), "logical_or": lambda a, b: (a.bool() | b.bool()).float(),
+    "logical_xor": lambda a, b: (a.bool() ^ b.bool()).float(), "outer": torch.outer, "dot": torch.dot,
+    "kron": torch.kron, "cross": lambda a, b: torch.linalg.cross(a, b), "cholesky_solve": lambda b, l: _LA.cholesky_solve(b, l),
+    "lstsq": lambda a, b: _LA.lstsq(a, b), "bias_add": lambda x, b: x + b, "cosine_similarity": lambda a, b: F.cosine_similarity(a, b, -1),
+    "l1_loss": lambda a, b: (a - b).abs().mean(), "kl_div": lambda logp, q: F.kl_div(logp, q, reduction="batchmean"),
+    "nll_loss": lambda logp, t: F.nll_loss(logp, t.long().reshape(-1)),
+    "binary_cross_entropy": lambda p, t: F.binary_cross_entropy(p, t), "log_cosh": lambda a, b: torch.log(torch.cosh(a - b)).mean(),
+    "hinge_loss": lambda y, t: torch.clamp(1 - y * t, min=0).mean(), "squared_hinge_loss": lambda y, t: torch.clamp(1 - y * t, min=0).pow(2).mean(),
+    "poisson_nll": lambda logr, t: F.poisson_nll_loss(logr, t), "embedding_lookup": lambda w, ids: F.embedding(ids.long(), w),
+    "prelu": lambda x, a: F.prelu(x, a), "masked_fill_zero": lambda x, m: x * (1 - m.float()),
+}
+
+_ATTR_EXTRA = {
+    "celu": lambda x, alpha: F.celu(x, alpha), "softshrink": lambda x, lambd: F.softshrink(x, lambd),
+    "hardshrink": lambda x, lambd: F.hardshrink(x, lambd), "glu": lambda x, axis: F.glu(x, axis),
+    "cumsum": lambda x, axis: torch.cumsum(x, axis), "cumprod": lambda x, axis: torch.cumprod(x, axis),
+    "reduce_logsumexp": lambda x, axes, keep_dims: torch.logsumexp(x, axes, keepdim=keep_dims),
+    "reduce_variance": lambda x, axes, keep_dims: x.var(axes, unbiased=False, keepdim=keep_dims),
+    "reduce_std": lambda x, axes, keep_dims: x.std(axes, unbiased=False, keepdim=keep_dims),
+    "reduce_l2": lambda x, axes, keep_dims: x.pow(2).sum(axes, keepdim=keep_dims).sqrt(),
+    "reduce_all": lambda x, axes, keep_dims: x.bool().all(axes, keepdim=keep_dims).float(),
+    "reduce_any": lambda x, axes, keep_dims: x.bool().any(axes, keepdim=keep_dims).float(),
+    "count_nonzero": lambda x, axes: torch.count_nonzero(x, axes).float(),
+    "argmin": lambda x, axis: x.argmin(axis), "argsort": lambda x, axis, descending: x.argsort(axis, descending),
+    "sort": lambda x, axis, descending: torch.sort(x, axis, descending).values,
+    "top_k": lambda x, k: torch.topk(x, k, -1).values, "tile": lambda x, reps: x.repeat(*reps),
+    "repeat": lambda x, n, axis: torch.repeat_interleave(x, n, axis), "pad": lambda x, pads, value: F.pad(x, pads, value=value),
+    "flip": lambda x, axes: torch.flip(x, axes), "roll": lambda x, shift, axis: torch.roll(x, shift, axis),
+    "broadcast_to": lambda x, shape: x.expand(*shape), "swap_axes": lambda x, a, b: x.transpose(a, b),
+    "split": lambda x, sizes, axis: tuple(torch.split(x, sizes, axis)), "unstack": lambda x, axis: tuple(torch.unbind(x, axis)),
+    "cast": lambda x, dtype: x.to(getattr(torch, dtype)), "fill": lambda shape, value: torch.full(tuple(shape), float(value)),
+    "eye": lambda n: torch.eye(n), "range": lambda start, end, step: torch.arange(start, end, step, dtype=torch.float32),
+    "linspace": lambda start, end, n: torch.linspace(start, end, n), "matrix_power": lambda a, n: _LA.matrix_power(a, n),
+    "tensordot": lambda a, b, axes: torch.tensordot(a, b, axes), "einsum": lambda *xs, eq: torch.einsum(eq, *xs),
+    "triangular_solve": lambda a, b, upper: torch.linalg.solve_triangular(a, b, upper=upper),
+    "moments": lambda x, axes, keep_dims: (x.mean(axes, keepdim=keep_dims), x.var(axes, unbiased=False, keepdim=keep_dims)),
+    "conv1d": lambda x, w, stride, padding: F.conv1d(x, w, None, stride, padding),
+    "conv3d": lambda x, w, stride, padding: F.conv3d(x, w, None, stride, padding),
+    "depthwise_conv2d": lambda x, w, stride, padding: F.conv2d(x, w, None, stride, padding, groups=x.shape[1]),
+    "max_pool1d": lambda x, size, stride: F.max_pool1d(x, size, stride), "avg_pool1d": lambda x, size, stride: F.avg_pool1d(x, size, stride),
+    "adaptive_avg_pool2d": lambda x, size: F.adaptive_avg_pool2d(x, size),
+    "upsample_nearest": lambda x, scale: F.interpolate(x, scale_factor=scale, mode="nearest"),
+    "upsample_bilinear": lambda x, scale: F.interpolate(x, scale_factor=scale, mode="bilinear", align_corners=False),
+    "group_norm": lambda x, g, b, groups, eps: F.group_norm(x, groups, g, b, eps),
+    "instance_norm": lambda x, eps: F.instance_norm(x, eps=eps), "rms_norm": _rms_norm,
+    "linear": lambda x, w, b: x @ w + b, "gather": lambda x, idx, axis: torch.gather(x, axis, idx.long()),
+    "index_select": lambda x, idx, axis: torch.index_select(x, axis, idx.long()),
+    "scatter_add": lambda x, idx, src, axis: x.scatter_add(axis, idx.long(), src),
+    "attention": lambda q, k, v, causal: F.scaled_dot_product_attention(q, k, v, is_causal=causal),
+    "huber_loss": lambda a, b, delta: F.huber_loss(a, b, delta=delta), "smooth_l1": lambda a, b, beta: F.smooth_l1_loss(a, b, beta=beta),
+    "focal_loss": _focal, "leaky_relu6": lambda x, alpha: torch.clamp(F.leaky_relu(x, alpha), max=6.0),
+    "norm_p": lambda x, p, axes: torch.linalg.vector_norm(x, p, axes),
+}
+
+OPS.update(_UNARY_EXTRA)
+OPS.update(_BINARY_EXTRA)
+OPS.update(_ATTR_EXTRA)
+
+
+def _builder(name):
+    def f(*inputs, **attrs):
+        return _n(name, *inputs, **attrs)
+
+    f.__name__ = name
+    f.__doc__ = f"Graph node for op '{name}'."
+    return f
+
+
+import builtins as _builtins  # noqa: E402
+
+for _name in list(_UNARY_EXTRA) + list(_BINARY_EXTRA) + list(_ATTR_EXTRA):
+    # names of Python builtins (range, round) get a trailing underscore so
+    # the module keeps using the builtins
+    _key = _name + "_" if hasattr(_builtins, _name) else _name
+    if _key not in globals():
+        globals()[_key] = _builder(_name)
+arange = globals()["range_"]
+
+
+def _multi(name, n):
+    def f(x):
+        node = _n(name, x)
+        return tuple(node[i] for i in range(n))
+
+    f.__name__ = name
+    return f
+
+
+# multi-output decompositions return one node per factor
+qr = _multi("qr", 2)  # (Q, R)
+svd = _multi("svd", 3)  # (U, S, V)   A = U diag(S) V^T
+eigh = _multi("eigh", 2)  # (w, V)    A = V diag(w) V^T
+eig = _multi("eig", 2)  # complex (w, V) of a general matrix
+moments = lambda x, axes, keep_dims=False: tuple(_n("moments", x, axes=axes, keep_dims=keep_dims)[i] for i in range(2))  # noqa: E731
+inverse = globals()["matrix_inverse"]
+det = globals()["determinant"]
+
+
+def op_names() -> list[str]:
+    """Every op the evaluator knows."""
+    return sorted(OPS)

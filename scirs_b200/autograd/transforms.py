@@ -94,7 +94,7 @@ class GradientChecker:
         self.eps, self.rtol, self.atol = eps, rtol, atol
 
     def check(self, fn, *inputs) -> GradCheckResult:
-        xs = [x.detach().double().clone().requires_grad_(True) for x in inputs]
+        xs = [x.detach().double().contiguous().clone().requires_grad_(True) for x in inputs]
         y = fn(*xs)
         analytic = torch.autograd.grad(y.sum(), xs, allow_unused=True)
         max_abs = max_rel = 0.0
