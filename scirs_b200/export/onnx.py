@@ -62,7 +62,8 @@ class OnnxTensor:
         return n
 
     def to_torch(self) -> torch.Tensor:
-        return torch.tensor(self.data, dtype=torch.float32).reshape(self.dims)
+        dt = torch.int64 if self.data_type == INT64 else torch.float32
+        return torch.tensor(self.data, dtype=dt).reshape(self.dims)
 
 
 @dataclass
@@ -444,6 +445,32 @@ def export_sequential(model, input_shape, name: str = "model") -> OnnxModel:
 
 
 # ---------------------------------------------------------------- interpreter
+_ELEMENTWISE = {
+    "Add": torch.add, "Sub": torch.sub, "Mul": torch.mul, "Div": torch.div, "Pow": torch.pow, "Neg": torch.neg,
+    "Exp": torch.exp, "Log": torch.log, "Sqrt": torch.sqrt, "Abs": torch.abs, "Sin": torch.sin, "Cos": torch.cos,
+    "Tan": torch.tan, "Asin": torch.asin, "Acos": torch.acos, "Atan": torch.atan, "Sinh": torch.sinh,
+    "Cosh": torch.cosh, "Erf": torch.erf, "Floor": torch.floor, "Ceil": torch.ceil, "Sign": torch.sign,
+    "Round": torch.round, "Reciprocal": torch.reciprocal, "Max": torch.maximum, "Min": torch.minimum,
+    "Softplus": lambda t: torch.nn.functional.softplus(t), "Selu": lambda t: torch.nn.functional.selu(t),
+    "Softsign": lambda t: torch.nn.functional.softsign(t), "HardSwish": lambda t: torch.nn.functional.hardswish(t),
+    "Mish": lambda t: torch.nn.functional.mish(t),
+}
+
+
+def _reduce(op, x, axes, keep):
+    fn = {"ReduceSum": torch.sum, "ReduceMean": torch.mean, "ReduceProd": None, "ReduceMax": torch.amax,
+          "ReduceMin": torch.amin}[op]
+    if axes is None:
+        if op == "ReduceProd":
+            return x.prod()
+        return x.max() if op == "ReduceMax" else (x.min() if op == "ReduceMin" else fn(x))
+    if op == "ReduceProd":
+        for ax in sorted(axes, reverse=True):
+            x = x.prod(ax, keepdim=keep)
+        return x
+    return fn(x, tuple(int(v) for v in axes), keepdim=keep)
+
+
 def run_graph(graph: OnnxGraph, feeds: dict) -> dict:
     import torch.nn.functional as F
 
@@ -487,6 +514,38 @@ def run_graph(graph: OnnxGraph, feeds: dict) -> dict:
             y = F.avg_pool2d(x[0], a["kernel_shape"], a.get("strides"))
         elif op == "GlobalAveragePool":
             y = x[0].mean(dim=(2, 3), keepdim=True)
+        elif op in _ELEMENTWISE:
+            y = _ELEMENTWISE[op](*x)
+        elif op in ("ReduceSum", "ReduceMean", "ReduceMax", "ReduceMin", "ReduceProd"):
+            y = _reduce(op, x[0], x[1].tolist() if len(x) > 1 else None, bool(a.get("keepdims", 1)))
+        elif op == "MatMul":
+            y = x[0] @ x[1]
+        elif op == "Reshape":
+            y = x[0].reshape([int(v) for v in x[1].tolist()])
+        elif op == "Transpose":
+            y = x[0].permute(*a["perm"])
+        elif op == "Concat":
+            y = torch.cat(x, a["axis"])
+        elif op == "Unsqueeze":
+            y = x[0]
+            for ax in sorted(int(v) for v in x[1].reshape(-1).tolist()):
+                y = y.unsqueeze(ax)
+        elif op == "Squeeze":
+            y = x[0].squeeze(int(x[1].reshape(-1)[0]))
+        elif op in ("Softmax", "LogSoftmax"):
+            y = (torch.softmax if op == "Softmax" else torch.log_softmax)(x[0], a.get("axis", -1))
+        elif op == "Clip":
+            y = x[0].clamp(float(x[1]), float(x[2]))
+        elif op == "Cast":
+            y = x[0].bool() if a.get("to") == 9 else x[0].float()
+        elif op == "Where":
+            y = torch.where(x[0].bool(), x[1], x[2])
+        elif op == "Gather":
+            y = torch.index_select(x[0], a.get("axis", 0), x[1].reshape(-1).long())
+            if x[1].dim() == 0:
+                y = y.squeeze(a.get("axis", 0))
+        elif op == "HardSigmoid":
+            y = (a.get("alpha", 0.2) * x[0] + a.get("beta", 0.5)).clamp(0, 1)
         else:
             raise NotImplementedError(op)
         env[n.outputs[0]] = y
