@@ -116,3 +116,153 @@ class GradientRepr:
             else:
                 d += other.to_dense().to(d.device, d.dtype)
             self.value = d
+
+
+class SparseTensor:
+    """N-dimensional sparse tensor: sorted unique flat (row-major) indices
+    with their values over a dense shape. Backed by torch COO tensors for
+    products with dense operands, so `matmul` is differentiable with respect
+    to the dense side and the values.
+
+    Reference parity: scirs2-autograd/src/sparse/sparse_tensor.rs:17-260
+    (new / zeros / from_dense / flat<->coords / to_dense / accumulate /
+    reshape / slice_first_dim / to_sparse_grad)."""
+
+    def __init__(self, shape, indices, values):
+        self.shape = tuple(int(s) for s in shape)
+        self.total = 1
+        for s in self.shape:
+            self.total *= s
+        g = SparseGrad(indices, values, self.total)
+        self.indices, self.values = g.indices, g.values
+
+    @classmethod
+    def zeros(cls, shape) -> "SparseTensor":
+        return cls(shape, [], [])
+
+    @classmethod
+    def from_dense(cls, dense: torch.Tensor, threshold: float = 0.0) -> "SparseTensor":
+        g = SparseGrad.from_dense(dense, threshold)
+        return cls(dense.shape, g.indices, g.values)
+
+    def total_size(self) -> int:
+        return self.total
+
+    def nnz(self) -> int:
+        return int(self.indices.numel())
+
+    def flat_to_coords(self, flat: int) -> list[int]:
+        out = []
+        for s in reversed(self.shape):
+            out.append(flat % s)
+            flat //= s
+        return out[::-1]
+
+    def coords_to_flat(self, coords) -> int:
+        if len(coords) != len(self.shape) or any(not 0 <= c < s for c, s in zip(coords, self.shape)):
+            raise ValueError(f"coordinates {coords} outside shape {self.shape}")
+        f = 0
+        for c, s in zip(coords, self.shape):
+            f = f * s + int(c)
+        return f
+
+    def coords(self) -> torch.Tensor:
+        """[ndim, nnz] coordinate matrix."""
+        out, rem = [], self.indices.clone()
+        for s in reversed(self.shape):
+            out.append(rem % s)
+            rem = rem // s
+        return torch.stack(out[::-1]) if out else rem.reshape(0, 0)
+
+    def to_dense(self) -> torch.Tensor:
+        d = torch.zeros(self.total, dtype=self.values.dtype, device=self.values.device)
+        d[self.indices] = self.values
+        return d.reshape(self.shape)
+
+    def to_torch(self) -> torch.Tensor:
+        return torch.sparse_coo_tensor(self.coords(), self.values, self.shape).coalesce()
+
+    def to_sparse_grad(self) -> SparseGrad:
+        return SparseGrad(self.indices.clone(), self.values.clone(), self.total)
+
+    def accumulate(self, other: "SparseTensor"):
+        if other.shape != self.shape:
+            raise ValueError(f"shape mismatch {self.shape} vs {other.shape}")
+        g = SparseGrad(torch.cat([self.indices, other.indices]), torch.cat([self.values, other.values]), self.total)
+        self.indices, self.values = g.indices, g.values
+
+    def reshape(self, shape) -> "SparseTensor":
+        t = SparseTensor.zeros(shape)
+        if t.total != self.total:
+            raise ValueError(f"cannot reshape {self.shape} to {tuple(shape)}")
+        t.indices, t.values = self.indices.clone(), self.values.clone()
+        return t
+
+    def slice_first_dim(self, start: int, end: int) -> "SparseTensor":
+        if not 0 <= start <= end <= self.shape[0]:
+            raise ValueError("slice outside the first dimension")
+        inner = self.total // self.shape[0] if self.shape[0] else 0
+        keep = (self.indices >= start * inner) & (self.indices < end * inner)
+        t = SparseTensor.zeros((end - start,) + self.shape[1:])
+        t.indices, t.values = self.indices[keep] - start * inner, self.values[keep]
+        return t
+
+    def matmul(self, dense: torch.Tensor) -> torch.Tensor:
+        """(sparse [m, k]) @ (dense [k, n]) -> dense [m, n]."""
+        if len(self.shape) != 2:
+            raise ValueError("matmul needs a 2-D sparse operand")
+        return torch.sparse.mm(self.to_torch().to(dense.dtype), dense)
+
+
+class SparseGradAccumulator:
+    """Per-parameter gradient accumulation over steps, keeping sparse
+    gradients sparse (reference: sparse_tensor.rs:290-380)."""
+
+    def __init__(self):
+        self.grads: dict[str, GradientRepr] = {}
+        self.steps = 0
+
+    def accumulate_sparse(self, name: str, grad: SparseGrad):
+        if name in self.grads:
+            self.grads[name].accumulate(GradientRepr(grad))
+        else:
+            self.grads[name] = GradientRepr(SparseGrad(grad.indices.clone(), grad.values.clone(), grad.shape))
+
+    def accumulate_dense(self, name: str, grad: torch.Tensor):
+        if name in self.grads:
+            self.grads[name].accumulate(GradientRepr(grad.reshape(-1)))
+        else:
+            self.grads[name] = GradientRepr(grad.reshape(-1).clone())
+
+    def step(self):
+        self.steps += 1
+
+    def num_steps(self) -> int:
+        return self.steps
+
+    def averaged_grad(self, name: str) -> torch.Tensor | None:
+        if name not in self.grads:
+            return None
+        return self.grads[name].to_dense() / max(1, self.steps)
+
+    def raw_grad(self, name: str):
+        return self.grads.get(name)
+
+    def param_names(self) -> list[str]:
+        return sorted(self.grads)
+
+    def clear(self):
+        self.grads.clear()
+        self.steps = 0
+
+
+def embedding_backward(ids: torch.Tensor, grad_out: torch.Tensor, num_embeddings: int) -> SparseTensor:
+    """Gradient of an embedding lookup as a sparse [num_embeddings, dim]
+    tensor holding only the rows that were looked up (duplicates summed)."""
+    dim = grad_out.shape[-1]
+    ids = ids.reshape(-1).long()
+    g = grad_out.reshape(-1, dim)
+    if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= num_embeddings):
+        raise ValueError("embedding id out of range")
+    flat = (ids[:, None] * dim + torch.arange(dim, device=ids.device)[None, :]).reshape(-1)
+    return SparseTensor((num_embeddings, dim), flat, g.reshape(-1).float())

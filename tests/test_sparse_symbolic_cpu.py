@@ -42,3 +42,39 @@ def test_symbolic_tape_reverse_mode():
     g = t.gradient({"a": 0.5, "b": 2.0}, out)
     s = 0.5 * 2.0 + math.exp(0.5)
     assert abs(g["a"] - (2.0 + math.exp(0.5)) / s) < 1e-12 and abs(g["b"] - 0.5 / s) < 1e-12
+
+
+def test_sparse_tensor_nd_and_products():
+    d = torch.zeros(3, 4, 5)
+    d[0, 1, 2], d[2, 3, 4], d[1, 0, 0] = 1.5, -2.0, 0.25
+    st = SP.SparseTensor.from_dense(d)
+    assert st.nnz() == 3 and st.total_size() == 60 and torch.equal(st.to_dense(), d)
+    f = st.coords_to_flat([2, 3, 4])
+    assert st.flat_to_coords(f) == [2, 3, 4]
+    assert torch.equal(st.reshape((12, 5)).to_dense(), d.reshape(12, 5))
+    assert torch.equal(st.slice_first_dim(1, 3).to_dense(), d[1:3])
+    st.accumulate(SP.SparseTensor.from_dense(d))
+    assert torch.equal(st.to_dense(), 2 * d)
+    m = SP.SparseTensor.from_dense(torch.tensor([[0.0, 2.0], [1.0, 0.0], [0.0, 0.0]]))
+    x = torch.randn(2, 3, requires_grad=True)
+    y = m.matmul(x)
+    assert torch.allclose(y, m.to_dense() @ x)
+    y.sum().backward()
+    assert torch.allclose(x.grad, m.to_dense().t() @ torch.ones(3, 3))
+
+
+def test_embedding_backward_and_accumulator():
+    ids = torch.tensor([3, 1, 3])
+    go = torch.arange(6.0).reshape(3, 2)
+    g = SP.embedding_backward(ids, go, num_embeddings=5)
+    dense = g.to_dense()
+    assert torch.equal(dense[3], go[0] + go[2]) and torch.equal(dense[1], go[1]) and dense[0].abs().sum() == 0
+    acc = SP.SparseGradAccumulator()
+    acc.accumulate_sparse("emb", g.to_sparse_grad())
+    acc.step()
+    acc.accumulate_sparse("emb", g.to_sparse_grad())
+    acc.step()
+    assert acc.raw_grad("emb").is_sparse()
+    assert torch.allclose(acc.averaged_grad("emb"), dense.reshape(-1))
+    acc.accumulate_dense("w", torch.ones(4))
+    assert acc.param_names() == ["emb", "w"]
