@@ -49,6 +49,17 @@ void ep_combine(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor s
 void ep_grad_w(std::vector<int64_t> srcs, torch::Tensor expert, torch::Tensor slot, torch::Tensor dout,
                torch::Tensor gw, int64_t L, int64_t C, int64_t rank);
 void tp_wait(torch::Tensor flags, torch::Tensor epoch, int64_t idx, int64_t rank, int64_t world, double timeout_s);
+void conv_im2col(torch::Tensor x, torch::Tensor cols, int64_t KH, int64_t KW, int64_t sh, int64_t sw, int64_t ph,
+                 int64_t pw, int64_t dh, int64_t dw);
+void conv_col2im(torch::Tensor dcols, torch::Tensor dx, int64_t KH, int64_t KW, int64_t sh, int64_t sw, int64_t ph,
+                 int64_t pw, int64_t dh, int64_t dw);
+void conv_rows_nchw(torch::Tensor rows, torch::Tensor y, bool to_nchw);
+void pool2d_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> arg, int64_t KH, int64_t KW,
+                int64_t sh, int64_t sw, int64_t ph, int64_t pw, bool is_max, bool count_pad);
+void pool2d_bwd(torch::Tensor dy, torch::Tensor dx, c10::optional<torch::Tensor> arg, int64_t KH, int64_t KW,
+                int64_t sh, int64_t sw, int64_t ph, int64_t pw, bool is_max, bool count_pad);
+void dgelu_mul(torch::Tensor gy, torch::Tensor pre, torch::Tensor out);
+void scale_by(torch::Tensor x, torch::Tensor g, torch::Tensor count, torch::Tensor out);
 void vocab_route(torch::Tensor tok, torch::Tensor dout, int64_t R, int64_t V, std::vector<int64_t> rows,
                  std::vector<int64_t> ids, int64_t rank, std::vector<int64_t> sig_flags, torch::Tensor epoch,
                  int64_t sig_idx);
@@ -103,6 +114,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("timeout_s") = 10.0);
   m.def("tp_signal", &scirs::tp_signal);
   m.def("tp_wait", &scirs::tp_wait);
+  m.def("conv_im2col", &scirs::conv_im2col, "NCHW input -> im2col rows for the convolution GEMM");
+  m.def("conv_col2im", &scirs::conv_col2im, "im2col-row gradients -> NCHW input gradient (deterministic gather)");
+  m.def("conv_rows_nchw", &scirs::conv_rows_nchw, "GEMM rows (NHWC) <-> NCHW");
+  m.def("pool2d_fwd", &scirs::pool2d_fwd, "2-D max / average pooling forward");
+  m.def("pool2d_bwd", &scirs::pool2d_bwd, "2-D max / average pooling backward");
+  m.def("dgelu_mul", &scirs::dgelu_mul, "out = gy * gelu'(pre)");
+  m.def("scale_by", &scirs::scale_by, "out = x * g / count (device scalars)");
   m.def("vocab_route", &scirs::vocab_route, "send embedding-gradient rows to the rank owning each vocabulary row");
   m.def("vocab_accum", &scirs::vocab_accum, "add the routed embedding-gradient rows into this rank's shard");
   m.def("ep_dispatch", &scirs::ep_dispatch, "expert-parallel dispatch: gather rows and store them into peers");

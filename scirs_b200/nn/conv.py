@@ -6,9 +6,13 @@
   GlobalAvgPool2D               scirs2-neural/src/layers/conv/pooling.rs
   ResNetBlock                   scirs2-python/tests/test_neural.py:354-415 (API)
 
-Convolutions are not on the benchmarked hot path of this framework; they
-use PyTorch's implementation (cuDNN on GPU) with the reference's layout
-(NCHW) and initialisation.
+On CUDA tensors the convolution runs on the framework's kernels (im2col
+kernel -> tcgen05 GEMM with the bias in its epilogue -> NCHW layout kernel;
+backward: dgrad GEMM + deterministic col2im gather, fp32 wgrad GEMM, bias
+column sums) and pooling on its own max / average kernels, see
+scirs_b200/ops/functional.py (conv2d, max_pool2d, avg_pool2d) and
+scirs_b200/csrc/conv.cu. On the CPU they use PyTorch (the oracle). Layout
+(NCHW) and initialisation follow the reference.
 """
 from __future__ import annotations
 
@@ -18,6 +22,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..ops import functional as FN
 from .base import Layer
 from .layers import BatchNorm
 
@@ -48,7 +53,7 @@ class Conv2D(Layer):
         self.padding_mode = padding if isinstance(padding, str) else "explicit"
 
     def forward(self, x):
-        return F.conv2d(x, self.weight, self.bias, self.stride, self.padding)
+        return FN.conv2d(x, self.weight, self.bias, self.stride, self.padding)
 
 
 class MaxPool2D(Layer):
@@ -57,7 +62,7 @@ class MaxPool2D(Layer):
         self.kernel_size, self.stride, self.padding = kernel_size, stride or kernel_size, padding
 
     def forward(self, x):
-        return F.max_pool2d(x, self.kernel_size, self.stride, self.padding)
+        return FN.max_pool2d(x, self.kernel_size, self.stride, self.padding)
 
 
 class AvgPool2D(Layer):
@@ -66,7 +71,7 @@ class AvgPool2D(Layer):
         self.kernel_size, self.stride, self.padding = kernel_size, stride or kernel_size, padding
 
     def forward(self, x):
-        return F.avg_pool2d(x, self.kernel_size, self.stride, self.padding)
+        return FN.avg_pool2d(x, self.kernel_size, self.stride, self.padding)
 
 
 class GlobalAvgPool2D(Layer):

@@ -18,6 +18,24 @@ def _native(*ts) -> bool:
     return all(t is None or (t.is_cuda and t.dtype == torch.bfloat16) for t in ts)
 
 
+_warned: set = set()
+
+
+def _fallback(op: str, *ts):
+    """Record (and warn once per op) that a CUDA call is served by PyTorch
+    instead of the framework's kernels (dtype other than bf16, or a shape the
+    kernels do not take). CPU calls are the reference semantics, not a
+    fallback."""
+    if any(t is not None and t.is_cuda for t in ts):
+        K.STATS.fallbacks[op] = K.STATS.fallbacks.get(op, 0) + 1
+        if op not in _warned:
+            import warnings
+
+            _warned.add(op)
+            warnings.warn(f"scirs_b200.{op}: CUDA call served by PyTorch (needs bf16 and aligned shapes for the "
+                          f"native kernels); counted in ops.kernels.STATS.fallbacks", stacklevel=3)
+
+
 def _aligned(*dims) -> bool:
     return all(d % 8 == 0 for d in dims)
 
@@ -54,8 +72,8 @@ class _LinearFn(torch.autograd.Function):
         kmaj = ctx.kmaj
         n_out = bw.shape[0] if kmaj else bw.shape[1]
         g2 = gy.reshape(-1, n_out).contiguous()
-        if pre is not None:
-            g2 = (g2.float() * K.gelu_tanh_grad(pre.float())).to(g2.dtype)
+        if pre is not None:  # gradient w.r.t. the pre-activation of the fused bias+GELU epilogue
+            g2 = K.dgelu_mul(g2, pre, torch.empty_like(g2))
         dx = torch.empty_like(x2)
         # dX = dY W^T: W[in,out] is a K-major [N=in, K=out] operand; W_oi [out,in] an MN-major one.
         K.gemm(g2, bw, dx, b_mn=kmaj)
@@ -82,6 +100,7 @@ def linear(x, w, b=None, activation: str | None = None):
     if _native(x, w, b) and layout_ok and _aligned(w.shape[0], w.shape[1]) and x.shape[-1] == w.shape[0]:
         y = _LinearFn.apply(x, w, b, gelu)
         return y if gelu or activation is None else apply_activation(y, activation)
+    _fallback("linear", x, w)
     y = x @ w
     if b is not None:
         y = y + b
@@ -142,6 +161,7 @@ class _LayerNormFn(torch.autograd.Function):
 def layer_norm(x, w, b, eps=1e-5):
     if _native(x, w, b) and _aligned(x.shape[-1]):
         return _LayerNormFn.apply(x, w, b, eps)
+    _fallback("layer_norm", x)
     return F.layer_norm(x, (x.shape[-1],), w, b, eps)
 
 
@@ -175,6 +195,7 @@ def attention(q, k, v, causal: bool = False, scale: float | None = None):
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if _native(q, k, v) and q.shape[-1] in (64, 128) and q.shape == k.shape == v.shape:
         return _AttnFn.apply(q, k, v, causal, scale)
+    _fallback("attention", q)
     o = F.scaled_dot_product_attention(
         q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=causal, scale=scale
     )
@@ -196,13 +217,15 @@ class _XentFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         lg, valid = ctx.saved_tensors
-        return (lg.float() * (g / valid)).to(lg.dtype), None, None
+        dl = K.scale_by(lg, g.float().reshape(1), valid.float().reshape(1), torch.empty_like(lg))
+        return dl, None, None
 
 
 def cross_entropy(logits, targets, ignore_index: int = -100):
     """Mean softmax cross-entropy of logits [M, V] against class indices."""
     if _native(logits) and logits.dim() == 2 and _aligned(logits.shape[1]):
         return _XentFn.apply(logits, targets.long(), ignore_index)
+    _fallback("cross_entropy", logits)
     return F.cross_entropy(logits.float(), targets.long(), ignore_index=ignore_index)
 
 
@@ -229,4 +252,130 @@ class _EmbFn(torch.autograd.Function):
 def embedding(tok, w):
     if _native(w) and tok.is_cuda and _aligned(w.shape[1]):
         return _EmbFn.apply(tok, w)
+    _fallback("embedding", w)
     return F.embedding(tok.long(), w)
+
+
+# ---------------------------------------------------------------------------- convolution
+def _pair(v):
+    return (int(v), int(v)) if isinstance(v, int) else (int(v[0]), int(v[1]))
+
+
+class _Conv2dFn(torch.autograd.Function):
+    """2-D convolution (NCHW, weight [Cout, Cin, KH, KW]) as im2col + the
+    tcgen05 GEMM; backward: dgrad GEMM + col2im, wgrad GEMM (fp32), bias
+    column sums. Output channels are padded to a multiple of 8 for the GEMM
+    (zero weight rows) and sliced off again."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, stride, padding, dilation):
+        x = x.contiguous()
+        N, C, H, W = x.shape
+        Cout, _, KH, KW = w.shape
+        OH, OW = K.conv_out_hw(H, W, KH, KW, stride, padding, dilation)
+        Kd = C * KH * KW
+        Kp = (Kd + 7) // 8 * 8
+        Np = (Cout + 7) // 8 * 8
+        M = N * OH * OW
+        cols = torch.empty(M, Kp, device=x.device, dtype=x.dtype)
+        K.conv_im2col(x, cols, KH, KW, stride, padding, dilation)
+        wp = torch.zeros(Np, Kp, device=w.device, dtype=w.dtype)
+        wp[:Cout, :Kd] = w.reshape(Cout, Kd)
+        bp = None
+        if b is not None:
+            bp = torch.zeros(Np, device=b.device, dtype=b.dtype)
+            bp[:Cout] = b
+        rows = torch.empty(M, Np, device=x.device, dtype=x.dtype)
+        K.gemm(cols, wp, rows, bias=bp)
+        y = torch.empty(N, Cout, OH, OW, device=x.device, dtype=x.dtype)
+        K.conv_rows_to_nchw(rows, y)
+        ctx.save_for_backward(cols, wp)
+        ctx.geom = (x.shape, w.shape, stride, padding, dilation, Np, Kp)
+        ctx.has_b = b is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        cols, wp = ctx.saved_tensors
+        xshape, wshape, stride, padding, dilation, Np, Kp = ctx.geom
+        N, C, H, W = xshape
+        Cout, _, KH, KW = wshape
+        gy = gy.contiguous()
+        M = cols.shape[0]
+        grows = torch.empty(M, Np, device=gy.device, dtype=gy.dtype)
+        K.conv_nchw_to_rows(gy, grows)
+        dcols = torch.empty(M, Kp, device=gy.device, dtype=gy.dtype)
+        K.gemm(grows, wp, dcols, b_mn=True)  # [M, Np] @ [Np, Kp]
+        dx = torch.empty(xshape, device=gy.device, dtype=gy.dtype)
+        K.conv_col2im(dcols, dx, KH, KW, stride, padding, dilation)
+        dw32 = torch.zeros(Np, Kp, device=gy.device, dtype=torch.float32)
+        K.gemm(grows, cols, dw32, a_mn=True, b_mn=True, epi=K.EPI_F32)  # [Np, M] @ [M, Kp]
+        dw = dw32[:Cout, : C * KH * KW].reshape(wshape).to(wp.dtype)
+        db = None
+        if ctx.has_b:
+            db32 = torch.zeros(Np, device=gy.device, dtype=torch.float32)
+            K.bias_grad(grows, db32)
+            db = db32[:Cout].to(wp.dtype)
+        return dx, dw, db, None, None, None
+
+
+def conv2d(x, w, b=None, stride=1, padding=0, dilation=1):
+    """2-D convolution on the framework's kernels for CUDA tensors (computed
+    in bf16, returned in the input dtype); PyTorch on the CPU (the oracle)."""
+    stride, padding, dilation = _pair(stride), _pair(padding), _pair(dilation)
+    if x.is_cuda and x.dim() == 4:
+        dt = x.dtype
+        cast = (lambda t: None if t is None else t.to(torch.bfloat16))  # noqa: E731
+        y = _Conv2dFn.apply(cast(x), cast(w), cast(b), stride, padding, dilation)
+        return y if dt == torch.bfloat16 else y.to(dt)
+    return F.conv2d(x, w, b, stride, padding, dilation)
+
+
+class _Pool2dFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, kernel, stride, padding, is_max, count_pad):
+        x = x.contiguous()
+        N, C, H, W = x.shape
+        OH, OW = K.conv_out_hw(H, W, kernel[0], kernel[1], stride, padding, (1, 1))
+        y = torch.empty(N, C, OH, OW, device=x.device, dtype=x.dtype)
+        arg = torch.empty(N, C, OH, OW, device=x.device, dtype=torch.int32) if is_max else None
+        K.pool2d_fwd(x, y, arg, kernel, stride, padding, is_max, count_pad)
+        if arg is not None:
+            ctx.save_for_backward(arg)
+        ctx.cfg = (x.shape, kernel, stride, padding, is_max, count_pad)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        xshape, kernel, stride, padding, is_max, count_pad = ctx.cfg
+        gy = gy.contiguous()
+        if is_max:
+            (arg,) = ctx.saved_tensors
+            dx = torch.empty(xshape, device=gy.device, dtype=torch.float32)
+            K.pool2d_bwd(gy, dx, arg, kernel, stride, padding, True, count_pad)
+            dx = dx.to(gy.dtype)
+        else:
+            dx = torch.empty(xshape, device=gy.device, dtype=gy.dtype)
+            K.pool2d_bwd(gy, dx, None, kernel, stride, padding, False, count_pad)
+        return dx, None, None, None, None, None
+
+
+def _pool(x, kernel, stride, padding, is_max, count_pad=True):
+    kernel = _pair(kernel)
+    stride = _pair(stride if stride is not None else kernel)
+    padding = _pair(padding)
+    if x.is_cuda and x.dim() == 4:
+        dt = x.dtype
+        y = _Pool2dFn.apply(x.to(torch.bfloat16), kernel, stride, padding, is_max, count_pad)
+        return y if dt == torch.bfloat16 else y.to(dt)
+    if is_max:
+        return F.max_pool2d(x, kernel, stride, padding)
+    return F.avg_pool2d(x, kernel, stride, padding, count_include_pad=count_pad)
+
+
+def max_pool2d(x, kernel, stride=None, padding=0):
+    return _pool(x, kernel, stride, padding, True)
+
+
+def avg_pool2d(x, kernel, stride=None, padding=0, count_include_pad=True):
+    return _pool(x, kernel, stride, padding, False, count_include_pad)

@@ -32,9 +32,12 @@ ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05")
 
 
 class _Stats:
-    """Counts native kernel launches issued through these wrappers."""
+    """Counts native kernel launches issued through these wrappers, and the
+    layer-API calls on CUDA tensors that PyTorch served instead (per op)."""
 
-    launches = 0
+    def __init__(self):
+        self.launches = 0
+        self.fallbacks: dict[str, int] = {}
 
 
 STATS = _Stats()
@@ -434,3 +437,120 @@ def vit_embed_bwd(dx, dpe, dpos, dcls, B: int):
     dpe.copy_(d[:, 1:].reshape(dpe.shape))
     dpos.add_(d.sum(0))
     dcls.add_(d[:, 0].sum(0))
+
+
+# ---------------------------------------------------------------------------
+# Elementwise helpers of the layer API's backward passes
+# ---------------------------------------------------------------------------
+def dgelu_mul(gy, pre, out):
+    """out = gy * gelu'(pre) (tanh form)."""
+    if gy.is_cuda:
+        _ext.kernels().dgelu_mul(gy, pre, out)
+        _count(1)
+        return out
+    out.copy_(gy.float() * gelu_tanh_grad(pre.float()))
+    return out
+
+
+def scale_by(x, g, count, out):
+    """out = x * g / max(count, 1) with g, count fp32 device scalars."""
+    if x.is_cuda:
+        _ext.kernels().scale_by(x, g, count, out)
+        _count(1)
+        return out
+    out.copy_(x.float() * (g.float() / count.float().clamp(min=1)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Convolution (implicit GEMM around the tcgen05 GEMM) and pooling
+# ---------------------------------------------------------------------------
+def conv_out_hw(H, W, KH, KW, stride, padding, dilation):
+    sh, sw = stride
+    ph, pw = padding
+    dh, dw = dilation
+    return (H + 2 * ph - dh * (KH - 1) - 1) // sh + 1, (W + 2 * pw - dw * (KW - 1) - 1) // sw + 1
+
+
+def conv_im2col(x, cols, KH, KW, stride, padding, dilation):
+    """cols [N*OH*OW, Kp] (Kp = C*KH*KW rounded up to 8; pad columns zero)."""
+    if x.is_cuda:
+        _ext.kernels().conv_im2col(x, cols, KH, KW, stride[0], stride[1], padding[0], padding[1], dilation[0],
+                                   dilation[1])
+        _count(1)
+        return cols
+    u = torch.nn.functional.unfold(x.float(), (KH, KW), dilation=dilation, padding=padding, stride=stride)
+    r = u.transpose(1, 2).reshape(-1, u.shape[1])
+    cols.zero_()
+    cols[:, : r.shape[1]] = r.to(cols.dtype)
+    return cols
+
+
+def conv_col2im(dcols, dx, KH, KW, stride, padding, dilation):
+    if dx.is_cuda:
+        _ext.kernels().conv_col2im(dcols, dx, KH, KW, stride[0], stride[1], padding[0], padding[1], dilation[0],
+                                   dilation[1])
+        _count(1)
+        return dx
+    N, C, H, W = dx.shape
+    OH, OW = conv_out_hw(H, W, KH, KW, stride, padding, dilation)
+    K = C * KH * KW
+    u = dcols[:, :K].float().reshape(N, OH * OW, K).transpose(1, 2)
+    dx.copy_(torch.nn.functional.fold(u, (H, W), (KH, KW), dilation=dilation, padding=padding, stride=stride))
+    return dx
+
+
+def conv_rows_to_nchw(rows, y):
+    if y.is_cuda:
+        _ext.kernels().conv_rows_nchw(rows, y, True)
+        _count(1)
+        return y
+    N, C, H, W = y.shape
+    y.copy_(rows[:, :C].reshape(N, H, W, C).permute(0, 3, 1, 2))
+    return y
+
+
+def conv_nchw_to_rows(y, rows):
+    if y.is_cuda:
+        _ext.kernels().conv_rows_nchw(rows, y, False)
+        _count(1)
+        return rows
+    N, C, H, W = y.shape
+    rows.zero_()
+    rows[:, :C] = y.permute(0, 2, 3, 1).reshape(-1, C)
+    return rows
+
+
+def pool2d_fwd(x, y, arg, kernel, stride, padding, is_max, count_pad=True):
+    if x.is_cuda:
+        _ext.kernels().pool2d_fwd(x, y, arg, kernel[0], kernel[1], stride[0], stride[1], padding[0], padding[1],
+                                  bool(is_max), bool(count_pad))
+        _count(1)
+        return y
+    F_ = torch.nn.functional
+    if is_max:
+        v, i = F_.max_pool2d(x.float(), kernel, stride, padding, return_indices=True)
+        y.copy_(v)
+        arg.copy_(i)
+    else:
+        y.copy_(F_.avg_pool2d(x.float(), kernel, stride, padding, count_include_pad=count_pad))
+    return y
+
+
+def pool2d_bwd(dy, dx, arg, kernel, stride, padding, is_max, count_pad=True):
+    if dy.is_cuda:
+        _ext.kernels().pool2d_bwd(dy, dx, arg, kernel[0], kernel[1], stride[0], stride[1], padding[0], padding[1],
+                                  bool(is_max), bool(count_pad))
+        _count(1)
+        return dx
+    N, C, H, W = dx.shape
+    if is_max:
+        dx.zero_()
+        dx.view(N, C, -1).scatter_add_(2, arg.view(N, C, -1).long(), dy.float().view(N, C, -1))
+    else:
+        with torch.enable_grad():
+            xx = torch.zeros(N, C, H, W, requires_grad=True)
+            yy = torch.nn.functional.avg_pool2d(xx, kernel, stride, padding, count_include_pad=count_pad)
+            (g,) = torch.autograd.grad(yy, xx, dy.float())
+        dx.copy_(g)
+    return dx

@@ -53,6 +53,8 @@ ext_modules = [
                 "attention_fwd_sm100.cu",
                 "attention_bwd_sm100.cu",
                 "paged_attention.cu",
+                "conv.cu",
+                "elementwise.cu",
             ]
         ),
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
