@@ -60,6 +60,17 @@ void pool2d_bwd(torch::Tensor dy, torch::Tensor dx, c10::optional<torch::Tensor>
                 int64_t sh, int64_t sw, int64_t ph, int64_t pw, bool is_max, bool count_pad);
 void dgelu_mul(torch::Tensor gy, torch::Tensor pre, torch::Tensor out);
 void scale_by(torch::Tensor x, torch::Tensor g, torch::Tensor count, torch::Tensor out);
+void lstm_cell_fwd(torch::Tensor gx, c10::optional<torch::Tensor> gh, c10::optional<torch::Tensor> c_prev,
+                   torch::Tensor c_out, torch::Tensor h_out, torch::Tensor acts);
+void lstm_cell_bwd(torch::Tensor dh, c10::optional<torch::Tensor> dc_in, torch::Tensor acts,
+                   c10::optional<torch::Tensor> c_prev, torch::Tensor c, torch::Tensor dc_out, torch::Tensor dgates);
+void gru_cell_fwd(torch::Tensor gx, c10::optional<torch::Tensor> gh, c10::optional<torch::Tensor> h_prev,
+                  torch::Tensor h_out, torch::Tensor acts);
+void gru_cell_bwd(torch::Tensor dh, torch::Tensor acts, c10::optional<torch::Tensor> h_prev, torch::Tensor dgx,
+                  torch::Tensor dgh, torch::Tensor dh_prev);
+void rnn_cell_fwd(torch::Tensor gx, c10::optional<torch::Tensor> gh, torch::Tensor h_out);
+void rnn_cell_bwd(torch::Tensor dh, torch::Tensor h, torch::Tensor dg);
+void add_bf16_f32(torch::Tensor a, c10::optional<torch::Tensor> b, torch::Tensor out);
 void vocab_route(torch::Tensor tok, torch::Tensor dout, int64_t R, int64_t V, std::vector<int64_t> rows,
                  std::vector<int64_t> ids, int64_t rank, std::vector<int64_t> sig_flags, torch::Tensor epoch,
                  int64_t sig_idx);
@@ -121,6 +132,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pool2d_bwd", &scirs::pool2d_bwd, "2-D max / average pooling backward");
   m.def("dgelu_mul", &scirs::dgelu_mul, "out = gy * gelu'(pre)");
   m.def("scale_by", &scirs::scale_by, "out = x * g / count (device scalars)");
+  m.def("lstm_cell_fwd", &scirs::lstm_cell_fwd);
+  m.def("lstm_cell_bwd", &scirs::lstm_cell_bwd);
+  m.def("gru_cell_fwd", &scirs::gru_cell_fwd);
+  m.def("gru_cell_bwd", &scirs::gru_cell_bwd);
+  m.def("rnn_cell_fwd", &scirs::rnn_cell_fwd);
+  m.def("rnn_cell_bwd", &scirs::rnn_cell_bwd);
+  m.def("add_bf16_f32", &scirs::add_bf16_f32);
   m.def("vocab_route", &scirs::vocab_route, "send embedding-gradient rows to the rank owning each vocabulary row");
   m.def("vocab_accum", &scirs::vocab_accum, "add the routed embedding-gradient rows into this rank's shard");
   m.def("ep_dispatch", &scirs::ep_dispatch, "expert-parallel dispatch: gather rows and store them into peers");

@@ -554,3 +554,109 @@ def pool2d_bwd(dy, dx, arg, kernel, stride, padding, is_max, count_pad=True):
             (g,) = torch.autograd.grad(yy, xx, dy.float())
         dx.copy_(g)
     return dx
+
+
+# ---------------------------------------------------------------------------
+# Recurrent cells (pointwise part of one time step; see csrc/rnn.cu). The CPU
+# branches are the same math in PyTorch and serve as the test oracle.
+# ---------------------------------------------------------------------------
+def _chk_bf16(*ts):
+    for t in ts:
+        if t is not None and (t.dtype != torch.bfloat16 or not t.is_contiguous()):
+            raise ValueError("recurrent-cell kernels take contiguous bf16 tensors")
+
+
+def lstm_cell_fwd(gx, gh, c_prev, c_out, h_out, acts):
+    if gx.is_cuda:
+        _chk_bf16(gx, gh, h_out, acts)
+        _ext.kernels().lstm_cell_fwd(gx, gh, c_prev, c_out, h_out, acts)
+        _count(1)
+        return
+    g = gx.float() + (gh.float() if gh is not None else 0.0)
+    i, f, gg, o = g.chunk(4, -1)
+    i, f, gg, o = torch.sigmoid(i), torch.sigmoid(f), torch.tanh(gg), torch.sigmoid(o)
+    c = f * (c_prev if c_prev is not None else 0.0) + i * gg
+    c_out.copy_(c)
+    h_out.copy_(o * torch.tanh(c))
+    acts.copy_(torch.cat([i, f, gg, o], -1))
+
+
+def lstm_cell_bwd(dh, dc_in, acts, c_prev, c, dc_out, dgates):
+    if dh.is_cuda:
+        _chk_bf16(dh, acts, dgates)
+        _ext.kernels().lstm_cell_bwd(dh, dc_in, acts, c_prev, c, dc_out, dgates)
+        _count(1)
+        return
+    i, f, gg, o = acts.float().chunk(4, -1)
+    tc = torch.tanh(c)
+    g = dh.float()
+    dct = (dc_in if dc_in is not None else 0.0) + g * o * (1 - tc * tc)
+    cp = c_prev if c_prev is not None else torch.zeros_like(c)
+    dgates.copy_(torch.cat([dct * gg * i * (1 - i), dct * cp * f * (1 - f), dct * i * (1 - gg * gg),
+                            g * tc * o * (1 - o)], -1))
+    dc_out.copy_(dct * f)
+
+
+def gru_cell_fwd(gx, gh, h_prev, h_out, acts):
+    if gx.is_cuda:
+        _chk_bf16(gx, gh, h_prev, h_out, acts)
+        _ext.kernels().gru_cell_fwd(gx, gh, h_prev, h_out, acts)
+        _count(1)
+        return
+    xr, xz, xn = gx.float().chunk(3, -1)
+    if gh is not None:
+        hr, hz, hn = gh.float().chunk(3, -1)
+    else:
+        hr = hz = hn = torch.zeros_like(xr)
+    r, z = torch.sigmoid(xr + hr), torch.sigmoid(xz + hz)
+    n = torch.tanh(xn + r * hn)
+    hp = h_prev.float() if h_prev is not None else 0.0
+    h_out.copy_((1 - z) * n + z * hp)
+    acts.copy_(torch.cat([r, z, n, hn], -1))
+
+
+def gru_cell_bwd(dh, acts, h_prev, dgx, dgh, dh_prev):
+    if dh.is_cuda:
+        _chk_bf16(dh, acts, h_prev, dgx, dgh)
+        _ext.kernels().gru_cell_bwd(dh, acts, h_prev, dgx, dgh, dh_prev)
+        _count(1)
+        return
+    r, z, n, hn = acts.float().chunk(4, -1)
+    g = dh.float()
+    hp = h_prev.float() if h_prev is not None else torch.zeros_like(g)
+    dn = g * (1 - z) * (1 - n * n)
+    dz = g * (hp - n) * z * (1 - z)
+    dr = dn * hn * r * (1 - r)
+    dgx.copy_(torch.cat([dr, dz, dn], -1))
+    dgh.copy_(torch.cat([dr, dz, dn * r], -1))
+    dh_prev.copy_(g * z)
+
+
+def rnn_cell_fwd(gx, gh, h_out):
+    if gx.is_cuda:
+        _chk_bf16(gx, gh, h_out)
+        _ext.kernels().rnn_cell_fwd(gx, gh, h_out)
+        _count(1)
+        return
+    h_out.copy_(torch.tanh(gx.float() + (gh.float() if gh is not None else 0.0)))
+
+
+def rnn_cell_bwd(dh, h, dg):
+    if dh.is_cuda:
+        _chk_bf16(dh, h, dg)
+        _ext.kernels().rnn_cell_bwd(dh, h, dg)
+        _count(1)
+        return
+    y = h.float()
+    dg.copy_(dh.float() * (1 - y * y))
+
+
+def add_bf16_f32(a, b, out):
+    """out (bf16) = a (bf16) + b (fp32, or None)."""
+    if a.is_cuda:
+        _chk_bf16(a, out)
+        _ext.kernels().add_bf16_f32(a, b, out)
+        _count(1)
+        return out
+    out.copy_(a.float() + (b if b is not None else 0.0))
+    return out

@@ -55,6 +55,7 @@ ext_modules = [
                 "paged_attention.cu",
                 "conv.cu",
                 "elementwise.cu",
+                "rnn.cu",
             ]
         ),
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
