@@ -215,7 +215,7 @@ def build_gpt(args, rank, world, local, dev):
 
         from scirs_b200.models.torch_gpt import TorchGPT
 
-        net = TorchGPT(cfg).to(dev)
+        net = TorchGPT(cfg, pad_vocab=True).to(dev)
         if world > 1:
             net = DDP(net, device_ids=[local], bucket_cap_mb=25, gradient_as_bucket_view=True)
             net.register_comm_hook(None, default_hooks.bf16_compress_hook)

@@ -54,14 +54,22 @@ def Block(cfg: GPTConfig) -> TorchBlock:
 
 
 class TorchGPT(nn.Module):
-    def __init__(self, cfg: GPTConfig):
+    """`pad_vocab=True` stores the tied embedding with cfg.vocab_padded rows
+    (a multiple of 128, so the LM-head GEMM has an aligned N) and slices the
+    logits back to the real vocabulary before the loss: the same function,
+    the usual way PyTorch GPT-2 trainers lay the head out."""
+
+    def __init__(self, cfg: GPTConfig, pad_vocab: bool = False):
         super().__init__()
         self.cfg = cfg
-        self.wte = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+        self.V = cfg.vocab_size
+        self.wte = nn.Embedding(cfg.vocab_padded if pad_vocab else cfg.vocab_size, cfg.hidden_size)
         self.wpe = nn.Embedding(cfg.max_position_embeddings, cfg.hidden_size)
         self.h = nn.ModuleList([Block(cfg) for _ in range(cfg.num_hidden_layers)])
         self.ln_f = nn.LayerNorm(cfg.hidden_size, eps=cfg.layer_norm_eps)
         self.apply(self._init)
+        with torch.no_grad():
+            self.wte.weight[cfg.vocab_size:] = 0.0  # padded vocabulary rows (never looked up, no loss gradient)
         for n, p in self.named_parameters():
             if n.endswith("c_proj.weight"):
                 nn.init.normal_(p, 0.0, cfg.initializer_range / math.sqrt(2 * cfg.num_hidden_layers))
@@ -80,9 +88,11 @@ class TorchGPT(nn.Module):
             x = blk(x)
         x = self.ln_f(x)
         logits = x @ self.wte.weight.t()
+        if logits.shape[-1] != self.V:
+            logits = logits[..., : self.V]
         if targets is None:
             return logits
-        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
+        return F.cross_entropy(logits.reshape(-1, self.V).float(), targets.reshape(-1))
 
     def load_flat_state(self, sd: dict):
         """Load a GPTModel.state_dict() (names map 1:1; `wte`/`wpe` are the
@@ -91,10 +101,13 @@ class TorchGPT(nn.Module):
         with torch.no_grad():
             for k, v in sd.items():
                 name = _to_torch_name(k)
-                own[name].copy_(v[: own[name].shape[0]].reshape(own[name].shape))
+                n = min(own[name].shape[0], v.shape[0]) if own[name].dim() == 2 else own[name].shape[0]
+                own[name][:n].copy_(v[:n].reshape(own[name][:n].shape))
 
     def flat_grads(self) -> dict:
-        return {_from_torch_name(n): p.grad for n, p in self.named_parameters()}
+        out = {_from_torch_name(n): p.grad for n, p in self.named_parameters()}
+        out["wte"] = out["wte"][: self.V]
+        return out
 
 
 def _to_torch_name(k: str) -> str:
