@@ -62,10 +62,31 @@ def parse():
     ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
                     help="gpt1.3b: fused collective GEMMs, or NCCL all-gather/reduce-scatter + separate GEMMs")
     ap.add_argument("--images", type=int, default=256, help="global batch of the ViT workload")
+    ap.add_argument("--config", default=None,
+                    help="run configuration file or packaged name (scirs_b200/configs): sets the model, global "
+                    "batch, sequence length, layers and the data-parallel / tensor-parallel modes")
     ap.add_argument("--kernel-summary", action="store_true",
                     help="after the timed runs, profile one extra step on rank 0 (torch.profiler, CUDA "
                     "activity) and print the top kernels by device time to stderr; not part of any number")
     a = ap.parse_args()
+    if a.config:
+        sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+        from scirs_b200.config import load_config
+
+        rc = load_config(a.config)
+        if rc.model not in ("gpt2", "vit", "gpt1.3b"):
+            raise SystemExit(f"config {rc.name}: model {rc.model!r} is not a training benchmark of bench.py")
+        a.model = rc.model
+        if rc.model == "vit":
+            a.images = rc.data.global_batch
+        else:
+            a.global_batch, a.seq = rc.data.global_batch, rc.data.seq_len
+        layers = rc.model_overrides.get("num_hidden_layers", rc.model_overrides.get("num_layers"))
+        if layers is not None:
+            a.layers = int(layers)
+        a.dp_mode = "zero-nccl" if (rc.parallel.dp_mode == "nccl" and rc.parallel.zero) else rc.parallel.dp_mode
+        a.tp_mode = rc.parallel.tp_mode
+        a.no_graph = not rc.runtime.cuda_graph
     if a.global_batch is None:
         a.global_batch = 32 if a.model == "gpt1.3b" else GLOBAL_BATCH
     if a.seq is None:

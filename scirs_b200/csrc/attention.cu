@@ -561,25 +561,37 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 // here); delta fp32 scratch [B*H*S].
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                        torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                       double scale);
+                       double scale, const AttnSparse& sp);
 
 // impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernel (head_dim 64).
 void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                          torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                         double scale);
+                         double scale, const AttnSparse& sp);
 
+// Sk = k.size(1) may differ from S (cross-attention; tcgen05 kernels only).
+// Optional block lists (per 128-key tile: the query blocks that see it, in
+// units of 128 queries for head_dim 64 and 64 for head_dim 128) and the
+// element predicate select the sparse kernels.
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
-                    torch::Tensor delta, bool causal, double scale, int64_t impl) {
+                    torch::Tensor delta, bool causal, double scale, int64_t impl,
+                    c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
+                    c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  const int64_t Sk = k.size(1);
   check_qkv_view(q, "q", B, S, H, HD);
-  check_qkv_view(k, "k", B, S, H, HD);
-  check_qkv_view(v, "v", B, S, H, HD);
+  check_qkv_view(k, "k", B, Sk, H, HD);
+  check_qkv_view(v, "v", B, Sk, H, HD);
   check_qkv_view(out, "out", B, S, H, HD);
   check_qkv_view(dout, "dout", B, S, H, HD);
   check_qkv_view(dq, "dq", B, S, H, HD);
-  check_qkv_view(dk, "dk", B, S, H, HD);
-  check_qkv_view(dv, "dv", B, S, H, HD);
+  check_qkv_view(dk, "dk", B, Sk, H, HD);
+  check_qkv_view(dv, "dv", B, Sk, H, HD);
+  TORCH_CHECK(!causal || Sk == S, "causal attention needs equal query and key lengths");
+  const AttnSparse sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, (Sk + 127) / 128);
+  const bool sparse = sp.ptr != nullptr || sp.bmap != nullptr || sp.wl >= 0 || sp.ng > 0;
+  TORCH_CHECK(!sparse || sp.ptr != nullptr, "a sparsity predicate needs block lists");
+  TORCH_CHECK(impl == 1 || (!sparse && Sk == S), "sparse and cross attention need the tcgen05 kernels");
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
   TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= B * S * H * HD, "dq_acc too small");
   TORCH_CHECK(delta.scalar_type() == at::kFloat && delta.numel() >= B * H * S, "delta too small");
@@ -618,9 +630,9 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
     SCIRS_CHECK_LAUNCH();
   }
   if (impl == 1 && HD == 64) {
-    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale);
+    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp);
   } else if (impl == 1 && HD == 128) {
-    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale);
+    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp);
   } else {
   dim3 grid((unsigned)((S + 63) / 64), (unsigned)(B * H));
 #define FA_BWD(HD_, CAUSAL_)                                                                             \

@@ -58,12 +58,14 @@ struct Params {
   bf16* dk;
   bf16* dv;
   long dk_rs, dv_rs;
-  int B, H, S;
+  int B, H, S;  // S: query length
+  int Sk;       // key / value length
   float scale, scale_log2;
   DevStatus* st;
+  AttnSparse sp;  // SPARSE: per key tile, the list of 64-query blocks to visit
 };
 
-template <bool CAUSAL>
+template <bool CAUSAL, bool SPARSE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_h128_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -87,13 +89,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* sLD = reinterpret_cast<float*>(smem + OFF_LD);  // [buf][0: lse2, 1: delta][64]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.S, H = p.H;
+  const int S = p.S, Sk = p.Sk, H = p.H;
   const int kb = blockIdx.x;
   const int b = blockIdx.y / H, h = blockIdx.y % H;
   const int k0 = kb * BK;
-  const int row_base = b * S;
+  const int row_base = b * S;   // query rows (Q, dO, dQ)
+  const int kv_base = b * Sk;   // key rows (K, V, dK, dV)
   const int nq = (S + BQ - 1) / BQ;
   const int i0 = CAUSAL ? k0 / BQ : 0;
+  const int lb = SPARSE ? __ldg(p.sp.ptr + kb) : 0;
+  const int niter = SPARSE ? __ldg(p.sp.ptr + kb + 1) - lb : max(nq - i0, 0);
+  auto qblk = [&](int n) -> int { return SPARSE ? __ldg(p.sp.idx + lb + n) : i0 + n; };
   const int col = h * HD;
 
   if (threadIdx.x == 0) {
@@ -133,10 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(kv_full, 2 * KV_BYTES);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        tma_load_2d(smem + OFF_K + c * (BK * 128), &tmK, kv_full, col + c * 64, row_base + k0);
-        tma_load_2d(smem + OFF_V + c * (BK * 128), &tmV, kv_full, col + c * 64, row_base + k0);
+        tma_load_2d(smem + OFF_K + c * (BK * 128), &tmK, kv_full, col + c * 64, kv_base + k0);
+        tma_load_2d(smem + OFF_V + c * (BK * 128), &tmV, kv_full, col + c * 64, kv_base + k0);
       }
-      for (int i = i0, n = 0; i < nq; ++i, ++n) {
+      for (int n = 0; n < niter; ++n) {
+        const int i = qblk(n);
         const int st = n & 1;
         if (!mbar_wait(&qdo_empty[st], ((n >> 1) & 1) ^ 1, p.st, 80, abort_flag)) break;
         mbar_arrive_expect_tx(&qdo_full[st], 2 * QT_BYTES);
@@ -156,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
       const uint32_t pt_addr = smem_u32(smem + OFF_PT), ds_addr = smem_u32(smem + OFF_DST);
-      for (int i = i0, n = 0; i < nq && ok; ++i, ++n) {
+      for (int n = 0; n < niter && ok; ++n) {
         const int st = n & 1;
         // the score tiles are free once the warps published P^T / dS^T of the
         // previous block (p_full, waited for below in iteration n - 1)
@@ -219,8 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* stage = reinterpret_cast<float*>(smem + OFF_DQS + w8 * 4096);  // [32 q][32 hd]
     const float LOG2E = 1.4426950408889634f;
     bool ok = true;
-    for (int i = i0, n = 0; i < nq && ok; ++i, ++n) {
-      const int q0 = i * BQ;
+    for (int n = 0; n < niter && ok; ++n) {
+      const int q0 = qblk(n) * BQ;
       float* sL = sLD + (n & 1) * 2 * BQ;
       if (w8 < 4) {  // 128 threads stage the 64 lse and 64 delta values
         const int t = w8 * 32 + lane;
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_32x32b_x32(lane_base + T_S + c0, sv);
       tmem_ld_32x32b_x32(lane_base + T_DP + c0, dv);
       tc_wait_ld();
-      const bool need_mask = (q0 + BQ > S) || (k0 + BK > S) || (CAUSAL && q0 < k0 + BK);
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) || SPARSE;
       uint32_t pp[16], dd[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
@@ -249,7 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ql = c0 + e + u;
           const int q = q0 + ql;
           float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
-          if (need_mask && (q >= S || key >= S || (CAUSAL && key > q))) pv = 0.f;
+          if (need_mask && (q >= S || key >= Sk || (CAUSAL && key > q) || (SPARSE && !attn_allowed(p.sp, q, key))))
+            pv = 0.f;
           pr[u] = pv;
           ds[u] = pv * (__uint_as_float(dv[e + u]) - sL[BQ + ql]);
         }
@@ -296,14 +304,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t kv[32];
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
-        bf16* dst = which ? (p.dv + (long)(row_base + key) * p.dv_rs + col)
-                          : (p.dk + (long)(row_base + key) * p.dk_rs + col);
+        bf16* dst = which ? (p.dv + (long)(kv_base + key) * p.dv_rs + col)
+                          : (p.dk + (long)(kv_base + key) * p.dk_rs + col);
         const float sc = which ? 1.f : p.scale;
+        const bool empty = SPARSE && niter == 0;  // no query sees these keys: zero gradients
 #pragma unroll 1
         for (int c = ch * 64; c < ch * 64 + 64; c += 32) {
           tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
           tc_wait_ld();
-          if (key < S) {
+          if (empty) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) kv[e] = 0u;
+          }
+          if (key < Sk) {
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
@@ -332,23 +345,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                          torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                         double scale) {
+                         double scale, const AttnSparse& sp) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 128, "this backward kernel is for head_dim 128");
   for (auto* t : {&q, &k, &v, &dout, &dk, &dv}) {
-    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == S &&
+    const int64_t St = (t == &k || t == &v || t == &dk || t == &dv) ? Sk : S;
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == St &&
                     t->size(2) == H && t->size(3) == HD,
-                "q/k/v/dout/dk/dv must be bf16 [B, S, H, HD]");
-    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == S * t->stride(1),
+                "q/dout must be bf16 [B, S, H, HD] and k/v/dk/dv bf16 [B, Sk, H, HD]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == St * t->stride(1),
                 "tensors must be token-major with contiguous heads");
   }
   TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= B * S * H * HD, "dq_acc fp32 [B*S*H*HD]");
   c10::cuda::CUDAGuard guard(q.get_device());
-  auto mk = [&](const torch::Tensor& t, uint32_t rows) {
-    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * S),
+  auto mk = [&](const torch::Tensor& t, int64_t len, uint32_t rows) {
+    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * len),
                         (uint64_t)t.stride(1) * 2, 64, rows, CU_TENSOR_MAP_SWIZZLE_128B);
   };
-  CUtensorMap tq = mk(q, 64), tk = mk(k, 128), tv = mk(v, 128), tdo = mk(dout, 64);
+  CUtensorMap tq = mk(q, S, 64), tk = mk(k, Sk, 128), tv = mk(v, Sk, 128), tdo = mk(dout, S, 64);
   // dQ staging tiles are plain row-major [32 q][32 hd] fp32
   CUtensorMap tdq = make_tmap_2d(dq_acc.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)(H * HD),
                                  (uint64_t)(B * S), (uint64_t)(H * HD) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -362,20 +377,26 @@ void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, t
   p.B = (int)B;
   p.H = (int)H;
   p.S = (int)S;
+  p.Sk = (int)Sk;
   p.scale = (float)scale;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
-  dim3 grid((unsigned)((S + 127) / 128), (unsigned)(B * H));
+  p.sp = sp;
+  const bool sparse = sp.ptr != nullptr;
+  dim3 grid((unsigned)((Sk + 127) / 128), (unsigned)(B * H));
   auto st = cur_stream();
-  if (causal) {
-    auto kern = fabw128::fa_bwd_h128_kernel<true>;
-    set_max_smem((const void*)kern, fabw128::SMEM);
-    kern<<<grid, fabw128::kThreads, fabw128::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
-  } else {
-    auto kern = fabw128::fa_bwd_h128_kernel<false>;
-    set_max_smem((const void*)kern, fabw128::SMEM);
-    kern<<<grid, fabw128::kThreads, fabw128::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
+#define FABW128(C_, SP_)                                                   \
+  {                                                                        \
+    auto kern = fabw128::fa_bwd_h128_kernel<C_, SP_>;                      \
+    set_max_smem((const void*)kern, fabw128::SMEM);                        \
+    kern<<<grid, fabw128::kThreads, fabw128::SMEM, st>>>(tq, tk, tv, tdo, tdq, p); \
   }
+  if (sparse) {
+    if (causal) FABW128(true, true) else FABW128(false, true)
+  } else {
+    if (causal) FABW128(true, false) else FABW128(false, false)
+  }
+#undef FABW128
   SCIRS_CHECK_LAUNCH();
 }
 

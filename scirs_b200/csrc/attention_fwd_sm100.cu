@@ -46,9 +46,11 @@ struct Params {
   bf16* out;
   float* lse;
   long o_rs;
-  int B, H, S;
+  int B, H, S;  // S: query length
+  int Sk;       // key / value length (cross-attention; = S for self-attention)
   float scale_log2;
   DevStatus* st;
+  AttnSparse sp;  // used by the SPARSE instantiations
   // optional phase timing (clock64 cycles summed over the loop) of one
   // softmax thread per tile: [CTA][tile][wait S, TMEM load, max/rescale,
   // exp + P store, signal]; nullptr = off
@@ -95,7 +97,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false, bool X2 = false>
+template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false, bool X2 = false, bool SPARSE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -116,15 +118,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.S, H = p.H;
+  const int S = p.S, Sk = p.Sk, H = p.H;
   const int qp = gridDim.x - 1 - blockIdx.x;  // longest causal work first
   const int b = blockIdx.y / H, h = blockIdx.y % H;
   const int q0 = qp * 2 * BM;
-  const int row_base = b * S;
-  const int nkv_all = (S + BN - 1) / BN;
+  const int row_base = b * S;   // query / output rows
+  const int kv_base = b * Sk;   // key / value rows
+  const int nkv_all = (Sk + BN - 1) / BN;
+  // SPARSE: this CTA visits the key blocks of its list (both tiles)
+  const int lb = SPARSE ? __ldg(p.sp.ptr + qp) : 0;
+  const int cnt = SPARSE ? __ldg(p.sp.ptr + qp + 1) - lb : 0;
+  auto kblk = [&](int j) -> int { return SPARSE ? __ldg(p.sp.idx + lb + j) : j; };
   // key blocks each tile needs (tile t covers queries [q0 + 128 t, +128))
-  const int nkv0 = (q0 >= S) ? 0 : (CAUSAL ? min(nkv_all, q0 / BM + 1) : nkv_all);
-  const int nkv1 = (q0 + BM >= S) ? 0 : (CAUSAL ? min(nkv_all, q0 / BM + 2) : nkv_all);
+  const int nkv0 = (q0 >= S) ? 0 : (SPARSE ? cnt : (CAUSAL ? min(nkv_all, q0 / BM + 1) : nkv_all));
+  const int nkv1 = (q0 + BM >= S) ? 0 : (SPARSE ? cnt : (CAUSAL ? min(nkv_all, q0 / BM + 2) : nkv_all));
   const int nkv = max(nkv0, nkv1);
 
   if (threadIdx.x == 0) {
@@ -173,12 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c)
           tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + c * (BN * 128), &tmK, &k_full[s], col + c * 64,
-                      row_base + j * BN);
+                      kv_base + kblk(j) * BN);
         mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c)
           tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + c * (BN * 128), &tmV, &v_full[s], col + c * 64,
-                      row_base + j * BN);
+                      kv_base + kblk(j) * BN);
       }
     }
   } else if (warp == 1) {
@@ -272,13 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_ld();
       }
       lap(1);
-      const int kv0 = j * BN;
-      const bool mask = (kv0 + BN > S) || (CAUSAL && kv0 + BN > q0 + t * BM);
+      const int kv0 = kblk(j) * BN;
+      const bool mask = (kv0 + BN > Sk) || (CAUSAL && kv0 + BN > q0 + t * BM) || SPARSE;
       if (mask) {
 #pragma unroll
         for (int e = 0; e < BN; ++e) {
           const int key = kv0 + e;
-          if (key >= S || (CAUSAL && key > qrow)) sv[e] = -INFINITY;
+          if (key >= Sk || (CAUSAL && key > qrow) || (SPARSE && !attn_allowed(p.sp, qrow, key))) sv[e] = -INFINITY;
         }
       }
       // row max: four independent chains of 3-input max instructions
@@ -385,6 +392,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (qrow < S) p.lse[((long)b * H + h) * S + qrow] = (m_ref + log2f(l)) * 0.6931471805599453f;
+    } else if (SPARSE && ok && my_nkv == 0 && qrow < S) {
+      // an empty key list: zero output, -inf log-sum-exp
+      bf16* orow = p.out + (long)(row_base + qrow) * p.o_rs + h * HD;
+      for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+      p.lse[((long)b * H + h) * S + qrow] = -INFINITY;
     }
   }
 
@@ -398,25 +410,62 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace fa2t
 
-// q/k/v/out: [B, S, H, HD] token-major views with contiguous heads; lse [B,H,S].
+// Fill an AttnSparse from optional tensors (block lists int32, bitmap uint8).
+AttnSparse attn_sparse_args(const c10::optional<torch::Tensor>& ptr, const c10::optional<torch::Tensor>& idx,
+                            const c10::optional<torch::Tensor>& bmap, int64_t wl, int64_t wr, int64_t ng,
+                            int64_t rows) {
+  AttnSparse a{};
+  a.wl = (int)wl;
+  a.wr = (int)wr;
+  a.ng = (int)ng;
+  const bool has = ptr.has_value() && ptr->defined();
+  TORCH_CHECK(has == (idx.has_value() && idx->defined()), "block lists need both ptr and idx");
+  if (has) {
+    TORCH_CHECK(ptr->scalar_type() == at::kInt && idx->scalar_type() == at::kInt && ptr->is_contiguous() &&
+                    idx->is_contiguous() && ptr->is_cuda() && idx->is_cuda(),
+                "block lists: contiguous int32 CUDA tensors");
+    TORCH_CHECK(ptr->numel() == rows + 1, "block list ptr must have one entry per CTA plus one");
+    a.ptr = ptr->data_ptr<int>();
+    a.idx = idx->data_ptr<int>();
+  }
+  if (bmap.has_value() && bmap->defined()) {
+    TORCH_CHECK(bmap->scalar_type() == at::kByte && bmap->dim() == 2 && bmap->is_contiguous() && bmap->is_cuda(),
+                "block bitmap: contiguous uint8 CUDA [q blocks, k blocks]");
+    a.bmap = bmap->data_ptr<uint8_t>();
+    a.bmap_ld = (int)bmap->size(1);
+  }
+  return a;
+}
+
+// q/out: [B, S, H, HD], k/v: [B, Sk, H, HD] token-major views with contiguous
+// heads; lse [B, H, S]. With block lists (blk_ptr / blk_idx: for CTA c, which
+// covers queries [256 c, 256 c + 256), the key blocks blk_idx[blk_ptr[c] ..
+// blk_ptr[c + 1]) of 128 keys) the kernel visits only those blocks and masks
+// with the element predicate (window wl / wr with ng global tokens, and the
+// optional 128 x 128 block bitmap).
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2) {
+                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2,
+                       c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
+                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(!causal || Sk == S, "causal attention needs equal query and key lengths");
   for (auto* t : {&q, &k, &v, &out}) {
-    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == S &&
+    const int64_t St = (t == &k || t == &v) ? Sk : S;
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == St &&
                     t->size(2) == H && t->size(3) == HD,
-                "q/k/v/out must be bf16 [B, S, H, HD]");
-    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == S * t->stride(1),
+                "q/out must be bf16 [B, S, H, HD] and k/v bf16 [B, Sk, H, HD]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == St * t->stride(1),
                 "q/k/v/out must be token-major with contiguous heads");
   }
   TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * H * S && lse.is_contiguous(), "lse fp32 [B,H,S]");
   c10::cuda::CUDAGuard guard(q.get_device());
-  auto mk = [&](const torch::Tensor& t) {
-    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * S),
+  auto mk = [&](const torch::Tensor& t, int64_t rows) {
+    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * rows),
                         (uint64_t)t.stride(1) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   };
-  CUtensorMap tq = mk(q), tk = mk(k), tv = mk(v);
+  CUtensorMap tq = mk(q, S), tk = mk(k, Sk), tv = mk(v, Sk);
   fa2t::Params p{};
   p.out = reinterpret_cast<fa2t::bf16*>(out.data_ptr());
   p.lse = lse.data_ptr<float>();
@@ -424,9 +473,13 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   p.B = (int)B;
   p.H = (int)H;
   p.S = (int)S;
+  p.Sk = (int)Sk;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
   dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
+  p.sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, (int64_t)grid.x);
+  const bool sparse = p.sp.ptr != nullptr || p.sp.bmap != nullptr || p.sp.wl >= 0 || p.sp.ng > 0;
+  TORCH_CHECK(!sparse || p.sp.ptr != nullptr, "a sparsity predicate needs block lists");
   if (trace.has_value() && trace->defined()) {
     TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_contiguous() &&
                     trace->numel() >= (long)grid.x * grid.y * 2 * 5,
@@ -434,33 +487,36 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
   }
   auto st = cur_stream();
-#define FA2T(HD_, C_, P_, R_, X_)                                              \
+#define FA2T(HD_, C_, P_, R_, X_, SP_)                                         \
   {                                                                            \
-    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_, X_>;                   \
+    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_, X_, SP_>;              \
     set_max_smem((const void*)kern, fa2t::Cfg<HD_>::SMEM);                     \
     kern<<<grid, fa2t::kThreads, fa2t::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);   \
   }
-#define FA2T_HD(P_, R_, X_)                                                    \
-  if (HD == 64) {                                                              \
-    if (causal) FA2T(64, true, P_, R_, X_) else FA2T(64, false, P_, R_, X_)    \
-  } else {                                                                     \
-    if (causal) FA2T(128, true, P_, R_, X_) else FA2T(128, false, P_, R_, X_)  \
+#define FA2T_HD(P_, R_, X_, SP_)                                                       \
+  if (HD == 64) {                                                                      \
+    if (causal) FA2T(64, true, P_, R_, X_, SP_) else FA2T(64, false, P_, R_, X_, SP_)  \
+  } else {                                                                             \
+    if (causal) FA2T(128, true, P_, R_, X_, SP_) else FA2T(128, false, P_, R_, X_, SP_) \
   }
   const bool traced = p.trace != nullptr;
   TORCH_CHECK(!(traced && poly), "the trace is available for the plain variant");
   TORCH_CHECK(!(x2 && poly), "poly and x2 variants are exclusive");
-  if (traced) {
+  TORCH_CHECK(!(sparse && (traced || poly || x2)), "sparse attention uses the plain variant");
+  if (sparse) {
+    FA2T_HD(false, false, false, true)
+  } else if (traced) {
     if (x2) {
-      FA2T_HD(false, true, true)
+      FA2T_HD(false, true, true, false)
     } else {
-      FA2T_HD(false, true, false)
+      FA2T_HD(false, true, false, false)
     }
   } else if (poly) {
-    FA2T_HD(true, false, false)
+    FA2T_HD(true, false, false, false)
   } else if (x2) {
-    FA2T_HD(false, false, true)
+    FA2T_HD(false, false, true, false)
   } else {
-    FA2T_HD(false, false, false)
+    FA2T_HD(false, false, false, false)
   }
 #undef FA2T_HD
 #undef FA2T

@@ -436,16 +436,18 @@ struct Params {
   bf16* dk;
   bf16* dv;
   long dk_rs, dv_rs;
-  int B, H, S;
+  int B, H, S;  // S: query length
+  int Sk;       // key / value length
   float scale, scale_log2;
   DevStatus* st;
+  AttnSparse sp;  // SPARSE: per key tile, the list of 128-query blocks to visit
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-template <bool CAUSAL>
+template <bool CAUSAL, bool SPARSE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -470,13 +472,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* sLD = reinterpret_cast<float*>(smem + OFF_LD);  // [buf][0: lse2, 1: delta][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.S, H = p.H;
+  const int S = p.S, Sk = p.Sk, H = p.H;
   const int kb = blockIdx.x;
   const int b = blockIdx.y / H, h = blockIdx.y % H;
   const int k0 = kb * BK;
-  const int row_base = b * S;
+  const int row_base = b * S;   // query rows (Q, dO, dQ)
+  const int kv_base = b * Sk;   // key rows (K, V, dK, dV)
   const int nq = (S + BQ - 1) / BQ;
   const int i0 = CAUSAL ? kb : 0;
+  const int lb = SPARSE ? __ldg(p.sp.ptr + kb) : 0;
+  const int niter = SPARSE ? __ldg(p.sp.ptr + kb + 1) - lb : max(nq - i0, 0);
+  auto qblk = [&](int n) -> int { return SPARSE ? __ldg(p.sp.idx + lb + n) : i0 + n; };
   const int col = h * HD;
 
   if (threadIdx.x == 0) {
@@ -517,9 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ TMA
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * T_BYTES);
-      tma_load_2d(smem + OFF_K, &tmK, kv_full, col, row_base + k0);
-      tma_load_2d(smem + OFF_V, &tmV, kv_full, col, row_base + k0);
-      for (int i = i0, n = 0; i < nq; ++i, ++n) {
+      tma_load_2d(smem + OFF_K, &tmK, kv_full, col, kv_base + k0);
+      tma_load_2d(smem + OFF_V, &tmV, kv_full, col, kv_base + k0);
+      for (int n = 0; n < niter; ++n) {
+        const int i = qblk(n);
         const int st = n & 1;
         if (!mbar_wait(&qdo_empty[st], ((n >> 1) & 1) ^ 1, p.st, 50, abort_flag)) break;
         mbar_arrive_expect_tx(&qdo_full[st], 2 * T_BYTES);
@@ -534,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
       const uint32_t pt_addr = smem_u32(smem + OFF_PT), ds_addr = smem_u32(smem + OFF_DST);
-      for (int i = i0, n = 0; i < nq && ok; ++i, ++n) {
+      for (int n = 0; n < niter && ok; ++n) {
         const int st = n & 1;
         ok = mbar_wait(&qdo_full[st], (n >> 1) & 1, p.st, 52, abort_flag) &&
              mbar_wait(s_free, (n & 1) ^ 1, p.st, 53, abort_flag);
@@ -602,7 +609,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* slot0 = smem + OFF_DQS + (dq_role ? (warp - 6) : 0) * 8192;
     uint8_t* slot1 = slot0 + 4096;
     bool ok = true;
-    for (int i = i0, n = 0; i < nq; ++i, ++n) {
+    for (int n = 0; n < niter; ++n) {
+      const int i = qblk(n);
       const int q0 = i * BQ;
       float* sL = sLD + (n & 1) * 256;
       if (!dq_role) {
@@ -616,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) { ok = false; break; }
       if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const bool need_mask = (q0 + BQ > S) || (k0 + BK > S) || (CAUSAL && i == i0);
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) || SPARSE;
 #pragma unroll 1
       for (int c = c_begin; c < c_begin + BQ / 2; c += 32) {
         uint32_t sv[32], dv[32];
@@ -632,7 +640,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ql = c + e + u;
             const int q = q0 + ql;
             float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
-            if (need_mask && (q >= S || key >= S || (CAUSAL && key > q))) pv = 0.f;
+            if (need_mask && (q >= S || key >= Sk || (CAUSAL && key > q) ||
+                              (SPARSE && !attn_allowed(p.sp, q, key))))
+              pv = 0.f;
             pr[u] = pv;
             ds[u] = pv * (__uint_as_float(dv[e + u]) - sL[128 + ql]);
           }
@@ -698,14 +708,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t kv[32];
   #pragma unroll
         for (int which = 0; which < 2; ++which) {
-          bf16* dst = which ? (p.dv + (long)(row_base + key) * p.dv_rs + col)
-                            : (p.dk + (long)(row_base + key) * p.dk_rs + col);
+          bf16* dst = which ? (p.dv + (long)(kv_base + key) * p.dv_rs + col)
+                            : (p.dk + (long)(kv_base + key) * p.dk_rs + col);
           const float sc = which ? 1.f : p.scale;
+          const bool empty = SPARSE && niter == 0;  // no query sees these keys: zero gradients
   #pragma unroll
           for (int c = 0; c < HD; c += 32) {
             tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
             tc_wait_ld();
-            if (key < S) {
+            if (empty) {
+  #pragma unroll
+              for (int e = 0; e < 32; ++e) kv[e] = 0u;
+            }
+            if (key < Sk) {
   #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
@@ -735,26 +750,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Attention backward core on tcgen05 (head_dim 64): writes dK, dV and
 // reduce-adds the unscaled dQ into dq_acc (fp32 [B*S, H*HD], pre-zeroed by
-// the caller). lse / delta fp32 [B, H, S].
+// the caller). lse / delta fp32 [B, H, S]. q/dout [B, S, H, 64], k/v/dk/dv
+// [B, Sk, H, 64]; `sp` (block lists of 128-query blocks per 128-key tile,
+// and the element predicate) selects the sparse instantiation.
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                        torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                       double scale) {
+                       double scale, const AttnSparse& sp) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
+  const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 64, "tcgen05 attention backward supports head_dim 64");
   for (auto* t : {&q, &k, &v, &dout, &dk, &dv}) {
-    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == S &&
+    const int64_t St = (t == &k || t == &v || t == &dk || t == &dv) ? Sk : S;
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4 && t->size(0) == B && t->size(1) == St &&
                     t->size(2) == H && t->size(3) == HD,
-                "q/k/v/dout/dk/dv must be bf16 [B, S, H, HD]");
-    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == S * t->stride(1),
+                "q/dout must be bf16 [B, S, H, HD] and k/v/dk/dv bf16 [B, Sk, H, HD]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == HD && t->stride(0) == St * t->stride(1),
                 "tensors must be token-major with contiguous heads");
   }
   TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= B * S * H * HD, "dq_acc fp32 [B*S*H*HD]");
   c10::cuda::CUDAGuard guard(q.get_device());
-  auto mk = [&](const torch::Tensor& t) {
-    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * S),
+  auto mk = [&](const torch::Tensor& t, int64_t len) {
+    return make_tmap_2d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)(H * HD), (uint64_t)(B * len),
                         (uint64_t)t.stride(1) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   };
-  CUtensorMap tq = mk(q), tk = mk(k), tv = mk(v), tdo = mk(dout);
+  CUtensorMap tq = mk(q, S), tk = mk(k, Sk), tv = mk(v, Sk), tdo = mk(dout, S);
   CUtensorMap tdq = make_tmap_2d(dq_acc.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)(H * HD),
                                  (uint64_t)(B * S), (uint64_t)(H * HD) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   fabw::Params p{};
@@ -767,20 +786,26 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   p.B = (int)B;
   p.H = (int)H;
   p.S = (int)S;
+  p.Sk = (int)Sk;
   p.scale = (float)scale;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
-  dim3 grid((unsigned)((S + 127) / 128), (unsigned)(B * H));
+  p.sp = sp;
+  const bool sparse = sp.ptr != nullptr;
+  dim3 grid((unsigned)((Sk + 127) / 128), (unsigned)(B * H));
   auto st = cur_stream();
-  if (causal) {
-    auto kern = fabw::fa_bwd_tc_kernel<true>;
-    set_max_smem((const void*)kern, fabw::SMEM);
-    kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
-  } else {
-    auto kern = fabw::fa_bwd_tc_kernel<false>;
-    set_max_smem((const void*)kern, fabw::SMEM);
-    kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
+#define FABW(C_, SP_)                                                  \
+  {                                                                    \
+    auto kern = fabw::fa_bwd_tc_kernel<C_, SP_>;                       \
+    set_max_smem((const void*)kern, fabw::SMEM);                       \
+    kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p); \
   }
+  if (sparse) {
+    if (causal) FABW(true, true) else FABW(false, true)
+  } else {
+    if (causal) FABW(true, false) else FABW(false, false)
+  }
+#undef FABW
   SCIRS_CHECK_LAUNCH();
 }
 

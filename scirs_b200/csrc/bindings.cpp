@@ -30,7 +30,9 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
                     bool causal, double scale);
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
-                    torch::Tensor delta, bool causal, double scale, int64_t impl);
+                    torch::Tensor delta, bool causal, double scale, int64_t impl,
+                    c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
+                    c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng);
 void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale);
 void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
@@ -82,7 +84,9 @@ void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                             torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
                             int64_t tokens_per_split, double scale);
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2);
+                       bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2,
+                       c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
+                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng);
 void tp_step_begin(torch::Tensor epoch, c10::optional<torch::Tensor> vals);
 void tp_reduce(torch::Tensor recv, torch::Tensor out, c10::optional<torch::Tensor> bias,
                c10::optional<torch::Tensor> resid, int64_t rank, c10::optional<torch::Tensor> flags,
@@ -148,7 +152,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_decode", &scirs::paged_attention_decode);
   m.def("flash_attn_fwd_pp", &scirs::flash_attn_fwd_pp, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("lse"), py::arg("causal"), py::arg("scale"), py::arg("poly") = false,
-        py::arg("trace") = py::none(), py::arg("x2") = false);
+        py::arg("trace") = py::none(), py::arg("x2") = false, py::arg("blk_ptr") = py::none(),
+        py::arg("blk_idx") = py::none(), py::arg("bmap") = py::none(), py::arg("wl") = -1, py::arg("wr") = -1,
+        py::arg("ng") = 0);
   m.def("tp_step_begin", &scirs::tp_step_begin, py::arg("epoch"), py::arg("vals") = py::none());
   m.def("tp_reduce", &scirs::tp_reduce);
   m.def("rope_apply", &scirs::rope_apply);
@@ -160,7 +166,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &scirs::flash_attn_fwd);
   m.def("flash_attn_bwd", &scirs::flash_attn_bwd, "attention backward", py::arg("dout"), py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"),
-        py::arg("delta"), py::arg("causal"), py::arg("scale"), py::arg("impl") = 1);
+        py::arg("delta"), py::arg("causal"), py::arg("scale"), py::arg("impl") = 1, py::arg("blk_ptr") = py::none(),
+        py::arg("blk_idx") = py::none(), py::arg("bmap") = py::none(), py::arg("wl") = -1, py::arg("wr") = -1,
+        py::arg("ng") = 0);
   m.def("flash_attn_fwd_tc", &scirs::flash_attn_fwd_tc);
   m.def("status_read_and_clear", &scirs::status_read_and_clear);
   m.def("num_sms", &scirs::num_sms);

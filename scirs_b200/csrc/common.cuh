@@ -14,6 +14,21 @@
 
 namespace scirs {
 
+// Sparsity of an attention call. Block lists (CSR, one row per CTA: the
+// forward's 256-query CTAs list 128-key blocks, the backward's 128-key CTAs
+// list query blocks) choose the tiles a CTA visits; the element predicate
+// masks inside them. A pair (q, k) is allowed when it is in the union of the
+// components given: the window [q - wl, q + wr], the global tokens (q < ng
+// or k < ng) and the 128 x 128 block bitmap (causal masking comes on top).
+struct AttnSparse {
+  const int* ptr;
+  const int* idx;
+  const uint8_t* bmap;
+  int bmap_ld;
+  int wl, wr, ng;  // wl < 0: no window
+};
+
+
 // ---------------------------------------------------------------------------
 // Device status word. Kernels record the FIRST error they meet here; the host
 // reads it after a synchronize (see status_check in host_common.h).
@@ -424,6 +439,14 @@ __device__ __forceinline__ uint64_t gelu_tanh_grad2(uint64_t x) {
   const uint64_t t = f2_pack(t0, t1), nt = f2_pack(-t0, -t1);
   const uint64_t c = f2_mul(f2_mul(x, half), f2_mul(k0, f2_fma(xx, k13, one)));  // 0.5 x k0 (1 + 3 k1 x^2)
   return f2_fma(c, f2_fma(nt, t, one), f2_fma(half, t, half));
+}
+
+__device__ __forceinline__ bool attn_allowed(const AttnSparse& a, int q, int k) {
+  // union of the components that are present (none present: everything)
+  if (a.bmap == nullptr && a.wl < 0 && a.ng <= 0) return true;
+  if (a.wl >= 0 && k >= q - a.wl && k <= q + a.wr) return true;
+  if (q < a.ng || k < a.ng) return true;
+  return a.bmap != nullptr && a.bmap[(long)(q >> 7) * a.bmap_ld + (k >> 7)] != 0;
 }
 
 #endif  // __CUDACC__

@@ -61,4 +61,9 @@ inline void set_max_smem(const void* kern, int bytes) {
   SCIRS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   done.insert({kern, dev});
 }
+// Attention sparsity arguments from optional tensors (attention_fwd_sm100.cu).
+AttnSparse attn_sparse_args(const c10::optional<torch::Tensor>& ptr, const c10::optional<torch::Tensor>& idx,
+                            const c10::optional<torch::Tensor>& bmap, int64_t wl, int64_t wr, int64_t ng,
+                            int64_t rows);
+
 }  // namespace scirs

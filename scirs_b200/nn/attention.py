@@ -282,35 +282,75 @@ class SlidingWindowConfig:
 
 class SlidingWindowAttention:
     """Token i attends to [i-w, i+w] plus `global_tokens` leading tokens that
-    attend everywhere and are attended by everyone."""
+    attend everywhere and are attended by everyone. On CUDA (bf16, head_dim
+    64 / 128) the kernels visit only the key blocks the window touches
+    (ops.sparse_attention); no S x S mask is built."""
 
-    def __init__(self, config: SlidingWindowConfig):
+    def __init__(self, config: SlidingWindowConfig, causal: bool = False):
         self.config = config
+        self.causal = causal
+
+    def pattern(self):
+        from ..ops.sparse_attention import sliding_window
+
+        return sliding_window(self.config.window_size, self.config.global_tokens, self.causal)
 
     def mask(self, S: int, device=None) -> torch.Tensor:
-        i = torch.arange(S, device=device)
-        m = (i[:, None] - i[None, :]).abs() <= self.config.window_size
-        g = self.config.global_tokens
-        if g > 0:
-            m[:g, :] = True
-            m[:, :g] = True
-        return m
+        """Dense [S, S] mask of the pattern (for inspection and the CPU path)."""
+        return self.pattern().allowed_dense(S, S, device=device)
 
     def forward(self, q, k, v, scale=None):
+        if q.is_cuda:
+            plan = self.pattern().plan(q.shape[1], k.shape[1], q.shape[-1], q.device)
+            return FN.attention(q, k, v, False, scale, plan=plan)
         return attention_with_bias(q, k, v, mask=self.mask(q.shape[1], q.device), scale=scale)
 
 
 class SparseAttention:
-    """Attention restricted by a boolean pattern: 'strided' (local band +
-    every stride-th column), 'fixed' (block-local + summary columns) or a
-    user mask."""
+    """Attention restricted to a sparse pattern.
 
-    def __init__(self, pattern: str = "strided", stride: int = 64, block: int = 64, mask: torch.Tensor | None = None):
+    Block patterns (run on the sparse kernels on CUDA, no dense mask):
+      'block_strided'  Sparse-Transformer layout over 128-token blocks: the
+                       `local` nearest key blocks plus every `block_stride`-th block
+      'bigbird'        window of `window` tokens + `num_global` global tokens
+                       + `num_random` random key blocks per query block
+      bitmap=          any [q blocks, k blocks] boolean layout of 128 x 128 blocks
+    Token patterns (dense mask, evaluated with the masked reference):
+      'strided' (local band + every stride-th column), 'fixed' (block-local +
+      summary columns) or a user `mask`."""
+
+    def __init__(self, pattern: str = "strided", stride: int = 64, block: int = 64, mask: torch.Tensor | None = None,
+                 local: int = 1, window: int = 128, num_global: int = 0, num_random: int = 2, seed: int = 0,
+                 causal: bool = False, bitmap: torch.Tensor | None = None, block_stride: int = 4):
         self.pattern, self.stride, self.block, self.user_mask = pattern, stride, block, mask
+        self.local, self.window, self.num_global, self.num_random = local, window, num_global, num_random
+        self.seed, self.causal, self.bitmap, self.block_stride = seed, causal, bitmap, block_stride
+
+    def block_pattern(self, Sq: int, Sk: int):
+        """The AttentionPattern of a block pattern (None for token patterns)."""
+        from ..ops import sparse_attention as SA
+
+        nq, nk = (Sq + 127) // 128, (Sk + 127) // 128
+        if self.bitmap is not None:
+            return SA.block_sparse(self.bitmap, causal=self.causal)
+        if self.pattern == "block_strided":
+            bm = SA.strided_bitmap(nq, nk, self.local, self.block_stride, self.causal)
+            return SA.block_sparse(bm, causal=self.causal, key=f"strided{nq}x{nk}:{self.local}:{self.block_stride}")
+        if self.pattern == "bigbird":
+            g = torch.Generator().manual_seed(self.seed)
+            bm = torch.zeros(nq, nk, dtype=torch.bool)
+            for i in range(nq):
+                bm[i, torch.randperm(nk, generator=g)[: self.num_random]] = True
+            return SA.AttentionPattern(causal=self.causal, window_left=self.window, num_global=self.num_global,
+                                       bitmap=bm, bitmap_key=f"bigbird{nq}x{nk}:{self.num_random}:{self.seed}")
+        return None
 
     def mask(self, S: int, device=None) -> torch.Tensor:
         if self.user_mask is not None:
             return self.user_mask.to(device)
+        bp = self.block_pattern(S, S)
+        if bp is not None:
+            return bp.allowed_dense(S, S, device=device)
         i = torch.arange(S, device=device)
         if self.pattern == "strided":
             local = (i[:, None] - i[None, :]).abs() < self.stride
@@ -321,6 +361,9 @@ class SparseAttention:
         return blk | summary
 
     def forward(self, q, k, v, scale=None):
+        bp = self.block_pattern(q.shape[1], k.shape[1]) if self.user_mask is None else None
+        if bp is not None and q.is_cuda:
+            return FN.attention(q, k, v, False, scale, plan=bp.plan(q.shape[1], k.shape[1], q.shape[-1], q.device))
         return attention_with_bias(q, k, v, mask=self.mask(q.shape[1], q.device), scale=scale)
 
 

@@ -66,6 +66,7 @@ class _RecurrentFn(torch.autograd.Function):
                 K.rnn_cell_fwd(gx[t], gh, hs[t + 1])
         ctx.kind = kind
         ctx.has_b = b_ih is not None
+        ctx.has_h0, ctx.has_c0 = h0 is not None, c0 is not None
         ctx.save_for_backward(xt, hs, cs if cs is not None else torch.empty(0, device=dev),
                               acts if acts is not None else torch.empty(0, device=dev), w_ih, w_hh)
         y = hs[1:].transpose(0, 1).contiguous()
@@ -120,8 +121,8 @@ class _RecurrentFn(torch.autograd.Function):
             K.bias_grad(dgh2, db_hh)
             db_ih, db_hh = db_ih.to(w_ih.dtype), db_hh.to(w_ih.dtype)
         dx = dxt.view(S, B, -1).transpose(0, 1)
-        dh0 = dh_next.to(dt)
-        dc0 = dc if kind == "lstm" else None
+        dh0 = dh_next.to(dt) if ctx.has_h0 else None
+        dc0 = dc if (kind == "lstm" and ctx.has_c0) else None
         return None, dx, dh0, dc0, dw_ih.to(w_ih.dtype), dw_hh.to(w_hh.dtype), db_ih, db_hh
 
 

@@ -8,6 +8,8 @@ softmax-cross-entropy, embedding). Other dtypes / devices use PyTorch
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -15,6 +17,8 @@ from . import kernels as K
 
 
 def _native(*ts) -> bool:
+    if os.environ.get("SCIRS_KERNELS", "custom") == "torch":  # explicitly requested: no warning
+        return False
     return all(t is None or (t.is_cuda and t.dtype == torch.bfloat16) for t in ts)
 
 
@@ -26,6 +30,8 @@ def _fallback(op: str, *ts):
     instead of the framework's kernels (dtype other than bf16, or a shape the
     kernels do not take). CPU calls are the reference semantics, not a
     fallback."""
+    if os.environ.get("SCIRS_KERNELS", "custom") == "torch":
+        return
     if any(t is not None and t.is_cuda for t in ts):
         K.STATS.fallbacks[op] = K.STATS.fallbacks.get(op, 0) + 1
         if op not in _warned:
@@ -167,15 +173,21 @@ def layer_norm(x, w, b, eps=1e-5):
 
 # ---------------------------------------------------------------------------- attention
 class _AttnFn(torch.autograd.Function):
+    """Flash attention on the tcgen05 kernels; q [B, S, H, D], k / v
+    [B, Sk, H, D] (Sk may differ: cross-attention); `plan` selects the
+    block-sparse / windowed kernels."""
+
     @staticmethod
-    def forward(ctx, q, k, v, causal, scale):
+    def forward(ctx, q, k, v, causal, scale, plan):
         B, S, H, D = q.shape
-        q, k, v = (t if t.stride(-1) == 1 and t.stride(2) == D else t.contiguous() for t in (q, k, v))
+        fix = lambda t: t if t.stride(-1) == 1 and t.stride(2) == D and t.stride(0) == t.shape[1] * t.stride(1) \
+            else t.contiguous()  # noqa: E731
+        q, k, v = fix(q), fix(k), fix(v)
         out = torch.empty(B, S, H, D, device=q.device, dtype=q.dtype)
         lse = torch.empty(B, H, S, device=q.device, dtype=torch.float32)
-        K.flash_attn_fwd(q, k, v, out, lse, causal, scale)
+        K.flash_attn_fwd(q, k, v, out, lse, causal, scale, plan=plan)
         ctx.save_for_backward(q, k, v, out, lse)
-        ctx.causal, ctx.scale = causal, scale
+        ctx.causal, ctx.scale, ctx.plan = causal, scale, plan
         return out
 
     @staticmethod
@@ -183,19 +195,30 @@ class _AttnFn(torch.autograd.Function):
         q, k, v, out, lse = ctx.saved_tensors
         B, S, H, D = q.shape
         do = do.contiguous()
-        dq, dk, dv = (torch.empty(B, S, H, D, device=q.device, dtype=q.dtype) for _ in range(3))
+        dq = torch.empty_like(q)
+        dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+        dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
         dq_acc = torch.empty(B * S * H * D, device=q.device, dtype=torch.float32)
         delta = torch.empty(B * H * S, device=q.device, dtype=torch.float32)
-        K.flash_attn_bwd(do, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, ctx.causal, ctx.scale)
-        return dq, dk, dv, None, None
+        K.flash_attn_bwd(do, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, ctx.causal, ctx.scale, plan=ctx.plan)
+        return dq, dk, dv, None, None, None
 
 
-def attention(q, k, v, causal: bool = False, scale: float | None = None):
-    """Scaled dot-product attention on [B, S, H, D] tensors (token-major)."""
+def attention(q, k, v, causal: bool = False, scale: float | None = None, plan=None):
+    """Scaled dot-product attention on [B, S, H, D] tensors (token-major);
+    k / v may have another sequence length (cross-attention). `plan`
+    (ops.sparse_attention.AttentionPlan) restricts it to a sparse / windowed
+    pattern without building a dense mask."""
     scale = scale if scale is not None else q.shape[-1] ** -0.5
-    if _native(q, k, v) and q.shape[-1] in (64, 128) and q.shape == k.shape == v.shape:
-        return _AttnFn.apply(q, k, v, causal, scale)
+    same_kv = k.shape == v.shape and k.shape[0] == q.shape[0] and k.shape[2:] == q.shape[2:]
+    if _native(q, k, v) and q.shape[-1] in (64, 128) and same_kv and (not causal or k.shape[1] == q.shape[1]):
+        return _AttnFn.apply(q, k, v, causal, scale, plan)
     _fallback("attention", q)
+    if plan is not None:
+        from .sparse_attention import reference_attention
+
+        o, _ = reference_attention(q, k, v, plan.pattern, scale)
+        return o.to(q.dtype)
     o = F.scaled_dot_product_attention(
         q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=causal, scale=scale
     )

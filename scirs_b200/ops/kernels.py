@@ -265,11 +265,16 @@ def attention_reference(q, k, v, causal, scale):
     return o, lse
 
 
-def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
-    """q/k/v/out: [B, S, H, D] token-major views (heads contiguous)."""
+def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None, plan=None):
+    """q/out: [B, S, H, D], k/v: [B, Sk, H, D] token-major views (heads
+    contiguous). `plan` (ops.sparse_attention.AttentionPlan) selects the
+    sparse / windowed kernels, which visit only the planned key blocks."""
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        if ATTN_FWD_IMPL in ("pingpong", "pingpong_poly", "pingpong_x2"):
+        if plan is not None:
+            _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(plan.pattern.causal), float(scale), False, None,
+                                             False, **plan.kernel_args())
+        elif ATTN_FWD_IMPL in ("pingpong", "pingpong_poly", "pingpong_x2"):
             _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(causal), float(scale),
                                              ATTN_FWD_IMPL == "pingpong_poly", None, ATTN_FWD_IMPL == "pingpong_x2")
         elif ATTN_FWD_IMPL == "tcgen05":
@@ -278,7 +283,12 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None):
             _ext.kernels().flash_attn_fwd(q, k, v, out, lse, bool(causal), float(scale))
         _count(1)
         return out
-    o, l = attention_reference(q, k, v, causal, scale)
+    if plan is not None:
+        from .sparse_attention import reference_attention
+
+        o, l = reference_attention(q, k, v, plan.pattern, scale)
+    else:
+        o, l = attention_reference(q, k, v, causal, scale)
     out.copy_(o)
     lse.copy_(l.reshape(lse.shape))
     return out
@@ -294,16 +304,25 @@ def flash_attn_fwd_impl(impl, q, k, v, out, lse, causal=True, scale=None):
         ATTN_FWD_IMPL = old
 
 
-def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=True, scale=None):
+def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=True, scale=None, plan=None):
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, bool(causal), float(scale),
-                                      1 if ATTN_BWD_IMPL == "tcgen05" else 0)
+        if plan is not None:
+            _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta,
+                                          bool(plan.pattern.causal), float(scale), 1, **plan.kernel_args(True))
+        else:
+            _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, bool(causal),
+                                          float(scale), 1 if ATTN_BWD_IMPL == "tcgen05" else 0)
         _count(3)
         return
     with torch.enable_grad():
         qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
-        o, _ = attention_reference(qf, kf, vf, causal, scale)
+        if plan is not None:
+            from .sparse_attention import reference_attention
+
+            o, _ = reference_attention(qf, kf, vf, plan.pattern, scale)
+        else:
+            o, _ = attention_reference(qf, kf, vf, causal, scale)
         gq, gk, gv = torch.autograd.grad(o, (qf, kf, vf), dout.float())
     dq.copy_(gq)
     dk.copy_(gk)

@@ -73,10 +73,14 @@ def data_parallel(model, mode: str = "fused", comm=None, area_bytes: int | None 
 
     Also broadcasts rank 0's parameters so all replicas start equal.
     """
+    import os
+
     from .nvlink import NVLinkComm
 
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return model
+    if mode == "fused" and os.environ.get("SCIRS_COMM") == "nccl":
+        mode = "nccl"
     fp = model.fp
     dist.broadcast(fp.master, src=0)
     fp.sync_bf16()

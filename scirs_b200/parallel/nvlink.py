@@ -20,14 +20,16 @@ from .. import _ext
 
 
 class NVLinkComm:
-    def __init__(self, area_bytes: int = 256 << 20, timeout_s: float = 5.0, group=None):
+    def __init__(self, area_bytes: int = 256 << 20, timeout_s: float | None = None, group=None):
         assert dist.is_initialized(), "init the process group first"
         self.mod = _ext.comm()
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.device = torch.cuda.current_device()
-        self.timeout_s = float(timeout_s)
+        import os
+
+        self.timeout_s = float(timeout_s if timeout_s is not None else os.environ.get("SCIRS_WAIT_TIMEOUT_S", 5.0))
         self.area_bytes = (int(area_bytes) + 255) // 256 * 256
         self.id, handle = self.mod.create(self.device, self.rank, self.world, self.area_bytes)
         handles = [None] * self.world

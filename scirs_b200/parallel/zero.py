@@ -397,9 +397,13 @@ def zero_data_parallel(model, mode: str = "fused", comm=None, lr=1e-3, betas=(0.
     Broadcasts rank 0's parameters first so all replicas start equal.
     Returns the model; its `optimizer` is the sharded AdamW.
     """
+    import os
+
     from .nvlink import NVLinkComm
 
     assert dist.is_initialized()
+    if mode == "fused" and os.environ.get("SCIRS_COMM") == "nccl":
+        mode = "nccl"
     fp = model.fp
     dist.broadcast(fp.master, src=0)
     fp.sync_bf16()

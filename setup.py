@@ -89,6 +89,7 @@ setup(
     name="scirs_b200",
     version="0.1.0",
     packages=["scirs_b200"],
+    package_data={"scirs_b200": ["configs/*.yaml"]},
     ext_modules=ext_modules,
     cmdclass={"build_ext": _BuildExt.with_options(use_ninja=True)},
 )

@@ -54,3 +54,12 @@ def test_layers_stack_and_bidirectional():
     assert bi(x).shape == (2, 5, 32)
     last = R.RNN(8, 16, return_sequences=False, seed=5)(x)
     assert last.shape == (2, 16)
+
+
+def test_recurrent_fn_without_initial_state():
+    """No h0 / c0: the Function returns no gradient for them."""
+    w = [t.requires_grad_(True) for t in _weights("lstm", 8, 16, 7)]
+    x = torch.randn(2, 4, 8, requires_grad=True)
+    y, h, c = R._RecurrentFn.apply("lstm", x, None, None, *w)
+    y.sum().backward()
+    assert x.grad is not None and w[0].grad is not None
