@@ -292,10 +292,13 @@ class GPTModel(FusedTrainerMixin):
         B, S = tokens.shape
         A = self.acts(B, S)
         tok = tokens.reshape(-1)
-        n = self._forward(tok, A)
-        K.xent_fwd_bwd(A.logits, targets.reshape(-1), A.losses, self.cfg.vocab_size, 1.0 / A.M)
+        with self._phase("forward"):
+            n = self._forward(tok, A)
+        with self._phase("loss"):
+            K.xent_fwd_bwd(A.logits, targets.reshape(-1), A.losses, self.cfg.vocab_size, 1.0 / A.M)
         n += 1
-        n += self._backward(tok, A)
+        with self._phase("backward"):
+            n += self._backward(tok, A)
         self.kernel_launches += n
         return A.losses.mean()
 

@@ -136,6 +136,12 @@ class FusedTrainerMixin:
 
     kernel_launches = 0
     param_sync = None
+    tracer = None  # utils.tracing.PhaseTimer: device time per phase of eager steps
+
+    def _phase(self, name: str):
+        import contextlib
+
+        return self.tracer.phase(name) if self.tracer is not None else contextlib.nullcontext()
 
     def _params_begin(self):
         """Start the (ZeRO) parameter all-gather for this forward, if any."""
@@ -165,8 +171,10 @@ class FusedTrainerMixin:
         self.zero_grad()
         loss = self.forward_backward(inputs, targets)
         if self.grad_sync is not None:
-            self.grad_sync.finish()
-        self.optimizer.step()
+            with self._phase("comm_wait"):
+                self.grad_sync.finish()
+        with self._phase("optimizer"):
+            self.optimizer.step()
         self.kernel_launches += self.optimizer.launches_per_step
         return loss
 
