@@ -28,6 +28,7 @@ def main():
     ap.add_argument("--schedule", default="1f1b", choices=["1f1b", "gpipe"])
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--no-graph", action="store_true", help="run each stage's step eagerly (no CUDA graph)")
     args = ap.parse_args()
     rank, world, local = sdist.init(timeout_s=120)
     dev = torch.device("cuda", local)
@@ -37,6 +38,8 @@ def main():
     st = GPTPipelineStage(cfg, stage=rank, num_stages=world, num_micro=args.micro, device=dev,
                           schedule=args.schedule)
     st.configure_adamw(lr=6e-4)
+    if not args.no_graph:
+        st.enable_cuda_graph()
     g = torch.Generator().manual_seed(0)
     tok = torch.randint(0, cfg.vocab_size, (args.batch, S + 1), generator=g)
     x, y = tok[:, :-1].contiguous().to(dev), tok[:, 1:].contiguous().to(dev)
@@ -53,6 +56,7 @@ def main():
     torch.cuda.synchronize()
     ms = sdist.max_over_ranks(e0.elapsed_time(e1) / args.steps)
     _ext.check_status(local)
+    st.release_cuda_graph()
     lv = float(loss) if loss is not None else None
     vals = [lv]
     if world > 1:
@@ -60,6 +64,7 @@ def main():
         torch.distributed.all_gather_object(vals, lv)
     if rank == 0:
         print(json.dumps({"model": f"gpt2-small-{args.layers}L", "pp": world, "schedule": args.schedule,
+                          "cuda_graph": not args.no_graph,
                           "global_batch": args.batch, "micro_batches": args.micro, "seq_len": S,
                           "ms_per_step": round(ms, 3), "tokens_per_s": round(args.batch * S / (ms * 1e-3)),
                           "loss": vals[-1]}), flush=True)

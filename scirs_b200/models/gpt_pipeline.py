@@ -116,6 +116,8 @@ class GPTPipelineStage(FusedTrainerMixin):
         self.g_tied = dist.new_group(tied) if num_stages > 1 else None
         self._pool: list[_StageActs] = []
         self._pool_key = None
+        self._graph = self._graph_key = self._warm_key = None
+        self._last_shape = None
         self.grad_sync = None
         self.optimizer = None
         self.kernel_launches = 0
@@ -187,14 +189,23 @@ class GPTPipelineStage(FusedTrainerMixin):
         return n
 
     # ----------------------------------------------------------------- API
-    def forward_backward(self, tokens: torch.Tensor, targets: torch.Tensor):
+    def forward_backward(self, tokens: torch.Tensor, targets: torch.Tensor, shape=None):
         """Forward + backward of all micro-batches of the step (gradients
         accumulate into the flat buffer; the tied embedding gradient is
         summed across its two stages). Returns the mean loss on the last
         stage (device scalar), None elsewhere. `tokens` / `targets` [B, S]
-        are needed on the first / last stage only (others may pass None)."""
+        are needed on the first / last stage only; a stage given neither
+        takes the batch shape from `shape` (or the previous step)."""
         ref = tokens if tokens is not None else targets
-        B, S = ref.shape
+        if ref is not None:
+            B, S = ref.shape
+        elif shape is not None:
+            B, S = shape
+        elif getattr(self, "_last_shape", None) is not None:
+            B, S = self._last_shape
+        else:
+            raise ValueError("a middle stage needs the batch shape (pass shape=(B, S))")
+        self._last_shape = (B, S)
         assert B % self.num_micro == 0, "batch must split into equal micro-batches"
         mb = B // self.num_micro
         pool = self._acts_pool(mb, S)
@@ -225,15 +236,53 @@ class GPTPipelineStage(FusedTrainerMixin):
         self.kernel_launches += n
         return loss
 
-    def train_step(self, tokens, targets):
+    def train_step(self, tokens, targets, shape=None):
         """zero_grad -> pipelined forward/backward -> tied-gradient sum ->
-        fused AdamW with the global-norm clip taken over all stages."""
+        fused AdamW with the global-norm clip taken over all stages. With
+        enable_cuda_graph() the whole step of this stage (its kernels, the
+        NCCL point-to-point transfers and the two all-reduces) is captured
+        once per batch shape and replayed; every stage must enable it."""
         if self.optimizer is None:
             self.configure_adamw()
+        if getattr(self, "use_graph", False) and self.device.type == "cuda":
+            return self._step_graphed(tokens, targets, shape)
+        return self._step_eager(tokens, targets, shape)
+
+    def _step_eager(self, tokens, targets, shape=None):
         self.fp.grad.zero_()
-        loss = self.forward_backward(tokens, targets)
+        loss = self.forward_backward(tokens, targets, shape)
         self._optimizer_step()
         return loss
+
+    def _step_graphed(self, tokens, targets, shape=None):
+        ref = tokens if tokens is not None else targets
+        key = tuple(ref.shape) if ref is not None else (tuple(shape) if shape is not None else self._last_shape)
+        if self._graph is not None and self._graph_key == key:
+            if tokens is not None:
+                self._g_tok.copy_(tokens, non_blocking=True)
+            if targets is not None:
+                self._g_tgt.copy_(targets, non_blocking=True)
+            self._graph.replay()
+            self.optimizer.t += 1
+            K.STATS.launches += self._graph_kernels
+            return self._g_loss
+        if self._warm_key != key:  # first step at this shape runs eagerly and allocates every buffer
+            self._warm_key = key
+            return self._step_eager(tokens, targets, shape)
+        self._g_tok = tokens.clone() if tokens is not None else None
+        self._g_tgt = targets.clone() if targets is not None else None
+        torch.cuda.synchronize()
+        if self.P > 1:
+            dist.barrier(group=self.g_all)
+        k0 = K.STATS.launches
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._g_loss = self._step_eager(self._g_tok, self._g_tgt, key)
+        self._graph_kernels = K.STATS.launches - k0
+        K.STATS.launches = k0
+        self.optimizer.t -= 1  # the capture did not execute a step; the replay below does
+        self._graph, self._graph_key = g, key
+        return self._step_graphed(tokens, targets, shape)
 
     def _optimizer_step(self):
         o, fp = self.optimizer, self.fp

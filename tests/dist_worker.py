@@ -376,16 +376,20 @@ def case_pp_gpt():
     tok = torch.randint(0, cfg.vocab_size, (8, 129), generator=g)
     x, y = tok[:, :-1].contiguous().to(dev), tok[:, 1:].contiguous().to(dev)
     res = {}
-    for sched in ("1f1b", "gpipe"):
-        st = GPTPipelineStage(cfg, stage=rank, num_stages=world, num_micro=4, device=dev, seed=5, schedule=sched)
+    for sched in ("1f1b", "gpipe", "1f1b_graph"):
+        st = GPTPipelineStage(cfg, stage=rank, num_stages=world, num_micro=4, device=dev, seed=5,
+                              schedule=sched.split("_")[0])
         st.configure_adamw(lr=1e-3, weight_decay=0.1, max_grad_norm=0.5)
+        if sched.endswith("graph"):
+            st.enable_cuda_graph()
         losses = []
-        for _ in range(3):
-            l = st.train_step(x if st.first else None, y if st.last else None)
+        for _ in range(4 if sched.endswith("graph") else 3):  # graph: eager, capture + replay, replays
+            l = st.train_step(x if st.first else None, y if st.last else None, shape=(8, 128))
             v = torch.tensor([float(l) if l is not None else 0.0], device=dev)
             dist.all_reduce(v)
             losses.append(float(v))
         torch.cuda.synchronize()
+        st.release_cuda_graph()
         wsum = float(st.fp.m("wte").double().abs().sum()) if (st.first or st.last) else 0.0
         sums = [None] * world
         dist.all_gather_object(sums, wsum)
@@ -393,7 +397,7 @@ def case_pp_gpt():
     if rank == 0:
         m = GPTModel(cfg, device=dev, seed=5)
         m.configure_adamw(lr=1e-3, weight_decay=0.1, max_grad_norm=0.5)
-        res["single"] = {"losses": [float(m.train_step(x, y)) for _ in range(3)]}
+        res["single"] = {"losses": [float(m.train_step(x, y)) for _ in range(4)]}
     _ext.check_status()
     return res
 

@@ -108,7 +108,7 @@ def test_expert_parallel_peer_kernels(tmp_path, nproc):
 def test_pipeline_parallel_gpt(tmp_path, nproc):
     res = _run("pp_gpt", tmp_path, nproc=nproc, port=29618)
     ref = res["single"]["losses"]
-    for sched in ("1f1b", "gpipe"):
+    for sched in ("1f1b", "gpipe", "1f1b_graph"):
         assert res[sched]["tied_diff"] == 0.0, (sched, res[sched])
         for a, b in zip(res[sched]["losses"], ref):
             assert abs(a - b) < 2e-2, (sched, res[sched]["losses"], ref)
