@@ -246,7 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_32x32b_x32(lane_base + T_S + c0, sv);
       tmem_ld_32x32b_x32(lane_base + T_DP + c0, dv);
       tc_wait_ld();
-      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) || SPARSE;
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
+                             (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
       uint32_t pp[16], dd[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {

@@ -12,7 +12,8 @@
 //              followed by S_t(j+1) = Q_t K_{j+1}^T, alternating t, so the
 //              tensor core works on one tile while the other tile's softmax
 //              warps run
-//   warps 2-5  softmax of tile 0, warps 6-9 softmax of tile 1: thread owns
+//   warps 2-3  idle (their registers go to the softmax warpgroups)
+//   warps 4-7  softmax of tile 0, warps 8-11 softmax of tile 1: thread owns
 //              one query row (TMEM lane); reads the 128 scores of its row in
 //              one go, takes the row max, and keeps a running reference max
 //              that is raised only when a score exceeds it by more than
@@ -39,7 +40,13 @@ namespace fa2t {
 
 using bf16 = __nv_bfloat16;
 constexpr int BM = 128, BN = 128;
-constexpr int kThreads = 320;
+// 12 warps = 3 warpgroups: warpgroup 0 = TMA warp, MMA warp and two idle
+// warps (registers given away), warpgroups 1 and 2 = the softmax warps of
+// tile 0 and tile 1 (registers taken). The block launches with 168 registers
+// per thread (65536 / 384 rounded down to 8): 128 x 56 + 256 x 224 = 384 x 168.
+constexpr int kThreads = 384;
+constexpr int kRegsLaunch = 168, kRegsCtl = 56, kRegsSoftmax = 224;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split exceeds the launch");
 constexpr float kRescaleLog2 = 8.f;  // raise the reference max only past 2^8
 
 struct Params {
@@ -161,7 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsCtl>();
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
@@ -245,9 +253,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 0, nullptr);
     }
+  }
   } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ---------------------------------------------------------------- softmax
-    const int t = (warp - 2) >> 2;   // tile of this warpgroup
+    const int t = (warp - 4) >> 2;   // tile of this warpgroup
     const int q = warp & 3;          // TMEM lane quarter
     const int r = q * 32 + lane;     // query row within the tile
     const int qrow = q0 + t * BM + r;
@@ -280,7 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       lap(1);
       const int kv0 = kblk(j) * BN;
-      const bool mask = (kv0 + BN > Sk) || (CAUSAL && kv0 + BN > q0 + t * BM) || SPARSE;
+      const bool mask = (kv0 + BN > Sk) || (CAUSAL && kv0 + BN > q0 + t * BM) ||
+                        (SPARSE && !attn_block_full(p.sp, q0 + t * BM, q0 + t * BM + BM - 1, kv0, kv0 + BN - 1));
       if (mask) {
 #pragma unroll
         for (int e = 0; e < BN; ++e) {

@@ -624,7 +624,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) { ok = false; break; }
       if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) || SPARSE;
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
+                             (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
 #pragma unroll 1
       for (int c = c_begin; c < c_begin + BQ / 2; c += 32) {
         uint32_t sv[32], dv[32];

@@ -441,6 +441,30 @@ __device__ __forceinline__ uint64_t gelu_tanh_grad2(uint64_t x) {
   return f2_fma(c, f2_fma(nt, t, one), f2_fma(half, t, half));
 }
 
+// Warpgroup register reallocation (all 128 threads of a warpgroup execute
+// the same instruction). The shares of all warpgroups must not exceed the
+// registers the block was launched with (threads x registers per thread).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg: multiple of 8 in [24, 256]");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg: multiple of 8 in [24, 256]");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// True when every pair of queries [q0, q1] x keys [k0, k1] is allowed, so a
+// tile needs no element mask (block bitmap entries cover whole 128 x 128
+// blocks; q0 / k0 are multiples of 64 / 128 and the ranges lie in one block).
+__device__ __forceinline__ bool attn_block_full(const AttnSparse& a, int q0, int q1, int k0, int k1) {
+  if (a.bmap == nullptr && a.wl < 0 && a.ng <= 0) return true;
+  if (a.bmap != nullptr && a.bmap[(long)(q0 >> 7) * a.bmap_ld + (k0 >> 7)] != 0) return true;
+  if (a.wl >= 0 && k0 >= q1 - a.wl && k1 <= q0 + a.wr) return true;
+  return q1 < a.ng || k1 < a.ng;
+}
+
 __device__ __forceinline__ bool attn_allowed(const AttnSparse& a, int q, int k) {
   // union of the components that are present (none present: everything)
   if (a.bmap == nullptr && a.wl < 0 && a.ng <= 0) return true;
