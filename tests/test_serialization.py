@@ -113,39 +113,8 @@ def test_safetensors_model_roundtrip(tmp_path):
     assert torch.equal(m(x), m2(x))
 
 
-def _numpy_mlp_oracle(W1, b1, W2, b2, x, y, steps, batch, lr, b1_=0.9, b2_=0.999, eps=1e-8):
-    """float64 restatement of the reference math: Dense y = xW + b (W [in,out]),
-    ReLU, softmax cross-entropy mean over the batch, bias-corrected Adam."""
-    import numpy as np
-
-    P = [W1.copy(), b1.copy(), W2.copy(), b2.copy()]
-    m = [np.zeros_like(p) for p in P]
-    v = [np.zeros_like(p) for p in P]
-    out = []
-    for t in range(1, steps + 1):
-        xb, yb = x[(t - 1) * batch : t * batch], y[(t - 1) * batch : t * batch]
-        h = xb @ P[0] + P[1]
-        a = np.maximum(h, 0)
-        z = a @ P[2] + P[3]
-        z = z - z.max(1, keepdims=True)
-        p = np.exp(z) / np.exp(z).sum(1, keepdims=True)
-        out.append(float(-np.log(p[np.arange(batch), yb]).mean()))
-        dz = p.copy()
-        dz[np.arange(batch), yb] -= 1
-        dz /= batch
-        G = [None] * 4
-        G[2], G[3] = a.T @ dz, dz.sum(0)
-        dh = (dz @ P[2].T) * (h > 0)
-        G[0], G[1] = xb.T @ dh, dh.sum(0)
-        for i in range(4):
-            m[i] = b1_ * m[i] + (1 - b1_) * G[i]
-            v[i] = b2_ * v[i] + (1 - b2_) * G[i] ** 2
-            P[i] = P[i] - lr * (m[i] / (1 - b1_**t)) / (np.sqrt(v[i] / (1 - b2_**t)) + eps)
-    return out
-
-
 def test_mlp_config_cpu(tmp_path):
-    from scirs_b200.models.mlp import synthetic_mnist
+    from scirs_b200.models.mlp import numpy_reference_losses, synthetic_mnist
 
     init = mnist_mlp(seed=0)
     r = train_mnist_mlp(steps=100, batch=64, lr=1e-3, seed=0, checkpoint_path=str(tmp_path / "mnist_model.json"))
@@ -154,7 +123,7 @@ def test_mlp_config_cpu(tmp_path):
     x, y = synthetic_mnist(100 * 64, seed=0)
     ws = [t.detach().double().numpy() for t in
           (init.layers()[0].weight, init.layers()[0].bias, init.layers()[1].weight, init.layers()[1].bias)]
-    ref = _numpy_mlp_oracle(*ws, x.double().numpy(), y.numpy(), 100, 64, 1e-3)
+    ref = numpy_reference_losses(*ws, x.double().numpy(), y.numpy(), 100, 64, 1e-3)
     assert max(abs(a - b) for a, b in zip(L, ref)) < 2e-3
     m2 = load_model(tmp_path / "mnist_model.json", dtype=torch.float32)
     x = torch.rand(3, 784)
