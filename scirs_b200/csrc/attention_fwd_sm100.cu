@@ -104,7 +104,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false, bool X2 = false, bool SPARSE = false>
+template <int HD, bool CAUSAL, bool POLY = false, bool TRACE = false, bool X2 = false, bool SPARSE = false,
+          bool BF2 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -346,6 +347,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float p0, p1;
+          if (BF2) {
+            // two exponentials per MUFU instruction; P comes out packed
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(sv[c + e], sv[c + e + 1]), sc2, nref2), x0, x1);
+            const uint32_t pp = ex2_bf16x2(x0, x1);
+            pk[e >> 1] = pp;
+            rs2[(e >> 1) & 1] = f2_add(rs2[(e >> 1) & 1], f2_pack(bf16_lo(pp), bf16_hi(pp)));
+            continue;
+          }
           if (X2) {
             float x0, x1;
             f2_unpack(f2_fma(f2_pack(sv[c + e], sv[c + e + 1]), sc2, nref2), x0, x1);
@@ -362,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_32x32b_x16(s_base + (c >> 1), pk);
       }
-      if (X2) {
+      if (X2 || BF2) {
         f2_unpack(f2_add(rs2[0], rs2[1]), rs[0], rs[1]);
         l += rs[0] + rs[1];
       } else {
@@ -457,7 +467,7 @@ AttnSparse attn_sparse_args(const c10::optional<torch::Tensor>& ptr, const c10::
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2,
                        c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
-                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng) {
+                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng, bool bf2) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
@@ -498,9 +508,9 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
   }
   auto st = cur_stream();
-#define FA2T(HD_, C_, P_, R_, X_, SP_)                                         \
+#define FA2T(HD_, C_, P_, R_, X_, SP_, ...)                                    \
   {                                                                            \
-    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_, X_, SP_>;              \
+    auto kern = fa2t::fa_fwd_pp_kernel<HD_, C_, P_, R_, X_, SP_, ##__VA_ARGS__>; \
     set_max_smem((const void*)kern, fa2t::Cfg<HD_>::SMEM);                     \
     kern<<<grid, fa2t::kThreads, fa2t::Cfg<HD_>::SMEM, st>>>(tq, tk, tv, p);   \
   }
@@ -513,8 +523,15 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   const bool traced = p.trace != nullptr;
   TORCH_CHECK(!(traced && poly), "the trace is available for the plain variant");
   TORCH_CHECK(!(x2 && poly), "poly and x2 variants are exclusive");
-  TORCH_CHECK(!(sparse && (traced || poly || x2)), "sparse attention uses the plain variant");
-  if (sparse) {
+  TORCH_CHECK(!(sparse && (traced || poly || x2 || bf2)), "sparse attention uses the plain variant");
+  TORCH_CHECK(!(bf2 && (traced || poly || x2)), "the bf16x2-exponential variant is exclusive");
+  if (bf2) {
+    if (HD == 64) {
+      if (causal) FA2T(64, true, false, false, false, false, true) else FA2T(64, false, false, false, false, false, true)
+    } else {
+      if (causal) FA2T(128, true, false, false, false, false, true) else FA2T(128, false, false, false, false, false, true)
+    }
+  } else if (sparse) {
     FA2T_HD(false, false, false, true)
   } else if (traced) {
     if (x2) {

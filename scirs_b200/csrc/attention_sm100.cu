@@ -413,7 +413,14 @@ namespace fabw {
 
 using bf16 = __nv_bfloat16;
 constexpr int HD = 64, BK = 128, BQ = 128;
-constexpr int kThreads = 320;
+// 16 warps = 4 warpgroups: 0 = TMA warp, MMA warp, two idle warps; 1 and 2 =
+// the eight dS warps; 3 = the dQ-drain / dK-dV epilogue warps. Launched with
+// 128 registers per thread (65536 / 512); the control and drain warpgroups
+// give registers to the dS warpgroups: 128 x 56 + 256 x 176 + 128 x 96 <= 512 x 128.
+constexpr int kThreads = 512;
+constexpr int kRegsLaunch = 128, kRegsCtl = 56, kRegsDs = 176, kRegsDrain = 96;
+static_assert(128 * kRegsCtl + 256 * kRegsDs + 128 * kRegsDrain <= kThreads * kRegsLaunch,
+              "register split exceeds the launch");
 constexpr int T_BYTES = 128 * HD * 2;    // one 128-row x 64-col bf16 tile (16 KB)
 constexpr int P_BYTES = BK * BQ * 2;     // 128 x 128 bf16 (32 KB)
 constexpr int OFF_K = 0;
@@ -519,6 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + HD, T_DQ = 256 + 2 * HD;
 
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsCtl>();
   if (warp == 0) {
     // ------------------------------------------------------------ TMA
     if (lane == 0) {
@@ -588,41 +597,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 0, nullptr);
     }
-  } else {
-    // ------------------------------------------------------------ dS (+ dQ) warps
-    // All eight warps compute P / dS for each query block: warps 2-5 the
-    // first 64 queries of every key row, warps 6-9 the other 64 (two warps
-    // per scheduler share the MUFU / issue work). Warps 6-9 then also copy
-    // the block's dQ out of TMEM while the tensor core starts the next block.
-    const bool dq_role = warp >= 6;
+  }
+  } else if (warp < 12) {
+    setmaxnreg_inc<kRegsDs>();
+    // ------------------------------------------------------------ dS warps
+    // Eight warps compute P / dS for each query block: warps 4-7 the first
+    // 64 queries of every key row, warps 8-11 the other 64 (two warps per
+    // scheduler share the MUFU / issue work).
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;   // key row in the tile
     const int key = k0 + r;
-    const int t128 = (warp - 2) * 32 + lane;
+    const bool stager = warp < 8;   // warps 4-7 stage the block's LSE / delta
+    const int t128 = (warp - 4) * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
     const float* lse_g = p.lse + ((long)b * H + h) * S;
     const float* del_g = p.delta + ((long)b * H + h) * S;
     uint8_t* pt_row = smem + OFF_PT + r * 128;
     uint8_t* ds_row = smem + OFF_DST + r * 128;
     const float LOG2E = 1.4426950408889634f;
-    const int c_begin = dq_role ? BQ / 2 : 0;
-    uint8_t* slot0 = smem + OFF_DQS + (dq_role ? (warp - 6) : 0) * 8192;
-    uint8_t* slot1 = slot0 + 4096;
-    bool ok = true;
+    const int c_begin = stager ? 0 : BQ / 2;
     for (int n = 0; n < niter; ++n) {
       const int i = qblk(n);
       const int q0 = i * BQ;
       float* sL = sLD + (n & 1) * 256;
-      if (!dq_role) {
+      if (stager) {
         const int q = q0 + t128;
         sL[t128] = q < S ? lse_g[q] * LOG2E : 0.f;
         sL[128 + t128] = q < S ? del_g[q] : 0.f;
         __syncwarp();
         if (lane == 0) mbar_arrive(&ld_bar[n & 1]);
       }
-      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) break;
+      if (!mbar_wait(s_full, n & 1, p.st, 56, abort_flag)) break;
+      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 57, abort_flag)) break;
       tc_fence_after();
       const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
                              (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
@@ -666,8 +673,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(s_free);
         mbar_arrive(p_full);
       }
-      if (!dq_role) continue;
-      // ---- dQ_i: TMEM -> fp32 smem slots -> TMA reduce-add into dq_acc
+    }
+  } else {
+    setmaxnreg_dec<kRegsDrain>();
+    // ------------------------------------------------------------ dQ drain, then dK / dV
+    // Warps 12-15 move each block's dQ out of TMEM (lane quarter warp % 4):
+    // TMEM -> 128B-swizzled fp32 smem slots -> TMA reduce-add into the fp32
+    // dQ accumulator [B*S, H*HD], while the dS warps work on the next block.
+    const int q4 = warp & 3;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    uint8_t* slot0 = smem + OFF_DQS + (warp - 12) * 8192;
+    uint8_t* slot1 = slot0 + 4096;
+    bool ok = true;
+    for (int n = 0; n < niter; ++n) {
+      const int i = qblk(n);
       if (!mbar_wait(dq_full, n & 1, p.st, 58, abort_flag)) { ok = false; break; }
       tc_fence_after();
       uint32_t a0[32], a1[32];
@@ -698,47 +717,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_commit();
       }
     }
-    if (dq_role) {
-      if (lane == 0) tma_store_wait0();
-      __syncwarp();
-      // dK, dV (TMEM lane = key row)
-      if (ok && mbar_wait(dkv_full, 0, p.st, 59, abort_flag)) {
-        tc_fence_after();
-        const int r = q4 * 32 + lane;
-        const int key = k0 + r;
-        uint32_t kv[32];
-  #pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          bf16* dst = which ? (p.dv + (long)(kv_base + key) * p.dv_rs + col)
-                            : (p.dk + (long)(kv_base + key) * p.dk_rs + col);
-          const float sc = which ? 1.f : p.scale;
-          const bool empty = SPARSE && niter == 0;  // no query sees these keys: zero gradients
-  #pragma unroll
-          for (int c = 0; c < HD; c += 32) {
-            tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
-            tc_wait_ld();
-            if (empty) {
-  #pragma unroll
-              for (int e = 0; e < 32; ++e) kv[e] = 0u;
-            }
-            if (key < Sk) {
-  #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
-                uint4 o;
-                o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
-                o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
-                o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
-                o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
-                *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
-              }
+    if (lane == 0) tma_store_wait0();
+    __syncwarp();
+    // dK, dV (TMEM lane = key row)
+    if (ok && mbar_wait(dkv_full, 0, p.st, 59, abort_flag)) {
+      tc_fence_after();
+      const int r = q4 * 32 + lane;
+      const int key = k0 + r;
+      uint32_t kv[32];
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        bf16* dst = which ? (p.dv + (long)(kv_base + key) * p.dv_rs + col)
+                          : (p.dk + (long)(kv_base + key) * p.dk_rs + col);
+        const float sc = which ? 1.f : p.scale;
+        const bool empty = SPARSE && niter == 0;  // no query sees these keys: zero gradients
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
+          tc_wait_ld();
+          if (empty) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) kv[e] = 0u;
+          }
+          if (key < Sk) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
+              uint4 o;
+              o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
+              o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
+              o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
+              o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
+              *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
             }
           }
         }
       }
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

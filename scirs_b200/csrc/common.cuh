@@ -367,6 +367,16 @@ __device__ __forceinline__ float ex2_fast(float x) {
   return y;
 }
 
+// 2^x of two values in one MUFU instruction: the arguments are rounded to
+// bf16 (round to nearest) and the results come back as packed bf16x2
+// {lo: 2^lo, hi: 2^hi}; -inf gives 0.
+__device__ __forceinline__ uint32_t ex2_bf16x2(float lo, float hi) {
+  uint32_t in, out;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(hi), "f"(lo));
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(out) : "r"(in));
+  return out;
+}
+
 // GELU, tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
 // The two constants are the definition of the approximation (Hendrycks &
 // Gimpel 2016), not taken from any library.

@@ -274,9 +274,10 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None, plan=None):
         if plan is not None:
             _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(plan.pattern.causal), float(scale), False, None,
                                              False, **plan.kernel_args())
-        elif ATTN_FWD_IMPL in ("pingpong", "pingpong_poly", "pingpong_x2"):
+        elif ATTN_FWD_IMPL in ("pingpong", "pingpong_poly", "pingpong_x2", "pingpong_bf2"):
             _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(causal), float(scale),
-                                             ATTN_FWD_IMPL == "pingpong_poly", None, ATTN_FWD_IMPL == "pingpong_x2")
+                                             ATTN_FWD_IMPL == "pingpong_poly", None, ATTN_FWD_IMPL == "pingpong_x2",
+                                             bf2=ATTN_FWD_IMPL == "pingpong_bf2")
         elif ATTN_FWD_IMPL == "tcgen05":
             _ext.kernels().flash_attn_fwd_tc(q, k, v, out, lse, bool(causal), float(scale))
         else:

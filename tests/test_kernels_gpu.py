@@ -224,7 +224,7 @@ def test_flash_attention(B, S, H, HD, causal, bwd_impl, monkeypatch):
     _ext.check_status()
 
 
-@pytest.mark.parametrize("impl", ["pingpong", "pingpong_poly", "pingpong_x2", "tcgen05", "mma"])
+@pytest.mark.parametrize("impl", ["pingpong", "pingpong_poly", "pingpong_x2", "pingpong_bf2", "tcgen05", "mma"])
 @pytest.mark.parametrize("B,S,H,HD,causal", [(2, 256, 4, 64, True), (1, 197, 3, 64, False), (1, 384, 2, 128, True),
                                              (2, 1024, 2, 64, True), (1, 300, 2, 128, False)])
 def test_flash_attention_fwd_impls(impl, B, S, H, HD, causal, monkeypatch):
@@ -243,7 +243,7 @@ def test_flash_attention_fwd_impls(impl, B, S, H, HD, causal, monkeypatch):
     assert torch.allclose(lse, lse_ref, atol=1e-2)
 
 
-@pytest.mark.parametrize("impl", ["pingpong", "pingpong_poly", "pingpong_x2"])
+@pytest.mark.parametrize("impl", ["pingpong", "pingpong_poly", "pingpong_x2", "pingpong_bf2"])
 @pytest.mark.parametrize("HD,causal", [(64, True), (128, True), (64, False), (128, False)])
 def test_flash_attention_fwd_pingpong_rescale(HD, causal, impl, monkeypatch):
     """Large scores: the running reference max is raised (and O rescaled in
