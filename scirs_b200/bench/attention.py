@@ -4,6 +4,7 @@ head_dim 64/128, seq 512..16384, 8-32 heads, causal, against PyTorch SDPA
 (the sparse kernels with a 256-token window against the dense kernel).
 
     python -m scirs_b200.bench.attention [--quick] [--heads 8,16,32] [--out sweep.jsonl]
+    python -m scirs_b200.bench.attention --window-only --seq 4096 --hd 64   (one window row)
 
 Device time from CUDA events after warm-up; inputs larger than L2 at the
 long sequences. TFLOP/s counts the causal half (fwd 2 GEMMs, bwd 5 GEMMs
@@ -40,6 +41,9 @@ def main():
     ap.add_argument("--heads", default="8,16,32")
     ap.add_argument("--tokens", type=int, default=1 << 16, help="batch * seq per call")
     ap.add_argument("--out", default=None, help="also append the JSON lines to this file")
+    ap.add_argument("--window-only", action="store_true", help="only the sliding-window row(s)")
+    ap.add_argument("--seq", type=int, default=0, help="sequence length of the window row (default: longest)")
+    ap.add_argument("--hd", default="64,128", help="head dims of the window row")
     args = ap.parse_args()
     outf = open(args.out, "a") if args.out else None
 
@@ -59,7 +63,8 @@ def main():
     dev = torch.device("cuda", 0)
     seqs = [1024, 4096] if args.quick else [512, 1024, 2048, 4096, 8192, 16384]
     heads = [int(h) for h in args.heads.split(",")]
-    for hd, S, H in ((hd, S, H) for hd in (64, 128) for S in seqs for H in heads):
+    sweep = [] if args.window_only else [(hd, S, H) for hd in (64, 128) for S in seqs for H in heads]
+    for hd, S, H in sweep:
         B = max(1, args.tokens // S)
         qkv = torch.randn(B, S, 3, H, hd, device=dev, dtype=torch.bfloat16)
         q, k, v = qkv.unbind(2)
@@ -92,8 +97,8 @@ def main():
     # sliding window (no dense mask): 256-token window at the longest sequence
     from ..ops.sparse_attention import sliding_window
 
-    S = seqs[-1]
-    for hd in (64, 128):
+    S = args.seq or seqs[-1]
+    for hd in (int(h) for h in args.hd.split(",")):
         H, B = 8, max(1, args.tokens // S)
         q, k, v = (torch.randn(B, S, H, hd, device=dev, dtype=torch.bfloat16) for _ in range(3))
         o = torch.empty_like(q)

@@ -9,6 +9,8 @@ Shapes (M tokens per GPU, weights stored [out, in]):
   gpt2  GPT-2 small, 64 x 1024 tokens: QKV 768->2304, proj 768->768,
         FC1 768->3072 (+bias+GELU), FC2 3072->768 (+bias+residual),
         LM head 768->50304
+  gpt2dp8  the same products at 8 x 1024 tokens (one of 8 data-parallel
+        ranks at global batch 64)
   vit   ViT-B/16, 32 images x 197 tokens per GPU (global batch 256 over 8):
         the same block shapes at M = 6304
   tp8   1.3B decoder, one tensor-parallel rank of 8, 32 x 2048 tokens:
@@ -54,6 +56,10 @@ def _time(fn, iters, warmup=5):
 def shapes(model: str):
     if model == "gpt2":
         M = 64 * 1024
+        return [("qkv", M, 2304, 768, "bias"), ("proj", M, 768, 768, "resid"), ("fc1", M, 3072, 768, "gelu"),
+                ("fc2", M, 768, 3072, "resid"), ("lm_head", M, 50304, 768, "none")]
+    if model == "gpt2dp8":
+        M = 8 * 1024
         return [("qkv", M, 2304, 768, "bias"), ("proj", M, 768, 768, "resid"), ("fc1", M, 3072, 768, "gelu"),
                 ("fc2", M, 768, 3072, "resid"), ("lm_head", M, 50304, 768, "none")]
     if model == "vit":
@@ -141,7 +147,7 @@ def bench_product(model, name, M, N, Kd, epi, iters, peak, dev):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--models", default="gpt2,vit,tp8")
+    ap.add_argument("--models", default="gpt2,gpt2dp8,vit,tp8")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--out", default=None)
     args = ap.parse_args()

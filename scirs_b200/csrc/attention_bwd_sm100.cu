@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_wait_ld();
       const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
                              (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
+      const AttnSpan span = attn_queries_of_key<SPARSE>(p.sp, key, q0, S, Sk, CAUSAL);
       uint32_t pp[16], dd[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
@@ -255,10 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int ql = c0 + e + u;
-          const int q = q0 + ql;
           float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
-          if (need_mask && (q >= S || key >= Sk || (CAUSAL && key > q) || (SPARSE && !attn_allowed(p.sp, q, key))))
-            pv = 0.f;
+          if (need_mask && !attn_span_has(span, ql)) pv = 0.f;
           pr[u] = pv;
           ds[u] = pv * (__uint_as_float(dv[e + u]) - sL[BQ + ql]);
         }

@@ -294,11 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool mask = (kv0 + BN > Sk) || (CAUSAL && kv0 + BN > q0 + t * BM) ||
                         (SPARSE && !attn_block_full(p.sp, q0 + t * BM, q0 + t * BM + BM - 1, kv0, kv0 + BN - 1));
       if (mask) {
+        const AttnSpan span = attn_keys_of_query<SPARSE>(p.sp, qrow, kv0, Sk, CAUSAL);
 #pragma unroll
-        for (int e = 0; e < BN; ++e) {
-          const int key = kv0 + e;
-          if (key >= Sk || (CAUSAL && key > qrow) || (SPARSE && !attn_allowed(p.sp, qrow, key))) sv[e] = -INFINITY;
-        }
+        for (int e = 0; e < BN; ++e) sv[e] = attn_span_has(span, e) ? sv[e] : -INFINITY;
       }
       // row max: four independent chains of 3-input max instructions
       float m4[4] = {sv[0], sv[1], sv[2], sv[3]};

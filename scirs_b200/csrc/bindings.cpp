@@ -4,7 +4,9 @@
 namespace scirs {
 void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
              c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
-             bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad);
+             bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad,
+             c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin, int64_t rope_S,
+             int64_t rope_hd, int64_t rope_cols);
 void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Tensor y, torch::Tensor mean,
                    torch::Tensor rstd, double eps);
 void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
@@ -40,7 +42,8 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
              bool accumulate, int64_t splits, int64_t rank, int64_t world, std::vector<int64_t> a_peers,
              std::vector<int64_t> b_peers, std::vector<int64_t> rs_dst, c10::optional<torch::Tensor> flags,
              c10::optional<torch::Tensor> epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
-             double timeout_s);
+             double timeout_s, c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+             int64_t rope_S, int64_t rope_hd, int64_t rope_cols);
 void tp_signal(std::vector<int64_t> sig_flags, torch::Tensor epoch, int64_t idx);
 void ep_dispatch(torch::Tensor src, torch::Tensor idx, c10::optional<torch::Tensor> scale, std::vector<int64_t> dst,
                  int64_t L, int64_t C, int64_t sl, int64_t sr, int64_t rank, std::vector<int64_t> sig_flags,
@@ -107,7 +110,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &scirs::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("a"), py::arg("b"), py::arg("out"),
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("bias") = py::none(), py::arg("aux") = py::none(),
         py::arg("out2") = py::none(), py::arg("accumulate") = false, py::arg("splits") = 0,
-        py::arg("bn_force") = 0, py::arg("bias_grad") = py::none());
+        py::arg("bn_force") = 0, py::arg("bias_grad") = py::none(), py::arg("rope_cos") = py::none(),
+        py::arg("rope_sin") = py::none(), py::arg("rope_S") = 0, py::arg("rope_hd") = 0, py::arg("rope_cols") = 0);
   m.def("layernorm_fwd", &scirs::layernorm_fwd);
   m.def("layernorm_bwd", &scirs::layernorm_bwd);
   m.def("xent_fwd_bwd", &scirs::xent_fwd_bwd);
@@ -126,7 +130,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_peers") = std::vector<int64_t>{}, py::arg("b_peers") = std::vector<int64_t>{},
         py::arg("rs_dst") = std::vector<int64_t>{}, py::arg("flags") = py::none(), py::arg("epoch") = py::none(),
         py::arg("wait_idx") = 0, py::arg("sig_flags") = std::vector<int64_t>{}, py::arg("sig_idx") = 0,
-        py::arg("timeout_s") = 10.0);
+        py::arg("timeout_s") = 10.0, py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none(),
+        py::arg("rope_S") = 0, py::arg("rope_hd") = 0, py::arg("rope_cols") = 0);
   m.def("tp_signal", &scirs::tp_signal);
   m.def("tp_wait", &scirs::tp_wait);
   m.def("conv_im2col", &scirs::conv_im2col, "NCHW input -> im2col rows for the convolution GEMM");

@@ -483,6 +483,57 @@ __device__ __forceinline__ bool attn_allowed(const AttnSparse& a, int q, int k) 
   return a.bmap != nullptr && a.bmap[(long)(q >> 7) * a.bmap_ld + (k >> 7)] != 0;
 }
 
+// The allowed positions of one row of a score block, as the union of at
+// most two inclusive intervals [a0, b0] and [a1, b1] of block-relative
+// indices. Built once per row and block, so that the element loop masks with
+// two compares and a select per score, without branches or memory loads.
+struct AttnSpan {
+  int a0, b0, a1, b1;
+};
+
+__device__ __forceinline__ bool attn_span_has(const AttnSpan& m, int e) {
+  return (e >= m.a0 && e <= m.b0) || (e >= m.a1 && e <= m.b1);
+}
+
+// Forward: keys k0 + e allowed for query q (k0 a multiple of 128): the key
+// length and causal bound, then the pattern (all keys when the row is a
+// global token or its 128 x 128 bitmap block is set; else the window and the
+// global keys).
+template <bool SPARSE>
+__device__ __forceinline__ AttnSpan attn_keys_of_query(const AttnSparse& a, int q, int k0, int Sk, bool causal) {
+  int hi = Sk - 1 - k0;
+  if (causal) hi = min(hi, q - k0);
+  AttnSpan m{0, hi, 1, 0};
+  if (!SPARSE) return m;
+  const bool none = a.bmap == nullptr && a.wl < 0 && a.ng <= 0;
+  if (none || q < a.ng || (a.bmap != nullptr && a.bmap[(long)(q >> 7) * a.bmap_ld + (k0 >> 7)] != 0)) return m;
+  m.a0 = a.wl >= 0 ? q - a.wl - k0 : 1;
+  m.b0 = a.wl >= 0 ? min(q + a.wr - k0, hi) : 0;
+  m.a1 = 0;
+  m.b1 = min(a.ng - 1 - k0, hi);
+  return m;
+}
+
+// Backward: queries q0 + e that see key k (q0 a multiple of the query block,
+// which divides 128): q < S, q >= k when causal, nothing for k >= Sk; then
+// the pattern (every query for a global key or a set bitmap block; else the
+// window q in [k - wr, k + wl] and the global queries q < ng).
+template <bool SPARSE>
+__device__ __forceinline__ AttnSpan attn_queries_of_key(const AttnSparse& a, int k, int q0, int S, int Sk,
+                                                        bool causal) {
+  const int lo = causal ? k - q0 : 0;
+  const int hi = k < Sk ? S - 1 - q0 : -1;
+  AttnSpan m{lo, hi, 1, 0};
+  if (!SPARSE) return m;
+  const bool none = a.bmap == nullptr && a.wl < 0 && a.ng <= 0;
+  if (none || k < a.ng || (a.bmap != nullptr && a.bmap[(long)(q0 >> 7) * a.bmap_ld + (k >> 7)] != 0)) return m;
+  m.a0 = a.wl >= 0 ? max(k - a.wr - q0, lo) : 1;
+  m.b0 = a.wl >= 0 ? min(k + a.wl - q0, hi) : 0;
+  m.a1 = lo;
+  m.b1 = min(a.ng - 1 - q0, hi);
+  return m;
+}
+
 #endif  // __CUDACC__
 
 }  // namespace scirs

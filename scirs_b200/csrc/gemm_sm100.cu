@@ -50,6 +50,7 @@ enum Epi : int {
   EPI_RESID = 2,      // C = acc (+ bias) + aux
   EPI_DGELU = 3,      // C = acc * gelu'(aux)
   EPI_F32 = 4,        // C(fp32) = acc, or += acc (atomic) when accumulating / split-K
+  EPI_ROPE = 5,       // C = rope(acc + bias) on the first rope_cols columns, acc + bias after
 };
 
 struct Args {
@@ -70,6 +71,14 @@ struct Args {
   float* bias_grad;  // EPI_DGELU: += column sums of the output (fp32 [N])
   int atomic_out;
   int gelu_x2;  // EPI_BIAS_GELU / EPI_DGELU: GELU and its derivative in packed f32x2 instructions
+  // EPI_ROPE: rotary embedding of the q and k parts of a fused [rows, 3, H, hd]
+  // output (columns [0, rope_cols) = q and k heads), half-rotation form
+  //   x[d]        -> x[d] cos(pos w_d) - x[d + hd/2] sin(pos w_d)
+  //   x[d + hd/2] -> x[d + hd/2] cos(pos w_d) + x[d] sin(pos w_d),  d < hd/2,
+  // pos = row % rope_S; tables fp32 [rope_S, hd/2]
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_S, rope_hd, rope_cols;
   DevStatus* st;
   int m_rot;   // rotation of the m-block order (tensor parallel: start with local rows)
   int kb_rot;  // rotation of the k-block order (tensor parallel: start with local K rows)
@@ -494,7 +503,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
       // TMEM reads are software-pipelined: chunk ci+1 is loaded while chunk
       // ci is processed (two register buffers; the dGELU epilogue, which
       // needs its registers for the column-sum butterfly, loads one at a time)
-      constexpr bool PREFETCH = (EPI != EPI_DGELU);
+      constexpr bool PREFETCH = (EPI != EPI_DGELU && EPI != EPI_ROPE);
       uint32_t rb0[32], rb1[32];
       if (PREFETCH && nch > 0) tmem_ld_32x32b_x32(trow + c_begin, rb0);
 #pragma unroll
@@ -503,12 +512,21 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
         const int c = c_begin + ci * 32;
         const int col0 = n_blk * BN + c;
         uint32_t* r = (ci & 1) ? rb1 : rb0;
+        // RoPE: the partner half of this chunk's head (same TMEM lane = same
+        // row, columns hd/2 away; heads never straddle a tile since BN % hd == 0)
+        uint32_t* pr = (ci & 1) ? rb0 : rb1;
+        const bool rot = (EPI == EPI_ROPE) && col0 < args.rope_cols;
+        const int rhalf = (EPI == EPI_ROPE) ? (args.rope_hd >> 1) : 0;
+        const int rd0 = rot ? col0 % args.rope_hd : 0;
+        const int rpoff = rd0 < rhalf ? rhalf : -rhalf;  // partner column offset
         if (PREFETCH) {
           tc_wait_ld_regs(r);
           if (ci + 1 < nch) tmem_ld_32x32b_x32(trow + c + 32, (ci & 1) ? rb0 : rb1);
         } else {
           tmem_ld_32x32b_x32(trow + c, r);
+          if (EPI == EPI_ROPE && rot) tmem_ld_32x32b_x32(trow + c + rpoff, pr);
           tc_wait_ld_regs(r);
+          if (EPI == EPI_ROPE && rot) tc_wait_ld_regs(pr);
         }
         if (ci == nch - 1) {
           // last TMEM read of this tile by this warp: release the accumulator
@@ -532,6 +550,37 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* pA, const CUtensorM
               v[g * 8 + 2 * e] += bf16_lo(bw[e]);
               v[g * 8 + 2 * e + 1] += bf16_hi(bw[e]);
             }
+          }
+        }
+        if (EPI == EPI_ROPE && rot) {
+          float pv[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) pv[j] = __uint_as_float(pr[j]);
+          if (args.bias != nullptr) {
+            const uint4* bp = reinterpret_cast<const uint4*>(args.bias + col0 + rpoff);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 b4 = __ldg(bp + g);
+              uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                pv[g * 8 + 2 * e] += bf16_lo(bw[e]);
+                pv[g * 8 + 2 * e + 1] += bf16_hi(bw[e]);
+              }
+            }
+          }
+          // first half: x cos - partner sin; second half: x cos + partner sin
+          const float sgn = rd0 < rhalf ? -1.f : 1.f;
+          const long toff = (long)(row % args.rope_S) * rhalf + (rd0 < rhalf ? rd0 : rd0 - rhalf);
+          const float4* cp = reinterpret_cast<const float4*>(args.rope_cos + toff);
+          const float4* sp4 = reinterpret_cast<const float4*>(args.rope_sin + toff);
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const float4 c4 = __ldg(cp + g), s4 = __ldg(sp4 + g);
+            v[4 * g + 0] = fmaf(v[4 * g + 0], c4.x, sgn * pv[4 * g + 0] * s4.x);
+            v[4 * g + 1] = fmaf(v[4 * g + 1], c4.y, sgn * pv[4 * g + 1] * s4.y);
+            v[4 * g + 2] = fmaf(v[4 * g + 2], c4.z, sgn * pv[4 * g + 2] * s4.z);
+            v[4 * g + 3] = fmaf(v[4 * g + 3], c4.w, sgn * pv[4 * g + 3] * s4.w);
           }
         }
         if (HAS_AUX) {
@@ -794,6 +843,10 @@ static void launch_epi(int epi, const Maps& m, const Args& args, int grid, cudaS
     case EPI_RESID: launch_t<BN, A_MN, B_MN, EPI_RESID>(m, args, grid, s); break;
     case EPI_DGELU: launch_t<BN, A_MN, B_MN, EPI_DGELU>(m, args, grid, s); break;
     case EPI_F32: launch_t<BN, A_MN, B_MN, EPI_F32>(m, args, grid, s); break;
+    case EPI_ROPE:
+      if (!A_MN && !B_MN) launch_t<BN, 0, 0, EPI_ROPE>(m, args, grid, s);
+      else TORCH_CHECK(false, "the RoPE epilogue takes K-major operands");
+      break;
     default: TORCH_CHECK(false, "bad epilogue ", epi);
   }
 }
@@ -851,6 +904,10 @@ static void launch_pair_epi(int epi, const Maps& m, const Args& args, int grid, 
     case EPI_RESID: launch_pair_t<A_MN, B_MN, EPI_RESID>(m, args, grid, s); break;
     case EPI_DGELU: launch_pair_t<A_MN, B_MN, EPI_DGELU>(m, args, grid, s); break;
     case EPI_F32: launch_pair_t<A_MN, B_MN, EPI_F32>(m, args, grid, s); break;
+    case EPI_ROPE:
+      if (!A_MN && !B_MN) launch_pair_t<0, 0, EPI_ROPE>(m, args, grid, s);
+      else TORCH_CHECK(false, "the RoPE epilogue takes K-major operands");
+      break;
     default: TORCH_CHECK(false, "bad epilogue ", epi);
   }
 }
@@ -902,10 +959,34 @@ static void launch_tp(int a_mn, int b_mn, int epi, const Maps& m, const PeerMaps
                       cudaStream_t s) {
   if (!a_mn && !b_mn && epi == EPI_BF16) launch_tp_t<0, 0, EPI_BF16>(m, pm, args, grid, s);
   else if (!a_mn && !b_mn && epi == EPI_BIAS_GELU) launch_tp_t<0, 0, EPI_BIAS_GELU>(m, pm, args, grid, s);
+  else if (!a_mn && !b_mn && epi == EPI_ROPE) launch_tp_t<0, 0, EPI_ROPE>(m, pm, args, grid, s);
   else if (!a_mn && b_mn && epi == EPI_BF16) launch_tp_t<0, 1, EPI_BF16>(m, pm, args, grid, s);
   else if (!a_mn && b_mn && epi == EPI_DGELU) launch_tp_t<0, 1, EPI_DGELU>(m, pm, args, grid, s);
   else if (a_mn && b_mn && epi == EPI_F32) launch_tp_t<1, 1, EPI_F32>(m, pm, args, grid, s);
   else TORCH_CHECK(false, "tensor-parallel GEMM form not supported: a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+// EPI_ROPE arguments: fp32 [S, hd/2] cos / sin tables, hd a multiple of 64
+// (so that a 32-column chunk and its partner lie in one half each), the
+// rotated columns a whole number of heads, N a whole number of heads.
+static void set_rope(Args& args, int64_t epi, const c10::optional<torch::Tensor>& cos_t,
+                     const c10::optional<torch::Tensor>& sin_t, int64_t S, int64_t hd, int64_t cols, int64_t N) {
+  if (epi != EPI_ROPE) return;
+  TORCH_CHECK(cos_t.has_value() && cos_t->defined() && sin_t.has_value() && sin_t->defined(),
+              "the RoPE epilogue needs cos / sin tables");
+  CHECK_DTYPE((*cos_t), at::kFloat);
+  CHECK_DTYPE((*sin_t), at::kFloat);
+  TORCH_CHECK(cos_t->is_contiguous() && sin_t->is_contiguous(), "rope tables must be contiguous");
+  TORCH_CHECK(hd > 0 && hd % 64 == 0, "RoPE epilogue: head_dim must be a multiple of 64");
+  TORCH_CHECK(S > 0 && cos_t->numel() >= S * hd / 2 && sin_t->numel() >= S * hd / 2, "rope tables too small");
+  TORCH_CHECK(cols >= 0 && cols % hd == 0 && cols <= N && N % hd == 0, "RoPE columns must be whole heads");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(cos_t->data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sin_t->data_ptr()) & 15) == 0, "rope tables must be 16-byte aligned");
+  args.rope_cos = cos_t->data_ptr<float>();
+  args.rope_sin = sin_t->data_ptr<float>();
+  args.rope_S = (int)S;
+  args.rope_hd = (int)hd;
+  args.rope_cols = (int)cols;
 }
 
 static unsigned* done_counter(int dev) {
@@ -936,7 +1017,8 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
              bool accumulate, int64_t splits, int64_t rank, int64_t world, std::vector<int64_t> a_peers,
              std::vector<int64_t> b_peers, std::vector<int64_t> rs_dst, c10::optional<torch::Tensor> flags,
              c10::optional<torch::Tensor> epoch, int64_t wait_idx, std::vector<int64_t> sig_flags, int64_t sig_idx,
-             double timeout_s) {
+             double timeout_s, c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+             int64_t rope_S, int64_t rope_hd, int64_t rope_cols) {
   using namespace gemm;
   CHECK_DTYPE(a, at::kBFloat16);
   CHECK_DTYPE(b, at::kBFloat16);
@@ -1067,6 +1149,7 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     }
     args.kb_rot = (int)(rank * (b.size(0) / BK));
   }
+  set_rope(args, epi, rope_cos, rope_sin, rope_S, rope_hd, rope_cols, N);
   args.n_blocks = (int)((N + 255) / 256);
   const long tiles = (long)args.m_blocks * args.n_blocks;
   int sp = 1;
@@ -1097,7 +1180,9 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
 //   splits   : split-K factor (0 = automatic; epi 4 only)
 void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
              c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
-             bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad) {
+             bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad,
+             c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin, int64_t rope_S,
+             int64_t rope_hd, int64_t rope_cols) {
   using namespace gemm;
   CHECK_CUDA_TENSOR(a);
   CHECK_CUDA_TENSOR(b);
@@ -1184,6 +1269,8 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     if (N <= 128 || (!can_split && cost(128) < cost(256))) BN = 128;
   }
   if (bn_force == 128 || bn_force == 256) BN = (int)bn_force;
+  set_rope(args, epi, rope_cos, rope_sin, rope_S, rope_hd, rope_cols, N);
+  TORCH_CHECK(epi != EPI_ROPE || (!a_mn && !b_mn && BN % rope_hd == 0), "RoPE epilogue: K-major operands, BN % hd == 0");
   // Pair mode (two SMs per 256 x 256 tile) when the tiles are wide and there
   // are enough of them to fill the GPU with pairs.
   // (fp32 weight gradients count their split-K work units: a long K splits

@@ -39,6 +39,7 @@ scirs2-neural/src/models/architectures/gpt.rs:19-62.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -142,6 +143,8 @@ class TPDecoder(FusedTrainerMixin):
         self.fp = fp
         self._init_weights(seed)
         self.cos, self.sin = rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
+        # the GEMM epilogue rotates whole 32-column halves: head_dim 64 or 128
+        self.rope_fused = cfg.head_dim in (64, 128) and os.environ.get("SCIRS_ROPE_FUSED", "1") == "1"
         self._alloc()
         self.grad_sync = None
         self.optimizer = None
@@ -269,9 +272,15 @@ class TPDecoder(FusedTrainerMixin):
             K.layernorm_fwd(self.x[l], fp.w(p + "ln_1.weight"), fp.w(p + "ln_1.bias"), self.ln1[l], self.mu[0][l],
                             self.rs[0][l], eps)
             s = ctx.gather(self.gln1[l])
-            ctx.ag_gemm(self.gln1[l], s, fp.w(p + "attn.c_attn.weight"), self.qkv[l],
-                        bias=fp.w(p + "attn.c_attn.bias"))
-            kx.rope_apply(self.qkv[l], self.cos, self.sin, S, Hl, hd, False)
+            if self.rope_fused:
+                # rotary embedding of q and k in the QKV GEMM's epilogue
+                ctx.ag_gemm(self.gln1[l], s, fp.w(p + "attn.c_attn.weight"), self.qkv[l],
+                            bias=fp.w(p + "attn.c_attn.bias"), epi=K.EPI_ROPE,
+                            rope=(self.cos, self.sin, S, hd, 2 * Hl * hd))
+            else:
+                ctx.ag_gemm(self.gln1[l], s, fp.w(p + "attn.c_attn.weight"), self.qkv[l],
+                            bias=fp.w(p + "attn.c_attn.bias"))
+                kx.rope_apply(self.qkv[l], self.cos, self.sin, S, Hl, hd, False)
             q, k, v = self.qkv[l].view(B, S, 3, Hl, hd).unbind(2)
             K.flash_attn_fwd(q, k, v, self.att[l].view(B, S, Hl, hd), self.lse[l], causal=True)
             recv, s = ctx.gemm_rs(self.att[l], fp.w(p + "attn.c_proj.weight"), Mr, partial=self.partial)

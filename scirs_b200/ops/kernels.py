@@ -19,6 +19,7 @@ EPI_BIAS_GELU = 1
 EPI_RESID = 2
 EPI_DGELU = 3
 EPI_F32 = 4
+EPI_ROPE = 5
 
 OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
 
@@ -78,6 +79,7 @@ def gemm(
     splits: int = 0,
     bn: int = 0,
     bias_grad: torch.Tensor | None = None,
+    rope: tuple | None = None,
 ) -> torch.Tensor:
     """out[M,N] = op(a) @ op(b) with a fused epilogue.
 
@@ -86,12 +88,16 @@ def gemm(
 
     Epilogues: EPI_BF16 (+bias), EPI_BIAS_GELU (out2 = pre-activation,
     out = gelu(out2)), EPI_RESID (+bias +aux), EPI_DGELU (out = acc *
-    gelu'(aux)), EPI_F32 (fp32 out, optionally accumulated). With
-    EPI_DGELU, `bias_grad` (fp32 [N]) accumulates the column sums of out.
+    gelu'(aux)), EPI_F32 (fp32 out, optionally accumulated), EPI_ROPE
+    (+bias, then the rotary embedding of the first `cols` columns, a fused
+    [rows, 3, H, hd] q/k/v output; rope = (cos, sin, S, hd, cols) with fp32
+    [S, hd/2] tables, position = row % S). With EPI_DGELU, `bias_grad` (fp32
+    [N]) accumulates the column sums of out.
     """
     if a.is_cuda:
+        rc, rsn, rS, rhd, rcols = rope if rope is not None else (None, None, 0, 0, 0)
         _ext.kernels().gemm(a, b, out, int(a_mn), int(b_mn), int(epi), bias, aux, out2, accumulate, splits, bn,
-                            bias_grad)
+                            bias_grad, rc, rsn, int(rS), int(rhd), int(rcols))
         _count(1)
         return out
     A = (a.t() if a_mn else a).float()
@@ -114,8 +120,29 @@ def gemm(
     elif epi == EPI_BIAS_GELU:
         out2.copy_(acc)
         acc = gelu_tanh(acc)
+    elif epi == EPI_ROPE:
+        acc = rope_rotate(acc, *rope)
     out.copy_(acc)
     return out
+
+
+def rope_rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, S: int, hd: int, cols: int,
+                inverse: bool = False) -> torch.Tensor:
+    """Half-rotation RoPE of columns [0, cols) of x [rows, N] (heads of hd
+    columns; position = row % S): (x1, x2) -> (x1 c - x2 s, x2 c + x1 s)."""
+    rows = x.shape[0]
+    y = x.float().clone()
+    half = hd // 2
+    pos = torch.arange(rows, device=x.device) % S
+    c = cos.reshape(-1, half)[pos].float()[:, None, :]
+    sn = sin.reshape(-1, half)[pos].float()[:, None, :]
+    if inverse:
+        sn = -sn
+    part = y[:, :cols].view(rows, cols // hd, hd)
+    x1, x2 = part[..., :half].clone(), part[..., half:].clone()
+    part[..., :half] = x1 * c - x2 * sn
+    part[..., half:] = x2 * c + x1 * sn
+    return y
 
 
 # ---------------------------------------------------------------------------

@@ -146,18 +146,22 @@ class TPContext:
         return i
 
     # ------------------------------------------------------------- GEMMs
-    def ag_gemm(self, full, ready: int, b, out, *, b_mn=False, epi=K.EPI_BF16, bias=None, aux=None, out2=None):
+    def ag_gemm(self, full, ready: int, b, out, *, b_mn=False, epi=K.EPI_BF16, bias=None, aux=None, out2=None,
+                rope=None):
         """out[M, N] = full[M, K] @ op(b), where `full` is a gathered buffer
-        whose peer segments arrive after signal `ready` (see :meth:`gather`)."""
+        whose peer segments arrive after signal `ready` (see :meth:`gather`).
+        epi=EPI_ROPE with rope=(cos, sin, S, hd, cols) applies the rotary
+        embedding in the epilogue."""
         if self.mode == "fused" and self.world > 1:
             seg = self.segment(full)
             step = seg.numel() * seg.element_size()
             addrs = [full.data_ptr() + r * step for r in range(self.world)]
+            rc, rsn, rS, rhd, rcols = rope if rope is not None else (None, None, 0, 0, 0)
             _ext.kernels().gemm_tp(seg, b, out, 0, int(b_mn), int(epi), bias, aux, out2, False, 0, self.rank,
                                    self.world, addrs, [], [], self.flags_ce, self.epoch, ready, [], 0,
-                                   self.timeout_s)
+                                   self.timeout_s, rc, rsn, int(rS), int(rhd), int(rcols))
         else:
-            K.gemm(full, b, out, b_mn=b_mn, epi=epi, bias=bias, aux=aux, out2=out2)
+            K.gemm(full, b, out, b_mn=b_mn, epi=epi, bias=bias, aux=aux, out2=out2, rope=rope)
         self.launches += 1
         return out
 

@@ -301,3 +301,37 @@ def test_fused_optimizer_clip_and_skip():
     before = p.clone()
     K.optim_step("adamw", p, s1, s2, g, None, n, hp, part=part, norm_out=norm)
     assert torch.equal(p, before)
+
+
+# ------------------------------------------------------------ RoPE in the GEMM epilogue
+def _rope_tables(S, hd, theta=10000.0):
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+    ang = torch.arange(S, dtype=torch.float64)[:, None] * inv[None, :]
+    return ang.cos().float().to(DEV).contiguous(), ang.sin().float().to(DEV).contiguous()
+
+
+@pytest.mark.parametrize("M,H,hd,bn", [(1000, 4, 64, 0), (512, 2, 128, 128), (512, 4, 128, 256), (4096, 16, 128, 0),
+                                       (8192, 12, 64, 0)])
+def test_gemm_rope_epilogue(M, H, hd, bn):
+    """EPI_ROPE (bias, then half-rotation RoPE of the q and k heads of a
+    fused [rows, 3, H, hd] output) against an fp32 reference; the last two
+    shapes run on 2-SM pair tiles."""
+    Kd, S = 256, 256
+    N = 3 * H * hd
+    a, w, bias = rnd(M, Kd, seed=41), rnd(N, Kd, scale=0.1, seed=42), rnd(N, seed=43)
+    cos, sin = _rope_tables(S, hd)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, w, out, epi=K.EPI_ROPE, bias=bias, bn=bn, rope=(cos, sin, S, hd, 2 * H * hd))
+    acc = a.float() @ w.float().t() + bias.float()
+    want = K.rope_rotate(acc, cos, sin, S, hd, 2 * H * hd)
+    torch.cuda.synchronize()
+    assert rel_err(out, want) < 1e-2
+    # v columns untouched by the rotation
+    assert rel_err(out[:, 2 * H * hd:], acc[:, 2 * H * hd:]) < 1e-2
+    # same result as the separate RoPE kernel on the plain GEMM output
+    ref2 = torch.empty_like(out)
+    K.gemm(a, w, ref2, bias=bias, bn=bn)
+    from scirs_b200 import _ext
+
+    _ext.kernels().rope_apply(ref2, cos, sin, S, H, hd, False)
+    assert rel_err(out, ref2) < 1e-2
