@@ -280,6 +280,11 @@ __global__ void fa_bwd_delta_kernel(const Params p) {
     const uint32_t oa[4] = {ov.x, ov.y, ov.z, ov.w}, da[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc += bf16_lo(oa[e]) * bf16_lo(da[e]) + bf16_hi(oa[e]) * bf16_hi(da[e]);
+    // zero this (token, head)'s slice of the fp32 dQ accumulator [B*S, H*HD]
+    // that the backward kernels reduce-add into
+    float4* z = reinterpret_cast<float4*>(p.dq_acc + tok * ((long)p.H * HD) + h * HD + sub * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll
   for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -622,8 +627,8 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
   p.S = (int)S;
   p.scale = (float)scale;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
-  SCIRS_CHECK_CUDA(cudaMemsetAsync(p.dq_acc, 0, sizeof(float) * B * S * H * HD, st));
   {
+    // delta = rowsum(O * dO), and the dQ accumulator zeroed in the same pass
     const long rows = B * S * H;  // one 8-lane group per (token, head), 16-byte loads
     if (HD == 64) attn::fa_bwd_delta_kernel<64><<<(unsigned)((rows * 8 + 255) / 256), 256, 0, st>>>(p);
     else attn::fa_bwd_delta_kernel<128><<<(unsigned)((rows * 16 + 255) / 256), 256, 0, st>>>(p);

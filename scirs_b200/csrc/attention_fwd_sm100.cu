@@ -98,6 +98,25 @@ __device__ __forceinline__ float exp2_poly3(float x) {
   return x < -125.f ? 0.f : r;
 }
 
+// exp2_poly3 for a pair, the floating-point steps as packed f32x2
+// instructions (one FADD2 / FFMA2 per step for both values): the same
+// rounding split and Remez cubic as exp2_poly3, 2^n added to the exponent
+// field per value.
+__device__ __forceinline__ void exp2_poly3_x2(float x0, float x1, float& r0, float& r1) {
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t j = f2_add(xc, f2_pack(12582912.f, 12582912.f));
+  const uint64_t jr = f2_add(j, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(jr, f2_pack(-1.f, -1.f), xc);
+  uint64_t q = f2_fma(f2_pack(5.517166906e-02f, 5.517166906e-02f), f, f2_pack(2.426111222e-01f, 2.426111222e-01f));
+  q = f2_fma(q, f, f2_pack(6.932609855e-01f, 6.932609855e-01f));
+  q = f2_fma(q, f, f2_pack(9.999280735e-01f, 9.999280735e-01f));
+  float q0, q1, j0, j1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(j, j0, j1);
+  r0 = x0 < -125.f ? 0.f : __int_as_float(__float_as_int(q0) + (__float_as_int(j0) << 23));
+  r1 = x1 < -125.f ? 0.f : __int_as_float(__float_as_int(q1) + (__float_as_int(j1) << 23));
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -357,8 +376,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (X2) {
             float x0, x1;
             f2_unpack(f2_fma(f2_pack(sv[c + e], sv[c + e + 1]), sc2, nref2), x0, x1);
-            p0 = ex2_fast(x0);
-            p1 = ex2_fast(x1);
+            if (POLY && ((e >> 1) & 1)) {
+              // every second pair on the FMA pipe: the MUFU unit is the
+              // busiest pipe of this loop
+              exp2_poly3_x2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2_fast(x0);
+              p1 = ex2_fast(x1);
+            }
             rs2[(e >> 1) & 1] = f2_add(rs2[(e >> 1) & 1], f2_pack(p0, p1));
           } else {
             p0 = ex2_fast(fmaf(sv[c + e], p.scale_log2, -ref));
@@ -520,8 +545,7 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   }
   const bool traced = p.trace != nullptr;
   TORCH_CHECK(!(traced && poly), "the trace is available for the plain variant");
-  TORCH_CHECK(!(x2 && poly), "poly and x2 variants are exclusive");
-  TORCH_CHECK(!(sparse && (traced || poly || x2 || bf2)), "sparse attention uses the plain variant");
+  TORCH_CHECK(!(sparse && (traced || poly || bf2)), "sparse attention uses the packed-pair variant");
   TORCH_CHECK(!(bf2 && (traced || poly || x2)), "the bf16x2-exponential variant is exclusive");
   if (bf2) {
     if (HD == 64) {
@@ -530,7 +554,7 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
       if (causal) FA2T(128, true, false, false, false, false, true) else FA2T(128, false, false, false, false, false, true)
     }
   } else if (sparse) {
-    FA2T_HD(false, false, false, true)
+    FA2T_HD(false, false, true, true)
   } else if (traced) {
     if (x2) {
       FA2T_HD(false, true, true, false)
@@ -538,7 +562,8 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
       FA2T_HD(false, true, false, false)
     }
   } else if (poly) {
-    FA2T_HD(true, false, false, false)
+    // packed-pair variant with every second pair's exponentials on the FMA pipe
+    FA2T_HD(true, false, true, false)
   } else if (x2) {
     FA2T_HD(false, false, true, false)
   } else {

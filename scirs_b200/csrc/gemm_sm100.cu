@@ -989,6 +989,57 @@ static void set_rope(Args& args, int64_t epi, const c10::optional<torch::Tensor>
   args.rope_cols = (int)cols;
 }
 
+// ---------------------------------------------------------------------------
+// Split-K for bf16 outputs (small M, long K): the product is reduce-added in
+// fp32 into a zeroed workspace (stream-ordered allocation, so it also works
+// under CUDA-graph capture) by the split-K weight-gradient path (2-SM pair
+// tiles), then one pass converts it to bf16 with the bias and the residual.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) splitk_finalize_kernel(const float* __restrict__ ws,
+                                                              __nv_bfloat16* __restrict__ out,
+                                                              long ldo, const __nv_bfloat16* __restrict__ bias,
+                                                              const __nv_bfloat16* __restrict__ aux, long ldaux, int M,
+                                                              int N) {
+  const long nvec = (long)M * (N / 8);
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < nvec; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / (N / 8);
+    const int col = (int)(i % (N / 8)) * 8;
+    const float4* w = reinterpret_cast<const float4*>(ws + row * N + col);
+    const float4 w0 = __ldcs(w), w1 = __ldcs(w + 1);
+    float f[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    if (bias != nullptr) {
+      const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(bias + col));
+      const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        f[2 * e] += bf16_lo(bw[e]);
+        f[2 * e + 1] += bf16_hi(bw[e]);
+      }
+    }
+    if (aux != nullptr) {
+      const uint4 a4 = *reinterpret_cast<const uint4*>(aux + row * ldaux + col);
+      const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        f[2 * e] += bf16_lo(aw[e]);
+        f[2 * e + 1] += bf16_hi(aw[e]);
+      }
+    }
+    *reinterpret_cast<uint4*>(out + row * ldo + col) =
+        make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+}
+
+// SCIRS_GEMM_SPLITK_BF16=0 disables the split-K path for bf16 outputs.
+static bool splitk_bf16_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SCIRS_GEMM_SPLITK_BF16");
+    v = (e == nullptr) ? 1 : atoi(e);
+  }
+  return v != 0;
+}
+
 static unsigned* done_counter(int dev) {
   static unsigned* ctr[64] = {nullptr};
   if (ctr[dev] == nullptr) {
@@ -1178,11 +1229,28 @@ void gemm_tp(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
 //   accumulate (epi 4): add into out instead of overwriting
 //   bias_grad (epi 3)  : fp32 [N], accumulates the column sums of out
 //   splits   : split-K factor (0 = automatic; epi 4 only)
+static void gemm_tc_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn,
+                         int64_t epi, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+                         c10::optional<torch::Tensor> out2, bool accumulate, int64_t splits, int64_t bn_force,
+                         c10::optional<torch::Tensor> bias_grad, c10::optional<torch::Tensor> rope_cos,
+                         c10::optional<torch::Tensor> rope_sin, int64_t rope_S, int64_t rope_hd, int64_t rope_cols,
+                         bool allow_split_bf16);
+
 void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn, int64_t epi,
              c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> out2,
              bool accumulate, int64_t splits, int64_t bn_force, c10::optional<torch::Tensor> bias_grad,
              c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin, int64_t rope_S,
              int64_t rope_hd, int64_t rope_cols) {
+  gemm_tc_impl(a, b, out, a_mn, b_mn, epi, bias, aux, out2, accumulate, splits, bn_force, bias_grad, rope_cos,
+               rope_sin, rope_S, rope_hd, rope_cols, true);
+}
+
+static void gemm_tc_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, int64_t b_mn,
+                         int64_t epi, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+                         c10::optional<torch::Tensor> out2, bool accumulate, int64_t splits, int64_t bn_force,
+                         c10::optional<torch::Tensor> bias_grad, c10::optional<torch::Tensor> rope_cos,
+                         c10::optional<torch::Tensor> rope_sin, int64_t rope_S, int64_t rope_hd, int64_t rope_cols,
+                         bool allow_split_bf16) {
   using namespace gemm;
   CHECK_CUDA_TENSOR(a);
   CHECK_CUDA_TENSOR(b);
@@ -1253,6 +1321,50 @@ void gemm_tc(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t a_mn, 
     args.C2 = out2->data_ptr();
     args.ldc2 = out2->stride(0);
     TORCH_CHECK((reinterpret_cast<uintptr_t>(args.C2) & 15) == 0, "out2 must be 16-byte aligned");
+  }
+
+  // Small M with a long K and few output tiles (e.g. a data gradient into
+  // d_model at a few thousand tokens): split K over 2-SM pair tiles into the
+  // fp32 workspace, then convert with the bias / residual.
+  if (allow_split_bf16 && (epi == EPI_BF16 || epi == EPI_RESID) && bn_force == 0 && !accumulate && splits == 0 &&
+      splitk_bf16_enabled() && pair_enabled() && M >= 2 * BM && N % 8 == 0 && args.num_kb >= 32) {
+    const long pair_tiles = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+    const int usms = pair_slots(dev);
+    // 2-4 splits of at least 16 k-blocks each, scored by how well the units
+    // fill whole waves of SM pairs, with a penalty per split for the fp32
+    // reduce-add traffic
+    int best_s = 0;
+    double best = -1e9;
+    for (int sp = 2; sp <= 4; ++sp) {
+      if (args.num_kb / sp < 16) break;
+      const double units = (double)pair_tiles * sp;
+      const double eff = units / (std::ceil(units / usms) * usms);
+      if (eff - 0.05 * sp > best) {
+        best = eff - 0.05 * sp;
+        best_s = sp;
+      }
+    }
+    // Worth it (measured on the GPT-2 / ViT per-rank shapes) when the
+    // unsplit 128 x 128 tiles fill their last wave poorly, or when K is so
+    // long (>= 8192) that the workspace passes are noise next to the product;
+    // otherwise the zeroing, reduce-add and conversion passes cost more than
+    // the better wave fill gains.
+    const long t128 = (long)args.m_blocks * ((N + 127) / 128);
+    const double e128 = (double)t128 / (std::ceil((double)t128 / sms) * sms);
+    if (pair_tiles < usms * 2L && best_s > 0 && (e128 < 0.75 || args.num_kb >= 128)) {
+      cudaStream_t st0 = cur_stream();
+      auto wst = torch::zeros({M, N}, torch::TensorOptions().dtype(torch::kFloat).device(out.device()));
+      const float* ws = wst.data_ptr<float>();
+      gemm_tc_impl(a, b, wst, a_mn, b_mn, EPI_F32, c10::nullopt, c10::nullopt, c10::nullopt, /*accumulate=*/true,
+                   best_s, 0, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0, 0, false);
+      const long nvec = (long)M * (N / 8);
+      const int grid = (int)std::min<long>((nvec + 255) / 256, (long)sms * 8);
+      splitk_finalize_kernel<<<grid, 256, 0, st0>>>(ws, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                                    out.stride(0), args.bias, epi == EPI_RESID ? args.aux : nullptr,
+                                                    args.ldaux, (int)M, (int)N);
+      SCIRS_CHECK_LAUNCH();
+      return;
+    }
   }
 
   // Tile width: BN=256 unless BN=128 gives fewer waves for this shape.

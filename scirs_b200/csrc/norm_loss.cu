@@ -276,16 +276,38 @@ __global__ void __launch_bounds__(256) ln_bwd_generic(const bf16* __restrict__ d
 // Sum per-block partials [nb, 3, D] into fp32 gradients (accumulating):
 // dgamma, dbeta and (optional) the column sum of the produced dx, which is
 // the bias gradient of the projection that wrote the residual stream.
-__global__ void ln_bwd_reduce(const float* __restrict__ part, int nb, int D, float* __restrict__ dw,
-                              float* __restrict__ db, float* __restrict__ dsum) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= 3 * D) return;
-  if (c >= 2 * D && dsum == nullptr) return;
-  float s = 0.f;
-  for (int k = 0; k < nb; ++k) s += part[(long)k * 3 * D + c];
-  if (c < D) dw[c] += s;
-  else if (c < 2 * D) db[c - D] += s;
-  else dsum[c - 2 * D] += s;
+// A block covers 32 consecutive columns; its 8 warps sum interleaved subsets
+// of the nb partials (four loads in flight per thread) and combine through
+// shared memory, so a few thousand rows' worth of partials reduce in one wave.
+__global__ void __launch_bounds__(256) ln_bwd_reduce(const float* __restrict__ part, int nb, int D,
+                                                     float* __restrict__ dw, float* __restrict__ db,
+                                                     float* __restrict__ dsum) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const bool live = c < 3 * D && (c < 2 * D || dsum != nullptr);
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (live) {
+    const long st = 3L * D;
+    int k = warp;
+    for (; k + 24 < nb; k += 32) {
+      s0 += __ldcs(part + (long)k * st + c);
+      s1 += __ldcs(part + (long)(k + 8) * st + c);
+      s2 += __ldcs(part + (long)(k + 16) * st + c);
+      s3 += __ldcs(part + (long)(k + 24) * st + c);
+    }
+    for (; k < nb; k += 8) s0 += __ldcs(part + (long)k * st + c);
+  }
+  red[warp][lane] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (warp == 0 && live) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += red[w][lane];
+    if (c < D) dw[c] += s;
+    else if (c < 2 * D) db[c - D] += s;
+    else dsum[c - 2 * D] += s;
+  }
 }
 
 // ===========================================================================
@@ -604,7 +626,7 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
     TORCH_CHECK(dsum->numel() == D, "dsum must have D entries");
     dsp = dsum->data_ptr<float>();
   }
-  ln_bwd_reduce<<<(3 * D + 255) / 256, 256, 0, s>>>(pp, nb, D, dw.data_ptr<float>(), db.data_ptr<float>(), dsp);
+  ln_bwd_reduce<<<(3 * D + 31) / 32, 256, 0, s>>>(pp, nb, D, dw.data_ptr<float>(), db.data_ptr<float>(), dsp);
   SCIRS_CHECK_LAUNCH();
 }
 
@@ -830,7 +852,7 @@ extern "C" __attribute__((visibility("default"))) int scirs_layernorm_bwd_noallo
 #undef NOALLOC_LNB
   e = cudaGetLastError();
   if (e != cudaSuccess) return (int)e;
-  ln_bwd_reduce<<<(3 * D + 255) / 256, 256, 0, s>>>(part, inb, D, dw, db, dsum);
+  ln_bwd_reduce<<<(3 * D + 31) / 32, 256, 0, s>>>(part, inb, D, dw, db, dsum);
   return (int)cudaGetLastError();
 }
 

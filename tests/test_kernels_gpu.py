@@ -335,3 +335,35 @@ def test_gemm_rope_epilogue(M, H, hd, bn):
 
     _ext.kernels().rope_apply(ref2, cos, sin, S, H, hd, False)
     assert rel_err(out, ref2) < 1e-2
+
+
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("M,N,K_", [(2048, 768, 3072), (6304, 768, 2304), (8192, 768, 50304 // 8 * 8)])
+def test_gemm_bf16_split_k(M, N, K_, b_mn):
+    """Small M, long K, few output tiles: the bf16 output goes through the
+    split-K fp32 workspace and the finalize pass (bias; bias + residual)."""
+    a = rnd(M, K_, scale=0.5, seed=51)
+    b = rnd(K_, N, scale=0.05, seed=52) if b_mn else rnd(N, K_, scale=0.05, seed=52)
+    bias, res = rnd(N, seed=53), rnd(M, N, seed=54)
+    acc = a.float() @ (b.float() if b_mn else b.float().t())
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    K.gemm(a, b, out, b_mn=b_mn)
+    assert rel_err(out, acc) < 1e-2
+    K.gemm(a, b, out, b_mn=b_mn, bias=bias)
+    assert rel_err(out, acc + bias.float()) < 1e-2
+    K.gemm(a, b, out, b_mn=b_mn, epi=K.EPI_RESID, bias=bias, aux=res)
+    assert rel_err(out, acc + bias.float() + res.float()) < 1e-2
+    # twice in a row inside a CUDA graph (the workspace is allocated and zeroed in stream order)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        K.gemm(a, b, out, b_mn=b_mn, epi=K.EPI_RESID, bias=bias, aux=res)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            K.gemm(a, b, out, b_mn=b_mn, epi=K.EPI_RESID, bias=bias, aux=res)
+    out.zero_()
+    g.replay()
+    g.replay()
+    torch.cuda.synchronize()
+    assert rel_err(out, acc + bias.float() + res.float()) < 1e-2
