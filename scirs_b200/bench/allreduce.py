@@ -1,7 +1,7 @@
 """Fused gradient all-reduce sweep: in-kernel NVLink all-reduce vs NCCL.
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
-        -m scirs_b200.bench.allreduce [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20]
+        -m scirs_b200.bench.allreduce [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20] [--zero]
 
 Payload sizes are bf16 bytes on the wire (fp32 gradients in, fp32 out; the
 push kernel scales by 1/N and casts to bf16 when publishing). NCCL runs
@@ -50,12 +50,16 @@ def main():
     ap.add_argument("--min-bytes", type=int, default=1024)
     ap.add_argument("--max-bytes", type=int, default=1 << 30)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--zero", action="store_true",
+                    help="also time the ZeRO collectives: NVLS reduce-scatter (fp32) and all-gather (bf16) vs NCCL")
     args = ap.parse_args()
     rank, world, local = sdist.init(timeout_s=120)
     dev = torch.device("cuda", local)
     comm = NVLinkComm(area_bytes=max(args.max_bytes, 1 << 20) + (1 << 20), timeout_s=10.0)
     nvls = comm.nvls_supported()
     nbuf = comm.nvls_buffer(max(args.max_bytes // 2, 1 << 20), torch.bfloat16) if nvls else None
+    zbuf32 = comm.nvls_buffer(max(args.max_bytes // 4, 1 << 20), torch.float32) if (nvls and args.zero) else None
+    zbuf16 = comm.nvls_buffer(max(args.max_bytes // 2, 1 << 20), torch.bfloat16) if (nvls and args.zero) else None
     size = args.min_bytes
     while size <= args.max_bytes:
         n = max(8 * world, (size // 2) // (8 * world) * (8 * world))
@@ -82,6 +86,31 @@ def main():
                     "nvls_speedup_vs_nccl": round(t_nccl / t_nvls, 3),
                     "nvls_roofline_frac": round((world + 1) / world * nbytes / (LINK_GBS * 1e9) * 1e3 / t_nvls, 3)}),
             }), flush=True)
+        if zbuf32 is not None:
+            # ZeRO collectives on `size` payload bytes: reduce-scatter of fp32
+            # gradients, all-gather of bf16 weights; roofline (N-1)/N of the
+            # payload into each GPU over NVLink
+            nf = max(64 * world, (size // 4) // (64 * world) * (64 * world))
+            full = zbuf32[:nf]
+            full.normal_()
+            shard = torch.empty(nf // world, device=dev)
+            t_rs = _time(lambda: comm.reduce_scatter_nvls(full, shard, 1.0 / world), args.iters)
+            src = full.clone()
+            t_rs_nccl = _time(lambda: dist.reduce_scatter_tensor(shard, src, op=dist.ReduceOp.AVG), args.iters)
+            nh = max(64 * world, (size // 2) // (64 * world) * (64 * world))
+            fullh = zbuf16[:nh]
+            shardh = torch.randn(nh // world, device=dev).to(torch.bfloat16)
+            t_ag = _time(lambda: comm.all_gather_nvls(shardh, fullh), args.iters)
+            outh = torch.empty(nh, device=dev, dtype=torch.bfloat16)
+            t_ag_nccl = _time(lambda: dist.all_gather_into_tensor(outh, shardh), args.iters)
+            if rank == 0:
+                for op, nb, t_o, t_n in (("reduce_scatter_fp32", 4 * nf, t_rs, t_rs_nccl),
+                                         ("all_gather_bf16", 2 * nh, t_ag, t_ag_nccl)):
+                    roof = (world - 1) / world * nb / (LINK_GBS * 1e9) * 1e3
+                    print(json.dumps({"op": op, "bytes": nb, "n_gpus": world, "nvls_ms": round(t_o, 4),
+                                      "nccl_ms": round(t_n, 4), "nvls_speedup_vs_nccl": round(t_n / t_o, 3),
+                                      "nvls_roofline_frac": round(roof / t_o, 3),
+                                      "nccl_roofline_frac": round(roof / t_n, 3)}), flush=True)
         size *= 4
     _ext.check_status(local)
     comm.close()
