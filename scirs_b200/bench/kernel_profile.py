@@ -33,6 +33,7 @@ from ..ops import kernels as K
 
 M, D, F, H, HD, S = 16384, 768, 3072, 12, 64, 1024
 NOPT = 32 << 20  # optimizer elements (a quarter of GPT-2 small; 640 MB of state)
+PB, PL = 32, 4096  # paged decode: sequences x tokens (K + V pages: 537 MB)
 B = M // S
 
 
@@ -87,6 +88,23 @@ def build(dev):
     t["hp"] = torch.tensor([6e-4, 0.9, 0.95, 1e-8, 0.1, 1.0, 1.0, 1.0, 1.0, 0.0, 1.0] + [0.0] * 5, device=dev)
     t["part"] = torch.zeros(1024, device=dev)
     t["mask"] = torch.ones((n + 63) // 64, device=dev, dtype=torch.uint8)
+    # embedding: GPT-2 vocabulary, M tokens
+    t["tok"] = torch.randint(0, 50257, (M,), device=dev)
+    t["wte"] = r(V, D)
+    t["wpe"] = r(S, D)
+    t["emb"] = torch.empty(M, D, device=dev, dtype=bf)
+    t["dwte"] = torch.zeros(V, D, device=dev, dtype=f32)
+    t["dwpe"] = torch.zeros(S, D, device=dev, dtype=f32)
+    # paged decode: PB sequences of PL tokens, 32 query heads over 8 KV heads, head_dim 128, 16-token pages
+    pages = PB * PL // 16
+    t["pk"] = r(pages, 16, 8, 128)
+    t["pv"] = r(pages, 16, 8, 128)
+    t["pq"] = r(PB, 32, 128)
+    t["pbt"] = torch.randperm(pages, generator=g).to(torch.int32).view(PB, PL // 16).to(dev)
+    t["plen"] = torch.full((PB,), PL, dtype=torch.int32, device=dev)
+    t["pout"] = torch.empty(PB, 32, 128, device=dev, dtype=bf)
+    t["ppo"] = torch.empty(PB, 32, PL // 512, 128, device=dev, dtype=f32)
+    t["ppml"] = torch.empty(PB, 32, PL // 512, 2, device=dev, dtype=f32)
     return t
 
 
@@ -209,6 +227,19 @@ def op_xent(t):
     K.xent_fwd_bwd(t["logits"], t["tgt"], t["losses"], 50257, 1.0 / (M // 4))
 
 
+def op_embed_fwd(t):
+    K.embedding_fwd(t["tok"], t["wte"], t["wpe"], t["emb"], S)
+
+
+def op_embed_bwd(t):
+    K.embedding_bwd(t["tok"], t["datt"], t["dwte"], t["dwpe"], S)
+
+
+def op_paged_decode(t):
+    _ext.kernels().paged_attention_decode(t["pq"], t["pk"], t["pv"], t["pbt"], t["plen"], t["pout"], t["ppo"],
+                                          t["ppml"], 512, 128 ** -0.5)
+
+
 def op_adamw(t):
     K.optim_step("adamw", t["p"], t["m1"], t["m2"], t["g"], t["p16"], t["p"].numel(), t["hp"], part=t["part"],
                  decay_mask=t["mask"])
@@ -235,6 +266,9 @@ OPS = {
     "ln_bwd": (op_ln_bwd, 0, 4 * M * D * 2),
     "xent": (op_xent, 0, 2 * (M // 4) * 50304 * 2),
     "adamw": (op_adamw, 0, NOPT * (4 * 2 + 8 * 2 + 4 + 2) + NOPT * 4),
+    "embed_fwd": (op_embed_fwd, 0, M * D * 2 * 3),
+    "embed_bwd": (op_embed_bwd, 0, M * D * 2 + 2 * M * D * 4),
+    "paged_decode": (op_paged_decode, 4 * PB * 32 * PL * 128, 2 * PB * PL * 8 * 128 * 2),
 }
 
 

@@ -566,12 +566,13 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 // here); delta fp32 scratch [B*H*S].
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                        torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                       double scale, const AttnSparse& sp);
+                       double scale, const AttnSparse& sp, bool pipelined);
 
-// impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernel (head_dim 64).
+// impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernels (serial schedule),
+// 2 = tcgen05 kernels with the pipelined schedule.
 void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                          torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                         double scale, const AttnSparse& sp);
+                         double scale, const AttnSparse& sp, bool pipelined);
 
 // Sk = k.size(1) may differ from S (cross-attention; tcgen05 kernels only).
 // Optional block lists (per 128-key tile: the query blocks that see it, in
@@ -596,7 +597,7 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
   const AttnSparse sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, (Sk + 127) / 128);
   const bool sparse = sp.ptr != nullptr || sp.bmap != nullptr || sp.wl >= 0 || sp.ng > 0;
   TORCH_CHECK(!sparse || sp.ptr != nullptr, "a sparsity predicate needs block lists");
-  TORCH_CHECK(impl == 1 || (!sparse && Sk == S), "sparse and cross attention need the tcgen05 kernels");
+  TORCH_CHECK(impl >= 1 || (!sparse && Sk == S), "sparse and cross attention need the tcgen05 kernels");
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
   TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= B * S * H * HD, "dq_acc too small");
   TORCH_CHECK(delta.scalar_type() == at::kFloat && delta.numel() >= B * H * S, "delta too small");
@@ -634,10 +635,10 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
     else attn::fa_bwd_delta_kernel<128><<<(unsigned)((rows * 16 + 255) / 256), 256, 0, st>>>(p);
     SCIRS_CHECK_LAUNCH();
   }
-  if (impl == 1 && HD == 64) {
-    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp);
-  } else if (impl == 1 && HD == 128) {
-    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp);
+  if (impl >= 1 && HD == 64) {
+    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, impl == 2);
+  } else if (impl >= 1 && HD == 128) {
+    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, impl == 2);
   } else {
   dim3 grid((unsigned)((S + 63) / 64), (unsigned)(B * H));
 #define FA_BWD(HD_, CAUSAL_)                                                                             \

@@ -341,11 +341,360 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Pipelined variant (same CTA shape, roles and outputs as fa_bwd_h128_kernel).
+// The tensor core no longer waits for the gradient warps between blocks:
+//   * the warps copy S^T out of TMEM first and release it, so S^T of the next
+//     block is computed while they work on this one;
+//   * P^T (bf16) goes to TMEM columns [448, 480) and dV += P^T dO reads it
+//     from there, issued as soon as P^T is written;
+//   * dS^T (bf16) goes to TMEM over the dP^T columns each warp has read (dK
+//     reads it from there) and to shared memory (B operand of dQ^T);
+//   * dQ^T of block n - 1 is drained between P and dS of block n, so the dQ
+//     MMA of block n never waits for it;
+//   * dP^T of the next block is issued right after dQ^T of this one.
+// dS is formed from the bf16 P that dV uses.
+// MMA issue order per block n: S_{n+1} | dV_n | dK_n | dQ^T_n | dP_{n+1}.
+// ---------------------------------------------------------------------------
+template <bool CAUSAL, bool SPARSE = false>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_h128_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                            const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;     // MMA commit
+  uint64_t* s_free = bars + 6;     // 8 warps copied S^T out
+  uint64_t* dp_full = bars + 7;    // MMA commit
+  uint64_t* pt_full = bars + 8;    // 8 warps wrote P^T
+  uint64_t* pt_free = bars + 9;    // MMA commit after dV
+  uint64_t* ds_full = bars + 10;   // 8 warps wrote dS^T
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_free = bars + 12;   // 8 warps
+  uint64_t* dkv_full = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint64_t* ld_bar = bars + 15;    // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* sLD = reinterpret_cast<float*>(smem + OFF_LD);  // [buf][0: lse2, 1: delta][64]
+  constexpr uint32_t T_PT = 448;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.S, Sk = p.Sk, H = p.H;
+  const int kb = blockIdx.x;
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int k0 = kb * BK;
+  const int row_base = b * S;
+  const int kv_base = b * Sk;
+  const int nq = (S + BQ - 1) / BQ;
+  const int i0 = CAUSAL ? k0 / BQ : 0;
+  const int lb = SPARSE ? __ldg(p.sp.ptr + kb) : 0;
+  const int niter = SPARSE ? __ldg(p.sp.ptr + kb + 1) - lb : max(nq - i0, 0);
+  auto qblk = [&](int n) -> int { return SPARSE ? __ldg(p.sp.idx + lb + n) : i0 + n; };
+  const int col = h * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&ld_bar[i], 8);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(dp_full, 1);
+    mbar_init(pt_full, 8);
+    mbar_init(pt_free, 1);
+    mbar_init(ds_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
+    mbar_init(dkv_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmDO);
+    prefetch_tmap(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * KV_BYTES);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tma_load_2d(smem + OFF_K + c * (BK * 128), &tmK, kv_full, col + c * 64, kv_base + k0);
+        tma_load_2d(smem + OFF_V + c * (BK * 128), &tmV, kv_full, col + c * 64, kv_base + k0);
+      }
+      for (int n = 0; n < niter; ++n) {
+        const int i = qblk(n);
+        const int st = n & 1;
+        if (!mbar_wait(&qdo_empty[st], ((n >> 1) & 1) ^ 1, p.st, 80, abort_flag)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * QT_BYTES);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tma_load_2d(smem + OFF_Q + st * QT_BYTES + c * (BQ * 128), &tmQ, &qdo_full[st], col + c * 64,
+                      row_base + i * BQ);
+          tma_load_2d(smem + OFF_DO + st * QT_BYTES + c * (BQ * 128), &tmDO, &qdo_full[st], col + c * 64,
+                      row_base + i * BQ);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane == 0) {
+      const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
+      const uint32_t ds_addr = smem_u32(smem + OFF_DST);
+      auto q_at = [&](int n) { return smem_u32(smem + OFF_Q + (n & 1) * QT_BYTES); };
+      auto do_at = [&](int n) { return smem_u32(smem + OFF_DO + (n & 1) * QT_BYTES); };
+      auto issue_s = [&](int n) {  // S^T = K Q_n^T
+        const uint32_t q_addr = q_at(n);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t ak = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
+          const uint32_t bq = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(tmem + T_S, umma_desc_sw128(k_addr + ak, 16, 1024), umma_desc_sw128(q_addr + bq, 16, 1024),
+                        IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+      };
+      auto issue_dp = [&](int n) {  // dP^T = V dO_n^T
+        const uint32_t do_addr = do_at(n);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t ak = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
+          const uint32_t bq = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(tmem + T_DP, umma_desc_sw128(v_addr + ak, 16, 1024),
+                        umma_desc_sw128(do_addr + bq, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(dp_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, p.st, 81, abort_flag);
+      if (ok && niter > 0) {
+        ok = mbar_wait(&qdo_full[0], 0, p.st, 82, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0);
+          issue_dp(0);
+        }
+      }
+      for (int n = 0; n < niter && ok; ++n) {
+        const int st = n & 1;
+        if (n + 1 < niter) {
+          ok = mbar_wait(&qdo_full[(n + 1) & 1], ((n + 1) >> 1) & 1, p.st, 82, abort_flag) &&
+               mbar_wait(s_free, n & 1, p.st, 90, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(n + 1);
+        }
+        const uint32_t q_addr = q_at(n), do_addr = do_at(n);
+        if (!mbar_wait(pt_full, n & 1, p.st, 83, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO, A = P^T in TMEM (8 packed columns per k-step)
+          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8, umma_desc_sw128(do_addr + kk * 2048, BQ * 128, 1024),
+                        IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(pt_free);
+        if (!mbar_wait(ds_full, n & 1, p.st, 91, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q, A = dS^T in TMEM over the dP^T columns
+          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 1) * 32 + (kk & 1) * 8,
+                        umma_desc_sw128(q_addr + kk * 2048, BQ * 128, 1024), IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(dq_free, (n & 1) ^ 1, p.st, 84, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_DQ, umma_desc_sw128(k_addr + kk * 2048, BK * 128, 1024),
+                        umma_desc_sw128(ds_addr + kk * 2048, BK * 128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+        tc_commit(dq_full);
+        tc_commit(&qdo_empty[st]);
+        if (n + 1 < niter) issue_dp(n + 1);
+      }
+      tc_commit(dkv_full);
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ gradient warps
+    const int w8 = warp - 2;
+    const int q4 = warp & 3;
+    const int ch = w8 >> 2;        // query half (32 of the block's 64)
+    const int r = q4 * 32 + lane;  // key row, or hd index for dQ^T
+    const int key = k0 + r;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    const float* lse_g = p.lse + ((long)b * H + h) * S;
+    const float* del_g = p.delta + ((long)b * H + h) * S;
+    uint8_t* ds_row = smem + OFF_DST + r * 128;
+    float* stage = reinterpret_cast<float*>(smem + OFF_DQS + w8 * 4096);  // [32 q][32 hd]
+    const float LOG2E = 1.4426950408889634f;
+    const int c0 = ch * 32;
+    const int t = w8 * 32 + lane;  // t < 128 stage the block's 64 lse and 64 delta values
+    float nv = 0.f;
+    if (t < 128 && niter > 0) {
+      const int q = qblk(0) * BQ + (t & 63);
+      nv = q < S ? (t < 64 ? lse_g[q] * LOG2E : del_g[q]) : 0.f;
+    }
+    // dQ^T of block m: lane = hd index, columns = this warp's 32 queries
+    auto drain_dq = [&](int m) -> bool {
+      if (!mbar_wait(dq_full, m & 1, p.st, 88, abort_flag)) return false;
+      tc_fence_after();
+      uint32_t a[32];
+      tmem_ld_32x32b_x32(lane_base + T_DQ + c0, a);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (lane == 0) tma_store_wait_read0();
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) stage[j * 32 + lane] = __uint_as_float(a[j]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int row = row_base + qblk(m) * BQ + c0;
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         &tmDQ), "r"(smem_u32(stage)), "r"(col + q4 * 32), "r"(row) : "memory");
+        tma_store_commit();
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int n = 0; n < niter && ok; ++n) {
+      const int q0 = qblk(n) * BQ;
+      float* sL = sLD + (n & 1) * 2 * BQ;
+      if (t < 128) {
+        sL[t] = nv;
+        if (n + 1 < niter) {
+          const int q = qblk(n + 1) * BQ + (t & 63);
+          nv = q < S ? (t < 64 ? lse_g[q] * LOG2E : del_g[q]) : 0.f;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ld_bar[n & 1]);
+      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 85, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(s_full, n & 1, p.st, 86, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sv[32];
+      tmem_ld_32x32b_x32(lane_base + T_S + c0, sv);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
+                             (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
+      const AttnSpan span = attn_queries_of_key<SPARSE>(p.sp, key, q0, S, Sk, CAUSAL);
+      uint32_t pp[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float pr[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int ql = c0 + e + u;
+          float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
+          if (need_mask && !attn_span_has(span, ql)) pv = 0.f;
+          pr[u] = pv;
+        }
+        pp[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+      }
+      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 87, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      tmem_st_32x32b_x16(lane_base + T_PT + (c0 >> 1), pp);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pt_full);
+      if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
+      if (!mbar_wait(dp_full, n & 1, p.st, 92, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t dv[32];
+      tmem_ld_32x32b_x32(lane_base + T_DP + c0, dv);
+      tc_wait_ld();
+      uint32_t dd[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const uint32_t pq = pp[e >> 1];
+        const float d0 = bf16_lo(pq) * (__uint_as_float(dv[e]) - sL[BQ + c0 + e]);
+        const float d1 = bf16_hi(pq) * (__uint_as_float(dv[e + 1]) - sL[BQ + c0 + e + 1]);
+        dd[e >> 1] = pack_bf16x2(d0, d1);
+      }
+      tmem_st_32x32b_x16(lane_base + T_DP + c0, dd);  // over dP^T columns this warp has read
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int so = ((ch * 4 + u) ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(ds_row + so) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (ok && niter > 0) ok = drain_dq(niter - 1);
+    if (lane == 0) tma_store_wait0();
+    __syncwarp();
+    if (ok && mbar_wait(dkv_full, 0, p.st, 89, abort_flag)) {
+      tc_fence_after();
+      uint32_t kv[32];
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        bf16* dst = which ? (p.dv + (long)(kv_base + key) * p.dv_rs + col)
+                          : (p.dk + (long)(kv_base + key) * p.dk_rs + col);
+        const float sc = which ? 1.f : p.scale;
+        const bool empty = SPARSE && niter == 0;
+#pragma unroll 1
+        for (int c = ch * 64; c < ch * 64 + 64; c += 32) {
+          tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
+          tc_wait_ld();
+          if (empty) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) kv[e] = 0u;
+          }
+          if (key < Sk) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
+              uint4 o;
+              o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
+              o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
+              o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
+              o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
+              *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace fabw128
 
 void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                          torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                         double scale, const AttnSparse& sp) {
+                         double scale, const AttnSparse& sp, bool pipelined) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 128, "this backward kernel is for head_dim 128");
@@ -387,7 +736,7 @@ void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, t
   auto st = cur_stream();
 #define FABW128(C_, SP_)                                                   \
   {                                                                        \
-    auto kern = fabw128::fa_bwd_h128_kernel<C_, SP_>;                      \
+    auto kern = pipelined ? fabw128::fa_bwd_h128_pipe_kernel<C_, SP_> : fabw128::fa_bwd_h128_kernel<C_, SP_>; \
     set_max_smem((const void*)kern, fabw128::SMEM);                        \
     kern<<<grid, fabw128::kThreads, fabw128::SMEM, st>>>(tq, tk, tv, tdo, tdq, p); \
   }

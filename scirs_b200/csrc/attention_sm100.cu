@@ -761,6 +761,383 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Pipelined variant of the head_dim-64 backward. Same CTA shape, warp roles
+// and outputs as fa_bwd_tc_kernel; the schedule differs so that the tensor
+// core and the dS warps overlap instead of taking turns, and fewer operand
+// bytes go through shared memory:
+//
+//   * the dS warps copy S^T of a query block out of TMEM first and release it
+//     at once, so the MMA warp computes S^T of the NEXT block while the dS
+//     warps are still on the exponentials of this one;
+//   * P^T (bf16) goes to TMEM columns [448, 512) and dV += P^T dO reads it
+//     from there (A operand in TMEM), issued as soon as P^T is written;
+//   * dS^T (bf16) goes both to TMEM, over the dP^T columns this warp has
+//     already read (dK += dS^T Q reads it from there), and to shared memory
+//     (dQ = dS K needs it as an MN-major A operand);
+//   * dP^T of the next block is issued right after dQ of this one;
+//   * the staging warps load LSE / delta of the next block while this block
+//     is in flight.
+// dS is formed from the bf16 P that dV uses (32 live registers instead of 64).
+//
+// MMA issue order per block n: S_{n+1} | dV_n | dK_n | dQ_n | dP_{n+1}.
+// TMEM columns: S^T [0,128), dP^T / dS^T [128,256), dV [256,320),
+// dK [320,384), dQ [384,448), P^T [448,512).
+// ---------------------------------------------------------------------------
+template <bool CAUSAL, bool SPARSE = false>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;     // S^T of a block is in TMEM (MMA commit)
+  uint64_t* s_free = bars + 6;     // the 8 dS warps have copied S^T out
+  uint64_t* dp_full = bars + 7;    // dP^T of a block is in TMEM (MMA commit)
+  uint64_t* pt_full = bars + 8;    // P^T written to TMEM (8 warps)
+  uint64_t* pt_free = bars + 9;    // dV MMA done with P^T (MMA commit)
+  uint64_t* ds_full = bars + 10;   // dS^T written to TMEM and smem (8 warps)
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_free = bars + 12;
+  uint64_t* dkv_full = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint64_t* ld_bar = bars + 15;    // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* sLD = reinterpret_cast<float*>(smem + OFF_LD);  // [buf][0: lse2, 1: delta][128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.S, Sk = p.Sk, H = p.H;
+  const int kb = blockIdx.x;
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int k0 = kb * BK;
+  const int row_base = b * S;
+  const int kv_base = b * Sk;
+  const int nq = (S + BQ - 1) / BQ;
+  const int i0 = CAUSAL ? kb : 0;
+  const int lb = SPARSE ? __ldg(p.sp.ptr + kb) : 0;
+  const int niter = SPARSE ? __ldg(p.sp.ptr + kb + 1) - lb : max(nq - i0, 0);
+  auto qblk = [&](int n) -> int { return SPARSE ? __ldg(p.sp.idx + lb + n) : i0 + n; };
+  const int col = h * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&ld_bar[i], 4);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(dp_full, 1);
+    mbar_init(pt_full, 8);
+    mbar_init(pt_free, 1);
+    mbar_init(ds_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(dkv_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmDO);
+    prefetch_tmap(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + HD, T_DQ = 256 + 2 * HD, T_PT = 448;
+
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsCtl>();
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * T_BYTES);
+      tma_load_2d(smem + OFF_K, &tmK, kv_full, col, kv_base + k0);
+      tma_load_2d(smem + OFF_V, &tmV, kv_full, col, kv_base + k0);
+      for (int n = 0; n < niter; ++n) {
+        const int i = qblk(n);
+        const int st = n & 1;
+        if (!mbar_wait(&qdo_empty[st], ((n >> 1) & 1) ^ 1, p.st, 50, abort_flag)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * T_BYTES);
+        tma_load_2d(smem + OFF_Q + st * T_BYTES, &tmQ, &qdo_full[st], col, row_base + i * BQ);
+        tma_load_2d(smem + OFF_DO + st * T_BYTES, &tmDO, &qdo_full[st], col, row_base + i * BQ);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane == 0) {
+      const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
+      const uint32_t ds_addr = smem_u32(smem + OFF_DST);
+      auto q_at = [&](int n) { return smem_u32(smem + OFF_Q + (n & 1) * T_BYTES); };
+      auto do_at = [&](int n) { return smem_u32(smem + OFF_DO + (n & 1) * T_BYTES); };
+      auto issue_s = [&](int n) {  // S^T = K Q_n^T -> T_S
+        const uint32_t q_addr = q_at(n);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_S, umma_desc_sw128(k_addr + kk * 32, 16, 1024),
+                        umma_desc_sw128(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        tc_commit(s_full);
+      };
+      auto issue_dp = [&](int n) {  // dP^T = V dO_n^T -> T_DP
+        const uint32_t do_addr = do_at(n);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_DP, umma_desc_sw128(v_addr + kk * 32, 16, 1024),
+                        umma_desc_sw128(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        tc_commit(dp_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, p.st, 51, abort_flag);
+      if (ok && niter > 0) {
+        ok = mbar_wait(&qdo_full[0], 0, p.st, 52, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0);
+          issue_dp(0);
+        }
+      }
+      for (int n = 0; n < niter && ok; ++n) {
+        const int st = n & 1;
+        if (n + 1 < niter) {
+          // next block's scores as soon as this block's S^T has been copied out
+          ok = mbar_wait(&qdo_full[(n + 1) & 1], ((n + 1) >> 1) & 1, p.st, 52, abort_flag) &&
+               mbar_wait(s_free, n & 1, p.st, 53, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(n + 1);
+        }
+        if (!mbar_wait(pt_full, n & 1, p.st, 54, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t q_addr = q_at(n), do_addr = do_at(n);
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO: A = P^T from TMEM (8 packed columns per k-step)
+          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8,
+                        umma_desc_sw128(do_addr + kk * 2048, 128 * 128, 1024), IDESC_KV,
+                        (n > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(pt_free);
+        if (!mbar_wait(ds_full, n & 1, p.st, 56, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q: A = dS^T from TMEM (over the dP^T columns)
+          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 2) * 64 + (kk & 3) * 8,
+                        umma_desc_sw128(q_addr + kk * 2048, 128 * 128, 1024), IDESC_KV,
+                        (n > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(dq_free, (n & 1) ^ 1, p.st, 55, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_DQ, umma_desc_sw128(ds_addr + kk * 2048, BK * 128, 1024),
+                        umma_desc_sw128(k_addr + kk * 2048, 128 * 128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+        tc_commit(dq_full);
+        tc_commit(&qdo_empty[st]);
+        if (n + 1 < niter) issue_dp(n + 1);
+      }
+      tc_commit(dkv_full);
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  }
+  } else if (warp < 12) {
+    setmaxnreg_inc<kRegsDs>();
+    // ------------------------------------------------------------ dS warps
+    // warps 4-7: queries [0, 64) of the block, warps 8-11: [64, 128);
+    // thread = key row r (TMEM lane).
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const int key = k0 + r;
+    const bool stager = warp < 8;
+    const int t128 = (warp - 4) * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    const float* lse_g = p.lse + ((long)b * H + h) * S;
+    const float* del_g = p.delta + ((long)b * H + h) * S;
+    uint8_t* ds_row = smem + OFF_DST + r * 128;
+    const float LOG2E = 1.4426950408889634f;
+    const int hq = stager ? 0 : 1;         // query half of the block
+    const int c_begin = hq * (BQ / 2);
+    float nl = 0.f, nd = 0.f;              // staged LSE / delta of the next block (stagers)
+    if (stager && niter > 0) {
+      const int q = qblk(0) * BQ + t128;
+      nl = q < S ? lse_g[q] * LOG2E : 0.f;
+      nd = q < S ? del_g[q] : 0.f;
+    }
+    for (int n = 0; n < niter; ++n) {
+      const int i = qblk(n);
+      const int q0 = i * BQ;
+      float* sL = sLD + (n & 1) * 256;
+      if (stager) {
+        sL[t128] = nl;
+        sL[128 + t128] = nd;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ld_bar[n & 1]);
+        if (n + 1 < niter) {  // prefetch the next block's rows while this one runs
+          const int q = qblk(n + 1) * BQ + t128;
+          nl = q < S ? lse_g[q] * LOG2E : 0.f;
+          nd = q < S ? del_g[q] : 0.f;
+        }
+      }
+      if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) break;
+      if (!mbar_wait(s_full, n & 1, p.st, 57, abort_flag)) break;
+      tc_fence_after();
+      uint32_t sv[64];
+      tmem_ld_32x32b_x32(lane_base + T_S + c_begin, sv);
+      tmem_ld_32x32b_x32(lane_base + T_S + c_begin + 32, sv + 32);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);  // the tensor core may overwrite S^T now
+      const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
+                             (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
+      const AttnSpan span = attn_queries_of_key<SPARSE>(p.sp, key, q0, S, Sk, CAUSAL);
+      uint32_t pk[32];
+#pragma unroll
+      for (int e = 0; e < 64; e += 2) {
+        float pr[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int ql = c_begin + e + u;
+          float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
+          if (need_mask && !attn_span_has(span, ql)) pv = 0.f;
+          pr[u] = pv;
+        }
+        pk[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+      }
+      if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 58, abort_flag)) break;
+      tc_fence_after();
+      tmem_st_32x32b_x16(lane_base + T_PT + (c_begin >> 1), pk);
+      tmem_st_32x32b_x16(lane_base + T_PT + (c_begin >> 1) + 16, pk + 16);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pt_full);
+      if (!mbar_wait(dp_full, n & 1, p.st, 59, abort_flag)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int c = c_begin + half * 32;
+        uint32_t dv[32];
+        tmem_ld_32x32b_x32(lane_base + T_DP + c, dv);
+        tc_wait_ld();
+        uint32_t dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const uint32_t pp = pk[(half * 32 + e) >> 1];
+          const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e]) - sL[128 + c + e]);
+          const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e + 1]) - sL[128 + c + e + 1]);
+          dd[e >> 1] = pack_bf16x2(d0, d1);
+        }
+        // TMEM copy for dK (over dP^T columns this thread has read), smem copy for dQ
+        tmem_st_32x32b_x16(lane_base + T_DP + hq * 64 + half * 16, dd);
+        const int blk = (c >> 6) * (BK * 128);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int unit = ((c & 63) >> 3) + u;
+          const int so = blk + ((unit ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(ds_row + so) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+  } else {
+    setmaxnreg_dec<kRegsDrain>();
+    // ------------------------------------------------------------ dQ drain, then dK / dV
+    const int q4 = warp & 3;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    uint8_t* slot0 = smem + OFF_DQS + (warp - 12) * 8192;
+    uint8_t* slot1 = slot0 + 4096;
+    bool ok = true;
+    for (int n = 0; n < niter; ++n) {
+      const int i = qblk(n);
+      if (!mbar_wait(dq_full, n & 1, p.st, 61, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t a0[32], a1[32];
+      tmem_ld_32x32b_x32(lane_base + T_DQ, a0);
+      tmem_ld_32x32b_x32(lane_base + T_DQ + 32, a1);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (lane == 0) tma_store_wait_read0();
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        *reinterpret_cast<uint4*>(slot0 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_uint4(a0[4 * u], a0[4 * u + 1], a0[4 * u + 2], a0[4 * u + 3]);
+        *reinterpret_cast<uint4*>(slot1 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_uint4(a1[4 * u], a1[4 * u + 1], a1[4 * u + 2], a1[4 * u + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int row = row_base + i * BQ + q4 * 32;
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         &tmDQ), "r"(smem_u32(slot0)), "r"(col), "r"(row) : "memory");
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         &tmDQ), "r"(smem_u32(slot1)), "r"(col + 32), "r"(row) : "memory");
+        tma_store_commit();
+      }
+    }
+    if (lane == 0) tma_store_wait0();
+    __syncwarp();
+    if (ok && mbar_wait(dkv_full, 0, p.st, 62, abort_flag)) {
+      tc_fence_after();
+      const int r = q4 * 32 + lane;
+      const int key = k0 + r;
+      uint32_t kv[32];
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        bf16* dst = which ? (p.dv + (long)(kv_base + key) * p.dv_rs + col)
+                          : (p.dk + (long)(kv_base + key) * p.dk_rs + col);
+        const float sc = which ? 1.f : p.scale;
+        const bool empty = SPARSE && niter == 0;
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
+          tc_wait_ld();
+          if (empty) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) kv[e] = 0u;
+          }
+          if (key < Sk) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
+              uint4 o;
+              o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
+              o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
+              o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
+              o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
+              *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace fabw
 
 // Attention backward core on tcgen05 (head_dim 64): writes dK, dV and
@@ -770,7 +1147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // and the element predicate) selects the sparse instantiation.
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                        torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                       double scale, const AttnSparse& sp) {
+                       double scale, const AttnSparse& sp, bool pipelined) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 64, "tcgen05 attention backward supports head_dim 64");
@@ -811,7 +1188,7 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   auto st = cur_stream();
 #define FABW(C_, SP_)                                                  \
   {                                                                    \
-    auto kern = fabw::fa_bwd_tc_kernel<C_, SP_>;                       \
+    auto kern = pipelined ? fabw::fa_bwd_pipe_kernel<C_, SP_> : fabw::fa_bwd_tc_kernel<C_, SP_>; \
     set_max_smem((const void*)kern, fabw::SMEM);                       \
     kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p); \
   }

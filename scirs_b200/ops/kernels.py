@@ -28,8 +28,17 @@ OPT_MODES = {"adam": 0, "adamw": 1, "sgd": 2, "rmsprop": 3, "adagrad": 4}
 # Attention forward: "tcgen05" (one 128-query tile per CTA, O in registers),
 # "pingpong" (two tiles per CTA, O in TMEM, P through TMEM) or "mma".
 ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "pingpong_x2")
-# Attention backward: "tcgen05" (head_dim 64; other head dims use mma) or "mma".
+# Attention backward: "tcgen05" (tcgen05 kernels, serial schedule), "tcgen05_pipe"
+# (tcgen05 kernels; the tensor core overlaps the softmax-gradient warps) or "mma".
 ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05")
+_BWD_CODES = {"mma": 0, "tcgen05": 1, "tcgen05_pipe": 2}
+
+
+def _bwd_code(sparse: bool = False) -> int:
+    code = _BWD_CODES.get(ATTN_BWD_IMPL)
+    if code is None:
+        raise ValueError(f"unknown attention backward implementation {ATTN_BWD_IMPL!r}")
+    return max(code, 1) if sparse else code
 
 
 class _Stats:
@@ -337,10 +346,11 @@ def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, causal=Tr
     if q.is_cuda:
         if plan is not None:
             _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta,
-                                          bool(plan.pattern.causal), float(scale), 1, **plan.kernel_args(True))
+                                          bool(plan.pattern.causal), float(scale), _bwd_code(True),
+                                          **plan.kernel_args(True))
         else:
             _ext.kernels().flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, dq_acc, delta, bool(causal),
-                                          float(scale), 1 if ATTN_BWD_IMPL == "tcgen05" else 0)
+                                          float(scale), _bwd_code())
         _count(3)
         return
     with torch.enable_grad():
