@@ -566,10 +566,11 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 // here); delta fp32 scratch [B*H*S].
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                        torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                       double scale, const AttnSparse& sp, bool pipelined);
+                       double scale, const AttnSparse& sp, int schedule);
 
 // impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernels (serial schedule),
-// 2 = tcgen05 kernels with the pipelined schedule.
+// 2 = tcgen05 kernels with the pipelined schedule, 3 = pipelined and, for head_dim 64
+// without a sparsity pattern, persistent (one CTA per SM).
 void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                          torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
                          double scale, const AttnSparse& sp, bool pipelined);
@@ -636,9 +637,9 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
     SCIRS_CHECK_LAUNCH();
   }
   if (impl >= 1 && HD == 64) {
-    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, impl == 2);
+    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, (int)impl - 1);
   } else if (impl >= 1 && HD == 128) {
-    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, impl == 2);
+    flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, impl >= 2);
   } else {
   dim3 grid((unsigned)((S + 63) / 64), (unsigned)(B * H));
 #define FA_BWD(HD_, CAUSAL_)                                                                             \

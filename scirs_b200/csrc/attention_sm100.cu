@@ -1138,6 +1138,431 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Persistent head_dim-64 backward (non-sparse): one CTA per SM walks the
+// (key tile, batch x head) work items j = blockIdx.x, + gridDim.x, ... in the
+// order kb-major (for causal attention the key tiles with the most query
+// blocks come first, so the tail of the launch is short). The per-block
+// schedule is the pipelined one above, run as ONE stream of query blocks
+// across all of a CTA's tiles, so the fixed cost of a tile (TMEM allocation,
+// barrier set-up, K / V load latency, pipeline fill and drain, dK / dV
+// write-out) overlaps the neighbouring tiles' work:
+//   * K / V are double-buffered; the TMA warp loads the next tile's pair
+//     while the current tile's last query blocks are in flight;
+//   * S^T of the next tile's first block is issued before this tile ends;
+//   * the drain warps copy dK / dV out of TMEM right after the tile's last
+//     MMA, release the columns (dkv_free) and write them to global memory
+//     while the next tile's first block runs.
+// Barrier phases follow a per-CTA block counter g (blocks) and tile counter lt.
+// ---------------------------------------------------------------------------
+namespace ps {
+constexpr int OFF_K = 0;                       // 2 stages x 16 KB
+constexpr int OFF_V = OFF_K + 2 * T_BYTES;     // 2 stages
+constexpr int OFF_Q = OFF_V + 2 * T_BYTES;     // 2 stages
+constexpr int OFF_DO = OFF_Q + 2 * T_BYTES;    // 2 stages
+constexpr int OFF_DST = OFF_DO + 2 * T_BYTES;  // dS^T [key][q] bf16, 32 KB
+constexpr int OFF_DQS = OFF_DST + P_BYTES;     // 4 warps x 2 slots x 4 KB
+constexpr int OFF_LD = OFF_DQS + 4 * 2 * 4096; // lse / delta [2][2][128] fp32
+constexpr int OFF_BAR = OFF_LD + 4 * 128 * 4;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+
+struct Tile {
+  int b, h, k0, i0, niter;
+};
+__device__ __forceinline__ Tile tile_of(int j, int BH, int H, int nq, bool causal) {
+  const int kb = j / BH, bh = j - kb * BH;
+  Tile t;
+  t.b = bh / H;
+  t.h = bh - t.b * H;
+  t.k0 = kb * BK;
+  t.i0 = causal ? kb : 0;
+  t.niter = causal ? nq - kb : nq;
+  return t;
+}
+}  // namespace ps
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                          const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  using namespace ps;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ps::OFF_BAR);
+  uint64_t* kv_full = bars + 0;    // [2]
+  uint64_t* kv_empty = bars + 2;   // [2]
+  uint64_t* qdo_full = bars + 4;   // [2]
+  uint64_t* qdo_empty = bars + 6;  // [2]
+  uint64_t* s_full = bars + 8;
+  uint64_t* s_free = bars + 9;
+  uint64_t* dp_full = bars + 10;
+  uint64_t* pt_full = bars + 11;
+  uint64_t* pt_free = bars + 12;
+  uint64_t* ds_full = bars + 13;
+  uint64_t* dq_full = bars + 14;
+  uint64_t* dq_free = bars + 15;
+  uint64_t* dkv_full = bars + 16;
+  uint64_t* dkv_free = bars + 17;
+  uint64_t* drain = bars + 18;
+  uint64_t* ld_bar = bars + 19;    // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 21);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* sLD = reinterpret_cast<float*>(smem + ps::OFF_LD);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.S, Sk = p.Sk, H = p.H;
+  const int BH = p.B * H;
+  const int nq = (S + BQ - 1) / BQ;
+  const int T = ((Sk + BK - 1) / BK) * BH;
+  const int G = gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&ld_bar[i], 4);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(dp_full, 1);
+    mbar_init(pt_full, 8);
+    mbar_init(pt_free, 1);
+    mbar_init(ds_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(dkv_full, 1);
+    mbar_init(dkv_free, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmDO);
+    prefetch_tmap(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + HD, T_DQ = 256 + 2 * HD, T_PT = 448;
+
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsCtl>();
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int j = blockIdx.x, lt = 0; j < T && ok; j += G, ++lt) {
+        const Tile tl = tile_of(j, BH, H, nq, CAUSAL);
+        const int col = tl.h * HD;
+        const int ks = lt & 1;
+        if (!mbar_wait(&kv_empty[ks], ((lt >> 1) & 1) ^ 1, p.st, 63, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[ks], 2 * T_BYTES);
+        tma_load_2d(smem + ps::OFF_K + ks * T_BYTES, &tmK, &kv_full[ks], col, tl.b * Sk + tl.k0);
+        tma_load_2d(smem + ps::OFF_V + ks * T_BYTES, &tmV, &kv_full[ks], col, tl.b * Sk + tl.k0);
+        for (int n = 0; n < tl.niter; ++n, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(&qdo_empty[st], ((g >> 1) & 1) ^ 1, p.st, 50, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&qdo_full[st], 2 * T_BYTES);
+          const int row = tl.b * S + (tl.i0 + n) * BQ;
+          tma_load_2d(smem + ps::OFF_Q + st * T_BYTES, &tmQ, &qdo_full[st], col, row);
+          tma_load_2d(smem + ps::OFF_DO + st * T_BYTES, &tmDO, &qdo_full[st], col, row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane == 0) {
+      const uint32_t ds_addr = smem_u32(smem + ps::OFF_DST);
+      auto k_at = [&](int lt) { return smem_u32(smem + ps::OFF_K + (lt & 1) * T_BYTES); };
+      auto v_at = [&](int lt) { return smem_u32(smem + ps::OFF_V + (lt & 1) * T_BYTES); };
+      auto q_at = [&](int g) { return smem_u32(smem + ps::OFF_Q + (g & 1) * T_BYTES); };
+      auto do_at = [&](int g) { return smem_u32(smem + ps::OFF_DO + (g & 1) * T_BYTES); };
+      auto issue_s = [&](int lt, int g) {
+        const uint32_t k_addr = k_at(lt), q_addr = q_at(g);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_S, umma_desc_sw128(k_addr + kk * 32, 16, 1024),
+                        umma_desc_sw128(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        tc_commit(s_full);
+      };
+      auto issue_dp = [&](int lt, int g) {
+        const uint32_t v_addr = v_at(lt), do_addr = do_at(g);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_DP, umma_desc_sw128(v_addr + kk * 32, 16, 1024),
+                        umma_desc_sw128(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        tc_commit(dp_full);
+      };
+      // cursor over the CTA's stream of query blocks: (tile counter, item, block in tile)
+      int lt = 0, j = blockIdx.x, n = 0;
+      int niter = j < T ? tile_of(j, BH, H, nq, CAUSAL).niter : 0;
+      bool ok = true;
+      if (j < T) {
+        ok = mbar_wait(&kv_full[0], 0, p.st, 64, abort_flag) && mbar_wait(&qdo_full[0], 0, p.st, 52, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_dp(0, 0);
+        }
+      }
+      for (int g = 0; j < T && ok; ++g) {
+        // the block after this one
+        int lt2 = lt, j2 = j, n2 = n + 1, niter2 = niter;
+        if (n2 == niter) {
+          ++lt2;
+          j2 += G;
+          n2 = 0;
+          niter2 = j2 < T ? tile_of(j2, BH, H, nq, CAUSAL).niter : 0;
+        }
+        const bool has_next = j2 < T;
+        if (has_next) {
+          ok = (n2 != 0 || mbar_wait(&kv_full[lt2 & 1], (lt2 >> 1) & 1, p.st, 64, abort_flag)) &&
+               mbar_wait(&qdo_full[(g + 1) & 1], ((g + 1) >> 1) & 1, p.st, 52, abort_flag) &&
+               mbar_wait(s_free, g & 1, p.st, 53, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(lt2, g + 1);
+        }
+        if (!mbar_wait(pt_full, g & 1, p.st, 54, abort_flag)) { ok = false; break; }
+        // a tile's first dV / dK overwrite the accumulators: the drain warps must
+        // have copied the previous tile's dK / dV out
+        if (n == 0 && lt > 0 && !mbar_wait(dkv_free, (lt - 1) & 1, p.st, 65, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t q_addr = q_at(g), do_addr = do_at(g), k_addr = k_at(lt);
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8, umma_desc_sw128(do_addr + kk * 2048, 128 * 128, 1024),
+                        IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(pt_free);
+        if (!mbar_wait(ds_full, g & 1, p.st, 56, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 2) * 64 + (kk & 3) * 8,
+                        umma_desc_sw128(q_addr + kk * 2048, 128 * 128, 1024), IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(dq_free, (g & 1) ^ 1, p.st, 55, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_f16_ss(tmem + T_DQ, umma_desc_sw128(ds_addr + kk * 2048, BK * 128, 1024),
+                        umma_desc_sw128(k_addr + kk * 2048, 128 * 128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+        tc_commit(dq_full);
+        tc_commit(&qdo_empty[g & 1]);
+        if (n + 1 == niter) {
+          tc_commit(dkv_full);
+          tc_commit(&kv_empty[lt & 1]);
+        }
+        if (has_next) issue_dp(lt2, g + 1);
+        lt = lt2;
+        j = j2;
+        n = n2;
+        niter = niter2;
+      }
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, nullptr);
+    }
+  }
+  } else if (warp < 12) {
+    setmaxnreg_inc<kRegsDs>();
+    // ------------------------------------------------------------ dS warps
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const bool stager = warp < 8;
+    const int t128 = (warp - 4) * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    uint8_t* ds_row = smem + ps::OFF_DST + r * 128;
+    const float LOG2E = 1.4426950408889634f;
+    const int hq = stager ? 0 : 1;
+    const int c_begin = hq * (BQ / 2);
+    // staged LSE / delta of the next block (stagers), across tile boundaries
+    auto load_ld = [&](int jj, int nn, float& l_, float& d_) {
+      const Tile tl = tile_of(jj, BH, H, nq, CAUSAL);
+      const long base = ((long)tl.b * H + tl.h) * S;
+      const int q = (tl.i0 + nn) * BQ + t128;
+      l_ = q < S ? p.lse[base + q] * LOG2E : 0.f;
+      d_ = q < S ? p.delta[base + q] : 0.f;
+    };
+    float nl = 0.f, nd = 0.f;
+    if (stager && (int)blockIdx.x < T) load_ld(blockIdx.x, 0, nl, nd);
+    bool ok = true;
+    int g = 0;
+    for (int j = blockIdx.x; j < T && ok; j += G) {
+      const Tile tl = tile_of(j, BH, H, nq, CAUSAL);
+      const int key = tl.k0 + r;
+      for (int n = 0; n < tl.niter; ++n, ++g) {
+        const int q0 = (tl.i0 + n) * BQ;
+        float* sL = sLD + (g & 1) * 256;
+        if (stager) {
+          sL[t128] = nl;
+          sL[128 + t128] = nd;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ld_bar[g & 1]);
+          if (n + 1 < tl.niter) load_ld(j, n + 1, nl, nd);
+          else if (j + G < T) load_ld(j + G, 0, nl, nd);
+        }
+        if (!mbar_wait(&ld_bar[g & 1], (g >> 1) & 1, p.st, 60, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(s_full, g & 1, p.st, 57, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sv[64];
+        tmem_ld_32x32b_x32(lane_base + T_S + c_begin, sv);
+        tmem_ld_32x32b_x32(lane_base + T_S + c_begin + 32, sv + 32);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        const bool need_mask = (q0 + BQ > S) || (tl.k0 + BK > Sk) || (CAUSAL && q0 < tl.k0 + BK);
+        const AttnSpan span = attn_queries_of_key<false>(p.sp, key, q0, S, Sk, CAUSAL);
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          float pr[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int ql = c_begin + e + u;
+            float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
+            if (need_mask && !attn_span_has(span, ql)) pv = 0.f;
+            pr[u] = pv;
+          }
+          pk[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+        }
+        if (!mbar_wait(pt_free, (g & 1) ^ 1, p.st, 58, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st_32x32b_x16(lane_base + T_PT + (c_begin >> 1), pk);
+        tmem_st_32x32b_x16(lane_base + T_PT + (c_begin >> 1) + 16, pk + 16);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pt_full);
+        if (!mbar_wait(dp_full, g & 1, p.st, 59, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int c = c_begin + half * 32;
+          uint32_t dv[32];
+          tmem_ld_32x32b_x32(lane_base + T_DP + c, dv);
+          tc_wait_ld();
+          uint32_t dd[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const uint32_t pp = pk[(half * 32 + e) >> 1];
+            const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e]) - sL[128 + c + e]);
+            const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e + 1]) - sL[128 + c + e + 1]);
+            dd[e >> 1] = pack_bf16x2(d0, d1);
+          }
+          tmem_st_32x32b_x16(lane_base + T_DP + hq * 64 + half * 16, dd);
+          const int blk = (c >> 6) * (BK * 128);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int unit = ((c & 63) >> 3) + u;
+            const int so = blk + ((unit ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(ds_row + so) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
+      }
+    }
+  } else {
+    setmaxnreg_dec<kRegsDrain>();
+    // ------------------------------------------------------------ dQ drain and dK / dV write-out
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(q4 * 32) << 16);
+    uint8_t* slot0 = smem + ps::OFF_DQS + (warp - 12) * 8192;
+    uint8_t* slot1 = slot0 + 4096;
+    bool ok = true;
+    int g = 0;
+    for (int j = blockIdx.x, lt = 0; j < T && ok; j += G, ++lt) {
+      const Tile tl = tile_of(j, BH, H, nq, CAUSAL);
+      const int col = tl.h * HD;
+      for (int n = 0; n < tl.niter; ++n, ++g) {
+        if (!mbar_wait(dq_full, g & 1, p.st, 61, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t a0[32], a1[32];
+        tmem_ld_32x32b_x32(lane_base + T_DQ, a0);
+        tmem_ld_32x32b_x32(lane_base + T_DQ + 32, a1);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        if (lane == 0) tma_store_wait_read0();
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          *reinterpret_cast<uint4*>(slot0 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_uint4(a0[4 * u], a0[4 * u + 1], a0[4 * u + 2], a0[4 * u + 3]);
+          *reinterpret_cast<uint4*>(slot1 + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_uint4(a1[4 * u], a1[4 * u + 1], a1[4 * u + 2], a1[4 * u + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int row = tl.b * S + (tl.i0 + n) * BQ + q4 * 32;
+          asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                           &tmDQ), "r"(smem_u32(slot0)), "r"(col), "r"(row) : "memory");
+          asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                           &tmDQ), "r"(smem_u32(slot1)), "r"(col + 32), "r"(row) : "memory");
+          tma_store_commit();
+        }
+      }
+      if (!ok || !mbar_wait(dkv_full, lt & 1, p.st, 62, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      // copy dK / dV out chunk by chunk (TMEM lane = key row); the columns are
+      // released after the last TMEM load, the global stores follow
+      const int key = tl.k0 + r;
+      const long kvrow = (long)tl.b * Sk + key;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const int which = ch >> 1, c = (ch & 1) * 32;
+        uint32_t kv[32];
+        tmem_ld_32x32b_x32(lane_base + (which ? T_DV : T_DK) + c, kv);
+        tc_wait_ld();
+        if (ch == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dkv_free);
+        }
+        if (key < Sk) {
+          bf16* dst = which ? (p.dv + kvrow * p.dv_rs + col) : (p.dk + kvrow * p.dk_rs + col);
+          const float sc = which ? 1.f : p.scale;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float* f = reinterpret_cast<const float*>(kv) + 8 * u;
+            uint4 o;
+            o.x = pack_bf16x2(f[0] * sc, f[1] * sc);
+            o.y = pack_bf16x2(f[2] * sc, f[3] * sc);
+            o.z = pack_bf16x2(f[4] * sc, f[5] * sc);
+            o.w = pack_bf16x2(f[6] * sc, f[7] * sc);
+            *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+          }
+        }
+      }
+    }
+    if (lane == 0) tma_store_wait0();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace fabw
 
 // Attention backward core on tcgen05 (head_dim 64): writes dK, dV and
@@ -1147,7 +1572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // and the element predicate) selects the sparse instantiation.
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                        torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
-                       double scale, const AttnSparse& sp, bool pipelined) {
+                       double scale, const AttnSparse& sp, int schedule) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 64, "tcgen05 attention backward supports head_dim 64");
@@ -1184,8 +1609,20 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   p.st = status_ptr(q.get_device());
   p.sp = sp;
   const bool sparse = sp.ptr != nullptr;
+  const bool pipelined = schedule >= 1;
   dim3 grid((unsigned)((Sk + 127) / 128), (unsigned)(B * H));
   auto st = cur_stream();
+  if (schedule == 2 && !sparse) {
+    // persistent: one CTA per SM over the (key tile, batch x head) items
+    const long items = (long)grid.x * grid.y;
+    const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    const unsigned g = (unsigned)std::min<long>(items, sms);
+    auto kern = causal ? fabw::fa_bwd_persist_kernel<true> : fabw::fa_bwd_persist_kernel<false>;
+    set_max_smem((const void*)kern, fabw::ps::SMEM);
+    kern<<<g, fabw::kThreads, fabw::ps::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
+    SCIRS_CHECK_LAUNCH();
+    return;
+  }
 #define FABW(C_, SP_)                                                  \
   {                                                                    \
     auto kern = pipelined ? fabw::fa_bwd_pipe_kernel<C_, SP_> : fabw::fa_bwd_tc_kernel<C_, SP_>; \
