@@ -43,10 +43,17 @@ constexpr int BM = 128, BN = 128;
 // 12 warps = 3 warpgroups: warpgroup 0 = TMA warp, MMA warp and two idle
 // warps (registers given away), warpgroups 1 and 2 = the softmax warps of
 // tile 0 and tile 1 (registers taken). The block launches with 168 registers
-// per thread (65536 / 384 rounded down to 8): 128 x 56 + 256 x 224 = 384 x 168.
+// per thread (65536 / 384 rounded down to 8), split as below.
 constexpr int kThreads = 384;
-constexpr int kRegsLaunch = 168, kRegsCtl = 56, kRegsSoftmax = 224;
-static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split exceeds the launch");
+// The control warps walk the persistent item list and keep 72 registers, the softmax warps
+// 216: 128 x 72 + 256 x 216 = 384 x 168 (ptxas: no spills at head_dim 64).
+constexpr int kRegsLaunch = 168;
+template <int HD>
+struct Regs {
+  static constexpr int kCtl = 72;
+  static constexpr int kSoftmax = 216;
+  static_assert(128 * kCtl + 256 * kSoftmax <= kThreads * kRegsLaunch, "register split exceeds the launch");
+};
 constexpr float kRescaleLog2 = 8.f;  // raise the reference max only past 2^8
 
 struct Params {
@@ -141,25 +148,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + 2;            // [2] tiles (4 warps each)
   uint64_t* o_final = p_full + 2;           // [2] tiles
   uint64_t* drain = o_final + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* q_empty = drain + 1;            // the MMAs of an item are done with Q
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(q_empty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.S, Sk = p.Sk, H = p.H;
-  const int qp = gridDim.x - 1 - blockIdx.x;  // longest causal work first
-  const int b = blockIdx.y / H, h = blockIdx.y % H;
-  const int q0 = qp * 2 * BM;
-  const int row_base = b * S;   // query / output rows
-  const int kv_base = b * Sk;   // key / value rows
+  // Work items: (query pair qp, batch x head bh); item i has qp = nqp - 1 - i / BH (the longest causal
+  // work first) and bh = i % BH. A CTA takes items item0, item0 + istride, ...: with a grid of
+  // (nqp, B*H) that is exactly one item per CTA, with a grid of one CTA per SM the kernel is persistent.
+  const int BH = p.B * H;
+  const int nqp = (S + 2 * BM - 1) / (2 * BM);
+  const int nitems = nqp * BH;
+  const int item0 = blockIdx.x * gridDim.y + blockIdx.y;
+  const int istride = gridDim.x * gridDim.y;
   const int nkv_all = (Sk + BN - 1) / BN;
-  // SPARSE: this CTA visits the key blocks of its list (both tiles)
-  const int lb = SPARSE ? __ldg(p.sp.ptr + qp) : 0;
-  const int cnt = SPARSE ? __ldg(p.sp.ptr + qp + 1) - lb : 0;
-  auto kblk = [&](int j) -> int { return SPARSE ? __ldg(p.sp.idx + lb + j) : j; };
-  // key blocks each tile needs (tile t covers queries [q0 + 128 t, +128))
-  const int nkv0 = (q0 >= S) ? 0 : (SPARSE ? cnt : (CAUSAL ? min(nkv_all, q0 / BM + 1) : nkv_all));
-  const int nkv1 = (q0 + BM >= S) ? 0 : (SPARSE ? cnt : (CAUSAL ? min(nkv_all, q0 / BM + 2) : nkv_all));
-  const int nkv = max(nkv0, nkv1);
+  struct Item {
+    int b, h, q0, lb, nkv0, nkv1, nkv;
+  };
+  auto item_of = [&](int i) -> Item {
+    Item I;
+    const int qp = nqp - 1 - i / BH, bh = i % BH;
+    I.b = bh / H;
+    I.h = bh % H;
+    I.q0 = qp * 2 * BM;
+    // SPARSE: the item visits the key blocks of its list (both tiles)
+    I.lb = SPARSE ? __ldg(p.sp.ptr + qp) : 0;
+    const int cnt = SPARSE ? __ldg(p.sp.ptr + qp + 1) - I.lb : 0;
+    // key blocks each tile needs (tile t covers queries [q0 + 128 t, +128))
+    I.nkv0 = (I.q0 >= S) ? 0 : (SPARSE ? cnt : (CAUSAL ? min(nkv_all, I.q0 / BM + 1) : nkv_all));
+    I.nkv1 = (I.q0 + BM >= S) ? 0 : (SPARSE ? cnt : (CAUSAL ? min(nkv_all, I.q0 / BM + 2) : nkv_all));
+    I.nkv = max(I.nkv0, I.nkv1);
+    return I;
+  };
+  auto kblk = [&](const Item& I, int j) -> int { return SPARSE ? __ldg(p.sp.idx + I.lb + j) : j; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -174,6 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_final[i], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(q_empty, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmQ);
@@ -189,41 +212,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   if (warp < 4) {
-  setmaxnreg_dec<kRegsCtl>();
+  setmaxnreg_dec<Regs<HD>::kCtl>();
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
-      const int col = h * HD;
-      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+      int jg = 0;  // K / V ring position over all of this CTA's key blocks
+      bool ok = true;
+      for (int it = item0, ii = 0; it < nitems && ok; it += istride, ++ii) {
+        const Item I = item_of(it);
+        const int col = I.h * HD;
+        // the previous item's score MMAs have read Q
+        if (!mbar_wait(q_empty, (ii & 1) ^ 1, p.st, 49, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
-          tma_load_2d(smem + C::OFF_Q + t * C::Q_BYTES + c * (BM * 128), &tmQ, q_full, col + c * 64,
-                      row_base + q0 + t * BM);
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % NST;
-        if (!mbar_wait(&kv_empty[s], ((j / NST) & 1) ^ 1, p.st, 50, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(smem + C::OFF_Q + t * C::Q_BYTES + c * (BM * 128), &tmQ, q_full, col + c * 64,
+                        I.b * S + I.q0 + t * BM);
+        for (int j = 0; j < I.nkv; ++j, ++jg) {
+          const int s = jg % NST;
+          if (!mbar_wait(&kv_empty[s], ((jg / NST) & 1) ^ 1, p.st, 50, abort_flag)) { ok = false; break; }
+          const int krow = I.b * Sk + kblk(I, j) * BN;
+          mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
-          tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + c * (BN * 128), &tmK, &k_full[s], col + c * 64,
-                      kv_base + kblk(j) * BN);
-        mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES + c * (BN * 128), &tmK, &k_full[s], col + c * 64, krow);
+          mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
-          tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + c * (BN * 128), &tmV, &v_full[s], col + c * 64,
-                      kv_base + kblk(j) * BN);
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES + c * (BN * 128), &tmV, &v_full[s], col + c * 64, krow);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, p.st, 51, abort_flag);
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      // jg: K / V ring position of the item's first key block; c0 / c1: blocks of
+      // tile 0 / 1 in earlier items (phases of s_full / p_full)
+      int jg = 0, c0 = 0, c1 = 0;
+      bool ok = true;
       auto issue_s = [&](int t, int j) -> bool {
-        const int s = j % NST;
-        if (!mbar_wait(&k_full[s], (j / NST) & 1, p.st, 52, abort_flag)) return false;
+        const int s = (jg + j) % NST;
+        if (!mbar_wait(&k_full[s], ((jg + j) / NST) & 1, p.st, 52, abort_flag)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + C::OFF_K + s * C::KV_BYTES);
         const uint32_t qa = q_addr + t * C::Q_BYTES;
@@ -237,19 +269,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(&s_full[t]);
         return true;
       };
+      for (int it = item0, ii = 0; it < nitems && ok; it += istride, ++ii) {
+      const Item I = item_of(it);
+      if (!mbar_wait(q_full, ii & 1, p.st, 51, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      if (nkv0 > 0) ok = issue_s(0, 0);
-      if (ok && nkv1 > 0) ok = issue_s(1, 0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % NST;
+      if (I.nkv0 > 0) ok = issue_s(0, 0);
+      if (ok && I.nkv1 > 0) ok = issue_s(1, 0);
+      if (ok && I.nkv <= 1) tc_commit(q_empty);  // every score MMA of the item is issued
+      for (int j = 0; j < I.nkv && ok; ++j) {
+        const int s = (jg + j) % NST;
         bool v_ready = false;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          const int nt = t ? nkv1 : nkv0;
+          const int nt = t ? I.nkv1 : I.nkv0;
           if (!ok || j >= nt) continue;
-          if (!mbar_wait(&p_full[t], j & 1, p.st, 53, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&p_full[t], ((t ? c1 : c0) + j) & 1, p.st, 53, abort_flag)) { ok = false; break; }
           if (!v_ready) {
-            if (!mbar_wait(&v_full[s], (j / NST) & 1, p.st, 54, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&v_full[s], ((jg + j) / NST) & 1, p.st, 54, abort_flag)) { ok = false; break; }
             v_ready = true;
           }
           tc_fence_after();
@@ -268,24 +304,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_commit(&o_final[t]);
           }
         }
+        if (ok && j == I.nkv - 2) tc_commit(q_empty);  // the item's last score MMAs are issued
         if (ok) tc_commit(&kv_empty[s]);
+      }
+      jg += I.nkv;
+      c0 += I.nkv0;
+      c1 += I.nkv1;
       }
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 0, nullptr);
     }
   }
   } else {
-    setmaxnreg_inc<kRegsSoftmax>();
+    setmaxnreg_inc<Regs<HD>::kSoftmax>();
     // ---------------------------------------------------------------- softmax
     const int t = (warp - 4) >> 2;   // tile of this warpgroup
     const int q = warp & 3;          // TMEM lane quarter
     const int r = q * 32 + lane;     // query row within the tile
-    const int qrow = q0 + t * BM + r;
     const uint32_t lane_off = uint32_t(q * 32) << 16;
     const uint32_t s_base = tmem + lane_off + t * BN;
     const uint32_t o_base = tmem + lane_off + 2 * BN + t * HD;
-    const int my_nkv = t ? nkv1 : nkv0;
-    float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     const bool tr = TRACE && q == 0 && lane == 0;
     unsigned long long ph[5] = {0, 0, 0, 0, 0};
@@ -297,8 +335,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tk = now;
       }
     };
+    int cb = 0, ni = 0;  // this tile's blocks in earlier items; earlier items with blocks
+    for (int it = item0; it < nitems && ok; it += istride) {
+    // only the query offset, the tile's block count and the block list start stay live across the
+    // block loop (the softmax warps are at their register limit); the rest is recomputed below
+    const Item I = item_of(it);
+    const int q0 = I.q0;
+    const int my_nkv = t ? I.nkv1 : I.nkv0;
+    float m_ref = -INFINITY, l = 0.f;
     for (int j = 0; j < my_nkv && ok; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, p.st, 55, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], (cb + j) & 1, p.st, 55, abort_flag)) { ok = false; break; }
       tc_fence_after();
       lap(0);
       float sv[BN];
@@ -309,11 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_ld();
       }
       lap(1);
-      const int kv0 = kblk(j) * BN;
+      const int kv0 = kblk(I, j) * BN;
       const bool mask = (kv0 + BN > Sk) || (CAUSAL && kv0 + BN > q0 + t * BM) ||
                         (SPARSE && !attn_block_full(p.sp, q0 + t * BM, q0 + t * BM + BM - 1, kv0, kv0 + BN - 1));
       if (mask) {
-        const AttnSpan span = attn_keys_of_query<SPARSE>(p.sp, qrow, kv0, Sk, CAUSAL);
+        const AttnSpan span = attn_keys_of_query<SPARSE>(p.sp, q0 + t * BM + r, kv0, Sk, CAUSAL);
 #pragma unroll
         for (int e = 0; e < BN; ++e) sv[e] = attn_span_has(span, e) ? sv[e] : -INFINITY;
       }
@@ -408,12 +454,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[t]);
       lap(4);
     }
-    if (TRACE && tr) {
-      unsigned long long* dst = p.trace + ((long)(blockIdx.y * gridDim.x + blockIdx.x) * 2 + t) * 5;
-#pragma unroll
-      for (int k = 0; k < 5; ++k) dst[k] = ph[k];
-    }
-    if (ok && my_nkv > 0 && mbar_wait(&o_final[t], 0, p.st, 56, abort_flag)) {
+    int it2 = it;
+    asm volatile("" : "+r"(it2));  // an opaque copy: recompute the item's fields instead of keeping them
+    const Item I2 = item_of(it2);
+    const int b = I2.b, h = I2.h;
+    const int row_base = b * S;
+    const int qrow = I2.q0 + t * BM + r;
+    const bool fin = ok && my_nkv > 0;
+    if (fin && !mbar_wait(&o_final[t], ni & 1, p.st, 56, abort_flag)) ok = false;
+    if (fin && ok) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       bf16* orow = p.out + (long)(row_base + qrow) * p.o_rs + h * HD;
@@ -441,6 +490,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       bf16* orow = p.out + (long)(row_base + qrow) * p.o_rs + h * HD;
       for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
       p.lse[((long)b * H + h) * S + qrow] = -INFINITY;
+    }
+    cb += my_nkv;
+    ni += my_nkv > 0 ? 1 : 0;
+    }
+    if (TRACE && tr) {
+      unsigned long long* dst = p.trace + ((long)(blockIdx.y * gridDim.x + blockIdx.x) * 2 + t) * 5;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) dst[k] = ph[k];
     }
   }
 
@@ -520,8 +577,11 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   p.Sk = (int)Sk;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
+  // one CTA per (query pair, batch x head) item, or (SCIRS_ATTN_FWD_PERSIST=1)
+  // one CTA per SM walking the items
   dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
-  p.sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, (int64_t)grid.x);
+  const int64_t nqp = grid.x;
+  p.sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, nqp);
   const bool sparse = p.sp.ptr != nullptr || p.sp.bmap != nullptr || p.sp.wl >= 0 || p.sp.ng > 0;
   TORCH_CHECK(!sparse || p.sp.ptr != nullptr, "a sparsity predicate needs block lists");
   if (trace.has_value() && trace->defined()) {
@@ -529,6 +589,13 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
                     trace->numel() >= (long)grid.x * grid.y * 2 * 5,
                 "trace: int64 [grid, 2, 5]");
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
+  }
+  {
+    const char* e = getenv("SCIRS_ATTN_FWD_PERSIST");
+    const bool persist = e != nullptr && e[0] == '1' && p.trace == nullptr;
+    const long items = (long)grid.x * grid.y;
+    const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    if (persist && items > sms) grid = dim3((unsigned)sms, 1u);
   }
   auto st = cur_stream();
 #define FA2T(HD_, C_, P_, R_, X_, SP_, ...)                                    \

@@ -1140,10 +1140,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 
 // ---------------------------------------------------------------------------
-// Persistent head_dim-64 backward (non-sparse): one CTA per SM walks the
-// (key tile, batch x head) work items j = blockIdx.x, + gridDim.x, ... in the
-// order kb-major (for causal attention the key tiles with the most query
-// blocks come first, so the tail of the launch is short). The per-block
+// Persistent head_dim-64 backward (non-sparse): one CTA per SM walks pairs
+// of key tiles (see Sched: balanced under a causal mask, heads in order so
+// that concurrent CTAs share L2-resident Q / dO / dQ). The per-block
 // schedule is the pipelined one above, run as ONE stream of query blocks
 // across all of a CTA's tiles, so the fixed cost of a tile (TMEM allocation,
 // barrier set-up, K / V load latency, pipeline fill and drain, dK / dV
@@ -1170,16 +1169,33 @@ constexpr int SMEM = OFF_BAR + 256 + 1024;
 struct Tile {
   int b, h, k0, i0, niter;
 };
-__device__ __forceinline__ Tile tile_of(int j, int BH, int H, int nq, bool causal) {
-  const int kb = j / BH, bh = j - kb * BH;
-  Tile t;
-  t.b = bh / H;
-  t.h = bh - t.b * H;
-  t.k0 = kb * BK;
-  t.i0 = causal ? kb : 0;
-  t.niter = causal ? nq - kb : nq;
-  return t;
-}
+// The CTA's tiles. Work is handed out in PAIRS p = blockIdx.x + m * gridDim.x: pair p of
+// (batch x head) bh = p / half covers the key tiles kp = p % half and nkb - 1 - kp (one tile
+// when they coincide), so under a causal mask every pair holds nkb + 1 query blocks and a static
+// assignment is balanced. Pairs are bh-major: the CTAs running at the same time share a few
+// heads, whose Q, dO and dQ accumulator then stay in L2. A tile is named by code = 2 m + second.
+struct Sched {
+  int P, half, nkb, G, BH, H, nq;
+  bool causal;
+  __device__ __forceinline__ int pair(int code) const { return (int)blockIdx.x + (code >> 1) * G; }
+  __device__ __forceinline__ bool valid(int code) const { return pair(code) < P; }
+  __device__ __forceinline__ int next(int code) const {
+    const int kp = pair(code) % half;
+    return ((code & 1) == 0 && nkb - 1 - kp != kp) ? code + 1 : (code | 1) + 1;
+  }
+  __device__ __forceinline__ Tile tile(int code) const {
+    const int p = pair(code);
+    const int bh = p / half, kp = p - bh * half;
+    const int kb = (code & 1) ? nkb - 1 - kp : kp;
+    Tile t;
+    t.b = bh / H;
+    t.h = bh - t.b * H;
+    t.k0 = kb * BK;
+    t.i0 = causal ? kb : 0;
+    t.niter = causal ? nq - kb : nq;
+    return t;
+  }
+};
 }  // namespace ps
 
 template <bool CAUSAL>
@@ -1215,8 +1231,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int S = p.S, Sk = p.Sk, H = p.H;
   const int BH = p.B * H;
   const int nq = (S + BQ - 1) / BQ;
-  const int T = ((Sk + BK - 1) / BK) * BH;
-  const int G = gridDim.x;
+  ps::Sched sc;
+  sc.nkb = (Sk + BK - 1) / BK;
+  sc.half = (sc.nkb + 1) / 2;
+  sc.BH = BH;
+  sc.P = BH * sc.half;
+  sc.G = gridDim.x;
+  sc.H = H;
+  sc.nq = nq;
+  sc.causal = CAUSAL;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -1262,8 +1285,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int g = 0;
       bool ok = true;
-      for (int j = blockIdx.x, lt = 0; j < T && ok; j += G, ++lt) {
-        const Tile tl = tile_of(j, BH, H, nq, CAUSAL);
+      for (int j = 0, lt = 0; sc.valid(j) && ok; j = sc.next(j), ++lt) {
+        const Tile tl = sc.tile(j);
         const int col = tl.h * HD;
         const int ks = lt & 1;
         if (!mbar_wait(&kv_empty[ks], ((lt >> 1) & 1) ^ 1, p.st, 63, abort_flag)) break;
@@ -1305,10 +1328,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(dp_full);
       };
       // cursor over the CTA's stream of query blocks: (tile counter, item, block in tile)
-      int lt = 0, j = blockIdx.x, n = 0;
-      int niter = j < T ? tile_of(j, BH, H, nq, CAUSAL).niter : 0;
+      int lt = 0, j = 0, n = 0;
+      int niter = sc.valid(j) ? sc.tile(j).niter : 0;
       bool ok = true;
-      if (j < T) {
+      if (sc.valid(j)) {
         ok = mbar_wait(&kv_full[0], 0, p.st, 64, abort_flag) && mbar_wait(&qdo_full[0], 0, p.st, 52, abort_flag);
         if (ok) {
           tc_fence_after();
@@ -1316,16 +1339,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_dp(0, 0);
         }
       }
-      for (int g = 0; j < T && ok; ++g) {
+      for (int g = 0; sc.valid(j) && ok; ++g) {
         // the block after this one
         int lt2 = lt, j2 = j, n2 = n + 1, niter2 = niter;
         if (n2 == niter) {
           ++lt2;
-          j2 += G;
+          j2 = sc.next(j);
           n2 = 0;
-          niter2 = j2 < T ? tile_of(j2, BH, H, nq, CAUSAL).niter : 0;
+          niter2 = sc.valid(j2) ? sc.tile(j2).niter : 0;
         }
-        const bool has_next = j2 < T;
+        const bool has_next = sc.valid(j2);
         if (has_next) {
           ok = (n2 != 0 || mbar_wait(&kv_full[lt2 & 1], (lt2 >> 1) & 1, p.st, 64, abort_flag)) &&
                mbar_wait(&qdo_full[(g + 1) & 1], ((g + 1) >> 1) & 1, p.st, 52, abort_flag) &&
@@ -1387,18 +1410,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c_begin = hq * (BQ / 2);
     // staged LSE / delta of the next block (stagers), across tile boundaries
     auto load_ld = [&](int jj, int nn, float& l_, float& d_) {
-      const Tile tl = tile_of(jj, BH, H, nq, CAUSAL);
+      const Tile tl = sc.tile(jj);
       const long base = ((long)tl.b * H + tl.h) * S;
       const int q = (tl.i0 + nn) * BQ + t128;
       l_ = q < S ? p.lse[base + q] * LOG2E : 0.f;
       d_ = q < S ? p.delta[base + q] : 0.f;
     };
     float nl = 0.f, nd = 0.f;
-    if (stager && (int)blockIdx.x < T) load_ld(blockIdx.x, 0, nl, nd);
+    if (stager && sc.valid(0)) load_ld(0, 0, nl, nd);
     bool ok = true;
     int g = 0;
-    for (int j = blockIdx.x; j < T && ok; j += G) {
-      const Tile tl = tile_of(j, BH, H, nq, CAUSAL);
+    for (int j = 0; sc.valid(j) && ok; j = sc.next(j)) {
+      const Tile tl = sc.tile(j);
       const int key = tl.k0 + r;
       for (int n = 0; n < tl.niter; ++n, ++g) {
         const int q0 = (tl.i0 + n) * BQ;
@@ -1409,7 +1432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&ld_bar[g & 1]);
           if (n + 1 < tl.niter) load_ld(j, n + 1, nl, nd);
-          else if (j + G < T) load_ld(j + G, 0, nl, nd);
+          else if (sc.valid(sc.next(j))) load_ld(sc.next(j), 0, nl, nd);
         }
         if (!mbar_wait(&ld_bar[g & 1], (g >> 1) & 1, p.st, 60, abort_flag)) { ok = false; break; }
         if (!mbar_wait(s_full, g & 1, p.st, 57, abort_flag)) { ok = false; break; }
@@ -1486,8 +1509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* slot1 = slot0 + 4096;
     bool ok = true;
     int g = 0;
-    for (int j = blockIdx.x, lt = 0; j < T && ok; j += G, ++lt) {
-      const Tile tl = tile_of(j, BH, H, nq, CAUSAL);
+    for (int j = 0, lt = 0; sc.valid(j) && ok; j = sc.next(j), ++lt) {
+      const Tile tl = sc.tile(j);
       const int col = tl.h * HD;
       for (int n = 0; n < tl.niter; ++n, ++g) {
         if (!mbar_wait(dq_full, g & 1, p.st, 61, abort_flag)) { ok = false; break; }
@@ -1614,9 +1637,9 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   auto st = cur_stream();
   if (schedule == 2 && !sparse) {
     // persistent: one CTA per SM over the (key tile, batch x head) items
-    const long items = (long)grid.x * grid.y;
+    const long pairs = (long)((grid.x + 1) / 2) * grid.y;
     const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-    const unsigned g = (unsigned)std::min<long>(items, sms);
+    const unsigned g = (unsigned)std::min<long>(pairs, sms);
     auto kern = causal ? fabw::fa_bwd_persist_kernel<true> : fabw::fa_bwd_persist_kernel<false>;
     set_max_smem((const void*)kern, fabw::ps::SMEM);
     kern<<<g, fabw::kThreads, fabw::ps::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
