@@ -22,6 +22,7 @@ override file values (`apply_env`):
     SCIRS_PRECISION    bf16 | fp32        compute dtype of the layer API on CUDA
     SCIRS_THREADS      n                  host threads (torch.set_num_threads)
     SCIRS_ATTN_FWD / SCIRS_ATTN_BWD       attention kernel variant
+    SCIRS_ATTN_FWD_PERSIST  0 | 1         attention forward on one CTA per SM
     SCIRS_<SECTION>_<FIELD>               any field, e.g. SCIRS_PARALLEL_DP=8,
                                           SCIRS_DATA_GLOBAL_BATCH=64
 

@@ -570,7 +570,7 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
 
 // impl: 0 = warp-level mma.sync kernel, 1 = tcgen05 kernels (serial schedule),
 // 2 = tcgen05 kernels with the pipelined schedule, 3 = pipelined and, for head_dim 64
-// without a sparsity pattern, persistent (one CTA per SM).
+// without a sparsity pattern, persistent (one CTA per SM), 4 = 3 up to 1,024 keys, else 2.
 void flash_attn_bwd_h128(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor lse,
                          torch::Tensor delta, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc, bool causal,
                          double scale, const AttnSparse& sp, bool pipelined);
@@ -637,7 +637,9 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
     SCIRS_CHECK_LAUNCH();
   }
   if (impl >= 1 && HD == 64) {
-    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, (int)impl - 1);
+    // auto (4): persistent up to 1,024 keys (measured faster there), pipelined above
+    const int sched = impl == 4 ? (Sk <= 1024 ? 2 : 1) : (int)impl - 1;
+    flash_attn_bwd_tc(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, sched);
   } else if (impl >= 1 && HD == 128) {
     flash_attn_bwd_h128(dout, q, k, v, lse, delta, dk, dv, dq_acc, causal, scale, sp, impl >= 2);
   } else {

@@ -577,8 +577,8 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   p.Sk = (int)Sk;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
-  // one CTA per (query pair, batch x head) item, or (SCIRS_ATTN_FWD_PERSIST=1)
-  // one CTA per SM walking the items
+  // one CTA per (query pair, batch x head) item, or one CTA per SM walking the
+  // items (SCIRS_ATTN_FWD_PERSIST=1 / 0 forces either)
   dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
   const int64_t nqp = grid.x;
   p.sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, nqp);
@@ -592,7 +592,9 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   }
   {
     const char* e = getenv("SCIRS_ATTN_FWD_PERSIST");
-    const bool persist = e != nullptr && e[0] == '1' && p.trace == nullptr;
+    // default: persistent for head_dim 64, and for 128 up to 1,024 queries (measured faster there)
+    const bool dflt = HD == 64 || S <= 1024;
+    const bool persist = (e != nullptr ? e[0] == '1' : dflt) && p.trace == nullptr;
     const long items = (long)grid.x * grid.y;
     const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
     if (persist && items > sms) grid = dim3((unsigned)sms, 1u);

@@ -416,9 +416,9 @@ constexpr int HD = 64, BK = 128, BQ = 128;
 // 16 warps = 4 warpgroups: 0 = TMA warp, MMA warp, two idle warps; 1 and 2 =
 // the eight dS warps; 3 = the dQ-drain / dK-dV epilogue warps. Launched with
 // 128 registers per thread (65536 / 512); the control and drain warpgroups
-// give registers to the dS warpgroups: 128 x 56 + 256 x 176 + 128 x 96 <= 512 x 128.
+// give registers to the dS warpgroups: 128 x 64 + 256 x 176 + 128 x 96 = 512 x 128.
 constexpr int kThreads = 512;
-constexpr int kRegsLaunch = 128, kRegsCtl = 56, kRegsDs = 176, kRegsDrain = 96;
+constexpr int kRegsLaunch = 128, kRegsCtl = 64, kRegsDs = 176, kRegsDrain = 96;
 static_assert(128 * kRegsCtl + 256 * kRegsDs + 128 * kRegsDrain <= kThreads * kRegsLaunch,
               "register split exceeds the launch");
 constexpr int T_BYTES = 128 * HD * 2;    // one 128-row x 64-col bf16 tile (16 KB)
@@ -448,6 +448,11 @@ struct Params {
   float scale, scale_log2;
   DevStatus* st;
   AttnSparse sp;  // SPARSE: per key tile, the list of 128-query blocks to visit
+  // optional phase timing of the pipelined kernel (clock64 cycles summed over a CTA's blocks):
+  // [CTA][16] = dS warp 4 lane 0: ld_bar, s_full, S copy, exponentials, pt_free, P store,
+  // dp_full, dS; MMA thread: next-S waits, S issue, pt_full, ds_full, dq_free, other issue;
+  // [14] = blocks; nullptr = off
+  unsigned long long* trace;
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -785,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // TMEM columns: S^T [0,128), dP^T / dS^T [128,256), dV [256,320),
 // dK [320,384), dQ [384,448), P^T [448,512).
 // ---------------------------------------------------------------------------
-template <bool CAUSAL, bool SPARSE = false>
+template <bool CAUSAL, bool SPARSE = false, bool TRACE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -884,21 +889,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ds_addr = smem_u32(smem + OFF_DST);
       auto q_at = [&](int n) { return smem_u32(smem + OFF_Q + (n & 1) * T_BYTES); };
       auto do_at = [&](int n) { return smem_u32(smem + OFF_DO + (n & 1) * T_BYTES); };
+      // loop-invariant descriptors (K, V, dS^T); the Q / dO ones are built once per block and
+      // stepped through k with desc_off
+      const uint64_t dk_km = umma_desc_sw128(k_addr, 16, 1024), dv_km = umma_desc_sw128(v_addr, 16, 1024);
+      const uint64_t dk_mn = umma_desc_sw128(k_addr, 128 * 128, 1024);
+      const uint64_t dds_mn = umma_desc_sw128(ds_addr, BK * 128, 1024);
       auto issue_s = [&](int n) {  // S^T = K Q_n^T -> T_S
-        const uint32_t q_addr = q_at(n);
+        const uint64_t dq = umma_desc_sw128(q_at(n), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          tc_mma_f16_ss(tmem + T_S, umma_desc_sw128(k_addr + kk * 32, 16, 1024),
-                        umma_desc_sw128(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_S, desc_off(dk_km, kk * 32), desc_off(dq, kk * 32), IDESC_S, kk > 0 ? 1u : 0u);
         tc_commit(s_full);
       };
       auto issue_dp = [&](int n) {  // dP^T = V dO_n^T -> T_DP
-        const uint32_t do_addr = do_at(n);
+        const uint64_t ddo = umma_desc_sw128(do_at(n), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          tc_mma_f16_ss(tmem + T_DP, umma_desc_sw128(v_addr + kk * 32, 16, 1024),
-                        umma_desc_sw128(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_DP, desc_off(dv_km, kk * 32), desc_off(ddo, kk * 32), IDESC_S, kk > 0 ? 1u : 0u);
         tc_commit(dp_full);
+      };
+      unsigned long long tm[6] = {0, 0, 0, 0, 0, 0};
+      long long tkm = TRACE ? clock64() : 0;
+      auto lapm = [&](int q) {
+        if (TRACE) {
+          const long long now = clock64();
+          tm[q] += (unsigned long long)(now - tkm);
+          tkm = now;
+        }
       };
       bool ok = mbar_wait(kv_full, 0, p.st, 51, abort_flag);
       if (ok && niter > 0) {
@@ -913,37 +930,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = n & 1;
         if (n + 1 < niter) {
           // next block's scores as soon as this block's S^T has been copied out
+          lapm(5);
           ok = mbar_wait(&qdo_full[(n + 1) & 1], ((n + 1) >> 1) & 1, p.st, 52, abort_flag) &&
                mbar_wait(s_free, n & 1, p.st, 53, abort_flag);
           if (!ok) break;
+          lapm(0);
           tc_fence_after();
           issue_s(n + 1);
+          lapm(1);
         }
         if (!mbar_wait(pt_full, n & 1, p.st, 54, abort_flag)) { ok = false; break; }
+        lapm(2);
         tc_fence_after();
-        const uint32_t q_addr = q_at(n), do_addr = do_at(n);
+        const uint64_t ddo_mn = umma_desc_sw128(do_at(n), 128 * 128, 1024);
+        const uint64_t dq_mn = umma_desc_sw128(q_at(n), 128 * 128, 1024);
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO: A = P^T from TMEM (8 packed columns per k-step)
-          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8,
-                        umma_desc_sw128(do_addr + kk * 2048, 128 * 128, 1024), IDESC_KV,
+          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8, desc_off(ddo_mn, kk * 2048), IDESC_KV,
                         (n > 0 || kk > 0) ? 1u : 0u);
         tc_commit(pt_free);
+        lapm(5);
         if (!mbar_wait(ds_full, n & 1, p.st, 56, abort_flag)) { ok = false; break; }
+        lapm(3);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q: A = dS^T from TMEM (over the dP^T columns)
-          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 2) * 64 + (kk & 3) * 8,
-                        umma_desc_sw128(q_addr + kk * 2048, 128 * 128, 1024), IDESC_KV,
-                        (n > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 2) * 64 + (kk & 3) * 8, desc_off(dq_mn, kk * 2048),
+                        IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+        lapm(5);
         if (!mbar_wait(dq_free, (n & 1) ^ 1, p.st, 55, abort_flag)) { ok = false; break; }
+        lapm(4);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          tc_mma_f16_ss(tmem + T_DQ, umma_desc_sw128(ds_addr + kk * 2048, BK * 128, 1024),
-                        umma_desc_sw128(k_addr + kk * 2048, 128 * 128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_DQ, desc_off(dds_mn, kk * 2048), desc_off(dk_mn, kk * 2048), IDESC_Q,
+                        kk > 0 ? 1u : 0u);
         tc_commit(dq_full);
         tc_commit(&qdo_empty[st]);
         if (n + 1 < niter) issue_dp(n + 1);
+        lapm(5);
+      }
+      if (TRACE) {
+        unsigned long long* dst = p.trace + (long)(blockIdx.y * gridDim.x + blockIdx.x) * 16;
+#pragma unroll
+        for (int q = 0; q < 6; ++q) dst[8 + q] = tm[q];
+        dst[14] = (unsigned long long)niter;
       }
       tc_commit(dkv_full);
       tc_commit(drain);
@@ -967,6 +998,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float LOG2E = 1.4426950408889634f;
     const int hq = stager ? 0 : 1;         // query half of the block
     const int c_begin = hq * (BQ / 2);
+    const bool tr = TRACE && warp == 4 && lane == 0;
+    unsigned long long td[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    long long tkd = tr ? clock64() : 0;
+    auto lapd = [&](int q) {
+      if (TRACE && tr) {
+        const long long now = clock64();
+        td[q] += (unsigned long long)(now - tkd);
+        tkd = now;
+      }
+    };
     float nl = 0.f, nd = 0.f;              // staged LSE / delta of the next block (stagers)
     if (stager && niter > 0) {
       const int q = qblk(0) * BQ + t128;
@@ -989,7 +1030,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!mbar_wait(&ld_bar[n & 1], (n >> 1) & 1, p.st, 60, abort_flag)) break;
+      lapd(0);
       if (!mbar_wait(s_full, n & 1, p.st, 57, abort_flag)) break;
+      lapd(1);
       tc_fence_after();
       uint32_t sv[64];
       tmem_ld_32x32b_x32(lane_base + T_S + c_begin, sv);
@@ -998,23 +1041,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);  // the tensor core may overwrite S^T now
+      lapd(2);
       const bool need_mask = (q0 + BQ > S) || (k0 + BK > Sk) || (CAUSAL && q0 < k0 + BK) ||
                              (SPARSE && !attn_block_full(p.sp, q0, q0 + BQ - 1, k0, k0 + BK - 1));
       const AttnSpan span = attn_queries_of_key<SPARSE>(p.sp, key, q0, S, Sk, CAUSAL);
       uint32_t pk[32];
 #pragma unroll
-      for (int e = 0; e < 64; e += 2) {
-        float pr[2];
+      for (int e = 0; e < 64; e += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(sL + c_begin + e);  // one broadcast load for 4 queries
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+        float pr[4];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < 4; ++u) {
           const int ql = c_begin + e + u;
-          float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
+          float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -lv[u]));
           if (need_mask && !attn_span_has(span, ql)) pv = 0.f;
           pr[u] = pv;
         }
         pk[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+        pk[(e >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
       }
+      lapd(3);
       if (!mbar_wait(pt_free, (n & 1) ^ 1, p.st, 58, abort_flag)) break;
+      lapd(4);
       tc_fence_after();
       tmem_st_32x32b_x16(lane_base + T_PT + (c_begin >> 1), pk);
       tmem_st_32x32b_x16(lane_base + T_PT + (c_begin >> 1) + 16, pk + 16);
@@ -1022,21 +1071,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pt_full);
+      lapd(5);
       if (!mbar_wait(dp_full, n & 1, p.st, 59, abort_flag)) break;
+      lapd(6);
       tc_fence_after();
+      uint32_t dva[64];  // both halves of this thread's dP^T columns, one TMEM round trip
+      tmem_ld_32x32b_x32(lane_base + T_DP + c_begin, dva);
+      tmem_ld_32x32b_x32(lane_base + T_DP + c_begin + 32, dva + 32);
+      tc_wait_ld();
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int c = c_begin + half * 32;
-        uint32_t dv[32];
-        tmem_ld_32x32b_x32(lane_base + T_DP + c, dv);
-        tc_wait_ld();
+        const uint32_t* dv = dva + half * 32;
         uint32_t dd[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const uint32_t pp = pk[(half * 32 + e) >> 1];
-          const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e]) - sL[128 + c + e]);
-          const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e + 1]) - sL[128 + c + e + 1]);
-          dd[e >> 1] = pack_bf16x2(d0, d1);
+        for (int e = 0; e < 32; e += 4) {
+          const float4 d4 = *reinterpret_cast<const float4*>(sL + 128 + c + e);
+          const uint32_t pa = pk[(half * 32 + e) >> 1], pb = pk[((half * 32 + e) >> 1) + 1];
+          dd[e >> 1] = pack_bf16x2(bf16_lo(pa) * (__uint_as_float(dv[e]) - d4.x),
+                                   bf16_hi(pa) * (__uint_as_float(dv[e + 1]) - d4.y));
+          dd[(e >> 1) + 1] = pack_bf16x2(bf16_lo(pb) * (__uint_as_float(dv[e + 2]) - d4.z),
+                                         bf16_hi(pb) * (__uint_as_float(dv[e + 3]) - d4.w));
         }
         // TMEM copy for dK (over dP^T columns this thread has read), smem copy for dQ
         tmem_st_32x32b_x16(lane_base + T_DP + hq * 64 + half * 16, dd);
@@ -1053,6 +1108,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);
+      lapd(7);
+    }
+    if (TRACE && tr) {
+      unsigned long long* dst = p.trace + (long)(blockIdx.y * gridDim.x + blockIdx.x) * 16;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) dst[q] = td[q];
     }
   } else {
     setmaxnreg_dec<kRegsDrain>();
@@ -1311,20 +1372,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto v_at = [&](int lt) { return smem_u32(smem + ps::OFF_V + (lt & 1) * T_BYTES); };
       auto q_at = [&](int g) { return smem_u32(smem + ps::OFF_Q + (g & 1) * T_BYTES); };
       auto do_at = [&](int g) { return smem_u32(smem + ps::OFF_DO + (g & 1) * T_BYTES); };
+      const uint64_t dds_mn = umma_desc_sw128(ds_addr, BK * 128, 1024);
       auto issue_s = [&](int lt, int g) {
-        const uint32_t k_addr = k_at(lt), q_addr = q_at(g);
+        const uint64_t dk = umma_desc_sw128(k_at(lt), 16, 1024), dq = umma_desc_sw128(q_at(g), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          tc_mma_f16_ss(tmem + T_S, umma_desc_sw128(k_addr + kk * 32, 16, 1024),
-                        umma_desc_sw128(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_S, desc_off(dk, kk * 32), desc_off(dq, kk * 32), IDESC_S, kk > 0 ? 1u : 0u);
         tc_commit(s_full);
       };
       auto issue_dp = [&](int lt, int g) {
-        const uint32_t v_addr = v_at(lt), do_addr = do_at(g);
+        const uint64_t dv = umma_desc_sw128(v_at(lt), 16, 1024), ddo = umma_desc_sw128(do_at(g), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          tc_mma_f16_ss(tmem + T_DP, umma_desc_sw128(v_addr + kk * 32, 16, 1024),
-                        umma_desc_sw128(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_DP, desc_off(dv, kk * 32), desc_off(ddo, kk * 32), IDESC_S, kk > 0 ? 1u : 0u);
         tc_commit(dp_full);
       };
       // cursor over the CTA's stream of query blocks: (tile counter, item, block in tile)
@@ -1362,24 +1422,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         // have copied the previous tile's dK / dV out
         if (n == 0 && lt > 0 && !mbar_wait(dkv_free, (lt - 1) & 1, p.st, 65, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t q_addr = q_at(g), do_addr = do_at(g), k_addr = k_at(lt);
+        const uint64_t ddo_mn = umma_desc_sw128(do_at(g), 128 * 128, 1024);
+        const uint64_t dq_mn = umma_desc_sw128(q_at(g), 128 * 128, 1024);
+        const uint64_t dk_mn = umma_desc_sw128(k_at(lt), 128 * 128, 1024);
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8, umma_desc_sw128(do_addr + kk * 2048, 128 * 128, 1024),
-                        IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem + T_DV, tmem + T_PT + kk * 8, desc_off(ddo_mn, kk * 2048), IDESC_KV,
+                        (n > 0 || kk > 0) ? 1u : 0u);
         tc_commit(pt_free);
         if (!mbar_wait(ds_full, g & 1, p.st, 56, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 2) * 64 + (kk & 3) * 8,
-                        umma_desc_sw128(q_addr + kk * 2048, 128 * 128, 1024), IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem + T_DK, tmem + T_DP + (kk >> 2) * 64 + (kk & 3) * 8, desc_off(dq_mn, kk * 2048),
+                        IDESC_KV, (n > 0 || kk > 0) ? 1u : 0u);
         if (!mbar_wait(dq_free, (g & 1) ^ 1, p.st, 55, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          tc_mma_f16_ss(tmem + T_DQ, umma_desc_sw128(ds_addr + kk * 2048, BK * 128, 1024),
-                        umma_desc_sw128(k_addr + kk * 2048, 128 * 128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + T_DQ, desc_off(dds_mn, kk * 2048), desc_off(dk_mn, kk * 2048), IDESC_Q,
+                        kk > 0 ? 1u : 0u);
         tc_commit(dq_full);
         tc_commit(&qdo_empty[g & 1]);
         if (n + 1 == niter) {
@@ -1448,16 +1510,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const AttnSpan span = attn_queries_of_key<false>(p.sp, key, q0, S, Sk, CAUSAL);
         uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          float pr[2];
+        for (int e = 0; e < 64; e += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(sL + c_begin + e);  // one broadcast load for 4 queries
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          float pr[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
+          for (int u = 0; u < 4; ++u) {
             const int ql = c_begin + e + u;
-            float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -sL[ql]));
+            float pv = ex2_fast(fmaf(__uint_as_float(sv[e + u]), p.scale_log2, -lv[u]));
             if (need_mask && !attn_span_has(span, ql)) pv = 0.f;
             pr[u] = pv;
           }
           pk[e >> 1] = pack_bf16x2(pr[0], pr[1]);
+          pk[(e >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
         }
         if (!mbar_wait(pt_free, (g & 1) ^ 1, p.st, 58, abort_flag)) { ok = false; break; }
         tc_fence_after();
@@ -1469,19 +1534,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(pt_full);
         if (!mbar_wait(dp_full, g & 1, p.st, 59, abort_flag)) { ok = false; break; }
         tc_fence_after();
+        uint32_t dva[64];
+        tmem_ld_32x32b_x32(lane_base + T_DP + c_begin, dva);
+        tmem_ld_32x32b_x32(lane_base + T_DP + c_begin + 32, dva + 32);
+        tc_wait_ld();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int c = c_begin + half * 32;
-          uint32_t dv[32];
-          tmem_ld_32x32b_x32(lane_base + T_DP + c, dv);
-          tc_wait_ld();
+          const uint32_t* dv = dva + half * 32;
           uint32_t dd[16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const uint32_t pp = pk[(half * 32 + e) >> 1];
-            const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e]) - sL[128 + c + e]);
-            const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e + 1]) - sL[128 + c + e + 1]);
-            dd[e >> 1] = pack_bf16x2(d0, d1);
+          for (int e = 0; e < 32; e += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(sL + 128 + c + e);
+            const uint32_t pa = pk[(half * 32 + e) >> 1], pb = pk[((half * 32 + e) >> 1) + 1];
+            dd[e >> 1] = pack_bf16x2(bf16_lo(pa) * (__uint_as_float(dv[e]) - d4.x),
+                                     bf16_hi(pa) * (__uint_as_float(dv[e + 1]) - d4.y));
+            dd[(e >> 1) + 1] = pack_bf16x2(bf16_lo(pb) * (__uint_as_float(dv[e + 2]) - d4.z),
+                                           bf16_hi(pb) * (__uint_as_float(dv[e + 3]) - d4.w));
           }
           tmem_st_32x32b_x16(lane_base + T_DP + hq * 64 + half * 16, dd);
           const int blk = (c >> 6) * (BK * 128);
@@ -1588,6 +1657,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace fabw
 
+// Phase trace of the last traced backward launch: [CTAs, 16] int64 (see fabw::Params::trace).
+static torch::Tensor g_bwd_trace;
+torch::Tensor attn_bwd_trace() { return g_bwd_trace; }
+
 // Attention backward core on tcgen05 (head_dim 64): writes dK, dV and
 // reduce-adds the unscaled dQ into dq_acc (fp32 [B*S, H*HD], pre-zeroed by
 // the caller). lse / delta fp32 [B, H, S]. q/dout [B, S, H, 64], k/v/dk/dv
@@ -1635,6 +1708,19 @@ void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, tor
   const bool pipelined = schedule >= 1;
   dim3 grid((unsigned)((Sk + 127) / 128), (unsigned)(B * H));
   auto st = cur_stream();
+  {
+    // phase trace of the pipelined kernel (profiling aid): SCIRS_ATTN_BWD_TRACE=1
+    const char* e = getenv("SCIRS_ATTN_BWD_TRACE");
+    if (e != nullptr && e[0] == '1' && pipelined && !sparse) {
+      g_bwd_trace = torch::zeros({(long)grid.x * grid.y, 16}, q.options().dtype(at::kLong));
+      p.trace = reinterpret_cast<unsigned long long*>(g_bwd_trace.data_ptr());
+      auto kern = causal ? fabw::fa_bwd_pipe_kernel<true, false, true> : fabw::fa_bwd_pipe_kernel<false, false, true>;
+      set_max_smem((const void*)kern, fabw::SMEM);
+      kern<<<grid, fabw::kThreads, fabw::SMEM, st>>>(tq, tk, tv, tdo, tdq, p);
+      SCIRS_CHECK_LAUNCH();
+      return;
+    }
+  }
   if (schedule == 2 && !sparse) {
     // persistent: one CTA per SM over the (key tile, batch x head) items
     const long pairs = (long)((grid.x + 1) / 2) * grid.y;

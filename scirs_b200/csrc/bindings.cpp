@@ -30,6 +30,7 @@ void vit_embed_fwd(torch::Tensor pe, torch::Tensor cls, torch::Tensor pos, torch
 void vit_embed_bwd(torch::Tensor dx, torch::Tensor dpe, torch::Tensor dpos, torch::Tensor dcls, int64_t B);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     bool causal, double scale);
+torch::Tensor attn_bwd_trace();
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
                     torch::Tensor delta, bool causal, double scale, int64_t impl,
@@ -169,6 +170,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vit_embed_fwd", &scirs::vit_embed_fwd);
   m.def("vit_embed_bwd", &scirs::vit_embed_bwd);
   m.def("flash_attn_fwd", &scirs::flash_attn_fwd);
+  m.def("attn_bwd_trace", &scirs::attn_bwd_trace, "phase trace of the last traced attention backward launch");
   m.def("flash_attn_bwd", &scirs::flash_attn_bwd, "attention backward", py::arg("dout"), py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"),
         py::arg("delta"), py::arg("causal"), py::arg("scale"), py::arg("impl") = 1, py::arg("blk_ptr") = py::none(),

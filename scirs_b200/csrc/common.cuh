@@ -320,6 +320,14 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t
   return d;
 }
 
+// The descriptor of an operand `bytes` further into the same swizzled tile: only
+// the start-address field (low 14 bits, in 16-byte units) changes, and it cannot
+// carry into the next field while the address stays inside shared memory, so a
+// 32-bit add on the low word is enough (one instruction per MMA in the k loops).
+__device__ __forceinline__ uint64_t desc_off(uint64_t d, uint32_t bytes) {
+  return (d & 0xFFFFFFFF00000000ull) | (uint64_t)((uint32_t)d + (bytes >> 4));
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulator.
 //   [4,6) c_format=1 (F32); [7,10) a_format=1 (BF16); [10,13) b_format=1;
 //   [15] a_major (1 = MN-major); [16] b_major; [17,23) N>>3; [24,29) M>>4.

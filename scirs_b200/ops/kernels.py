@@ -31,9 +31,9 @@ ATTN_FWD_IMPL = os.environ.get("SCIRS_ATTN_FWD", "pingpong_x2")
 # Attention backward: "tcgen05" (tcgen05 kernels, serial schedule), "tcgen05_pipe"
 # (tcgen05 kernels; the tensor core overlaps the softmax-gradient warps),
 # "tcgen05_persist" (pipelined; head_dim 64 dense patterns as one persistent CTA
-# per SM) or "mma".
-ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05_pipe")
-_BWD_CODES = {"mma": 0, "tcgen05": 1, "tcgen05_pipe": 2, "tcgen05_persist": 3}
+# per SM), "tcgen05_auto" (persistent up to 1,024 keys, pipelined above) or "mma".
+ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05_auto")
+_BWD_CODES = {"mma": 0, "tcgen05": 1, "tcgen05_pipe": 2, "tcgen05_persist": 3, "tcgen05_auto": 4}
 
 
 def _bwd_code(sparse: bool = False) -> int:

@@ -193,7 +193,7 @@ def test_embedding_and_bias_grad():
 
 
 # ---------------------------------------------------------------------------- attention
-@pytest.mark.parametrize("bwd_impl", ["tcgen05", "tcgen05_pipe", "tcgen05_persist", "mma"])
+@pytest.mark.parametrize("bwd_impl", ["tcgen05", "tcgen05_pipe", "tcgen05_persist", "tcgen05_auto", "mma"])
 @pytest.mark.parametrize("B,S,H,HD,causal", [(2, 256, 4, 64, True), (1, 197, 3, 64, False), (1, 384, 2, 128, True),
                                              (2, 1024, 2, 64, True), (1, 300, 2, 64, True), (1, 300, 2, 128, True),
                                              (2, 197, 2, 128, False), (1, 1024, 2, 128, True)])
