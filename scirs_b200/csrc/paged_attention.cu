@@ -20,6 +20,8 @@
 // kv_page.rs:96-140 (write_kv), block_manager.rs:161-196 (write_token_kv).
 #include "host_common.h"
 
+#include <type_traits>
+
 namespace scirs {
 namespace paged {
 
@@ -149,7 +151,34 @@ __global__ void __launch_bounds__(kT) decode_kernel(const __nv_bfloat16* __restr
 #pragma unroll
       for (int e = 0; e < ODIM; ++e) acc[e] *= al;
       const int n = min(kT, t_end - c0);
-      for (int i = 0; i < n; ++i) {
+      int i = 0;
+      // eight tokens per step: their page ids and V slices are all loaded before the FMAs,
+      // so each thread has eight independent loads in flight instead of one
+      constexpr int kU = 8;
+      using VT = typename std::conditional<ODIM == 8, uint4, uint2>::type;
+      for (; i + kU <= n; i += kU) {
+        VT vv[kU];
+        float pw[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int tt = c0 + i + u;
+          const int page = bt[tt / bs];
+          const bool okp = page >= 0 && page < num_pages;  // a bad page was reported in the score pass
+          const __nv_bfloat16* vr = v_pool + ((long)(okp ? page : 0) * bs + tt % bs) * row + (long)hk * HD + od;
+          vv[u] = *reinterpret_cast<const VT*>(vr);
+          pw[u] = okp ? ps[og][i + u] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(&vv[u]);
+#pragma unroll
+          for (int e = 0; e < ODIM / 2; ++e) {
+            acc[2 * e] = fmaf(pw[u], bf16_lo(w[e]), acc[2 * e]);
+            acc[2 * e + 1] = fmaf(pw[u], bf16_hi(w[e]), acc[2 * e + 1]);
+          }
+        }
+      }
+      for (; i < n; ++i) {
         const int tt = c0 + i;
         const int page = bt[tt / bs];
         if (page < 0 || page >= num_pages) continue;  // reported in the score pass; its score is -inf
