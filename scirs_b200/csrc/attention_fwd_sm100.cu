@@ -547,7 +547,8 @@ AttnSparse attn_sparse_args(const c10::optional<torch::Tensor>& ptr, const c10::
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2,
                        c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
-                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng, bool bf2) {
+                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng, bool bf2,
+                       int64_t persist_req) {
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), HD = q.size(3);
   const int64_t Sk = k.size(1);
   TORCH_CHECK(HD == 64 || HD == 128, "head_dim must be 64 or 128");
@@ -578,7 +579,7 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.st = status_ptr(q.get_device());
   // one CTA per (query pair, batch x head) item, or one CTA per SM walking the
-  // items (SCIRS_ATTN_FWD_PERSIST=1 / 0 forces either)
+  // items
   dim3 grid((unsigned)((S + 255) / 256), (unsigned)(B * H));
   const int64_t nqp = grid.x;
   p.sp = attn_sparse_args(blk_ptr, blk_idx, bmap, wl, wr, ng, nqp);
@@ -592,8 +593,9 @@ void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   }
   {
     const char* e = getenv("SCIRS_ATTN_FWD_PERSIST");
-    // default: persistent for head_dim 64, and for 128 up to 1,024 queries (measured faster there)
-    const bool dflt = HD == 64 || S <= 1024;
+    // persist_req: 1 / 0 = the caller's choice, -1 = by size: persistent for head_dim 64, and for
+    // 128 up to 1,024 queries (measured faster there). SCIRS_ATTN_FWD_PERSIST=0 / 1 overrides.
+    const bool dflt = persist_req >= 0 ? persist_req == 1 : (HD == 64 || S <= 1024);
     const bool persist = (e != nullptr ? e[0] == '1' : dflt) && p.trace == nullptr;
     const long items = (long)grid.x * grid.y;
     const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;

@@ -90,7 +90,8 @@ void paged_attention_decode(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
 void flash_attn_fwd_pp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        bool causal, double scale, bool poly, c10::optional<torch::Tensor> trace, bool x2,
                        c10::optional<torch::Tensor> blk_ptr, c10::optional<torch::Tensor> blk_idx,
-                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng, bool bf2);
+                       c10::optional<torch::Tensor> bmap, int64_t wl, int64_t wr, int64_t ng, bool bf2,
+                       int64_t persist);
 void tp_step_begin(torch::Tensor epoch, c10::optional<torch::Tensor> vals);
 void tp_reduce(torch::Tensor recv, torch::Tensor out, c10::optional<torch::Tensor> bias,
                c10::optional<torch::Tensor> resid, int64_t rank, c10::optional<torch::Tensor> flags,
@@ -160,7 +161,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse"), py::arg("causal"), py::arg("scale"), py::arg("poly") = false,
         py::arg("trace") = py::none(), py::arg("x2") = false, py::arg("blk_ptr") = py::none(),
         py::arg("blk_idx") = py::none(), py::arg("bmap") = py::none(), py::arg("wl") = -1, py::arg("wr") = -1,
-        py::arg("ng") = 0, py::arg("bf2") = false);
+        py::arg("ng") = 0, py::arg("bf2") = false, py::arg("persist") = -1);
   m.def("tp_step_begin", &scirs::tp_step_begin, py::arg("epoch"), py::arg("vals") = py::none());
   m.def("tp_reduce", &scirs::tp_reduce);
   m.def("rope_apply", &scirs::rope_apply);

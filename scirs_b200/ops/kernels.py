@@ -36,11 +36,27 @@ ATTN_BWD_IMPL = os.environ.get("SCIRS_ATTN_BWD", "tcgen05_auto")
 _BWD_CODES = {"mma": 0, "tcgen05": 1, "tcgen05_pipe": 2, "tcgen05_persist": 3, "tcgen05_auto": 4}
 
 
+def _shared_sms() -> bool:
+    """True inside a multi-rank process group: collective kernels then run next to the attention
+    kernels, and the persistent schedules (a fixed work list per CTA, one CTA per SM) would wait
+    for whole SMs; the per-tile grids spread over whatever SMs are free."""
+    import torch.distributed as dist
+
+    return dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+
+
 def _bwd_code(sparse: bool = False) -> int:
     code = _BWD_CODES.get(ATTN_BWD_IMPL)
     if code is None:
         raise ValueError(f"unknown attention backward implementation {ATTN_BWD_IMPL!r}")
+    if code == 4 and _shared_sms():
+        code = 2
     return max(code, 1) if sparse else code
+
+
+def _fwd_persist() -> int:
+    """-1: the kernel chooses by size; 0: per-item grid (multi-rank runs, see _shared_sms)."""
+    return 0 if _shared_sms() else -1
 
 
 class _Stats:
@@ -311,11 +327,11 @@ def flash_attn_fwd(q, k, v, out, lse, causal=True, scale=None, plan=None):
     if q.is_cuda:
         if plan is not None:
             _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(plan.pattern.causal), float(scale), False, None,
-                                             False, **plan.kernel_args())
+                                             False, **plan.kernel_args(), persist=_fwd_persist())
         elif ATTN_FWD_IMPL in ("pingpong", "pingpong_poly", "pingpong_x2", "pingpong_bf2"):
             _ext.kernels().flash_attn_fwd_pp(q, k, v, out, lse, bool(causal), float(scale),
                                              ATTN_FWD_IMPL == "pingpong_poly", None, ATTN_FWD_IMPL == "pingpong_x2",
-                                             bf2=ATTN_FWD_IMPL == "pingpong_bf2")
+                                             bf2=ATTN_FWD_IMPL == "pingpong_bf2", persist=_fwd_persist())
         elif ATTN_FWD_IMPL == "tcgen05":
             _ext.kernels().flash_attn_fwd_tc(q, k, v, out, lse, bool(causal), float(scale))
         else:
