@@ -848,3 +848,108 @@ def clip_contrastive_loss(image_emb: torch.Tensor, text_emb: torch.Tensor, logit
     logits = logit_scale.exp() * i @ t.t()
     y = torch.arange(i.shape[0], device=i.device)
     return 0.5 * (F.cross_entropy(logits, y) + F.cross_entropy(logits.t(), y))
+
+
+# ---------------------------------------------------------------------------- framework kernels
+# The zoo's layers are declared with torch.nn; `use_framework_kernels` swaps the
+# ones the framework has kernels for (Linear, Conv2d, LayerNorm, max / average
+# pooling) for modules that call scirs_b200.ops.functional, so on CUDA the
+# model runs on the tcgen05 GEMM, the im2col convolution, the LayerNorm and the
+# pooling kernels. The new modules hold the same Parameter objects under the same
+# names, so state dicts are unchanged. Grouped or padded-mode convolutions,
+# ceil-mode / dilated pooling and non-last-dim LayerNorms stay on PyTorch.
+class KernelLinear(nn.Module):
+    def __init__(self, lin: nn.Linear):
+        super().__init__()
+        self.in_features, self.out_features = lin.in_features, lin.out_features
+        self.weight, self.bias = lin.weight, lin.bias
+
+    def forward(self, x):
+        from ..ops import functional as OF
+
+        return OF.linear(x, self.weight.t(), self.bias)
+
+
+class KernelConv2d(nn.Module):
+    def __init__(self, conv: nn.Conv2d):
+        super().__init__()
+        self.in_channels, self.out_channels, self.kernel_size = conv.in_channels, conv.out_channels, conv.kernel_size
+        self.stride, self.padding, self.dilation = conv.stride, conv.padding, conv.dilation
+        self.weight, self.bias = conv.weight, conv.bias
+
+    def forward(self, x):
+        from ..ops import functional as OF
+
+        return OF.conv2d(x, self.weight, self.bias, self.stride, self.padding, self.dilation)
+
+
+class KernelLayerNorm(nn.Module):
+    def __init__(self, ln: nn.LayerNorm):
+        super().__init__()
+        self.normalized_shape, self.eps = ln.normalized_shape, ln.eps
+        self.weight, self.bias = ln.weight, ln.bias
+
+    def forward(self, x):
+        from ..ops import functional as OF
+
+        return OF.layer_norm(x, self.weight, self.bias, self.eps)
+
+
+class KernelPool2d(nn.Module):
+    def __init__(self, pool, is_max: bool):
+        super().__init__()
+        self.kernel_size, self.stride, self.padding = pool.kernel_size, pool.stride, pool.padding
+        self.is_max = is_max
+        self.count_include_pad = getattr(pool, "count_include_pad", True)
+
+    def forward(self, x):
+        from ..ops import functional as OF
+
+        if self.is_max:
+            return OF.max_pool2d(x, self.kernel_size, self.stride, self.padding)
+        return OF.avg_pool2d(x, self.kernel_size, self.stride, self.padding, self.count_include_pad)
+
+
+def _kernel_module(m: nn.Module):
+    if type(m) is nn.Linear:
+        return KernelLinear(m)
+    if type(m) is nn.Conv2d and m.groups == 1 and m.padding_mode == "zeros" and not isinstance(m.padding, str):
+        return KernelConv2d(m)
+    if (type(m) is nn.LayerNorm and len(m.normalized_shape) == 1 and m.elementwise_affine
+            and m.weight is not None and m.bias is not None):
+        return KernelLayerNorm(m)
+    if type(m) is nn.MaxPool2d and not m.ceil_mode and m.dilation in (1, (1, 1)) and not m.return_indices:
+        return KernelPool2d(m, True)
+    if type(m) is nn.AvgPool2d and not m.ceil_mode and m.divisor_override is None:
+        return KernelPool2d(m, False)
+    return None
+
+
+def use_framework_kernels(model: nn.Module) -> nn.Module:
+    """Replace, in place, every layer of `model` that has a framework kernel
+    (see above) and return the model."""
+    for name, child in list(model.named_children()):
+        rep = _kernel_module(child)
+        if rep is not None:
+            setattr(model, name, rep)
+        else:
+            use_framework_kernels(child)
+    return model
+
+
+def _with_kernels(cls):
+    raw = cls.build
+
+    def build(self, kernels: bool = True):
+        """Build the model; with `kernels` (default) its Linear / Conv2d / LayerNorm /
+        pooling layers run on the framework's kernels (use_framework_kernels)."""
+        m = raw(self)
+        return use_framework_kernels(m) if kernels else m
+
+    cls.build = build
+    return cls
+
+
+for _n, _c in list(globals().items()):
+    if isinstance(_c, type) and _n.endswith("Config") and callable(getattr(_c, "build", None)):
+        _with_kernels(_c)

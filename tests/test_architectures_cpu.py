@@ -128,3 +128,26 @@ def test_swin_clip():
     loss = A.clip_contrastive_loss(img, img.clone(), torch.tensor(math.log(100.0)))
     loss_rand = A.clip_contrastive_loss(img, txt, torch.tensor(math.log(100.0)))
     assert loss < loss_rand
+
+
+def test_zoo_layers_run_on_framework_kernels():
+    """build() swaps Linear / Conv2d / LayerNorm / pooling for the framework's kernel-backed
+    modules (same parameters, same state-dict keys); on the CPU they compute what torch.nn does."""
+    from scirs_b200.models import architectures as A
+
+    torch.manual_seed(0)
+    for cfg, x in ((A.ResNetConfig.resnet18(num_classes=10), torch.randn(2, 3, 64, 64)),
+                   (A.MLPMixerConfig(image_size=32, patch_size=8, hidden_dim=64, num_layers=2,
+                                     token_mlp_dim=32, channel_mlp_dim=128, num_classes=10),
+                    torch.randn(2, 3, 32, 32))):
+        torch.manual_seed(1)
+        ref = cfg.build(kernels=False).eval()
+        torch.manual_seed(1)
+        m = cfg.build().eval()
+        kinds = {type(mod).__name__ for mod in m.modules()}
+        assert "KernelLinear" in kinds
+        assert not any(type(mod) is torch.nn.Linear for mod in m.modules())
+        assert list(m.state_dict()) == list(ref.state_dict())
+        m.load_state_dict(ref.state_dict())
+        with torch.no_grad():
+            assert torch.allclose(m(x), ref(x), atol=1e-5, rtol=1e-4)
