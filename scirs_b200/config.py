@@ -23,6 +23,8 @@ override file values (`apply_env`):
     SCIRS_THREADS      n                  host threads (torch.set_num_threads)
     SCIRS_ATTN_FWD / SCIRS_ATTN_BWD       attention kernel variant
     SCIRS_ATTN_FWD_PERSIST  0 | 1         attention forward on one CTA per SM
+    SCIRS_ATTN_BWD_TRACE    1             phase trace of the pipelined attention
+                                          backward (profiling; kernels.attn_bwd_trace())
     SCIRS_<SECTION>_<FIELD>               any field, e.g. SCIRS_PARALLEL_DP=8,
                                           SCIRS_DATA_GLOBAL_BATCH=64
 
