@@ -98,3 +98,55 @@ def perplexity(mean_nll: float) -> float:
     import math
 
     return math.exp(mean_nll)
+
+
+# ---------------------------------------------------------------------------- evaluation summaries
+class FeatureImportance:
+    """Named importance scores with a top-k selection and a text bar chart.
+    Reference parity: scirs2-neural/src/utils/evaluation/feature_importance.rs:20-160."""
+
+    def __init__(self, feature_names: list, importance):
+        imp = torch.as_tensor(importance, dtype=torch.float64).reshape(-1)
+        if len(feature_names) != imp.numel():
+            raise ValueError("Number of feature names must match number of importance scores")
+        self.feature_names, self.importance = list(feature_names), imp
+
+    def top_k(self, k: int):
+        k = min(int(k), len(self.feature_names))
+        order = torch.argsort(self.importance, descending=True, stable=True)[:k]
+        return [self.feature_names[i] for i in order.tolist()], self.importance[order]
+
+    def to_ascii(self, title: str | None = None, width: int = 40, k: int | None = None) -> str:
+        names, vals = self.top_k(k if k is not None else len(self.feature_names))
+        top = float(vals.abs().max()) if vals.numel() else 0.0
+        pad = max((len(n) for n in names), default=0)
+        lines = [title] if title else []
+        for n, v in zip(names, vals.tolist()):
+            bar = "#" * (int(round(abs(v) / top * width)) if top > 0 else 0)
+            lines.append(f"{n.ljust(pad)} | {bar} {v:.4f}")
+        return "\n".join(lines)
+
+
+class LearningCurve:
+    """Scores [n_sizes, n_folds] for the training and validation sets at each training size, with
+    per-size means and (population) standard deviations over the folds.
+    Reference parity: scirs2-neural/src/utils/evaluation/learning_curve.rs:19-160."""
+
+    def __init__(self, train_sizes, train_scores, val_scores):
+        self.train_sizes = [int(s) for s in train_sizes]
+        tr = torch.as_tensor(train_scores, dtype=torch.float64)
+        va = torch.as_tensor(val_scores, dtype=torch.float64)
+        if tr.dim() != 2 or va.dim() != 2 or tr.shape[0] != len(self.train_sizes) or va.shape[0] != len(self.train_sizes):
+            raise ValueError("Number of scores must match number of training sizes")
+        if tr.shape[1] != va.shape[1]:
+            raise ValueError("Training and validation scores must have the same number of CV folds")
+        self.train_scores, self.val_scores = tr, va
+        self.train_mean, self.val_mean = tr.mean(1), va.mean(1)
+        self.train_std, self.val_std = tr.std(1, unbiased=False), va.std(1, unbiased=False)
+
+    def to_ascii(self, title: str | None = None, width: int = 50, height: int = 12) -> str:
+        from .utils.visualization import ascii_plot
+
+        head = (title + "\n") if title else ""
+        return (head + "train\n" + ascii_plot(self.train_mean.tolist(), width, height)
+                + "\nvalidation\n" + ascii_plot(self.val_mean.tolist(), width, height))
