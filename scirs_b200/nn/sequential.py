@@ -88,6 +88,8 @@ class Sequential(Layer):
         self.optimizer.zero_grad()
         loss = self.loss_fn(self(x), y)
         loss.backward()
+        for cb in getattr(self, "_pre_step_callbacks", ()):
+            cb.on_before_step(self)  # e.g. gradient clipping
         self.optimizer.step()
         return float(loss.detach())
 
@@ -129,6 +131,7 @@ class Sequential(Layer):
         xt, yt = x[:split], y[:split]
         xv, yv = (x[split:], y[split:]) if split < n else (None, None)
         cbs = callbacks or []
+        self._pre_step_callbacks = [cb for cb in cbs if hasattr(cb, "on_before_step")]
         g = torch.Generator().manual_seed(seed)
         for cb in cbs:
             cb.on_train_begin(self)
@@ -160,4 +163,5 @@ class Sequential(Layer):
                 break
         for cb in cbs:
             cb.on_train_end(self)
+        self._pre_step_callbacks = []
         return self.history
