@@ -1,6 +1,8 @@
 """Host and device timing, counters and a run-time configuration store.
 
-* `Timer` / `Profiler`: named wall-clock sections with call counts (host).
+* `Timer` / `Profiler`: named wall-clock sections with call counts (host); nested
+  sections give folded stacks and a flame-graph SVG.
+* `SystemMonitor`: background sampling of host CPU / memory and device memory.
 * `cuda_timer`: CUDA-event timing of a region on the current stream (the
   synchronise-on-both-sides rule of device timing).
 * `Metrics`: counters / gauges / histograms with labels, exportable as
@@ -51,6 +53,8 @@ class Profiler:
     def __init__(self):
         self.totals = defaultdict(float)
         self.calls = defaultdict(int)
+        self.stacks = defaultdict(float)  # "outer;inner" -> seconds (nested sections, for flame graphs)
+        self._tls = threading.local()
         self._lock = threading.Lock()
 
     @classmethod
@@ -61,14 +65,61 @@ class Profiler:
 
     @contextlib.contextmanager
     def section(self, name: str):
+        stack = getattr(self._tls, "stack", None)
+        if stack is None:
+            stack = self._tls.stack = []
+        stack.append(name)
+        path = ";".join(stack)
         t0 = time.perf_counter()
         try:
             yield
         finally:
             dt = time.perf_counter() - t0
+            stack.pop()
             with self._lock:
                 self.totals[name] += dt
                 self.calls[name] += 1
+                self.stacks[path] += dt
+
+    def folded(self) -> str:
+        """Self time per call stack in the folded format of flame-graph tools ("a;b 123" in us)."""
+        lines = []
+        for path, t in sorted(self.stacks.items()):
+            child = sum(v for p, v in self.stacks.items() if p.startswith(path + ";") and p.count(";") == path.count(";") + 1)
+            lines.append(f"{path} {max(0, int(round((t - child) * 1e6)))}")
+        return "\n".join(lines)
+
+    def flame_graph_svg(self, path: str, width: int = 1000, row: int = 18) -> str:
+        """A flame graph of the nested sections (widths proportional to inclusive time)."""
+        roots = {p: t for p, t in self.stacks.items() if ";" not in p}
+        total = sum(roots.values()) or 1.0
+        rects = []
+
+        def place(prefix, x0, depth):
+            kids = sorted((p, t) for p, t in self.stacks.items()
+                          if p.startswith(prefix + ";" if prefix else "") and p.count(";") == (prefix.count(";") + 1 if prefix else 0))
+            x = x0
+            for p, t in kids:
+                w = t / total * width
+                rects.append((x, depth, w, p.split(";")[-1], t))
+                place(p, x, depth + 1)
+                x += w
+
+        place("", 0.0, 0)
+        depth = max((d for _, d, _, _, _ in rects), default=0) + 1
+        h = depth * row
+        out = [f'<svg xmlns="http://www.w3.org/2000/svg" width="{width}" height="{h}">']
+        for x, d, w, name, t in rects:
+            y = h - (d + 1) * row
+            hue = 20 + (hash(name) % 40)
+            out.append(f'<g><title>{name} {t * 1e3:.3f} ms</title><rect x="{x:.2f}" y="{y}" width="{max(w, 0.5):.2f}" '
+                       f'height="{row - 1}" fill="hsl({hue},90%,60%)"/>'
+                       f'<text x="{x + 2:.2f}" y="{y + row - 5}" font-size="11">{name if w > 40 else ""}</text></g>')
+        out.append("</svg>")
+        svg = "\n".join(out)
+        with open(path, "w") as f:
+            f.write(svg)
+        return svg
 
     def report(self) -> str:
         rows = sorted(self.totals.items(), key=lambda kv: -kv[1])
@@ -80,6 +131,47 @@ class Profiler:
     def reset(self):
         self.totals.clear()
         self.calls.clear()
+        self.stacks.clear()
+
+
+class SystemMonitor:
+    """Samples host CPU utilisation and resident memory (psutil) and, when CUDA is available, device
+    memory in use, every `interval` seconds on a background thread."""
+
+    def __init__(self, interval: float = 0.5):
+        self.interval, self.samples = interval, []
+        self._stop = threading.Event()
+        self._thread = None
+
+    @staticmethod
+    def sample() -> dict:
+        import psutil
+
+        proc = psutil.Process()
+        d = {"time": time.time(), "cpu_percent": psutil.cpu_percent(interval=None),
+             "rss_bytes": proc.memory_info().rss, "host_available_bytes": psutil.virtual_memory().available}
+        if torch.cuda.is_available():
+            free, total = torch.cuda.mem_get_info()
+            d["gpu_used_bytes"], d["gpu_total_bytes"] = total - free, total
+        return d
+
+    def start(self):
+        self._stop.clear()
+
+        def run():
+            while not self._stop.is_set():
+                self.samples.append(self.sample())
+                self._stop.wait(self.interval)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self) -> list:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+        return self.samples
 
 
 @contextlib.contextmanager
