@@ -32,7 +32,6 @@ grouped-query attention), utils.rs:14-49 (AttentionMask, AttentionConfig).
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
