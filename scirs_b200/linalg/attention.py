@@ -166,10 +166,11 @@ def flash_attention(query, key, value, mask: AttentionMask | None = None, scale:
         raise ValueError("block_size must be positive")
     B, Lq, _ = query.shape
     Lk = key.shape[1]
-    qf, kf, vf = query.float(), key.float(), value.float()
-    m = torch.full((B, Lq, 1), float("-inf"), device=query.device)
-    den = torch.zeros(B, Lq, 1, device=query.device)
-    acc = torch.zeros(B, Lq, value.shape[-1], device=query.device)
+    ct = torch.float64 if query.dtype == torch.float64 else torch.float32  # accumulate in >= fp32
+    qf, kf, vf = query.to(ct), key.to(ct), value.to(ct)
+    m = torch.full((B, Lq, 1), float("-inf"), device=query.device, dtype=ct)
+    den = torch.zeros(B, Lq, 1, device=query.device, dtype=ct)
+    acc = torch.zeros(B, Lq, value.shape[-1], device=query.device, dtype=ct)
     rows = torch.arange(Lq, device=query.device)[:, None]
     for j0 in range(0, Lk, block_size):
         j1 = min(Lk, j0 + block_size)
@@ -179,7 +180,7 @@ def flash_attention(query, key, value, mask: AttentionMask | None = None, scale:
                 cols = torch.arange(j0, j1, device=query.device)[None, :]
                 s = s.masked_fill(cols > rows, float("-inf"))
             elif mask.kind == "additive":
-                s = s + mask.tensor[..., j0:j1].float()
+                s = s + mask.tensor[..., j0:j1].to(ct)
             elif mask.kind == "boolean":
                 s = s.masked_fill(~mask.tensor[..., j0:j1].to(torch.bool), float("-inf"))
         m_new = torch.maximum(m, s.amax(-1, keepdim=True))
