@@ -177,10 +177,13 @@ class BatchPrefetcher {
   std::vector<std::thread> workers_;
 };
 
+void register_host_runtime(py::module& m);  // host_runtime.cpp
+
 }  // namespace scirs
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.doc() = "scirs_b200 native batch prefetcher";
+  m.doc() = "scirs_b200 native host runtime: batch prefetcher, task graph, scans, sort, lock-free ring";
+  scirs::register_host_runtime(m);
   py::class_<scirs::BatchPrefetcher>(m, "BatchPrefetcher")
       .def(py::init<std::vector<torch::Tensor>, int64_t, int64_t, int64_t, bool, int64_t, bool, bool>(),
            py::arg("arrays"), py::arg("batch_size"), py::arg("num_slots") = 3, py::arg("num_threads") = 2,

@@ -62,7 +62,7 @@ ext_modules = [
     ),
     CppExtension(
         name="scirs_b200._data",
-        sources=_sources(["dataloader.cpp"]),
+        sources=_sources(["dataloader.cpp", "host_runtime.cpp"]),
         extra_compile_args={"cxx": CXX_FLAGS},
     ),
     CUDAExtension(
