@@ -112,6 +112,82 @@ class KLDivLoss(Loss):
         return F.kl_div(log_p, q, reduction="batchmean")
 
 
+# ---------------------------------------------------------------------------- functional forms
+# Binary / segmentation and metric-learning losses on probabilities and embeddings, differentiable
+# (scirs2-neural/src/losses/extended.rs:52-330: focal_loss, dice_loss, tversky_loss,
+# contrastive_loss, triplet_loss; the same definitions and smoothing constants).
+
+
+def _same_shape(a, b, what):
+    if a.shape != b.shape:
+        raise ValueError(f"{what}: shape mismatch {tuple(a.shape)} vs {tuple(b.shape)}")
+    if a.numel() == 0:
+        raise ValueError(f"{what}: empty tensors")
+
+
+def focal_loss(preds, targets, alpha: float = 0.25, gamma: float = 2.0):
+    """Binary focal loss on probabilities: mean of -alpha_t (1 - p_t)^gamma log p_t, with
+    p_t = p for targets > 0.5 (else 1 - p), alpha_t = alpha (else 1 - alpha), p clamped to
+    [1e-12, 1 - 1e-12]."""
+    _same_shape(preds, targets, "focal_loss")
+    p = preds.clamp(1e-12, 1 - 1e-12)
+    pos = targets > 0.5
+    pt = torch.where(pos, p, 1 - p)
+    at = torch.where(pos, torch.full_like(p, alpha), torch.full_like(p, 1 - alpha))
+    return (-at * (1 - pt) ** gamma * pt.log()).mean()
+
+
+def dice_loss(preds, targets):
+    """1 - (2 sum(p t) + eps) / (sum p + sum t + eps), eps = 1e-8."""
+    _same_shape(preds, targets, "dice_loss")
+    eps = 1e-8
+    return 1 - (2 * (preds * targets).sum() + eps) / (preds.sum() + targets.sum() + eps)
+
+
+def tversky_loss(preds, targets, alpha: float = 0.5, beta: float = 0.5):
+    """1 - (TP + eps) / (TP + alpha FP + beta FN + eps) with soft counts TP = sum p t,
+    FP = sum p (1 - t), FN = sum (1 - p) t; alpha = beta = 0.5 is the dice loss."""
+    _same_shape(preds, targets, "tversky_loss")
+    eps = 1e-8
+    tp = (preds * targets).sum()
+    fp = (preds * (1 - targets)).sum()
+    fn = ((1 - preds) * targets).sum()
+    return 1 - (tp + eps) / (tp + alpha * fp + beta * fn + eps)
+
+
+def contrastive_loss(e1, e2, labels, margin: float = 1.0):
+    """mean over pairs of y d^2 + (1 - y) max(0, margin - d)^2, d the Euclidean distance of the
+    [batch, dim] embeddings (labels 1 = similar)."""
+    if e1.dim() != 2 or e1.shape != e2.shape or labels.shape != (e1.shape[0],):
+        raise ValueError("contrastive_loss: embeddings must be matching [batch, dim], labels [batch]")
+    d2 = ((e1 - e2) ** 2).sum(1)
+    d = d2.sqrt()
+    y = labels.to(d.dtype)
+    return (y * d2 + (1 - y) * torch.clamp(margin - d, min=0) ** 2).mean()
+
+
+def triplet_loss(anchor, positive, negative, margin: float = 1.0):
+    """mean of max(0, |a - p|^2 - |a - n|^2 + margin) over [batch, dim] triplets (squared distances)."""
+    if anchor.dim() != 2 or anchor.shape != positive.shape or anchor.shape != negative.shape:
+        raise ValueError("triplet_loss: inputs must be matching [batch, dim]")
+    dap = ((anchor - positive) ** 2).sum(1)
+    dan = ((anchor - negative) ** 2).sum(1)
+    return torch.clamp(dap - dan + margin, min=0).mean()
+
+
+class DiceLoss(Loss):
+    def forward(self, p, t):
+        return dice_loss(p, t)
+
+
+class TverskyLoss(Loss):
+    def __init__(self, alpha: float = 0.5, beta: float = 0.5):
+        self.alpha, self.beta = alpha, beta
+
+    def forward(self, p, t):
+        return tversky_loss(p, t, self.alpha, self.beta)
+
+
 def get_loss(name) -> Loss:
     if isinstance(name, Loss):
         return name
@@ -120,6 +196,7 @@ def get_loss(name) -> Loss:
         "mse": MSELoss, "mean_squared_error": MSELoss, "mae": MAELoss, "huber": HuberLoss,
         "crossentropy": CrossEntropyLoss, "cross_entropy": CrossEntropyLoss, "categorical_crossentropy": CrossEntropyLoss,
         "bce": BinaryCrossEntropyLoss, "binary_crossentropy": BinaryCrossEntropyLoss, "focal": FocalLoss,
+        "dice": DiceLoss, "tversky": TverskyLoss, "kl_div": KLDivLoss,
     }
     if n not in table:
         raise ValueError(f"unknown loss {name}")
