@@ -194,6 +194,15 @@ class Evaluator:
         self.as_numpy = False
         return self
 
+    def parallel(self, n_threads: int = 0) -> "Evaluator":
+        """Evaluate independent nodes concurrently: the needed subgraph becomes a task graph on the
+        native dataflow scheduler (a node starts when its inputs are ready). Tensor operations release
+        the interpreter lock, so independent branches overlap (reference: scirs2-autograd/src/parallel,
+        work-stealing graph evaluation)."""
+        self.n_threads = n_threads
+        self._parallel = True
+        return self
+
     def run(self):
         from .ops import OPS
 
@@ -228,11 +237,46 @@ class Evaluator:
             memo[node.id] = v
             return v
 
+        if getattr(self, "_parallel", False):
+            self._run_parallel(ev)
         with torch.enable_grad():
             outs = [ev(t) for t in self.targets]
         if self.as_numpy:
             return [o.detach().cpu().numpy() if isinstance(o, torch.Tensor) else o for o in outs]
         return [o.detach() if isinstance(o, torch.Tensor) else o for o in outs]
+
+
+    def _run_parallel(self, ev) -> None:
+        from ..parallel.primitives import TaskGraph
+
+        def deps(n: Tensor):
+            if n.op == "grad":
+                return list(n.attrs["ys"]) + list(n.attrs["xs"]) + list(n.attrs.get("gys") or [])
+            return list(n.inputs)
+
+        order, seen, stack = [], set(), [(t, False) for t in reversed(self.targets)]
+        while stack:  # iterative post-order DFS: dependencies before dependents
+            n, done = stack.pop()
+            if done:
+                order.append(n)
+                continue
+            if n.id in seen:
+                continue
+            seen.add(n.id)
+            stack.append((n, True))
+            stack.extend((d, False) for d in reversed(deps(n)) if d.id not in seen)
+        tg = TaskGraph(getattr(self, "n_threads", 0))
+
+        def task(n):
+            def body(_):
+                with torch.enable_grad():
+                    ev(n)
+
+            return body
+
+        for n in order:
+            tg.add_task(str(n.id), sorted({str(d.id) for d in deps(n)}), task(n))
+        tg.execute()
 
 
 def _eval_grad(node: Tensor, ev):
