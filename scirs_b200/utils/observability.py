@@ -19,7 +19,8 @@ Tracing
     service reaches the same decision), `RateLimitingSampler` (token bucket),
     `AdaptiveSampler` (probability re-tuned each second toward a target rate).
   * Exporters: in-memory, console, JSON lines, Chrome trace-event JSON
-    (chrome://tracing / Perfetto; pid = rank) and a batching wrapper.
+    (chrome://tracing / Perfetto; pid = rank), OpenTelemetry OTLP/JSON and a
+    batching wrapper.
 
 Audit log
   * `AuditEvent` (category, severity, action, outcome, user / resource ids,
@@ -475,6 +476,57 @@ class ChromeTraceExporter:
         with open(self.path, "w") as f:
             json.dump({"traceEvents": self.events, "displayTimeUnit": "ms"}, f)
         return self.path
+
+
+def _otlp_value(v) -> dict:
+    if isinstance(v, bool):
+        return {"boolValue": v}
+    if isinstance(v, int):
+        return {"intValue": str(v)}  # 64-bit integers are strings in OTLP/JSON
+    if isinstance(v, float):
+        return {"doubleValue": v}
+    return {"stringValue": str(v)}
+
+
+def _otlp_attrs(d: dict) -> list:
+    return [{"key": str(k), "value": _otlp_value(v)} for k, v in d.items()]
+
+
+_OTLP_KIND = {SpanKind.INTERNAL: 1, SpanKind.SERVER: 2, SpanKind.CLIENT: 3, SpanKind.PRODUCER: 4,
+              SpanKind.CONSUMER: 5}
+_OTLP_STATUS = {SpanStatus.UNSET: 0, SpanStatus.OK: 1, SpanStatus.ERROR: 2}
+
+
+class OtlpJsonExporter:
+    """OpenTelemetry OTLP/JSON trace documents (resourceSpans -> scopeSpans -> spans, hex ids, times in
+    Unix nanoseconds as strings, typed attribute values), one document per export appended as a line
+    to `path`, the file format OpenTelemetry collectors' file receivers read. Span metrics become
+    attributes named `metric.<name>`."""
+
+    def __init__(self, path: str, service_name: str = "scirs_b200", resource: dict | None = None):
+        self.path, self.resource = path, {"service.name": service_name, **(resource or {})}
+
+    def document(self, spans: list[Span]) -> dict:
+        out = []
+        for s in spans:
+            attrs = dict(s.attributes)
+            attrs.update({f"metric.{k}": v for k, v in s.metrics.items()})
+            d = {"traceId": s.context.trace_id, "spanId": s.context.span_id, "name": s.name,
+                 "kind": _OTLP_KIND[s.kind], "startTimeUnixNano": str(s.start_ns),
+                 "endTimeUnixNano": str(s.end_ns or s.start_ns), "attributes": _otlp_attrs(attrs),
+                 "events": [{"timeUnixNano": str(e.time_ns), "name": e.name, "attributes": _otlp_attrs(e.attributes)}
+                            for e in s.events],
+                 "status": {"code": _OTLP_STATUS[s.status], **({"message": s.error} if s.error else {})}}
+            if s.context.parent_span_id:
+                d["parentSpanId"] = s.context.parent_span_id
+            out.append(d)
+        return {"resourceSpans": [{"resource": {"attributes": _otlp_attrs(self.resource)},
+                                   "scopeSpans": [{"scope": {"name": "scirs_b200.observability"},
+                                                   "spans": out}]}]}
+
+    def export(self, spans: list[Span]) -> None:
+        with open(self.path, "a") as f:
+            f.write(json.dumps(self.document(spans)) + "\n")
 
 
 class BatchExporter:

@@ -254,3 +254,28 @@ def test_alert_manager_thresholds_and_cooldown(tmp_path):
     log.log_authentication("m", False)
     log.log_authentication("m", False)
     assert got == [("failed_authentication", "m")]
+
+
+def test_otlp_json_exporter(tmp_path):
+    p = tmp_path / "otlp.jsonl"
+    exp = O.OtlpJsonExporter(str(p), "trainer", {"rank": 3})
+    tr = O.TracingSystem(exporter=exp)
+    with tr.start_span("step", kind=O.SpanKind.SERVER, attributes={"step": 7, "lr": 0.1, "ok": True}) as s:
+        s.add_metric("tokens", 2048).add_event("ckpt", {"path": "x"})
+        with tr.start_span("fwd"):
+            pass
+    tr.flush()
+    doc = json.loads(p.read_text().splitlines()[0])
+    rs = doc["resourceSpans"][0]
+    assert {"key": "service.name", "value": {"stringValue": "trainer"}} in rs["resource"]["attributes"]
+    assert {"key": "rank", "value": {"intValue": "3"}} in rs["resource"]["attributes"]
+    spans = {x["name"]: x for x in rs["scopeSpans"][0]["spans"]}
+    st, fwd = spans["step"], spans["fwd"]
+    assert len(st["traceId"]) == 32 and len(st["spanId"]) == 16 and "parentSpanId" not in st
+    assert fwd["parentSpanId"] == st["spanId"] and fwd["traceId"] == st["traceId"]
+    assert st["kind"] == 2 and st["status"] == {"code": 1}
+    assert int(st["endTimeUnixNano"]) >= int(st["startTimeUnixNano"])
+    attrs = {a["key"]: a["value"] for a in st["attributes"]}
+    assert attrs["step"] == {"intValue": "7"} and attrs["lr"] == {"doubleValue": 0.1}
+    assert attrs["ok"] == {"boolValue": True} and attrs["metric.tokens"] == {"doubleValue": 2048.0}
+    assert st["events"][0]["name"] == "ckpt"
