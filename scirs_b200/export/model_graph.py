@@ -27,7 +27,6 @@ import dataclasses
 import json
 import operator
 from pathlib import Path
-from typing import Any
 
 import torch
 import torch.nn as nn

@@ -31,6 +31,7 @@ registry names kernels that run, and user kernels are launched for real.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import dataclasses
 import enum
@@ -199,8 +200,6 @@ class GpuContext:
         return "CUDA (sm_100a)" if self.backend is GpuBackend.CUDA else "CPU"
 
     def _stream_ctx(self):
-        import contextlib
-
         return torch.cuda.stream(self.stream) if self.stream is not None else contextlib.nullcontext()
 
     # buffers and transfers
@@ -398,8 +397,8 @@ def kernel_registry() -> dict[str, dict]:
             if name.startswith("_") or not callable(fn) or isinstance(fn, type):
                 continue
             src = _SOURCES.get(name, "comm.cu" if modname == "_comm" else None)
-            reg[name] = {"module": modname, "source": src, "doc": (fn.__doc__ or "").strip().splitlines()[-1:] or [""]}
-            reg[name]["doc"] = reg[name]["doc"][0]
+            doc_lines = (fn.__doc__ or "").strip().splitlines()
+            reg[name] = {"module": modname, "source": src, "doc": doc_lines[-1] if doc_lines else ""}
     return reg
 
 

@@ -63,7 +63,7 @@ import urllib.parse
 import uuid
 from collections import defaultdict, deque
 from datetime import datetime, timedelta, timezone
-from typing import Any, Callable
+from typing import Callable
 
 import torch
 
