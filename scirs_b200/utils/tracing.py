@@ -10,8 +10,9 @@ per-step JSONL metrics.
   of a step replayed from a CUDA graph are not separated; time eager steps
   (enable_cuda_graph(False)) when a breakdown is wanted.
 * `roofline(...)` relates a measured time to the measured peaks (bf16 GEMM
-  rate and copy bandwidth from MEASURED_PEAKS.json when present, else the
-  pool's earlier measurement) and to NVLink for collectives.
+  rate and copy bandwidth from MEASURED_PEAKS.json when present, else an
+  earlier B200 measurement: 6.65 TB/s, 1.59 PFLOP/s) and to NVLink for
+  collectives.
 * `StepLogger` appends one JSON line per step: loss, device step time
   (maximum over ranks), tokens/s, gradient norm, bytes the step's
   collectives moved per rank, model-FLOP utilisation and the phase times.
@@ -108,7 +109,7 @@ NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this hardware 
 
 def measured_peaks() -> dict:
     """MEASURED_PEAKS.json next to the package when present (with a
-    `source` key saying which), else the earlier pool measurement."""
+    `source` key saying which), else an earlier B200 measurement."""
     path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
                         "MEASURED_PEAKS.json")
     try:
