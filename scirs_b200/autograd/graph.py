@@ -237,25 +237,29 @@ class Evaluator:
             memo[node.id] = v
             return v
 
+        order = self._topo_order()
         if getattr(self, "_parallel", False):
-            self._run_parallel(ev)
+            self._run_parallel(ev, order)
+        else:
+            with torch.enable_grad():
+                for n in order:  # dependencies first: ev never recurses deeply, whatever the graph depth
+                    ev(n)
         with torch.enable_grad():
             outs = [ev(t) for t in self.targets]
         if self.as_numpy:
             return [o.detach().cpu().numpy() if isinstance(o, torch.Tensor) else o for o in outs]
         return [o.detach() if isinstance(o, torch.Tensor) else o for o in outs]
 
+    @staticmethod
+    def _deps(n: Tensor) -> list:
+        if n.op == "grad":
+            return list(n.attrs["ys"]) + list(n.attrs["xs"]) + list(n.attrs.get("gys") or [])
+        return list(n.inputs)
 
-    def _run_parallel(self, ev) -> None:
-        from ..parallel.primitives import TaskGraph
-
-        def deps(n: Tensor):
-            if n.op == "grad":
-                return list(n.attrs["ys"]) + list(n.attrs["xs"]) + list(n.attrs.get("gys") or [])
-            return list(n.inputs)
-
+    def _topo_order(self) -> list:
+        """Every node the targets need, dependencies before dependents (iterative post-order DFS)."""
         order, seen, stack = [], set(), [(t, False) for t in reversed(self.targets)]
-        while stack:  # iterative post-order DFS: dependencies before dependents
+        while stack:
             n, done = stack.pop()
             if done:
                 order.append(n)
@@ -264,7 +268,13 @@ class Evaluator:
                 continue
             seen.add(n.id)
             stack.append((n, True))
-            stack.extend((d, False) for d in reversed(deps(n)) if d.id not in seen)
+            stack.extend((d, False) for d in reversed(self._deps(n)) if d.id not in seen)
+        return order
+
+    def _run_parallel(self, ev, order) -> None:
+        from ..parallel.primitives import TaskGraph
+
+        deps = self._deps
         tg = TaskGraph(getattr(self, "n_threads", 0))
 
         def task(n):
