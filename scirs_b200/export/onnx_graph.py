@@ -216,19 +216,19 @@ def export_graph(outputs, feeds: dict, name: str = "autograd_graph", opset: int 
     values = ev.extend(outputs).run()
 
     order, seen = [], set()
-
-    def visit(n: Tensor):
+    stack: list[tuple[Tensor, bool]] = [(o, False) for o in reversed(outputs)]
+    while stack:  # iterative post-order: inputs before their users, any graph depth
+        n, done = stack.pop()
+        if done:
+            order.append(n)
+            continue
         if n.id in seen:
-            return
+            continue
         seen.add(n.id)
         if n.op == "grad":
             raise NotImplementedError("gradient nodes are not exported; export the forward graph")
-        for i in n.inputs:
-            visit(i)
-        order.append(n)
-
-    for o in outputs:
-        visit(o)
+        stack.append((n, True))
+        stack.extend((i, False) for i in reversed(n.inputs) if i.id not in seen)
 
     em = _Emitter(name, graph.env)
     b = em.b
