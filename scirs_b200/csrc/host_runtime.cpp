@@ -206,9 +206,11 @@ class TaskGraphCore {
         {
           py::gil_scoped_acquire gil;
           try {
-            ok = callback(u).cast<bool>();
+            ok = py::bool_(callback(u));  // any truthy return value counts as success
           } catch (py::error_already_set& e) {
             e.discard_as_unraisable(__func__);
+            ok = false;
+          } catch (const std::exception&) {  // never let an exception leave a worker thread
             ok = false;
           }
         }
@@ -265,6 +267,8 @@ void parallel_for(const py::function& callback, int64_t n, int64_t n_threads) {
         callback(i);
       } catch (py::error_already_set& e) {
         e.discard_as_unraisable(__func__);
+        failed = true;
+      } catch (const std::exception&) {
         failed = true;
       }
     }
