@@ -126,7 +126,12 @@ class BlockManager:
         self._row[seq_id] = self._free_rows.pop()
         self._pages[seq_id] = []
         self._lens[seq_id] = 0
-        self.extend_sequence(seq_id)
+        try:
+            self.extend_sequence(seq_id)
+        except InferenceError:  # no page for it: leave no half-created sequence behind
+            self._free_rows.append(self._row.pop(seq_id))
+            del self._pages[seq_id], self._lens[seq_id]
+            raise
 
     def extend_sequence(self, seq_id: int) -> int:
         pages = self._pages[seq_id]
