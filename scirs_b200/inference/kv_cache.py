@@ -180,6 +180,15 @@ class BlockManager:
         (row, position) of every new token in order."""
         rows, pos = [], []
         bs = self.pool.config.block_size
+        # all or nothing: check the whole batch's page needs before changing any sequence
+        need, lens = {}, dict(self._lens)
+        for s, n in zip(seq_ids, counts):
+            lens[s] += n
+            need[s] = max(0, (lens[s] + bs - 1) // bs - len(self._pages[s]))
+        if any(len(self._pages[s]) + k > self.config.max_pages_per_seq for s, k in need.items()):
+            raise InferenceError("sequence exceeds max_pages_per_seq")
+        if sum(need.values()) > self.pool.free_count():
+            raise InferenceError("KV page pool exhausted")
         for s, n in zip(seq_ids, counts):
             start = self._lens[s]
             while (start + n + bs - 1) // bs > len(self._pages[s]):

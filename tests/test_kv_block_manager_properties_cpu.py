@@ -53,3 +53,18 @@ def test_failed_allocation_releases_the_row():
     bm.free_sequence(0)
     bm.allocate_sequence(1)
     assert bm.active_sequences() == 1
+
+
+def test_reserve_is_all_or_nothing():
+    import torch
+
+    pool = KvPagePool(3, KvPageConfig(block_size=4, num_heads=1, head_dim=8), device="cpu")
+    bm = BlockManager(pool, BlockManagerConfig(max_sequences=2, max_pages_per_seq=4))
+    bm.allocate_sequence(0)
+    bm.allocate_sequence(1)
+    k = torch.ones(16, 1, 8, dtype=torch.bfloat16)
+    with pytest.raises(InferenceError):
+        bm.append([0, 1], [8, 8], k, k)  # needs 2 more pages, 1 is free
+    assert bm.seq_len(0) == 0 and bm.seq_len(1) == 0 and pool.free_count() == 1
+    bm.append([0, 1], [4, 4], k[:8], k[:8])
+    assert bm.seq_len(0) == 4 and bm.seq_len(1) == 4 and pool.free_count() == 1
